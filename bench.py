@@ -1,0 +1,585 @@
+"""Benchmark of the NKIPy -> B200 path on the benchmark configurations.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl nkb|reference]
+
+A step is one execution of the traced kernel body of the workload on its
+full-size seeded synthetic inputs, resident in HBM.  Rank 0 prints one JSON
+line.  Workloads (``--workload``):
+
+  softmax  fp32 (4096, 4096) row softmax                    HBM GB/s
+  rmsnorm  fp32 (16384, 4096) residual add + RMSNorm         HBM GB/s
+  gemm     bf16 8192^3 matmul, fp32 accumulate               TFLOP/s
+  bmm      bf16 32 x 2048^3 batched matmul                   TFLOP/s
+  layer    Llama decoder layer, batch 4 x 2048, TP = N       tokens/s
+
+Timing: W untimed warm-up steps, then K steps each preceded by an L2 flush
+(a 256 MiB device write outside the timed events) and timed with CUDA events
+on the plan's stream; barrier + synchronize on both sides; the max over
+ranks is reported.  ``e2e`` repeats the K steps through the public API with
+pinned host buffers (H2D of every input, execute, D2H of the result).
+``--impl reference`` times the CPU path of the same kernel (the NumPy
+direct call restated in ``oracle/``) on a bounded sample, on rank 0 only.
+"""
+
+import argparse
+import concurrent.futures
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import ml_dtypes  # noqa: E402
+
+BF16 = np.dtype(ml_dtypes.bfloat16)
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+class Workload:
+    name = ""
+    metric = ""
+    unit = ""
+    bound = "hbm"
+    dtype = "f32"
+    scaling = "weak"
+    dominant = ""
+
+    def kernel_and_args(self, rank, world):
+        raise NotImplementedError
+
+    def units_per_step(self, world):
+        raise NotImplementedError
+
+    def dominant_work(self):
+        """Algorithmic bytes (hbm) or flops (tensor) of one dominant launch."""
+        raise NotImplementedError
+
+    def cpu_step(self, threads):
+        """One bounded CPU sample: returns (units processed, description)."""
+        raise NotImplementedError
+
+    def config(self, world):
+        return {}
+
+
+class Softmax(Workload):
+    name, metric, unit, bound, dtype, dominant = "softmax", "HBM GB/s (row softmax)", "GB/s", "hbm", "f32", "softmax_rows"
+    ROWS, COLS = 4096, 4096
+
+    def kernel_and_args(self, rank, world):
+        from nkipy_b200 import workloads as W
+
+        x = np.random.default_rng(100 + rank).standard_normal((self.ROWS, self.COLS), dtype=np.float32)
+        return W.softmax_kernel, (x,), {}
+
+    def units_per_step(self, world):
+        return 2 * self.ROWS * self.COLS * 4 / 1e9
+
+    def dominant_work(self):
+        return 2 * self.ROWS * self.COLS * 4
+
+    def cpu_step(self, threads):
+        from oracle import numpy_ref as O
+
+        rows = 1024
+        x = np.random.default_rng(7).standard_normal((rows, self.COLS), dtype=np.float32)
+        _parallel_rows(O.softmax, [x], threads)
+        return 2 * rows * self.COLS * 4 / 1e9, f"{rows} of {self.ROWS} rows per step"
+
+    def config(self, world):
+        return {"workload": "softmax fp32 (4096, 4096) last axis", "shape": [self.ROWS, self.COLS],
+                "l2": "flushed between steps (256 MiB write)"}
+
+
+class RmsNorm(Workload):
+    name, metric, unit, bound, dtype, dominant = "rmsnorm", "HBM GB/s (residual add + RMSNorm)", "GB/s", "hbm", "f32", "rmsnorm_rows"
+    ROWS, COLS = 16384, 4096
+
+    def kernel_and_args(self, rank, world):
+        from nkipy_b200 import workloads as W
+
+        rng = np.random.default_rng(200 + rank)
+        x = rng.standard_normal((self.ROWS, self.COLS), dtype=np.float32)
+        r = rng.standard_normal((self.ROWS, self.COLS), dtype=np.float32)
+        w = rng.uniform(0.5, 1.5, self.COLS).astype(np.float32)
+        return W.residual_rmsnorm_kernel, (x, r, w), {}
+
+    def units_per_step(self, world):
+        return (3 * self.ROWS * self.COLS * 4 + self.COLS * 4) / 1e9
+
+    def dominant_work(self):
+        return 3 * self.ROWS * self.COLS * 4 + self.COLS * 4
+
+    def cpu_step(self, threads):
+        from oracle import numpy_ref as O
+
+        rows = 2048
+        rng = np.random.default_rng(8)
+        x = rng.standard_normal((rows, self.COLS), dtype=np.float32)
+        r = rng.standard_normal((rows, self.COLS), dtype=np.float32)
+        w = rng.uniform(0.5, 1.5, self.COLS).astype(np.float32)
+        _parallel_rows(lambda a, b: O.residual_rmsnorm(a, b, w, 1e-6), [x, r], threads)
+        return (3 * rows * self.COLS * 4 + self.COLS * 4) / 1e9, f"{rows} of {self.ROWS} rows per step"
+
+    def config(self, world):
+        return {"workload": "residual add + RMSNorm fp32 (16384, 4096), eps 1e-6", "shape": [self.ROWS, self.COLS],
+                "l2": "inputs (805 MB) exceed L2; also flushed between steps"}
+
+
+class Gemm(Workload):
+    name, metric, unit, bound, dtype, dominant = "gemm", "bf16 TFLOP/s (dense matmul)", "TFLOP/s", "tensor", "bf16", "gemm_bf16"
+    N = 8192
+
+    def kernel_and_args(self, rank, world):
+        from nkipy_b200 import workloads as W
+
+        rng = np.random.default_rng(300 + rank)
+        a = (rng.standard_normal((self.N, self.N), dtype=np.float32) * 0.02).astype(BF16)
+        b = (rng.standard_normal((self.N, self.N), dtype=np.float32) * 0.02).astype(BF16)
+        return W.matmul_kernel, (a, b), {}
+
+    def units_per_step(self, world):
+        return 2 * self.N**3 / 1e12
+
+    def dominant_work(self):
+        return 2 * self.N**3
+
+    def cpu_step(self, threads):
+        from oracle import numpy_ref as O
+
+        m = 1024
+        rng = np.random.default_rng(9)
+        a = (rng.standard_normal((m, self.N), dtype=np.float32) * 0.02).astype(BF16)
+        b = (rng.standard_normal((self.N, self.N), dtype=np.float32) * 0.02).astype(BF16)
+        O.matmul(a, b)
+        return 2 * m * self.N * self.N / 1e12, f"{m} of {self.N} rows of A per step (fp32 BLAS, {threads} threads)"
+
+    def config(self, world):
+        return {"workload": "matmul bf16 (8192,8192)@(8192,8192), fp32 acc, bf16 out", "M": self.N, "N": self.N,
+                "K": self.N, "l2": "operands+result 384 MB exceed L2; also flushed between steps"}
+
+
+class Bmm(Gemm):
+    name, metric, dominant = "bmm", "bf16 TFLOP/s (batched matmul)", "gemm_bf16"
+    B, S = 32, 2048
+
+    def kernel_and_args(self, rank, world):
+        from nkipy_b200 import workloads as W
+
+        rng = np.random.default_rng(400 + rank)
+        a = (rng.standard_normal((self.B, self.S, self.S), dtype=np.float32) * 0.02).astype(BF16)
+        b = (rng.standard_normal((self.B, self.S, self.S), dtype=np.float32) * 0.02).astype(BF16)
+        return W.bmm_kernel, (a, b), {}
+
+    def units_per_step(self, world):
+        return 2 * self.B * self.S**3 / 1e12
+
+    def dominant_work(self):
+        return 2 * self.B * self.S**3
+
+    def cpu_step(self, threads):
+        from oracle import numpy_ref as O
+
+        rng = np.random.default_rng(10)
+        a = (rng.standard_normal((2, self.S, self.S), dtype=np.float32) * 0.02).astype(BF16)
+        b = (rng.standard_normal((2, self.S, self.S), dtype=np.float32) * 0.02).astype(BF16)
+        O.matmul(a, b)
+        return 2 * 2 * self.S**3 / 1e12, f"2 of {self.B} batches per step"
+
+    def config(self, world):
+        return {"workload": "batched matmul bf16 bmk,bkn->bmn b=32 m=n=k=2048", "batch": self.B, "M": self.S,
+                "l2": "operands 805 MB exceed L2; also flushed between steps"}
+
+
+class Layer(Workload):
+    name, metric, unit, bound, dtype, dominant = "layer", "TP decoder layer tokens/s", "tokens/s", "tensor", "bf16", "gemm_bf16"
+    scaling = "strong"
+
+    def __init__(self):
+        from nkipy_b200 import workloads as W
+
+        self.shape = W.LayerShape()
+
+    def kernel_and_args(self, rank, world):
+        from nkipy_b200 import workloads as W
+
+        s = self.shape
+        full = W.layer_weights(s, seed=0)
+        shard = W.shard_layer_weights(full, s, rank, world)
+        x = np.random.default_rng(500).standard_normal((s.batch, s.seq, s.hidden), dtype=np.float32).astype(BF16)
+        args, kwargs = W.layer_args(x, shard, s, world)
+        return W.llama_decoder_layer_kernel, args, kwargs
+
+    def units_per_step(self, world):
+        return self.shape.batch * self.shape.seq
+
+    def layer_flops(self):
+        s = self.shape
+        t = s.batch * s.seq
+        hd = s.head_dim
+        f = 2 * t * s.hidden * (s.n_heads + 2 * s.n_kv_heads) * hd + 2 * t * s.n_heads * hd * s.hidden
+        f += 2 * t * s.hidden * 2 * s.ffn + 2 * t * s.ffn * s.hidden
+        f += 0.5 * 4 * s.batch * s.n_heads * s.seq * s.seq * hd
+        return f
+
+    def dominant_work(self):
+        return None  # computed from the per-launch table
+
+    def cpu_step(self, threads):
+        from nkipy_b200 import workloads as W
+        from oracle import numpy_ref as O
+
+        s = W.LayerShape(batch=1, seq=256)
+        full = W.layer_weights(s, seed=0)
+        x = np.random.default_rng(501).standard_normal((1, 256, s.hidden), dtype=np.float32).astype(BF16)
+        O.llama_layer(x, full, s.n_heads, s.n_kv_heads, s.head_dim, s.eps, s.theta)
+        return 256, "1 x 256 tokens of the layer per step"
+
+    def config(self, world):
+        s = self.shape
+        return {"workload": "Llama decoder layer bf16, hidden 4096, 32q/8kv x 128, SwiGLU 14336, RoPE 5e5, causal",
+                "global_batch": s.batch, "seq_len": s.seq, "parallelism": f"tp{world}",
+                "l2": "weights + activations exceed L2"}
+
+
+WORKLOADS = {w.name: w for w in (Softmax, RmsNorm, Gemm, Bmm, Layer)}
+DEFAULT_WORKLOAD = "rmsnorm"
+
+
+def _parallel_rows(fn, arrays, threads):
+    n = arrays[0].shape[0]
+    chunks = max(1, min(threads, n))
+    bounds = np.linspace(0, n, chunks + 1).astype(int)
+    with concurrent.futures.ThreadPoolExecutor(max_workers=chunks) as ex:
+        list(ex.map(lambda i: fn(*[a[bounds[i] : bounds[i + 1]] for a in arrays]), range(chunks)))
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                p = [x.strip() for x in line.split(",")]
+                if len(p) < 9:
+                    continue
+                try:
+                    sm.append(float(p[1]))
+                    mx = max(mx, float(p[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, p[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# reference arm / CPU baseline
+# ---------------------------------------------------------------------------
+def cpu_measure(wl, steps, warmup, threads):
+    for _ in range(warmup):
+        wl.cpu_step(threads)
+    units, t, desc = 0.0, 0.0, ""
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        u, desc = wl.cpu_step(threads)
+        t += time.perf_counter() - t0
+        units += u
+    return units / t, desc, t / steps
+
+
+def run_reference(args, wl, rank, world):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    value, desc, step_s = cpu_measure(wl, args.steps, max(0, min(args.warmup, 1)), threads)
+    line = {
+        "impl": "reference",
+        "metric": wl.metric,
+        "value": value,
+        "unit": wl.unit,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step_s * 1e3,
+        "higher_is_better": True,
+        "scaling": wl.scaling,
+        "vs_baseline": None,
+        "dtype": wl.dtype,
+        "data": "synthetic (seeded numpy), bounded sample",
+        "config": wl.config(world),
+        "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+def profile_traffic(wl):
+    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", f"{wl.dominant}_{wl.name}.md")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            if line.startswith("dram_bytes_per_launch:"):
+                try:
+                    return float(line.split(":", 1)[1].strip().split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+def run_nkb(args, wl, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    os.environ["NKB_DEVICE"] = str(local_rank)
+    torch.cuda.set_device(local_rank)
+    from nkipy_b200.runtime import DeviceKernel, DeviceTensor
+    from nkipy_b200.spike import get_spike_singleton
+
+    spike = get_spike_singleton()
+    fn, np_args, kwargs = wl.kernel_and_args(rank, world)
+    cc = world > 1 and wl.name == "layer"
+    kernel = DeviceKernel.compile_and_load(
+        fn, *np_args, name=f"bench_{wl.name}", cc_enabled=cc, rank_id=rank if cc else None,
+        world_size=world if cc else None, is_spmd=False, **kwargs
+    )
+    in_names = [s["name"] for s in kernel.model_ref.io["inputs"]]
+    arrays = [a for a in np_args if isinstance(a, np.ndarray)]
+    ins = {n: DeviceTensor.from_numpy(a, name=n) for n, a in zip(in_names, arrays)}
+    outs = {t.name: t for t in kernel.allocate_output_tensors()}
+    in_refs = {k: v.tensor_ref for k, v in ins.items()}
+    out_refs = {k: v.tensor_ref for k, v in outs.items()}
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=f"cuda:{local_rank}")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        spike.execute(kernel.model_ref, in_refs, out_refs, use_graph=True)
+    barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    total_ms = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        total_ms += spike.time_execute(kernel.model_ref, in_refs, out_refs, warmup=0, iters=1, use_graph=True)[0]
+    barrier()
+    clocks = sampler.stop()
+    t = torch.tensor([total_ms], dtype=torch.float64, device=f"cuda:{local_rank}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+
+    # per-launch times for the roofline of the dominant kernel
+    step_ms = spike.time_steps(kernel.model_ref, in_refs, out_refs, iters=max(3, min(args.steps, 10)))
+    plan_steps = _plan_steps(kernel.plan_path)
+
+    # end to end through the public API, pinned host memory
+    pinned_in = [torch.empty(a.nbytes, dtype=torch.uint8, pin_memory=True).numpy() for a in arrays]
+    for p, a in zip(pinned_in, arrays):
+        p[:] = np.frombuffer(np.ascontiguousarray(a).tobytes(), dtype=np.uint8)
+    out_specs = kernel.model_ref.io["outputs"]
+    pinned_out = [torch.empty(outs[s["name"]].tensor_ref.size, dtype=torch.uint8, pin_memory=True).numpy() for s in out_specs]
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for n, p in zip(in_names, pinned_in):
+            spike.tensor_write_from_pybuffer(ins[n].tensor_ref, p)
+        spike.execute(kernel.model_ref, in_refs, out_refs, use_graph=True)
+        for s, p in zip(out_specs, pinned_out):
+            spike.tensor_read_to_pybuffer(outs[s["name"]].tensor_ref, p)
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=f"cuda:{local_rank}")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_s = float(te.item())
+
+    units = wl.units_per_step(world)
+    if wl.scaling == "weak":
+        value = world * units * args.steps / (total_ms / 1e3)
+        e2e_value = world * units * args.steps / e2e_s
+    else:
+        value = units * args.steps / (total_ms / 1e3)
+        e2e_value = units * args.steps / e2e_s
+
+    if rank != 0:
+        return
+    peaks, peak_kind = load_peaks()
+    dom = [i for i, s in enumerate(plan_steps) if s["kernel"] == wl.dominant]
+    roof = None
+    if dom:
+        if wl.bound == "hbm":
+            work = wl.dominant_work()
+            dur = sum(step_ms[i] for i in dom) / len(dom)
+            achieved = work / (dur / 1e3) / 1e9
+            peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+            unit = "GB/s"
+        else:
+            flops = [s["flops"] for s in plan_steps]
+            dur = sum(step_ms[i] for i in dom)
+            work = sum(flops[i] for i in dom)
+            achieved = work / (dur / 1e3) / 1e12
+            key = "bf16_tflops" if wl.name != "layer" else "bf16_tflops_sustained"
+            peak = float(peaks.get(key, PEAKS_FALLBACK[key]))
+            unit = "TFLOP/s"
+            work = work / len(dom)
+            dur = dur / len(dom)
+        traffic = profile_traffic(wl)
+        roof = {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+                "traffic": traffic, "peak_source": f"{peak_kind} ({key if wl.bound != 'hbm' else 'hbm_gbs'})",
+                "kernel": wl.dominant, "launch_ms": dur, "work_per_launch": work}
+
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        cv, desc, _ = cpu_measure(wl, 2, 1, threads)
+        cpu = {"value": cv, "unit": wl.unit, "cores": threads, "kind": "port", "sample": desc}
+
+    in_bytes = int(sum(a.nbytes for a in arrays))
+    out_bytes = int(sum(outs[s["name"]].tensor_ref.size for s in out_specs))
+    line = {
+        "metric": wl.metric,
+        "value": value,
+        "unit": wl.unit,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": wl.scaling,
+        "vs_baseline": None,
+        "dtype": wl.dtype,
+        "data": "synthetic (seeded numpy; random-init weights for the layer)",
+        "config": wl.config(world),
+        "roofline": roof,
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes},
+        "gpu_launches": kernel.model_ref.num_launches * args.steps,
+        "launches_per_step": kernel.model_ref.num_launches,
+        "clocks": clocks,
+        "per_launch_ms": {f"{i}:{s['kernel']}": round(ms, 4) for i, (s, ms) in enumerate(zip(plan_steps, step_ms))}
+        if len(step_ms) <= 64 else None,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _plan_steps(path):
+    """Kernel name and flop count of every launch of a plan file."""
+    out = []
+    with open(path) as f:
+        for line in f:
+            if not line.startswith("step "):
+                continue
+            p = line.split()
+            kern = p[1]
+            nb = int(p[2])
+            k = 3 + 2 * nb
+            ni = int(p[k])
+            ints = [int(v) for v in p[k + 1 : k + 1 + ni]]
+            flops = 0
+            if kern == "gemm_bf16":
+                M, N, K, batch = ints[0], ints[1], ints[2], ints[6]
+                flops = 2 * M * N * K * batch
+            elif kern == "gemm_simt":
+                M, N, K, batch = ints[3], ints[4], ints[5], ints[6]
+                flops = 2 * M * N * K * batch
+            out.append({"kernel": kern, "flops": flops})
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="nkb", choices=["nkb", "reference"])
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    wl = WORKLOADS[args.workload]()
+    if args.impl == "reference":
+        return run_reference(args, wl, rank, world)
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local_rank}"))
+    try:
+        run_nkb(args, wl, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

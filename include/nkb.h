@@ -1,0 +1,161 @@
+/*
+ * nkb.h -- C ABI of libnkb.so, the B200 (sm_100a) runtime that replaces
+ * NKIPy's Spike/libnrt layer.
+ *
+ * Every function returns an int status (NKB_OK == 0); on failure
+ * nkb_last_error() gives a thread-local message.  Handles are opaque and
+ * plain pointers/sizes cross the boundary: no torch or Python types.
+ *
+ * Reference interfaces replaced (paths inside shaojiex-aws/nkipy):
+ *   spike/src/include/spike.h:28-86      Spike class (runtime, tensors, execute)
+ *   spike/src/include/nrt_wrapper.h:13-33 NrtRuntime (init/close/core count)
+ *   spike/src/include/tensor.h:14-53     NrtTensor (alloc, slice, read, write)
+ *   spike/src/include/model.h:12-55      NrtModel (load NEFF, load_collectives, execute)
+ *   spike/src/include/sys_trace.h:16-39  SystemTraceSession (device timing)
+ *   spike/src/include/error.h:12-43      SpikeError / NrtError(status)
+ *
+ * A "plan" takes the place of a NEFF: a text launch plan produced by the
+ * Python planner (kernel ids, launch parameters, buffer map); loading it
+ * resolves every kernel and sizes the scratch arena, executing it launches
+ * the kernels in order on one CUDA stream.
+ */
+#ifndef NKB_H
+#define NKB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NKB_API __attribute__((visibility("default")))
+#else
+#define NKB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum nkb_status {
+  NKB_OK = 0,
+  NKB_ERR_INVALID = 1,     /* bad argument (size, index, handle)            */
+  NKB_ERR_CUDA = 2,        /* a CUDA runtime call failed                     */
+  NKB_ERR_PLAN = 3,        /* plan text malformed / unknown kernel           */
+  NKB_ERR_UNSUPPORTED = 4, /* shape/dtype the kernel library does not cover  */
+  NKB_ERR_NCCL = 5,        /* NCCL missing or a NCCL call failed             */
+  NKB_ERR_STATE = 6,       /* runtime not initialised / handle freed         */
+  NKB_ERR_DEVICE = 7       /* a kernel reported an error flag (bounded wait,
+                              bad index); the CUDA context stays usable      */
+};
+
+typedef struct nkb_buf_s *nkb_buf;
+typedef struct nkb_plan_s *nkb_plan;
+typedef struct nkb_comm_s *nkb_comm;
+
+/* ---- runtime (Spike::Spike / close / get_visible_neuron_core_count,
+ *      spike.h:30-42; NrtRuntime nrt_wrapper.h:13-33) ----------------------- */
+NKB_API int nkb_init(int device);
+NKB_API int nkb_shutdown(void);
+NKB_API int nkb_device_count(int *count);
+NKB_API const char *nkb_last_error(void);
+NKB_API const char *nkb_status_str(int status);
+NKB_API int nkb_version(int *major, int *minor);
+
+/* ---- device buffers (Spike::allocate_tensor / slice_from_tensor /
+ *      free_tensor, spike.h:51-58; NrtTensor tensor.h:14-53) --------------- */
+NKB_API int nkb_alloc(size_t bytes, int device, nkb_buf *out);
+NKB_API int nkb_slice(nkb_buf src, size_t offset, size_t bytes, nkb_buf *out);
+NKB_API int nkb_wrap(void *device_ptr, size_t bytes, int device, nkb_buf *out);
+NKB_API int nkb_free(nkb_buf buf);
+NKB_API int nkb_buf_info(nkb_buf buf, size_t *bytes, int *device, void **device_ptr);
+
+/* ---- data movement, bounds-checked (Spike::tensor_write / tensor_read,
+ *      spike.h:59-63; NrtTensor::write/read tensor.cpp:65-105) ------------- */
+NKB_API int nkb_h2d(nkb_buf dst, const void *src, size_t bytes, size_t offset);
+NKB_API int nkb_d2h(nkb_buf src, void *dst, size_t bytes, size_t offset);
+NKB_API int nkb_memset(nkb_buf dst, int value, size_t bytes, size_t offset);
+/* device-to-device copy between buffers (synchronous, bounds-checked) */
+NKB_API int nkb_copy(nkb_buf dst, size_t dst_offset, nkb_buf src, size_t src_offset, size_t bytes);
+
+/* ---- plans (Spike::load_model / unload_model / get_tensor_info,
+ *      spike.h:46-48,69; NrtModel model.h:12-55) ---------------------------- */
+NKB_API int nkb_plan_load(const char *text, size_t len, int device, nkb_plan *out);
+NKB_API int nkb_plan_free(nkb_plan plan);
+NKB_API int nkb_plan_num_io(nkb_plan plan, int *n_inputs, int *n_outputs);
+NKB_API int nkb_plan_io_bytes(nkb_plan plan, int is_output, int index, size_t *bytes);
+NKB_API int nkb_plan_num_consts(nkb_plan plan, int *n_consts);
+NKB_API int nkb_plan_set_const(nkb_plan plan, int const_index, const void *host, size_t bytes);
+NKB_API int nkb_plan_num_launches(nkb_plan plan, int *n_launches);
+NKB_API int nkb_plan_scratch_bytes(nkb_plan plan, size_t *bytes);
+
+/* ---- execution (Spike::execute spike.h:65-68, nrt_execute model.cpp:90-110).
+ * ins/outs are indexed as the plan's io table; stream may be NULL (the
+ * runtime's stream).  use_graph != 0 captures the launch sequence into a
+ * CUDA graph on first use and replays it while the buffers are unchanged. */
+NKB_API int nkb_execute(nkb_plan plan, const nkb_buf *ins, int n_in, const nkb_buf *outs, int n_out,
+                void *stream, int use_graph);
+
+/* Device timing of `iters` back-to-back executes after `warmup` (CUDA events
+ * on the execute stream), replacing SystemTraceSession + nc_exec_running
+ * durations (sys_trace.h:16-39, spike_model.py:42-79).  Writes per-iteration
+ * milliseconds into ms_out[0..iters-1]. */
+NKB_API int nkb_time_execute(nkb_plan plan, const nkb_buf *ins, int n_in, const nkb_buf *outs, int n_out,
+                     int warmup, int iters, int use_graph, float *ms_out);
+NKB_API int nkb_synchronize(void);
+
+/* Per-launch device time: runs the plan `iters` times with CUDA events
+ * between consecutive kernel launches and writes the mean duration of each
+ * launch (milliseconds) into step_ms[0..n_launches-1]. */
+NKB_API int nkb_time_steps(nkb_plan plan, const nkb_buf *ins, int n_in, const nkb_buf *outs, int n_out, int iters,
+                           float *step_ms);
+
+/* Reads and clears the device error flag that a kernel raises when one of
+ * its bounded waits expires (the kernel then frees its resources and exits
+ * instead of hanging; the CUDA context stays usable). */
+NKB_API int nkb_device_error(int *flag);
+
+/* ---- collectives (NrtModel load with nrt_load_collectives(rank, world),
+ *      model.cpp:38-52).  NCCL is resolved at run time (dlopen).  The unique
+ *      id is NKB_COMM_ID_BYTES bytes, produced on rank 0 and broadcast by the
+ *      caller's control plane (torch.distributed in the Python layer). ------ */
+#define NKB_COMM_ID_BYTES 128
+NKB_API int nkb_comm_unique_id(void *id_out);
+NKB_API int nkb_comm_init(const void *id, int rank, int world, int device, nkb_comm *out);
+NKB_API int nkb_comm_free(nkb_comm comm);
+NKB_API int nkb_plan_bind_comm(nkb_plan plan, nkb_comm comm);
+NKB_API int nkb_comm_all_reduce(nkb_comm comm, nkb_buf buf, size_t count, int dtype, void *stream);
+
+/* dtype codes used by plans and nkb_comm_all_reduce */
+enum nkb_dtype {
+  NKB_F32 = 0, NKB_BF16 = 1, NKB_F16 = 2, NKB_I32 = 3, NKB_U32 = 4,
+  NKB_I8 = 5, NKB_U8 = 6, NKB_BOOL = 7, NKB_I16 = 8, NKB_U16 = 9,
+  NKB_F8E4M3 = 10, NKB_F8E5M2 = 11
+};
+
+/* ---- direct kernel entry points (no plan): used by the Python layer's
+ *      micro-benchmarks and by the parity tests.  All pointers are device
+ *      pointers of the current device; stream may be NULL. ----------------- */
+
+/* Row softmax over the last axis: out[r,:] = exp(x[r,:]-max)/sum.  The
+ * composition traced from tests/kernels/softmax.py:7-10. */
+NKB_API int nkb_softmax_rows(const void *x, int x_dtype, void *out, int out_dtype, int64_t rows, int64_t cols,
+                     void *stream);
+
+/* out = (x + r) / sqrt(mean((x + r)^2) + eps) * w, rows of `cols`; r and
+ * sum_out may be NULL.  examples/models/qwen3_embedding/kernels/rmsnorm.py:4-16
+ * with the residual add of examples/models/qwen3/kernels/transformer_layer.py:60. */
+NKB_API int nkb_rmsnorm_rows(const void *x, const void *r, const void *w, void *out, void *sum_out, int dtype,
+                     int w_dtype, int64_t rows, int64_t cols, float eps, void *stream);
+
+/* C[b] = A[b] @ B[b], bf16 inputs, fp32 accumulation, bf16 or fp32 output
+ * (core/ops/linalg.py:15-125, HLO dot).  A is (M,K) row-major with row
+ * stride lda, B is (K,N) row-major with row stride ldb, C is (M,N) with row
+ * stride ldc; batch strides in elements (0 = broadcast). */
+NKB_API int nkb_gemm_bf16(const void *A, const void *B, void *C, int c_dtype, int64_t M, int64_t N, int64_t K,
+                  int64_t lda, int64_t ldb, int64_t ldc, int64_t batch, int64_t sA, int64_t sB, int64_t sC,
+                  void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NKB_H */

@@ -1,0 +1,5 @@
+"""Backward-compatible entry points (reference: ``core/tensor_apis.py``)."""
+
+from nkipy_b200.core.ops import constant, full, rms_norm, softmax, topk, zeros
+
+__all__ = ["constant", "topk", "rms_norm", "softmax", "zeros", "full"]

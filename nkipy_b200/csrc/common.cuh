@@ -1,0 +1,130 @@
+// Shared definitions of libnkb: error state, dtype helpers, the launch-step
+// record that plans are decoded into, and the kernel registry.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/nkb.h"
+
+namespace nkb {
+
+// ---- error reporting ------------------------------------------------------
+void set_error(const std::string &msg);
+int fail(int status, const std::string &msg);
+
+#define NKB_CUDA_TRY(expr)                                                              \
+  do {                                                                                  \
+    cudaError_t _e = (expr);                                                            \
+    if (_e != cudaSuccess)                                                              \
+      return ::nkb::fail(NKB_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
+  } while (0)
+
+#define NKB_CHECK(cond, status, msg)       \
+  do {                                     \
+    if (!(cond)) return ::nkb::fail(status, msg); \
+  } while (0)
+
+// ---- dtypes -----------------------------------------------------------------
+inline int dtype_size(int dt) {
+  switch (dt) {
+    case NKB_F32: case NKB_I32: case NKB_U32: return 4;
+    case NKB_BF16: case NKB_F16: case NKB_I16: case NKB_U16: return 2;
+    case NKB_I8: case NKB_U8: case NKB_BOOL: case NKB_F8E4M3: case NKB_F8E5M2: return 1;
+    default: return 0;
+  }
+}
+inline bool dtype_is_float(int dt) {
+  return dt == NKB_F32 || dt == NKB_BF16 || dt == NKB_F16 || dt == NKB_F8E4M3 || dt == NKB_F8E5M2;
+}
+
+// Load one element of storage type `dt` at p[i] as raw 32-bit register bits:
+// float dtypes widen to an fp32 bit pattern, integers to int32, bool to 0/1.
+__device__ __forceinline__ uint32_t load_as_reg(const void *p, int64_t i, int dt) {
+  switch (dt) {
+    case NKB_F32: return __float_as_uint(static_cast<const float *>(p)[i]);
+    case NKB_BF16: return __float_as_uint(__bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]));
+    case NKB_F16: return __float_as_uint(__half2float(static_cast<const __half *>(p)[i]));
+    case NKB_I32: case NKB_U32: return static_cast<const uint32_t *>(p)[i];
+    case NKB_I16: return static_cast<uint32_t>(static_cast<int32_t>(static_cast<const int16_t *>(p)[i]));
+    case NKB_U16: return static_cast<const uint16_t *>(p)[i];
+    case NKB_I8: return static_cast<uint32_t>(static_cast<int32_t>(static_cast<const int8_t *>(p)[i]));
+    case NKB_U8: return static_cast<const uint8_t *>(p)[i];
+    case NKB_BOOL: return static_cast<const uint8_t *>(p)[i] ? 1u : 0u;
+    default: return 0u;
+  }
+}
+
+__device__ __forceinline__ void store_from_reg(void *p, int64_t i, int dt, uint32_t v) {
+  switch (dt) {
+    case NKB_F32: static_cast<float *>(p)[i] = __uint_as_float(v); break;
+    case NKB_BF16: static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(__uint_as_float(v)); break;
+    case NKB_F16: static_cast<__half *>(p)[i] = __float2half_rn(__uint_as_float(v)); break;
+    case NKB_I32: case NKB_U32: static_cast<uint32_t *>(p)[i] = v; break;
+    case NKB_I16: case NKB_U16: static_cast<uint16_t *>(p)[i] = static_cast<uint16_t>(v); break;
+    case NKB_I8: case NKB_U8: static_cast<uint8_t *>(p)[i] = static_cast<uint8_t>(v); break;
+    case NKB_BOOL: static_cast<uint8_t *>(p)[i] = v ? 1 : 0; break;
+    default: break;
+  }
+}
+
+// ---- launch steps -------------------------------------------------------------
+// One kernel launch of a plan, after buffer resolution: device pointers (with
+// byte offsets applied), integer and float parameters, and the stream.
+struct Step {
+  std::string kernel;
+  std::vector<int> buf_ids;        // plan buffer id per pointer argument
+  std::vector<int64_t> buf_offsets;  // byte offset inside that buffer
+  std::vector<int64_t> ints;
+  std::vector<float> floats;
+};
+
+struct LaunchArgs {
+  const Step *step;
+  void *const *ptrs;  // resolved device pointers, one per buf_ids entry
+  cudaStream_t stream;
+  void *comm;         // bound NCCL communicator (collective steps only)
+  int device;
+};
+
+using LaunchFn = int (*)(const LaunchArgs &);
+// Validation at plan load: returns NKB_OK or fails with a message.
+using CheckFn = int (*)(const Step &);
+
+struct KernelEntry {
+  const char *name;
+  LaunchFn launch;
+  CheckFn check;
+};
+
+// Registry filled by each kernel translation unit (static initialisers).
+void register_kernel(const char *name, LaunchFn fn, CheckFn check);
+const KernelEntry *find_kernel(const std::string &name);
+
+struct Registrar {
+  Registrar(const char *name, LaunchFn fn, CheckFn check) { register_kernel(name, fn, check); }
+};
+
+#define NKB_CAT2(a, b) a##b
+#define NKB_CAT(a, b) NKB_CAT2(a, b)
+#define NKB_REGISTER_KERNEL(name, fn, check) \
+  static ::nkb::Registrar NKB_CAT(_nkb_reg_, __LINE__)(name, fn, check)
+
+// Kernel launch error check (kernel launches report via cudaGetLastError).
+inline int launch_status(const char *what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(NKB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  return NKB_OK;
+}
+
+int num_sms(int device);
+
+// NCCL all-reduce entry (implemented in the runtime, which owns the dlopen).
+int comm_all_reduce(void *comm, const void *src, void *dst, size_t count, int dtype, cudaStream_t stream);
+
+}  // namespace nkb

@@ -1,0 +1,313 @@
+// Fused elementwise chains: one launch evaluates a whole group of traced
+// elementwise nodes (add/multiply/exponential/compare/select/convert ...,
+// core/ops/binary.py + unary.py + indexing.py:20-110 of the reference) over
+// the output's index space.
+//
+// Every operand is a strided view of a device buffer (offset + per-axis
+// element strides), so broadcast (stride 0), transpose, slice and reshape of
+// a dense buffer cost no copy: they are folded into the view by the planner.
+// The group's arithmetic is a short register program decoded per launch from
+// the kernel parameters (a fixed kernel, not generated code).  Registers hold
+// 32-bit values: fp32 for every float dtype, int32 for integers and bools.
+// Results of bf16/fp16-typed nodes are rounded to that type after each node
+// (program op RBF/RF16), matching NumPy's per-op rounding.
+//
+// Hot path: when every operand is either dense over the output or a scalar,
+// the offsets are affine in the flat index and each thread works on VEC
+// consecutive elements with no index decomposition.
+
+#include <math.h>
+
+#include "common.cuh"
+
+namespace nkb {
+namespace ew {
+
+constexpr int kMaxIn = 8;
+constexpr int kMaxRank = 6;
+constexpr int kMaxInstr = 64;
+constexpr int kRegs = 24;
+constexpr int kVec = 4;
+
+enum Opcode : uint8_t {
+  NOP = 0, LD = 1, CF = 2, CI = 3, IOTA = 4,
+  FADD = 10, FSUB, FMUL, FDIV, FPOW, FMAX, FMIN, FATAN2, FREM,
+  FNEG = 20, FABS, FEXP, FLOG, FSQRT, FRSQRT, FTANH, FSIN, FCOS, FFLOOR, FCEIL, FSIGN, RBF, RF16, FRCP,
+  FEQ = 40, FNE, FLT, FLE, FGT, FGE,
+  IADD = 50, ISUB, IMUL, IDIV, IMAX, IMIN, IAND, IOR, IXOR, IREM,
+  ISHL = 64, ISHR = 65,
+  INEG = 60, IABS, INOT, ISIGN,
+  IEQ = 70, INE, ILT, ILE, IGT, IGE, ULT, ULE, UGT, UGE, UDIV, UMAX, UMIN, UREM,
+  SEL = 90,
+  F2I = 100, I2F, U2F, F2U, INZ, FNZ
+};
+
+struct Instr {
+  uint8_t op, dst, a, b, c, pad0, pad1, pad2;
+  uint32_t imm;
+};
+
+struct Params {
+  int n_in, rank, n_instr, out_dtype, out_reg, contig;
+  int64_t n;
+  int64_t shape[kMaxRank];
+  void *out;
+  int64_t out_off;
+  int64_t out_strides[kMaxRank];
+  const void *in[kMaxIn];
+  int in_dtype[kMaxIn];
+  int64_t in_off[kMaxIn];
+  int64_t in_strides[kMaxIn][kMaxRank];
+  Instr prog[kMaxInstr];
+};
+
+__device__ __forceinline__ float rnd_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ float rnd_f16(float x) { return __half2float(__float2half_rn(x)); }
+__device__ __forceinline__ float fsignf(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : x); }
+
+// Executes the program for VEC lanes whose per-input element offsets and
+// per-axis indices are given.
+__device__ __forceinline__ void run_program(const Params &p, const int64_t (*off)[kVec], const int64_t (*idx)[kVec],
+                                            int nlanes, uint32_t (*r)[kVec]) {
+  for (int pc = 0; pc < p.n_instr; ++pc) {
+    const Instr I = p.prog[pc];
+    uint32_t *d = r[I.dst];
+    const uint32_t *A = r[I.a];
+    const uint32_t *B = r[I.b];
+    const uint32_t *C = r[I.c];
+#define LANES for (int v = 0; v < kVec; ++v)
+#define FA __uint_as_float(A[v])
+#define FB __uint_as_float(B[v])
+#define IA static_cast<int32_t>(A[v])
+#define IB static_cast<int32_t>(B[v])
+#define SETF(x) d[v] = __float_as_uint(x)
+#define SETI(x) d[v] = static_cast<uint32_t>(x)
+    switch (I.op) {
+      case LD:
+        LANES if (v < nlanes) d[v] = load_as_reg(p.in[I.a], off[I.a][v], p.in_dtype[I.a]);
+        break;
+      case CF: case CI: LANES d[v] = I.imm; break;
+      case IOTA: LANES SETI(static_cast<int32_t>(idx[I.a][v])); break;
+      case FADD: LANES SETF(FA + FB); break;
+      case FSUB: LANES SETF(FA - FB); break;
+      case FMUL: LANES SETF(FA * FB); break;
+      case FDIV: LANES SETF(FA / FB); break;
+      case FPOW: LANES SETF(powf(FA, FB)); break;
+      case FMAX: LANES SETF((FA != FA || FB != FB) ? __int_as_float(0x7fc00000) : fmaxf(FA, FB)); break;
+      case FMIN: LANES SETF((FA != FA || FB != FB) ? __int_as_float(0x7fc00000) : fminf(FA, FB)); break;
+      case FATAN2: LANES SETF(atan2f(FA, FB)); break;
+      case FREM: LANES SETF(fmodf(FA, FB)); break;
+      case FNEG: LANES SETF(-FA); break;
+      case FABS: LANES SETF(fabsf(FA)); break;
+      case FEXP: LANES SETF(expf(FA)); break;
+      case FLOG: LANES SETF(logf(FA)); break;
+      case FSQRT: LANES SETF(sqrtf(FA)); break;
+      case FRSQRT: LANES SETF(1.0f / sqrtf(FA)); break;
+      case FTANH: LANES SETF(tanhf(FA)); break;
+      case FSIN: LANES SETF(sinf(FA)); break;
+      case FCOS: LANES SETF(cosf(FA)); break;
+      case FFLOOR: LANES SETF(floorf(FA)); break;
+      case FCEIL: LANES SETF(ceilf(FA)); break;
+      case FSIGN: LANES SETF(fsignf(FA)); break;
+      case RBF: LANES SETF(rnd_bf16(FA)); break;
+      case RF16: LANES SETF(rnd_f16(FA)); break;
+      case FRCP: LANES SETF(1.0f / FA); break;
+      case FEQ: LANES SETI(FA == FB); break;
+      case FNE: LANES SETI(FA != FB); break;
+      case FLT: LANES SETI(FA < FB); break;
+      case FLE: LANES SETI(FA <= FB); break;
+      case FGT: LANES SETI(FA > FB); break;
+      case FGE: LANES SETI(FA >= FB); break;
+      case IADD: LANES SETI(A[v] + B[v]); break;
+      case ISUB: LANES SETI(A[v] - B[v]); break;
+      case IMUL: LANES SETI(A[v] * B[v]); break;
+      case IDIV: LANES SETI(IB == 0 ? -1 : (IA == INT32_MIN && IB == -1 ? IA : IA / IB)); break;
+      case IREM: LANES SETI(IB == 0 ? IA : (IB == -1 ? 0 : IA % IB)); break;
+      case IMAX: LANES SETI(max(IA, IB)); break;
+      case IMIN: LANES SETI(min(IA, IB)); break;
+      case IAND: LANES SETI(A[v] & B[v]); break;
+      case IOR: LANES SETI(A[v] | B[v]); break;
+      case IXOR: LANES SETI(A[v] ^ B[v]); break;
+      case ISHL: LANES SETI(B[v] < 32 ? A[v] << B[v] : 0u); break;
+      case ISHR: LANES SETI(B[v] < 32 ? (uint32_t)(IA >> B[v]) : (IA < 0 ? 0xffffffffu : 0u)); break;
+      case INEG: LANES SETI(-IA); break;
+      case IABS: LANES SETI(IA < 0 ? -IA : IA); break;
+      case INOT: LANES SETI(~A[v]); break;
+      case ISIGN: LANES SETI(IA > 0 ? 1 : (IA < 0 ? -1 : 0)); break;
+      case IEQ: LANES SETI(A[v] == B[v]); break;
+      case INE: LANES SETI(A[v] != B[v]); break;
+      case ILT: LANES SETI(IA < IB); break;
+      case ILE: LANES SETI(IA <= IB); break;
+      case IGT: LANES SETI(IA > IB); break;
+      case IGE: LANES SETI(IA >= IB); break;
+      case ULT: LANES SETI(A[v] < B[v]); break;
+      case ULE: LANES SETI(A[v] <= B[v]); break;
+      case UGT: LANES SETI(A[v] > B[v]); break;
+      case UGE: LANES SETI(A[v] >= B[v]); break;
+      case UDIV: LANES SETI(B[v] == 0 ? 0xffffffffu : A[v] / B[v]); break;
+      case UREM: LANES SETI(B[v] == 0 ? A[v] : A[v] % B[v]); break;
+      case UMAX: LANES SETI(max(A[v], B[v])); break;
+      case UMIN: LANES SETI(min(A[v], B[v])); break;
+      case SEL: LANES d[v] = A[v] ? B[v] : C[v]; break;
+      case F2I: {
+        // float -> int32, truncating; NaN -> 0, saturating at the int32 range
+        LANES {
+          float f = FA;
+          int32_t x = (f != f) ? 0 : (f >= 2147483648.f ? INT32_MAX : (f <= -2147483648.f ? INT32_MIN : (int32_t)f));
+          SETI(x);
+        }
+        break;
+      }
+      case F2U: {
+        LANES {
+          float f = FA;
+          uint32_t x = (f != f || f <= 0.f) ? 0u : (f >= 4294967296.f ? 0xffffffffu : (uint32_t)f);
+          SETI(x);
+        }
+        break;
+      }
+      case I2F: LANES SETF((float)IA); break;
+      case U2F: LANES SETF((float)A[v]); break;
+      case INZ: LANES SETI(A[v] != 0u); break;
+      case FNZ: LANES SETI(FA != 0.f); break;
+      default: break;
+    }
+#undef LANES
+#undef FA
+#undef FB
+#undef IA
+#undef IB
+#undef SETF
+#undef SETI
+  }
+}
+
+__global__ void __launch_bounds__(256) ew_kernel(const __grid_constant__ Params p) {
+  uint32_t r[kRegs][kVec];
+  int64_t off[kMaxIn][kVec];
+  int64_t idx[kMaxRank][kVec];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * kVec;
+  for (int64_t base = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * kVec; base < p.n; base += stride) {
+    const int nl = (p.n - base) < kVec ? (int)(p.n - base) : kVec;
+    int64_t oo[kVec];
+    if (p.contig) {
+      // every operand is dense over the output or a scalar
+#pragma unroll
+      for (int v = 0; v < kVec; ++v) {
+        const int64_t i = base + v;
+        for (int k = 0; k < p.n_in; ++k) off[k][v] = p.in_off[k] + (p.in_strides[k][p.rank - 1] ? i : 0);
+        oo[v] = p.out_off + i;
+        for (int d = 0; d < p.rank; ++d) idx[d][v] = 0;
+      }
+      // axis indices are only needed by IOTA; derive them when the program uses it
+      for (int pc = 0; pc < p.n_instr; ++pc)
+        if (p.prog[pc].op == IOTA) {
+#pragma unroll
+          for (int v = 0; v < kVec; ++v) {
+            int64_t rem = base + v;
+            for (int d = p.rank - 1; d >= 0; --d) {
+              idx[d][v] = rem % p.shape[d];
+              rem /= p.shape[d];
+            }
+          }
+          break;
+        }
+    } else {
+#pragma unroll
+      for (int v = 0; v < kVec; ++v) {
+        int64_t rem = base + v;
+        if (rem >= p.n) rem = p.n - 1;
+        int64_t o = p.out_off;
+        for (int k = 0; k < p.n_in; ++k) off[k][v] = p.in_off[k];
+        for (int d = p.rank - 1; d >= 0; --d) {
+          const int64_t s = p.shape[d];
+          const int64_t q = rem / s;
+          const int64_t id = rem - q * s;
+          rem = q;
+          idx[d][v] = id;
+          o += id * p.out_strides[d];
+          for (int k = 0; k < p.n_in; ++k) off[k][v] += id * p.in_strides[k][d];
+        }
+        oo[v] = o;
+      }
+    }
+    run_program(p, off, idx, nl, r);
+#pragma unroll
+    for (int v = 0; v < kVec; ++v)
+      if (v < nl) store_from_reg(p.out, oo[v], p.out_dtype, r[p.out_reg][v]);
+  }
+}
+
+// Step layout ("ew"):
+//   ptrs:  out, in_0 .. in_{n_in-1}
+//   ints:  n_in rank n_instr out_dtype out_reg contig n
+//          shape[rank] out_off out_strides[rank]
+//          per input: dtype off strides[rank]
+//          per instr: op dst a b c imm_bits
+int check(const Step &s) {
+  if (s.ints.size() < 7) return fail(NKB_ERR_PLAN, "ew: short parameter list");
+  const int64_t n_in = s.ints[0], rank = s.ints[1], n_instr = s.ints[2];
+  if (n_in < 0 || n_in > kMaxIn) return fail(NKB_ERR_UNSUPPORTED, "ew: too many inputs");
+  if (rank < 1 || rank > kMaxRank) return fail(NKB_ERR_UNSUPPORTED, "ew: rank out of range");
+  if (n_instr < 1 || n_instr > kMaxInstr) return fail(NKB_ERR_UNSUPPORTED, "ew: program too long");
+  const size_t want = 7 + rank + 1 + rank + n_in * (2 + rank) + n_instr * 6;
+  if (s.ints.size() != want || s.buf_ids.size() != (size_t)(1 + n_in))
+    return fail(NKB_ERR_PLAN, "ew: parameter count mismatch");
+  const int64_t *q = s.ints.data() + 7 + rank + 1 + rank + n_in * (2 + rank);
+  for (int i = 0; i < n_instr; ++i, q += 6) {
+    if (q[1] >= kRegs || q[2] >= kRegs || q[3] >= kRegs || q[4] >= kRegs || q[1] < 0)
+      return fail(NKB_ERR_PLAN, "ew: register index out of range");
+    if (q[0] == LD && (q[2] < 0 || q[2] >= n_in)) return fail(NKB_ERR_PLAN, "ew: load of a missing input");
+    if (q[0] == IOTA && (q[2] < 0 || q[2] >= rank)) return fail(NKB_ERR_PLAN, "ew: iota axis out of range");
+  }
+  if (s.ints[4] < 0 || s.ints[4] >= kRegs) return fail(NKB_ERR_PLAN, "ew: output register out of range");
+  return NKB_OK;
+}
+
+int launch(const LaunchArgs &a) {
+  const Step &s = *a.step;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  const int64_t *q = s.ints.data();
+  p.n_in = (int)q[0];
+  p.rank = (int)q[1];
+  p.n_instr = (int)q[2];
+  p.out_dtype = (int)q[3];
+  p.out_reg = (int)q[4];
+  p.contig = (int)q[5];
+  p.n = q[6];
+  q += 7;
+  for (int d = 0; d < p.rank; ++d) p.shape[d] = *q++;
+  p.out_off = *q++;
+  for (int d = 0; d < p.rank; ++d) p.out_strides[d] = *q++;
+  p.out = a.ptrs[0];
+  for (int k = 0; k < p.n_in; ++k) {
+    p.in[k] = a.ptrs[1 + k];
+    p.in_dtype[k] = (int)*q++;
+    p.in_off[k] = *q++;
+    for (int d = 0; d < p.rank; ++d) p.in_strides[k][d] = *q++;
+  }
+  for (int i = 0; i < p.n_instr; ++i) {
+    Instr &I = p.prog[i];
+    I.op = (uint8_t)q[0];
+    I.dst = (uint8_t)q[1];
+    I.a = (uint8_t)q[2];
+    I.b = (uint8_t)q[3];
+    I.c = (uint8_t)q[4];
+    I.imm = (uint32_t)q[5];
+    q += 6;
+  }
+  if (p.n == 0) return NKB_OK;
+  const int threads = 256;
+  int64_t blocks = (p.n + (int64_t)threads * kVec - 1) / ((int64_t)threads * kVec);
+  const int64_t cap = (int64_t)num_sms(a.device) * 16;
+  if (blocks > cap) blocks = cap;
+  ew_kernel<<<(unsigned)blocks, threads, 0, a.stream>>>(p);
+  return launch_status("ew_kernel");
+}
+
+}  // namespace ew
+
+NKB_REGISTER_KERNEL("ew", ew::launch, ew::check);
+
+}  // namespace nkb

@@ -1,0 +1,557 @@
+// bf16 GEMM on the 5th-generation tensor cores (sm_100a): the HLO ``dot`` of
+// NKIPy's matmul (reference core/ops/linalg.py:15-125) for bf16 operands with
+// fp32 accumulation.
+//
+// Structure (one CTA per SM, persistent over output tiles of 128 x 256):
+//   warp 0      TMA producer: 128B-swizzled A (128 x 64) and B (64 x 256)
+//               tiles into a 4-stage shared-memory ring (mbarrier complete_tx);
+//   warp 1      allocates 512 TMEM columns, then one lane issues
+//               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16) and
+//               tcgen05.commit to release smem stages / publish accumulators;
+//   warps 2..5  epilogue: tcgen05.ld 32x32b.x32 of their TMEM lane quadrant,
+//               fp32 -> bf16/fp32, 16-byte stores.
+// Two TMEM accumulators (2 x 256 columns) let the epilogue of tile i overlap
+// the main loop of tile i+1.  No cluster multicast is used anywhere: each CTA
+// fetches its own tiles and L2 provides the reuse, so the same kernel is safe
+// on multi-GPU runs.
+//
+// A may be K-major (row-major M x K) or M-major (stored K x M); B may be
+// N-major (row-major K x N) or K-major (stored N x K).  Tensor maps are 3-D
+// (inner, outer, batch).  Every mbarrier wait is bounded by a clock budget;
+// on expiry the CTA raises a device error flag, stops issuing work, waits
+// (bounded) for its in-flight copies, frees its TMEM and exits.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace nkb {
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
+constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 1024 /*barriers*/ + 1024 /*align*/;
+constexpr int TMEM_COLS = 512;
+constexpr int THREADS = 192;
+constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
+
+__device__ int g_device_error = 0;  // set when a bounded wait expires
+
+struct Args {
+  void *C;
+  int64_t M, N, K, ldc, sC, batch;
+  int c_f32, a_mn_major, b_k_major;
+  int tiles_m, tiles_n;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false when the budget ran out or another role aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > WAIT_CYCLES) {
+      *abort_flag = 1;
+      atomicExch(&g_device_error, 1);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor, SWIZZLE_128B, sm_100 version field.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= 1ull << 46;  // descriptor version (Blackwell)
+  d |= 2ull << 61;  // SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum));
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t *r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Instruction descriptor, kind::f16: D fp32, A/B bf16, M=128, N=256.
+__host__ __device__ constexpr uint32_t make_idesc(int a_mn_major, int b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn_major << 15) | ((uint32_t)b_mn_major << 16) |
+         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tile_coords(int t, const Args &a, int &bm, int &bn, int &bb) {
+  const int per_batch = a.tiles_m * a.tiles_n;
+  bb = t / per_batch;
+  int r = t - bb * per_batch;
+  // group 16 M-tiles together so a wave of CTAs shares B column panels in L2
+  constexpr int GROUP = 16;
+  const int group_span = GROUP * a.tiles_n;
+  const int g = r / group_span;
+  const int first_m = g * GROUP;
+  const int gsize = min(a.tiles_m - first_m, GROUP);
+  const int within = r - g * group_span;
+  bm = first_m + within % gsize;
+  bn = within / gsize;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Args args) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sA = smem;
+  uint8_t *sB = smem + STAGES * A_STAGE_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + STAGES * B_STAGE_BYTES);
+  uint64_t *full = bars;                  // [STAGES]
+  uint64_t *empty = bars + STAGES;        // [STAGES]
+  uint64_t *acc_full = bars + 2 * STAGES;   // [2]
+  uint64_t *acc_empty = bars + 2 * STAGES + 2;  // [2]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int num_tiles = args.tiles_m * args.tiles_n * (int)args.batch;
+  const int k_blocks = (int)((args.K + BK - 1) / BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int bm, bn, bb;
+        tile_coords(t, args, bm, bn, bb);
+        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], A_STAGE_BYTES + B_STAGE_BYTES);
+          uint8_t *a_dst = sA + s * A_STAGE_BYTES;
+          uint8_t *b_dst = sB + s * B_STAGE_BYTES;
+          if (!args.a_mn_major) {
+            tma_load_3d(a_dst, &map_a, &full[s], kb * BK, bm * BM, bb);
+          } else {
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_3d(a_dst + j * (64 * BK * 2), &map_a, &full[s], bm * BM + j * 64, kb * BK, bb);
+          }
+          if (args.b_k_major) {
+            tma_load_3d(b_dst, &map_b, &full[s], kb * BK, bn * BN, bb);
+          } else {
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_3d(b_dst + j * (64 * BK * 2), &map_b, &full[s], bn * BN + j * 64, kb * BK, bb);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(args.a_mn_major, args.b_k_major ? 0 : 1);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_ph = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * A_STAGE_BYTES);
+          const uint32_t b_addr = smem_u32(sB + s * B_STAGE_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // K-major: advance 16 elements = 32 bytes inside the 128B swizzle row;
+            // MN-major: advance 16 K-rows = 2048 bytes.
+            const uint64_t da = args.a_mn_major ? smem_desc(a_addr + k * 2048, 64 * BK * 2, 1024)
+                                                : smem_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t db = args.b_k_major ? smem_desc(b_addr + k * 32, 16, 1024)
+                                               : smem_desc(b_addr + k * 2048, 64 * BK * 2, 1024);
+            umma_f16(d_tmem, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);  // stage s free once these MMAs have read it
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);  // accumulator ready for the epilogue
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quad = warp % 4;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      int bm, bn, bb;
+      tile_coords(t, args, bm, bn, bb);
+      const int acc = local & 1;
+      const uint32_t acc_ph = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[acc], acc_ph, abort_flag)) break;
+      tc_fence_after();
+      const int64_t row = (int64_t)bm * BM + row_in_tile;
+      const int64_t col0 = (int64_t)bn * BN;
+      const bool row_ok = row < args.M;
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
+        const int64_t col = col0 + c * 32;
+        if (!row_ok || col >= args.N) continue;
+        const bool full_chunk = col + 32 <= args.N;
+        if (args.c_f32) {
+          float *dst = static_cast<float *>(args.C) + bb * args.sC + row * args.ldc + col;
+          if (full_chunk && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<uint4 *>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+          } else {
+            for (int j = 0; j < 32 && col + j < args.N; ++j) dst[j] = __uint_as_float(r[j]);
+          }
+        } else {
+          __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(args.C) + bb * args.sC + row * args.ldc + col;
+          uint32_t packed[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+            packed[j] = *reinterpret_cast<uint32_t *>(&h);
+          }
+          if (full_chunk && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              *reinterpret_cast<uint4 *>(dst + 2 * j) = make_uint4(packed[j], packed[j + 1], packed[j + 2], packed[j + 3]);
+          } else {
+            for (int j = 0; j < 32 && col + j < args.N; ++j)
+              dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  // teardown: every role has left its loop (normally or after an abort)
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag && warp == 0 && lane == 0) {
+    // bounded drain of copies that may still be landing in shared memory
+    const long long t0 = clock64();
+    while (clock64() - t0 < 2000000) {
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+static int make_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t batch,
+                    uint64_t outer_stride_elems, uint64_t batch_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  auto enc = get_encode();
+  if (!enc) return fail(NKB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t gdim[3] = {inner, outer, batch};
+  cuuint64_t gstride[2] = {outer_stride_elems * 2, (batch > 1 ? batch_stride_elems : outer * outer_stride_elems) * 2};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), gdim, gstride, box, estride,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NKB_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return NKB_OK;
+}
+
+// Can the tcgen05 path take these operands?  (16-byte aligned bases and
+// strides, as TMA requires; batch strides of broadcast operands are 0.)
+bool tc_eligible(const void *A, const void *B, int64_t lda, int64_t ldb, int64_t sA, int64_t sB, int64_t batch) {
+  auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al(A) || !al(B)) return false;
+  if (lda % 8 || ldb % 8) return false;
+  if (batch > 1 && ((sA % 8) || (sB % 8))) return false;
+  return true;
+}
+
+// C[b] = op(A[b]) @ op(B[b]).  a_mn_major: A stored K x M (lda = row stride of
+// that storage); b_k_major: B stored N x K.
+int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t N, int64_t K, int64_t lda,
+            int64_t ldb, int64_t ldc, int64_t batch, int64_t sA, int64_t sB, int64_t sC, int a_mn_major, int b_k_major,
+            cudaStream_t st, int device) {
+  if (M == 0 || N == 0 || batch == 0) return NKB_OK;
+  if (K == 0) return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: K == 0 takes the strided path");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(NKB_ERR_UNSUPPORTED, "gemm: dims exceed int32");
+  // broadcast operands (batch stride 0) reuse batch index 0 via a size-1 batch dim
+  const uint64_t ba = sA ? batch : 1, bb = sB ? batch : 1;
+  if ((sA == 0 && batch > 1) || (sB == 0 && batch > 1))
+    return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: broadcast batch operands take the strided path");
+  CUtensorMap ma, mb;
+  int s;
+  if (!a_mn_major) s = make_map(&ma, A, K, M, ba, lda, sA, BK, BM);
+  else s = make_map(&ma, A, M, K, ba, lda, sA, 64, BK);
+  if (s) return s;
+  if (b_k_major) s = make_map(&mb, B, K, N, bb, ldb, sB, BK, BN);
+  else s = make_map(&mb, B, N, K, bb, ldb, sB, 64, BK);
+  if (s) return s;
+  Args args;
+  args.C = C;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.ldc = ldc;
+  args.sC = sC;
+  args.batch = batch;
+  args.c_f32 = c_f32;
+  args.a_mn_major = a_mn_major;
+  args.b_k_major = b_k_major;
+  args.tiles_m = (int)((M + BM - 1) / BM);
+  args.tiles_n = (int)((N + BN - 1) / BN);
+  const int64_t tiles = (int64_t)args.tiles_m * args.tiles_n * batch;
+  if (tiles > INT32_MAX) return fail(NKB_ERR_UNSUPPORTED, "gemm: too many tiles");
+  static bool attr_set[64] = {false};
+  if (device >= 0 && device < 64 && !attr_set[device]) {
+    NKB_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    attr_set[device] = true;
+  }
+  const int grid = (int)std::min<int64_t>(tiles, num_sms(device));
+  gemm_bf16_tcgen05<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, args);
+  return launch_status("gemm_bf16_tcgen05");
+}
+
+// ---------------------------------------------------------------------------
+// strided fallback: any float dtypes, arbitrary element strides, fp32
+// accumulation on CUDA cores.  Used for fp32 dots (the bf16 tensor-core path
+// would lose the fp32 tolerance) and for operands TMA cannot describe.
+// ---------------------------------------------------------------------------
+struct SimtArgs {
+  const void *A, *B;
+  void *C;
+  int adt, bdt, cdt;
+  int64_t M, N, K, batch;
+  int64_t a_rs, a_cs, b_rs, b_cs, c_rs, c_cs, sA, sB, sC;
+};
+
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const __grid_constant__ SimtArgs p) {
+  constexpr int T = 64, TK = 16;
+  __shared__ float As[TK][T + 1];
+  __shared__ float Bs[TK][T + 1];
+  const int64_t bz = blockIdx.z;
+  const int64_t m0 = (int64_t)blockIdx.y * T, n0 = (int64_t)blockIdx.x * T;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  float acc[4][4] = {};
+  for (int64_t k0 = 0; k0 < p.K; k0 += TK) {
+    for (int i = threadIdx.x; i < T * TK; i += 256) {
+      const int mm = i / TK, kk = i % TK;
+      const int64_t gm = m0 + mm, gk = k0 + kk;
+      As[kk][mm] = (gm < p.M && gk < p.K)
+                       ? __uint_as_float(load_as_reg(p.A, bz * p.sA + gm * p.a_rs + gk * p.a_cs, p.adt))
+                       : 0.f;
+      const int nn = i % T, kb = i / T;
+      const int64_t gn = n0 + nn, gk2 = k0 + kb;
+      Bs[kb][nn] = (gn < p.N && gk2 < p.K)
+                       ? __uint_as_float(load_as_reg(p.B, bz * p.sB + gk2 * p.b_rs + gn * p.b_cs, p.bdt))
+                       : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < TK; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t gm = m0 + ty * 4 + i, gn = n0 + tx * 4 + j;
+      if (gm < p.M && gn < p.N) store_from_reg(p.C, bz * p.sC + gm * p.c_rs + gn * p.c_cs, p.cdt, __float_as_uint(acc[i][j]));
+    }
+}
+
+int gemm_simt(const SimtArgs &p, cudaStream_t st) {
+  if (p.M == 0 || p.N == 0 || p.batch == 0) return NKB_OK;
+  if (p.batch > 65535) return fail(NKB_ERR_UNSUPPORTED, "gemm_simt: batch too large");
+  dim3 grid((unsigned)((p.N + 63) / 64), (unsigned)((p.M + 63) / 64), (unsigned)p.batch);
+  if (grid.y > 65535) return fail(NKB_ERR_UNSUPPORTED, "gemm_simt: M too large");
+  gemm_simt_kernel<<<grid, 256, 0, st>>>(p);
+  return launch_status("gemm_simt_kernel");
+}
+
+// ---- plan steps ---------------------------------------------------------------
+// "gemm_bf16": ptrs A B C; ints M N K lda ldb ldc batch sA sB sC c_f32 a_mn_major b_k_major
+int tc_check(const Step &s) {
+  if (s.buf_ids.size() != 3 || s.ints.size() != 13) return fail(NKB_ERR_PLAN, "gemm_bf16: bad parameters");
+  return NKB_OK;
+}
+int tc_launch(const LaunchArgs &a) {
+  const auto &q = a.step->ints;
+  return gemm_tc(a.ptrs[0], a.ptrs[1], a.ptrs[2], (int)q[10], q[0], q[1], q[2], q[3], q[4], q[5], q[6], q[7], q[8],
+                 q[9], (int)q[11], (int)q[12], a.stream, a.device);
+}
+
+// "gemm_simt": ptrs A B C; ints adt bdt cdt M N K batch a_rs a_cs b_rs b_cs c_rs c_cs sA sB sC
+int simt_check(const Step &s) {
+  if (s.buf_ids.size() != 3 || s.ints.size() != 16) return fail(NKB_ERR_PLAN, "gemm_simt: bad parameters");
+  return NKB_OK;
+}
+int simt_launch(const LaunchArgs &a) {
+  const auto &q = a.step->ints;
+  SimtArgs p;
+  p.A = a.ptrs[0];
+  p.B = a.ptrs[1];
+  p.C = a.ptrs[2];
+  p.adt = (int)q[0];
+  p.bdt = (int)q[1];
+  p.cdt = (int)q[2];
+  p.M = q[3];
+  p.N = q[4];
+  p.K = q[5];
+  p.batch = q[6];
+  p.a_rs = q[7];
+  p.a_cs = q[8];
+  p.b_rs = q[9];
+  p.b_cs = q[10];
+  p.c_rs = q[11];
+  p.c_cs = q[12];
+  p.sA = q[13];
+  p.sB = q[14];
+  p.sC = q[15];
+  return gemm_simt(p, a.stream);
+}
+
+}  // namespace gemm
+
+NKB_REGISTER_KERNEL("gemm_bf16", gemm::tc_launch, gemm::tc_check);
+NKB_REGISTER_KERNEL("gemm_simt", gemm::simt_launch, gemm::simt_check);
+
+// Device error flag of the bounded waits (read by nkb_check_device_error).
+int gemm_read_and_clear_error(int *flag) {
+  int zero = 0;
+  NKB_CUDA_TRY(cudaMemcpyFromSymbol(flag, gemm::g_device_error, sizeof(int)));
+  if (*flag) NKB_CUDA_TRY(cudaMemcpyToSymbol(gemm::g_device_error, &zero, sizeof(int)));
+  return NKB_OK;
+}
+
+}  // namespace nkb
+
+extern "C" int nkb_gemm_bf16(const void *A, const void *B, void *C, int c_dtype, int64_t M, int64_t N, int64_t K,
+                             int64_t lda, int64_t ldb, int64_t ldc, int64_t batch, int64_t sA, int64_t sB, int64_t sC,
+                             void *stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (c_dtype != NKB_BF16 && c_dtype != NKB_F32) return nkb::fail(NKB_ERR_UNSUPPORTED, "gemm: output must be bf16 or fp32");
+  if (K > 0 && nkb::gemm::tc_eligible(A, B, lda, ldb, sA, sB, batch) && (batch == 1 || (sA && sB)))
+    return nkb::gemm::gemm_tc(A, B, C, c_dtype == NKB_F32, M, N, K, lda, ldb, ldc, batch, sA, sB, sC, 0, 0, st, dev);
+  nkb::gemm::SimtArgs p{A, B, C, NKB_BF16, NKB_BF16, c_dtype, M, N, K, batch, lda, 1, ldb, 1, ldc, 1, sA, sB, sC};
+  return nkb::gemm::gemm_simt(p, st);
+}

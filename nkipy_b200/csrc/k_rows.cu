@@ -1,0 +1,607 @@
+// Row kernels: last-axis softmax, residual-add + RMSNorm, first-occurrence
+// argmax, and a generic strided reduction.
+//
+// softmax_rows / rmsnorm_rows keep a whole row in registers (one HBM read,
+// one HBM write per element): the row is split over THREADS threads in
+// 4-element chunks loaded with 16-byte (fp32) or 8-byte (bf16) vector loads,
+// reductions use warp shuffles and, across warps, a small shared-memory
+// array.  Short rows use one warp per row so that a CTA still moves enough
+// bytes; rows longer than the register budget stream twice through L2.
+//
+// Numerics follow the traced NumPy compositions (reference
+// tests/kernels/softmax.py:7-10; qwen3_embedding/kernels/rmsnorm.py:4-16):
+// fp32 accumulation, exp(x - max) / sum with IEEE division, and
+// h / sqrt(sum(h*h)/N + eps) * w in that order.
+
+#include <float.h>
+#include <math.h>
+
+#include "common.cuh"
+
+namespace nkb {
+namespace rows {
+
+template <typename T>
+struct Vec4;
+template <>
+struct Vec4<float> {
+  using type = float4;
+};
+template <>
+struct Vec4<__nv_bfloat16> {
+  using type = uint2;  // 4 x bf16
+};
+
+__device__ __forceinline__ void load4(const float *p, float *v) {
+  float4 t = *reinterpret_cast<const float4 *>(p);
+  v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16 *p, float *v) {
+  uint2 t = *reinterpret_cast<const uint2 *>(p);
+  __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162 *>(&t.x);
+  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162 *>(&t.y);
+  float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+  v[0] = fa.x; v[1] = fa.y; v[2] = fb.x; v[3] = fb.y;
+}
+__device__ __forceinline__ void store4(float *p, const float *v) {
+  *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void store4(__nv_bfloat16 *p, const float *v) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+  __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+  uint2 t;
+  t.x = *reinterpret_cast<uint32_t *>(&a);
+  t.y = *reinterpret_cast<uint32_t *>(&b);
+  *reinterpret_cast<uint2 *>(p) = t;
+}
+__device__ __forceinline__ float load1(const float *p) { return *p; }
+__device__ __forceinline__ float load1(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
+__device__ __forceinline__ void store1(float *p, float v) { *p = v; }
+__device__ __forceinline__ void store1(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
+
+template <int THREADS>
+__device__ __forceinline__ float row_reduce_max(float v, float *smem) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (THREADS > 32) {
+    const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+    __syncthreads();
+    if (l == 0) smem[w] = v;
+    __syncthreads();
+    v = (l < THREADS / 32) ? smem[l] : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  }
+  return v;
+}
+
+template <int THREADS>
+__device__ __forceinline__ float row_reduce_sum(float v, float *smem) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (THREADS > 32) {
+    const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+    __syncthreads();
+    if (l == 0) smem[w] = v;
+    __syncthreads();
+    v = (l < THREADS / 32) ? smem[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  }
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// softmax
+// ---------------------------------------------------------------------------
+// THREADS threads per row (32 or 256); CHUNKS 4-element chunks per thread.
+// Rows per CTA = 256 / THREADS.  cols must be a multiple of 4 here.
+template <int THREADS, int CHUNKS, typename Tin, typename Tout>
+__global__ void __launch_bounds__(256) softmax_reg_kernel(const Tin *__restrict__ x, Tout *__restrict__ y,
+                                                          int64_t rows, int cols) {
+  __shared__ float smem[32];
+  constexpr int RPB = 256 / THREADS;
+  const int sub = threadIdx.x / THREADS;
+  const int t = threadIdx.x % THREADS;
+  for (int64_t row = (int64_t)blockIdx.x * RPB + sub; row - sub < rows; row += (int64_t)gridDim.x * RPB) {
+    const bool active = row < rows;
+    const Tin *xr = x + (active ? row : 0) * cols;
+    float v[CHUNKS][4];
+    float m = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+      const int col = (c * THREADS + t) * 4;
+      if (active && col < cols) {
+        load4(xr + col, v[c]);
+      } else {
+        v[c][0] = v[c][1] = v[c][2] = v[c][3] = -INFINITY;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) m = fmaxf(m, v[c][j]);
+    }
+    m = row_reduce_max<THREADS>(m, smem);
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[c][j] = expf(v[c][j] - m);
+        s += v[c][j];
+      }
+    s = row_reduce_sum<THREADS>(s, smem);
+    if (active) {
+      Tout *yr = y + row * cols;
+#pragma unroll
+      for (int c = 0; c < CHUNKS; ++c) {
+        const int col = (c * THREADS + t) * 4;
+        if (col < cols) {
+          float o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[j] = __fdiv_rn(v[c][j], s);
+          store4(yr + col, o);
+        }
+      }
+    }
+  }
+}
+
+// Rows too long for registers (or cols % 4 != 0): online max/sum pass, then
+// a second pass that re-reads the row (from L2 for moderate rows).
+template <typename Tin, typename Tout>
+__global__ void __launch_bounds__(256) softmax_stream_kernel(const Tin *__restrict__ x, Tout *__restrict__ y,
+                                                             int64_t rows, int64_t cols) {
+  __shared__ float smem[32];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const Tin *xr = x + row * cols;
+    float m = -INFINITY, s = 0.f;
+    for (int64_t c = threadIdx.x; c < cols; c += 256) {
+      const float v = load1(xr + c);
+      if (v > m) {
+        s = s * expf(m - v) + 1.f;
+        m = v;
+      } else {
+        s += expf(v - m);
+      }
+    }
+    const float gm = row_reduce_max<256>(m, smem);
+    s = (m == -INFINITY) ? 0.f : s * expf(m - gm);
+    s = row_reduce_sum<256>(s, smem);
+    Tout *yr = y + row * cols;
+    for (int64_t c = threadIdx.x; c < cols; c += 256) store1(yr + c, __fdiv_rn(expf(load1(xr + c) - gm), s));
+    __syncthreads();
+  }
+}
+
+template <typename Tin, typename Tout>
+int softmax_dispatch(const void *x, void *y, int64_t rows, int64_t cols, cudaStream_t st, int device) {
+  if (rows == 0 || cols == 0) return NKB_OK;
+  const Tin *xi = static_cast<const Tin *>(x);
+  Tout *yo = static_cast<Tout *>(y);
+  const bool aligned = (cols % 4 == 0) && ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0);
+  const int64_t cap = (int64_t)num_sms(device) * 32;
+  auto grid = [&](int rpb) { return (unsigned)std::min<int64_t>((rows + rpb - 1) / rpb, cap); };
+  if (aligned && cols <= 1024) {
+    const int chunks = (int)((cols + 127) / 128);
+    if (chunks <= 1) softmax_reg_kernel<32, 1, Tin, Tout><<<grid(8), 256, 0, st>>>(xi, yo, rows, (int)cols);
+    else if (chunks <= 2) softmax_reg_kernel<32, 2, Tin, Tout><<<grid(8), 256, 0, st>>>(xi, yo, rows, (int)cols);
+    else if (chunks <= 4) softmax_reg_kernel<32, 4, Tin, Tout><<<grid(8), 256, 0, st>>>(xi, yo, rows, (int)cols);
+    else softmax_reg_kernel<32, 8, Tin, Tout><<<grid(8), 256, 0, st>>>(xi, yo, rows, (int)cols);
+  } else if (aligned && cols <= 8192) {
+    const int chunks = (int)((cols + 1023) / 1024);
+    if (chunks <= 1) softmax_reg_kernel<256, 1, Tin, Tout><<<grid(1), 256, 0, st>>>(xi, yo, rows, (int)cols);
+    else if (chunks <= 2) softmax_reg_kernel<256, 2, Tin, Tout><<<grid(1), 256, 0, st>>>(xi, yo, rows, (int)cols);
+    else if (chunks <= 4) softmax_reg_kernel<256, 4, Tin, Tout><<<grid(1), 256, 0, st>>>(xi, yo, rows, (int)cols);
+    else softmax_reg_kernel<256, 8, Tin, Tout><<<grid(1), 256, 0, st>>>(xi, yo, rows, (int)cols);
+  } else {
+    softmax_stream_kernel<Tin, Tout><<<grid(1), 256, 0, st>>>(xi, yo, rows, cols);
+  }
+  return launch_status("softmax_rows");
+}
+
+int softmax_any(const void *x, int xdt, void *y, int ydt, int64_t rows, int64_t cols, cudaStream_t st, int dev) {
+  if (xdt == NKB_F32 && ydt == NKB_F32) return softmax_dispatch<float, float>(x, y, rows, cols, st, dev);
+  if (xdt == NKB_BF16 && ydt == NKB_BF16)
+    return softmax_dispatch<__nv_bfloat16, __nv_bfloat16>(x, y, rows, cols, st, dev);
+  if (xdt == NKB_BF16 && ydt == NKB_F32) return softmax_dispatch<__nv_bfloat16, float>(x, y, rows, cols, st, dev);
+  if (xdt == NKB_F32 && ydt == NKB_BF16) return softmax_dispatch<float, __nv_bfloat16>(x, y, rows, cols, st, dev);
+  return fail(NKB_ERR_UNSUPPORTED, "softmax_rows: dtype combination not supported");
+}
+
+// ---------------------------------------------------------------------------
+// residual add + RMSNorm
+// ---------------------------------------------------------------------------
+template <int THREADS, int CHUNKS, typename T, typename TW, bool RES, bool SUM_OUT>
+__global__ void __launch_bounds__(256) rmsnorm_reg_kernel(const T *__restrict__ x, const T *__restrict__ r,
+                                                          const TW *__restrict__ w, T *__restrict__ y,
+                                                          T *__restrict__ hsum, int64_t rows, int cols, float eps) {
+  __shared__ float smem[32];
+  constexpr int RPB = 256 / THREADS;
+  const int sub = threadIdx.x / THREADS;
+  const int t = threadIdx.x % THREADS;
+  const float inv_n = (float)cols;
+  for (int64_t row = (int64_t)blockIdx.x * RPB + sub; row - sub < rows; row += (int64_t)gridDim.x * RPB) {
+    const bool active = row < rows;
+    const int64_t base = (active ? row : 0) * cols;
+    float v[CHUNKS][4];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+      const int col = (c * THREADS + t) * 4;
+      if (active && col < cols) {
+        load4(x + base + col, v[c]);
+        if (RES) {
+          float rv[4];
+          load4(r + base + col, rv);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[c][j] += rv[j];
+          if (sizeof(T) == 2) {
+            // the residual sum is a bf16 tensor in the trace: round it first
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[c][j] = __bfloat162float(__float2bfloat16_rn(v[c][j]));
+          }
+        }
+      } else {
+        v[c][0] = v[c][1] = v[c][2] = v[c][3] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ss += v[c][j] * v[c][j];
+    }
+    ss = row_reduce_sum<THREADS>(ss, smem);
+    const float denom = sqrtf(__fdiv_rn(ss, inv_n) + eps);
+    if (active) {
+#pragma unroll
+      for (int c = 0; c < CHUNKS; ++c) {
+        const int col = (c * THREADS + t) * 4;
+        if (col < cols) {
+          if (SUM_OUT) store4(hsum + base + col, v[c]);
+          float wv[4], o[4];
+          load4(w + col, wv);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[j] = __fdiv_rn(v[c][j], denom) * wv[j];
+          store4(y + base + col, o);
+        }
+      }
+    }
+  }
+}
+
+template <typename T, typename TW, bool RES, bool SUM_OUT>
+__global__ void __launch_bounds__(256) rmsnorm_stream_kernel(const T *__restrict__ x, const T *__restrict__ r,
+                                                             const TW *__restrict__ w, T *__restrict__ y,
+                                                             T *__restrict__ hsum, int64_t rows, int64_t cols,
+                                                             float eps) {
+  __shared__ float smem[32];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int64_t base = row * cols;
+    float ss = 0.f;
+    for (int64_t c = threadIdx.x; c < cols; c += 256) {
+      float h = load1(x + base + c);
+      if (RES) {
+        h += load1(r + base + c);
+        if (sizeof(T) == 2) h = __bfloat162float(__float2bfloat16_rn(h));
+      }
+      ss += h * h;
+    }
+    ss = row_reduce_sum<256>(ss, smem);
+    const float denom = sqrtf(__fdiv_rn(ss, (float)cols) + eps);
+    for (int64_t c = threadIdx.x; c < cols; c += 256) {
+      float h = load1(x + base + c);
+      if (RES) {
+        h += load1(r + base + c);
+        if (sizeof(T) == 2) h = __bfloat162float(__float2bfloat16_rn(h));
+      }
+      if (SUM_OUT) store1(hsum + base + c, h);
+      store1(y + base + c, __fdiv_rn(h, denom) * load1(w + c));
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T, typename TW, bool RES, bool SUM_OUT>
+int rmsnorm_dispatch3(const void *x, const void *r, const void *w, void *y, void *hs, int64_t rows, int64_t cols,
+                      float eps, cudaStream_t st, int device) {
+  const T *xi = static_cast<const T *>(x);
+  const T *ri = static_cast<const T *>(r);
+  const TW *wi = static_cast<const TW *>(w);
+  T *yo = static_cast<T *>(y);
+  T *ho = static_cast<T *>(hs);
+  const bool aligned = (cols % 4 == 0) && ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) &&
+                       ((uintptr_t)w % 16 == 0) && (!RES || (uintptr_t)r % 16 == 0) &&
+                       (!SUM_OUT || (uintptr_t)hs % 16 == 0);
+  const int64_t cap = (int64_t)num_sms(device) * 32;
+  auto grid = [&](int rpb) { return (unsigned)std::min<int64_t>((rows + rpb - 1) / rpb, cap); };
+#define RMS_LAUNCH(TH, CH, RPB) \
+  rmsnorm_reg_kernel<TH, CH, T, TW, RES, SUM_OUT><<<grid(RPB), 256, 0, st>>>(xi, ri, wi, yo, ho, rows, (int)cols, eps)
+  if (aligned && cols <= 1024) {
+    const int ch = (int)((cols + 127) / 128);
+    if (ch <= 1) RMS_LAUNCH(32, 1, 8);
+    else if (ch <= 2) RMS_LAUNCH(32, 2, 8);
+    else if (ch <= 4) RMS_LAUNCH(32, 4, 8);
+    else RMS_LAUNCH(32, 8, 8);
+  } else if (aligned && cols <= 8192) {
+    const int ch = (int)((cols + 1023) / 1024);
+    if (ch <= 1) RMS_LAUNCH(256, 1, 1);
+    else if (ch <= 2) RMS_LAUNCH(256, 2, 1);
+    else if (ch <= 4) RMS_LAUNCH(256, 4, 1);
+    else RMS_LAUNCH(256, 8, 1);
+  } else {
+    rmsnorm_stream_kernel<T, TW, RES, SUM_OUT><<<grid(1), 256, 0, st>>>(xi, ri, wi, yo, ho, rows, cols, eps);
+  }
+#undef RMS_LAUNCH
+  return launch_status("rmsnorm_rows");
+}
+
+template <typename T, typename TW>
+int rmsnorm_dispatch2(const void *x, const void *r, const void *w, void *y, void *hs, int64_t rows, int64_t cols,
+                      float eps, cudaStream_t st, int dev) {
+  if (r && hs) return rmsnorm_dispatch3<T, TW, true, true>(x, r, w, y, hs, rows, cols, eps, st, dev);
+  if (r) return rmsnorm_dispatch3<T, TW, true, false>(x, r, w, y, hs, rows, cols, eps, st, dev);
+  return rmsnorm_dispatch3<T, TW, false, false>(x, r, w, y, hs, rows, cols, eps, st, dev);
+}
+
+int rmsnorm_any(const void *x, const void *r, const void *w, void *y, void *hs, int dt, int wdt, int64_t rows,
+                int64_t cols, float eps, cudaStream_t st, int dev) {
+  if (rows == 0 || cols == 0) return NKB_OK;
+  if (!r && hs) return fail(NKB_ERR_INVALID, "rmsnorm_rows: sum output requires a residual input");
+  if (dt == NKB_F32 && wdt == NKB_F32) return rmsnorm_dispatch2<float, float>(x, r, w, y, hs, rows, cols, eps, st, dev);
+  if (dt == NKB_BF16 && wdt == NKB_BF16)
+    return rmsnorm_dispatch2<__nv_bfloat16, __nv_bfloat16>(x, r, w, y, hs, rows, cols, eps, st, dev);
+  if (dt == NKB_BF16 && wdt == NKB_F32)
+    return rmsnorm_dispatch2<__nv_bfloat16, float>(x, r, w, y, hs, rows, cols, eps, st, dev);
+  return fail(NKB_ERR_UNSUPPORTED, "rmsnorm_rows: dtype combination not supported");
+}
+
+// ---------------------------------------------------------------------------
+// argmax / argmin over the last axis: first occurrence of the extreme value
+// (reference core/ops/reduce.py:227-311 lowers it to max -> compare -> iota
+// -> select -> min, i.e. the smallest index holding the maximum).
+// ---------------------------------------------------------------------------
+template <typename T, bool IS_MAX>
+__global__ void __launch_bounds__(256) argext_kernel(const T *__restrict__ x, int32_t *__restrict__ out, int64_t rows,
+                                                     int64_t cols) {
+  __shared__ float sv[8];
+  __shared__ int64_t si[8];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const T *xr = x + row * cols;
+    float best = IS_MAX ? -INFINITY : INFINITY;
+    int64_t bi = cols;  // sentinel: larger than any index
+    for (int64_t c = threadIdx.x; c < cols; c += 256) {
+      const float v = load1(xr + c);
+      if (IS_MAX ? (v > best) : (v < best)) {
+        best = v;
+        bi = c;
+      } else if (v == best && c < bi) {
+        bi = c;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if ((IS_MAX ? ov > best : ov < best) || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+    if (l == 0) {
+      sv[w] = best;
+      si[w] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int k = 1; k < 8; ++k)
+        if ((IS_MAX ? sv[k] > best : sv[k] < best) || (sv[k] == best && si[k] < bi)) {
+          best = sv[k];
+          bi = si[k];
+        }
+      // all-NaN / empty rows: report 0 like an all-equal row
+      out[row] = (int32_t)(bi >= cols ? 0 : bi);
+    }
+    __syncthreads();
+  }
+}
+
+int argext_any(const void *x, int dt, int32_t *out, int64_t rows, int64_t cols, bool is_max, cudaStream_t st,
+               int dev) {
+  if (rows == 0) return NKB_OK;
+  const unsigned g = (unsigned)std::min<int64_t>(rows, (int64_t)num_sms(dev) * 8);
+  if (dt == NKB_F32) {
+    if (is_max) argext_kernel<float, true><<<g, 256, 0, st>>>((const float *)x, out, rows, cols);
+    else argext_kernel<float, false><<<g, 256, 0, st>>>((const float *)x, out, rows, cols);
+  } else if (dt == NKB_BF16) {
+    if (is_max) argext_kernel<__nv_bfloat16, true><<<g, 256, 0, st>>>((const __nv_bfloat16 *)x, out, rows, cols);
+    else argext_kernel<__nv_bfloat16, false><<<g, 256, 0, st>>>((const __nv_bfloat16 *)x, out, rows, cols);
+  } else {
+    return fail(NKB_ERR_UNSUPPORTED, "argmax_rows: dtype not supported");
+  }
+  return launch_status("argmax_rows");
+}
+
+// ---------------------------------------------------------------------------
+// generic reduce: out[o] = reduce_{i} view[o, i] over a strided view split
+// into outer axes (kept) and inner axes (reduced).  HLO reduce with
+// computation add/maximum/minimum/multiply (reference core/ops/reduce.py:14-92).
+// ---------------------------------------------------------------------------
+constexpr int kRR = 4;
+struct ReduceParams {
+  const void *in;
+  void *out;
+  int in_dtype, out_dtype, comp, ro, ri, is_float;
+  int64_t n_outer, n_inner, off;
+  int64_t oshape[kRR], ostr[kRR], ishape[kRR], istr[kRR];
+  float init;
+};
+
+__device__ __forceinline__ float fcombine(int comp, float a, float b) {
+  switch (comp) {
+    case 0: return a + b;
+    case 1: return (a != a || b != b) ? __int_as_float(0x7fc00000) : fmaxf(a, b);
+    case 2: return (a != a || b != b) ? __int_as_float(0x7fc00000) : fminf(a, b);
+    default: return a * b;
+  }
+}
+__device__ __forceinline__ int32_t icombine(int comp, int32_t a, int32_t b) {
+  switch (comp) {
+    case 0: return (int32_t)((uint32_t)a + (uint32_t)b);
+    case 1: return max(a, b);
+    case 2: return min(a, b);
+    default: return (int32_t)((uint32_t)a * (uint32_t)b);
+  }
+}
+
+// WARPS_PER_OUT warps cooperate on one output element.
+template <int WARPS_PER_OUT>
+__global__ void __launch_bounds__(256) reduce_kernel(const __grid_constant__ ReduceParams p) {
+  constexpr int OPB = 8 / WARPS_PER_OUT;  // outputs per block
+  __shared__ uint32_t smem[8];
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int slot = warp / WARPS_PER_OUT, wi = warp % WARPS_PER_OUT;
+  for (int64_t o0 = (int64_t)blockIdx.x * OPB; o0 < p.n_outer; o0 += (int64_t)gridDim.x * OPB) {
+    const int64_t o = o0 + slot;
+    const bool active = o < p.n_outer;
+    int64_t base = p.off;
+    if (active) {
+      int64_t rem = o;
+      for (int d = p.ro - 1; d >= 0; --d) {
+        const int64_t q = rem / p.oshape[d];
+        base += (rem - q * p.oshape[d]) * p.ostr[d];
+        rem = q;
+      }
+    }
+    float facc = p.init;
+    int32_t iacc = (int32_t)p.init;
+    if (active) {
+      for (int64_t i = (int64_t)wi * 32 + lane; i < p.n_inner; i += 32 * WARPS_PER_OUT) {
+        int64_t rem = i, offs = base;
+        for (int d = p.ri - 1; d >= 0; --d) {
+          const int64_t q = rem / p.ishape[d];
+          offs += (rem - q * p.ishape[d]) * p.istr[d];
+          rem = q;
+        }
+        const uint32_t raw = load_as_reg(p.in, offs, p.in_dtype);
+        if (p.is_float) facc = fcombine(p.comp, facc, __uint_as_float(raw));
+        else iacc = icombine(p.comp, iacc, (int32_t)raw);
+      }
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+      if (p.is_float) facc = fcombine(p.comp, facc, __shfl_xor_sync(0xffffffffu, facc, s));
+      else iacc = icombine(p.comp, iacc, __shfl_xor_sync(0xffffffffu, iacc, s));
+    }
+    if (WARPS_PER_OUT > 1) {
+      __syncthreads();
+      if (lane == 0) smem[warp] = p.is_float ? __float_as_uint(facc) : (uint32_t)iacc;
+      __syncthreads();
+      if (wi == 0 && lane == 0) {
+        for (int k = 1; k < WARPS_PER_OUT; ++k) {
+          const uint32_t v = smem[warp + k];
+          if (p.is_float) facc = fcombine(p.comp, facc, __uint_as_float(v));
+          else iacc = icombine(p.comp, iacc, (int32_t)v);
+        }
+      }
+    }
+    if (active && wi == 0 && lane == 0)
+      store_from_reg(p.out, o, p.out_dtype, p.is_float ? __float_as_uint(facc) : (uint32_t)iacc);
+  }
+}
+
+// ---- plan steps -------------------------------------------------------------
+// "softmax_rows": ptrs x, y; ints rows cols x_dtype y_dtype
+int softmax_check(const Step &s) {
+  if (s.buf_ids.size() != 2 || s.ints.size() != 4) return fail(NKB_ERR_PLAN, "softmax_rows: bad parameters");
+  return NKB_OK;
+}
+int softmax_launch(const LaunchArgs &a) {
+  const auto &q = a.step->ints;
+  return softmax_any(a.ptrs[0], (int)q[2], a.ptrs[1], (int)q[3], q[0], q[1], a.stream, a.device);
+}
+
+// "rmsnorm_rows": ptrs x r w y hsum (r/hsum may be unused per flags);
+// ints rows cols dtype w_dtype has_res has_sum; floats eps
+int rmsnorm_check(const Step &s) {
+  if (s.buf_ids.size() != 5 || s.ints.size() != 6 || s.floats.size() != 1)
+    return fail(NKB_ERR_PLAN, "rmsnorm_rows: bad parameters");
+  return NKB_OK;
+}
+int rmsnorm_launch(const LaunchArgs &a) {
+  const auto &q = a.step->ints;
+  return rmsnorm_any(a.ptrs[0], q[4] ? a.ptrs[1] : nullptr, a.ptrs[2], a.ptrs[3], q[5] ? a.ptrs[4] : nullptr,
+                     (int)q[2], (int)q[3], q[0], q[1], a.step->floats[0], a.stream, a.device);
+}
+
+// "argmax_rows": ptrs x out; ints rows cols dtype is_max
+int argext_check(const Step &s) {
+  if (s.buf_ids.size() != 2 || s.ints.size() != 4) return fail(NKB_ERR_PLAN, "argmax_rows: bad parameters");
+  return NKB_OK;
+}
+int argext_launch(const LaunchArgs &a) {
+  const auto &q = a.step->ints;
+  return argext_any(a.ptrs[0], (int)q[2], static_cast<int32_t *>(a.ptrs[1]), q[0], q[1], q[3] != 0, a.stream,
+                    a.device);
+}
+
+// "reduce": ptrs in out; ints in_dtype out_dtype comp ro ri off n_outer n_inner
+//           oshape[ro] ostr[ro] ishape[ri] istr[ri]; floats init
+int reduce_check(const Step &s) {
+  if (s.buf_ids.size() != 2 || s.ints.size() < 8 || s.floats.size() != 1)
+    return fail(NKB_ERR_PLAN, "reduce: bad parameters");
+  const int64_t ro = s.ints[3], ri = s.ints[4];
+  if (ro < 0 || ro > kRR || ri < 1 || ri > kRR) return fail(NKB_ERR_UNSUPPORTED, "reduce: rank out of range");
+  if ((int64_t)s.ints.size() != 8 + 2 * ro + 2 * ri) return fail(NKB_ERR_PLAN, "reduce: parameter count");
+  return NKB_OK;
+}
+int reduce_launch(const LaunchArgs &a) {
+  const auto &q = a.step->ints;
+  ReduceParams p;
+  memset(&p, 0, sizeof(p));
+  p.in = a.ptrs[0];
+  p.out = a.ptrs[1];
+  p.in_dtype = (int)q[0];
+  p.out_dtype = (int)q[1];
+  p.comp = (int)q[2];
+  p.ro = (int)q[3];
+  p.ri = (int)q[4];
+  p.off = q[5];
+  p.n_outer = q[6];
+  p.n_inner = q[7];
+  int k = 8;
+  for (int d = 0; d < p.ro; ++d) p.oshape[d] = q[k++];
+  for (int d = 0; d < p.ro; ++d) p.ostr[d] = q[k++];
+  for (int d = 0; d < p.ri; ++d) p.ishape[d] = q[k++];
+  for (int d = 0; d < p.ri; ++d) p.istr[d] = q[k++];
+  p.is_float = dtype_is_float(p.in_dtype);
+  p.init = a.step->floats[0];
+  if (p.n_outer == 0) return NKB_OK;
+  const int64_t cap = (int64_t)num_sms(a.device) * 16;
+  if (p.n_inner >= 4096) {
+    reduce_kernel<8><<<(unsigned)std::min<int64_t>(p.n_outer, cap), 256, 0, a.stream>>>(p);
+  } else {
+    reduce_kernel<1><<<(unsigned)std::min<int64_t>((p.n_outer + 7) / 8, cap), 256, 0, a.stream>>>(p);
+  }
+  return launch_status("reduce_kernel");
+}
+
+}  // namespace rows
+
+NKB_REGISTER_KERNEL("softmax_rows", rows::softmax_launch, rows::softmax_check);
+NKB_REGISTER_KERNEL("rmsnorm_rows", rows::rmsnorm_launch, rows::rmsnorm_check);
+NKB_REGISTER_KERNEL("argmax_rows", rows::argext_launch, rows::argext_check);
+NKB_REGISTER_KERNEL("reduce", rows::reduce_launch, rows::reduce_check);
+
+}  // namespace nkb
+
+extern "C" int nkb_softmax_rows(const void *x, int x_dtype, void *out, int out_dtype, int64_t rows, int64_t cols,
+                                void *stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return nkb::rows::softmax_any(x, x_dtype, out, out_dtype, rows, cols, static_cast<cudaStream_t>(stream), dev);
+}
+
+extern "C" int nkb_rmsnorm_rows(const void *x, const void *r, const void *w, void *out, void *sum_out, int dtype,
+                                int w_dtype, int64_t rows, int64_t cols, float eps, void *stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return nkb::rows::rmsnorm_any(x, r, w, out, sum_out, dtype, w_dtype, rows, cols, eps,
+                                static_cast<cudaStream_t>(stream), dev);
+}

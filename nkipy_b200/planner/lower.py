@@ -1,0 +1,600 @@
+"""Lower a traced graph onto the libnkb kernel library: the fusion/tiling pass.
+
+This is the B200 replacement for the reference's compile step
+(``core/compile.py:115-309``: HLO proto -> neuronx-cc -> NEFF).  One pass
+over the nodes in trace order:
+
+* nodes claimed by a recogniser (``patterns.py``) become one fused launch
+  (``softmax_rows``, ``rmsnorm_rows``, ``argmax_rows``);
+* view nodes (``reshape``/``transpose``/``slice``/``broadcast``/``copy``)
+  only rewrite a strided view or a lazy expression -- no launch;
+* elementwise nodes extend a lazy expression; the expression is compiled
+  into a single ``ew`` launch where its value is needed in memory (a
+  non-elementwise consumer, a graph output, a multi-use intermediate);
+* ``dot`` becomes ``gemm_bf16`` (tcgen05) when both operands are bf16 and
+  TMA can describe them, ``gemm_simt`` otherwise; ``reduce`` -> ``reduce``;
+  ``gather`` -> ``take`` / ``gather_pts``; ``concatenate`` writes each part
+  straight into its slice of the result; ``pad``, ``dynamic-update-slice``,
+  ``scatter``, ``all-reduce`` map to their kernels.
+
+Intermediates live in one scratch arena whose offsets are packed by
+lifetime.  A graph output that is a whole intermediate buffer is produced in
+place in the caller's output buffer.  Anything without a lowering raises
+``NotImplementedError`` at plan time: there is no host fallback.
+"""
+
+from typing import Dict, List, Optional, Union
+
+import ml_dtypes
+import numpy as np
+
+from nkipy_b200.planner import ewprog as E
+from nkipy_b200.planner import views as V
+from nkipy_b200.planner.patterns import find_claims, tkey
+from nkipy_b200.planner.plan import BufDecl, IoSpec, Plan, StepRec, pack_arena
+
+Value = Union[V.View, E.Expr]
+
+BF16 = np.dtype(ml_dtypes.bfloat16)
+
+
+def _nbytes(shape, dtype) -> int:
+    n = int(np.prod(shape, dtype=np.int64)) if len(shape) else 1
+    return n * np.dtype(dtype).itemsize
+
+
+class Lowering:
+    def __init__(self, graph, world: int = 1):
+        self.g = graph
+        self.world = world
+        self.buffers: List[BufDecl] = []
+        self.steps: List[StepRec] = []
+        self.consts: List[np.ndarray] = []
+        self.vals: Dict[tuple, Value] = {}
+        self.uses: Dict[tuple, int] = {}
+        for op in graph.operations:
+            for t in op.operands:
+                self.uses[tkey(t)] = self.uses.get(tkey(t), 0) + 1
+        for r in graph.results:
+            self.uses[tkey(r)] = self.uses.get(tkey(r), 0) + 1
+        self.claims, self.claimed = find_claims(graph)
+        self.needs_comm = False
+
+    # ------------------------------------------------------------ buffers
+    def new_buf(self, kind, index, nbytes) -> int:
+        self.buffers.append(BufDecl(kind, index, int(nbytes)))
+        return len(self.buffers) - 1
+
+    def tmp_view(self, shape, dtype) -> V.View:
+        b = self.new_buf("tmp", -1, max(1, _nbytes(shape, dtype)))
+        return V.View(b, 0, tuple(shape), V.dense_strides(shape), np.dtype(dtype))
+
+    def const_view(self, arr: np.ndarray) -> V.View:
+        arr = np.ascontiguousarray(arr)
+        self.consts.append(arr)
+        b = self.new_buf("const", len(self.consts) - 1, max(1, arr.nbytes))
+        return V.View(b, 0, tuple(arr.shape), V.dense_strides(arr.shape), arr.dtype)
+
+    def step(self, kernel, bufs, ints=(), floats=(), note=""):
+        self.steps.append(StepRec(kernel, list(bufs), [int(i) for i in ints], [float(f) for f in floats], note))
+
+    @staticmethod
+    def bref(v: V.View):
+        return (v.buf, v.offset * np.dtype(v.dtype).itemsize)
+
+    # ------------------------------------------------------------ values
+    def expr_of(self, val: Value) -> E.Expr:
+        return val if isinstance(val, E.Expr) else E.leaf(val)
+
+    def materialize(self, val: Value, dense=True, out: Optional[V.View] = None) -> V.View:
+        """A view holding ``val``; written into ``out`` when given."""
+        if isinstance(val, V.View) and out is None:
+            if not dense or val.is_dense():
+                return val
+        if out is None:
+            out = self.tmp_view(val.shape, val.dtype)
+        self.emit_ew(self.expr_of(val), out)
+        return out
+
+    def emit_ew(self, expr: E.Expr, out: V.View, depth=0):
+        try:
+            c = E.compile_ew(expr, out)
+        except E.TooBig:
+            if depth > 16 or expr.kind != "op":
+                raise
+            # split: materialise the operand subtrees, then retry the root
+            args = []
+            for a in expr.args:
+                if a.kind == "op":
+                    args.append(E.leaf(self.materialize(a)))
+                else:
+                    args.append(a)
+            root = E.Expr("op", expr.shape, expr.dtype, op=expr.op, attrs=expr.attrs, args=args)
+            return self.emit_ew(root, out, depth + 1)
+        bufs = [(out.buf, 0)] + [(v.buf, 0) for v in c.in_views]
+        self.step("ew", bufs, c.ints, note=f"{c.n_instr} instr {tuple(out.shape)} {np.dtype(out.dtype).name}")
+
+    def get(self, t) -> Value:
+        return self.vals[tkey(t)]
+
+    def put(self, t_or_op, val: Value):
+        key = ("o", t_or_op.id)
+        if isinstance(val, E.Expr) and val.kind == "op" and self.uses.get(key, 0) > 1 and key not in self.result_keys:
+            # a shared intermediate is computed once
+            val = self.materialize(val)
+        self.vals[key] = val
+
+    # ------------------------------------------------------------ main pass
+    def run(self, name="kernel") -> Plan:
+        g = self.g
+        self.result_keys = {tkey(r) for r in g.results}
+        inputs = []
+        for p in g.parameters:
+            spec = IoSpec(p.name, tuple(p.shape), np.dtype(p.dtype))
+            inputs.append(spec)
+            b = self.new_buf("in", p.parameter_id, max(1, spec.nbytes))
+            self.vals[("p", p.parameter_id)] = V.View(b, 0, tuple(p.shape), V.dense_strides(p.shape), np.dtype(p.dtype))
+        for op in g.operations:
+            if id(op) in self.claimed and op.id not in self.claims:
+                continue
+            if op.id in self.claims:
+                self.lower_claim(self.claims[op.id])
+                continue
+            fn = getattr(self, "op_" + op.op_name.replace("-", "_"), None)
+            if fn is None:
+                if op.op_name in E.ELEMENTWISE:
+                    self.op_elementwise(op)
+                    continue
+                raise NotImplementedError(f"no B200 lowering for HLO op '{op.op_name}'")
+            fn(op)
+        outputs = []
+        for i, r in enumerate(g.results):
+            odt = np.dtype(np.uint8) if np.dtype(r.dtype) == np.bool_ else np.dtype(r.dtype)
+            spec = IoSpec(r.name, tuple(r.shape), odt)
+            outputs.append(spec)
+            self.bind_output(i, r, spec)
+        lifetimes = self.lifetimes()
+        scratch = pack_arena(self.buffers, lifetimes)
+        aliases = [(a.output_index, a.param_index) for a in g.aliases]
+        return Plan(name, inputs, outputs, self.consts, self.buffers, self.steps, scratch, aliases, self.needs_comm)
+
+    def bind_output(self, i, r, spec):
+        val = self.vals[tkey(r)]
+        out_dt = np.dtype(np.bool_) if np.dtype(r.dtype) == np.bool_ else spec.dtype
+        if isinstance(val, V.View) and val.is_dense() and val.offset == 0:
+            b = self.buffers[val.buf]
+            if b.kind == "tmp" and b.nbytes == max(1, spec.nbytes) and not getattr(b, "_bound", False):
+                b.kind, b.index = "out", i
+                b._bound = True
+                return
+        ob = self.new_buf("out", i, max(1, spec.nbytes))
+        out_view = V.View(ob, 0, tuple(r.shape), V.dense_strides(r.shape), out_dt)
+        self.emit_ew(self.expr_of(val), out_view)
+
+    def lifetimes(self):
+        life = {}
+        for si, s in enumerate(self.steps):
+            for bid, _ in s.bufs:
+                lo, hi = life.get(bid, (si, si))
+                life[bid] = (min(lo, si), max(hi, si))
+        return life
+
+    # ------------------------------------------------------------ claims
+    def dense_rows(self, t):
+        v = self.materialize(self.get(t), dense=True)
+        cols = int(t.shape[-1]) if t.shape else 1
+        rows = int(np.prod(t.shape[:-1])) if len(t.shape) > 1 else 1
+        return v, rows, cols
+
+    def lower_claim(self, c):
+        root = c.root
+        if c.kind == "softmax":
+            x = c.params["x"]
+            xv, rows, cols = self.dense_rows(x)
+            if np.dtype(xv.dtype) not in (np.dtype(np.float32), BF16):
+                raise NotImplementedError("softmax on this dtype")
+            out = self.tmp_view(root.result_shape, c.params["out_dtype"])
+            self.step(
+                "softmax_rows",
+                [self.bref(xv), self.bref(out)],
+                [rows, cols, E.dt_code(xv.dtype), E.dt_code(out.dtype)],
+                note=f"{rows}x{cols}",
+            )
+            self.vals[("o", root.id)] = out
+        elif c.kind == "rmsnorm":
+            p = c.params
+            out = self.tmp_view(root.result_shape, p["out_dtype"])
+            wv = self.materialize(self.get(p["w"]), dense=True)
+            dt = np.dtype(p["out_dtype"])
+            if p["residual"] is not None:
+                a, b = p["residual"]
+                av, rows, cols = self.dense_rows(a)
+                bv, _, _ = self.dense_rows(b)
+                hs = self.tmp_view(p["sum_tensor"].shape, p["sum_tensor"].dtype) if p["sum_needed"] else None
+                bufs = [self.bref(av), self.bref(bv), self.bref(wv), self.bref(out), self.bref(hs if hs else out)]
+                self.step(
+                    "rmsnorm_rows",
+                    bufs,
+                    [rows, cols, E.dt_code(dt), E.dt_code(wv.dtype), 1, 1 if hs else 0],
+                    [p["eps"]],
+                    note=f"{rows}x{cols} residual{'+sum' if hs else ''}",
+                )
+                if hs is not None:
+                    self.vals[tkey(p["sum_tensor"])] = hs
+            else:
+                xv, rows, cols = self.dense_rows(p["x"])
+                bufs = [self.bref(xv), self.bref(xv), self.bref(wv), self.bref(out), self.bref(out)]
+                self.step(
+                    "rmsnorm_rows",
+                    bufs,
+                    [rows, cols, E.dt_code(dt), E.dt_code(wv.dtype), 0, 0],
+                    [p["eps"]],
+                    note=f"{rows}x{cols}",
+                )
+            self.vals[("o", root.id)] = out
+        elif c.kind == "argmax":
+            x = c.params["x"]
+            xv, rows, cols = self.dense_rows(x)
+            out = self.tmp_view(root.result_shape, np.int32)
+            self.step(
+                "argmax_rows",
+                [self.bref(xv), self.bref(out)],
+                [rows, cols, E.dt_code(xv.dtype), 1 if c.params["is_max"] else 0],
+                note=f"{rows}x{cols}",
+            )
+            self.vals[("o", root.id)] = out
+        else:
+            raise NotImplementedError(c.kind)
+
+    # ------------------------------------------------------------ view ops
+    def op_reshape(self, op):
+        v = self.get(op.operands[0])
+        shape = tuple(op.result_shape)
+        if isinstance(v, V.View):
+            st = V.reshape_strides(v.shape, v.strides, shape)
+            if st is None:
+                v = self.materialize(v)
+                st = V.dense_strides(shape)
+            self.put(op, v.with_(shape=shape, strides=st))
+            return
+        e = E.t_reshape(v, shape)
+        if e is None:
+            m = self.materialize(v)
+            self.put(op, m.with_(shape=shape, strides=V.dense_strides(shape)))
+        else:
+            self.put(op, e)
+
+    def op_broadcast(self, op):
+        v = self.get(op.operands[0])
+        shape = tuple(op.result_shape)
+        bd = list(op.attributes.get("broadcast_dimensions", []))
+        if isinstance(v, V.View):
+            self.put(op, v.with_(shape=shape, strides=V.broadcast_strides(v.shape, v.strides, shape, bd)))
+        else:
+            self.put(op, E.t_broadcast(v, shape, bd))
+
+    def op_transpose(self, op):
+        v = self.get(op.operands[0])
+        perm = list(op.attributes["permutation"])
+        if isinstance(v, V.View):
+            self.put(
+                op, v.with_(shape=tuple(v.shape[p] for p in perm), strides=V.transpose_strides(v.strides, perm))
+            )
+        else:
+            self.put(op, E.t_transpose(v, perm))
+
+    def op_slice(self, op):
+        v = self.get(op.operands[0])
+        a = op.attributes
+        starts, limits, steps = a["start_indices"], a["limit_indices"], a["strides"]
+        if isinstance(v, V.View):
+            off, st = V.slice_view(v.offset, v.strides, starts, steps)
+            self.put(op, v.with_(offset=off, shape=tuple(op.result_shape), strides=st))
+        else:
+            self.put(op, E.t_slice(v, starts, limits, steps))
+
+    def op_copy(self, op):
+        self.put(op, self.get(op.operands[0]))
+
+    def op_constant(self, op):
+        val = op.attributes.get("value")
+        if isinstance(val, np.ndarray) and val.ndim > 0:
+            arr = np.asarray(val).astype(op.result_dtype)
+            if np.dtype(op.result_dtype) == np.bool_:
+                arr = arr.astype(np.uint8)
+                v = self.const_view(arr).with_(dtype=np.dtype(np.bool_))
+            else:
+                v = self.const_view(arr)
+            self.vals[("o", op.id)] = v
+            return
+        if isinstance(val, np.ndarray):
+            val = val.item()
+        self.vals[("o", op.id)] = E.const(val, op.result_dtype, op.result_shape)
+
+    def op_iota(self, op):
+        self.vals[("o", op.id)] = E.iota(op.result_shape, op.result_dtype, op.attributes["iota_dimension"])
+
+    # ------------------------------------------------------------ elementwise
+    def op_elementwise(self, op):
+        args = [self.expr_of(self.get(t)) for t in op.operands]
+        e = E.op(op.op_name, args, op.result_shape, op.result_dtype, op.attributes)
+        if e.n_nodes() > 48 or len(e.leaves()) > 6:
+            args = [E.leaf(self.materialize(a)) if a.kind == "op" else a for a in args]
+            e = E.op(op.op_name, args, op.result_shape, op.result_dtype, op.attributes)
+        self.put(op, e)
+
+    def op_convert(self, op):
+        src = op.operands[0]
+        if np.dtype(src.dtype) == np.dtype(op.result_dtype):
+            self.put(op, self.get(src))
+        else:
+            self.op_elementwise(op)
+
+    # ------------------------------------------------------------ reduce
+    def op_reduce(self, op):
+        x = op.operands[0]
+        xv = self.materialize(self.get(x), dense=False)
+        init_op = op.operands[1].source_op
+        init = float(np.asarray(init_op.attributes["value"]).reshape(()).item()) if init_op is not None else 0.0
+        comp = {"add": 0, "maximum": 1, "minimum": 2, "multiply": 3}[op.attributes["computation"]]
+        dims = sorted(op.attributes["dimensions"])
+        outer = [d for d in range(len(x.shape)) if d not in dims]
+        out = self.tmp_view(op.result_shape, op.result_dtype)
+
+        def grouped(axes):
+            if not axes:
+                return (), ()
+            shp, (st,) = V.collapse([xv.shape[d] for d in axes], [tuple(xv.strides[d] for d in axes)])
+            if shp == (1,) and all(xv.shape[d] == 1 for d in axes):
+                return (1,), (0,)
+            return shp, st
+
+        oshape, ostr = grouped(outer)
+        ishape, istr = grouped(dims)
+        if len(oshape) > 4 or len(ishape) > 4:
+            xv = self.materialize(xv, dense=True)
+            oshape, ostr = grouped(outer)
+            ishape, istr = grouped(dims)
+        n_outer = int(np.prod(oshape)) if oshape else 1
+        n_inner = int(np.prod(ishape)) if ishape else 1
+        ints = [E.dt_code(xv.dtype), E.dt_code(out.dtype), comp, len(oshape), len(ishape), xv.offset, n_outer, n_inner]
+        ints += list(oshape) + list(ostr) + list(ishape) + list(istr)
+        self.step("reduce", [(xv.buf, 0), self.bref(out)], ints, [init], note=f"{n_outer}x{n_inner}")
+        self.vals[("o", op.id)] = out
+
+    # ------------------------------------------------------------ dot
+    def op_dot(self, op):
+        a_t, b_t = op.operands
+        at = op.attributes
+        lb, rb = list(at["lhs_batch_dimensions"]), list(at["rhs_batch_dimensions"])
+        lc, rc = list(at["lhs_contracting_dimensions"]), list(at["rhs_contracting_dimensions"])
+        av = self.materialize(self.get(a_t), dense=False)
+        bv = self.materialize(self.get(b_t), dense=False)
+        na, nb = len(a_t.shape), len(b_t.shape)
+        if len(lc) != 1 or len(rc) != 1:
+            raise NotImplementedError("dot with several contracting dimensions")
+        a_free = [d for d in range(na) if d not in lb and d not in lc]
+        b_free = [d for d in range(nb) if d not in rb and d not in rc]
+        if lb != list(range(len(lb))) or rb != list(range(len(rb))) or len(a_free) > 1 or len(b_free) > 1:
+            raise NotImplementedError("dot layout outside the matmul form")
+        M = int(a_t.shape[a_free[0]]) if a_free else 1
+        N = int(b_t.shape[b_free[0]]) if b_free else 1
+        K = int(a_t.shape[lc[0]])
+        a_ms = av.strides[a_free[0]] if a_free else 0
+        a_ks = av.strides[lc[0]]
+        b_ks = bv.strides[rc[0]]
+        b_ns = bv.strides[b_free[0]] if b_free else 0
+        bshape = [int(a_t.shape[d]) for d in lb]
+        a_bst = [av.strides[d] for d in lb]
+        b_bst = [bv.strides[d] for d in rb]
+        out_dt = np.dtype(op.result_dtype)
+        out = self.tmp_view(op.result_shape, out_dt)
+        # fold a broadcast rhs (weights shared across the batch) into M
+        if bshape and all(s == 0 for s in b_bst) and M > 0:
+            shp, (st,) = V.collapse(bshape + [M], [tuple(a_bst + [a_ms])])
+            if len(shp) == 1:
+                bshape, a_bst, b_bst, M, a_ms = [], [], [], int(shp[0]), st[0]
+        batch = int(np.prod(bshape)) if bshape else 1
+        # collapse the batch axes of A, B and C together
+        c_bst = list(V.dense_strides(tuple(bshape) + (M, N)))[: len(bshape)] if bshape else []
+        if len(bshape) > 1:
+            shp, sts = V.collapse(bshape, [tuple(a_bst), tuple(b_bst), tuple(c_bst)])
+            if len(shp) > 1:
+                av = self.materialize(av, dense=True)
+                bv = self.materialize(bv, dense=True)
+                return self.op_dot_dense(op, av, bv, out)
+            a_bst, b_bst, c_bst = [sts[0][0]], [sts[1][0]], [sts[2][0]]
+        sA = a_bst[0] if a_bst else 0
+        sB = b_bst[0] if b_bst else 0
+        sC = c_bst[0] if c_bst else 0
+        if M == 1 and not a_free:
+            a_ms = K
+        if N == 1 and not b_free:
+            b_ns = 1
+        is_bf = np.dtype(av.dtype) == BF16 and np.dtype(bv.dtype) == BF16 and out_dt in (BF16, np.dtype(np.float32))
+        a_mn = a_ms == 1 and a_ks != 1
+        a_k = a_ks == 1
+        b_n = b_ns == 1
+        b_k = b_ks == 1 and b_ns != 1
+        eb = np.dtype(BF16).itemsize
+
+        def aligned(v, *strides):
+            return (v.offset * eb) % 16 == 0 and all(int(s) % 8 == 0 for s in strides)
+
+        use_tc = (
+            is_bf
+            and K > 0
+            and (a_k or a_mn)
+            and (b_n or b_k)
+            and (batch == 1 or (sA != 0 and sB != 0))
+            and aligned(av, a_ks if a_mn else a_ms, sA)
+            and aligned(bv, b_ks if b_n else b_ns, sB)
+        )
+        if use_tc:
+            lda = a_ms if a_k else a_ks
+            ldb = b_ks if b_n else b_ns
+            self.step(
+                "gemm_bf16",
+                [self.bref(av), self.bref(bv), self.bref(out)],
+                [M, N, K, lda, ldb, N, batch, sA, sB, sC, int(out_dt == np.float32), int(a_mn and not a_k), int(b_k and not b_n)],
+                note=f"tc {batch}x{M}x{N}x{K}",
+            )
+        else:
+            self.step(
+                "gemm_simt",
+                [self.bref(av), self.bref(bv), self.bref(out)],
+                [E.dt_code(av.dtype), E.dt_code(bv.dtype), E.dt_code(out_dt), M, N, K, batch, a_ms, a_ks, b_ks, b_ns, N, 1, sA, sB, sC],
+                note=f"simt {batch}x{M}x{N}x{K}",
+            )
+        self.vals[("o", op.id)] = out
+
+    def op_dot_dense(self, op, av, bv, out):
+        """Matmul-form dot with dense operands (batch axes flattened)."""
+        a_t, b_t = op.operands
+        M, K = int(a_t.shape[-2]), int(a_t.shape[-1])
+        N = int(b_t.shape[-1])
+        batch = int(np.prod(a_t.shape[:-2]))
+        out_dt = np.dtype(op.result_dtype)
+        is_bf = np.dtype(av.dtype) == BF16 and np.dtype(bv.dtype) == BF16 and out_dt in (BF16, np.dtype(np.float32))
+        if is_bf and K % 8 == 0 and N % 8 == 0 and K > 0:
+            self.step(
+                "gemm_bf16",
+                [self.bref(av), self.bref(bv), self.bref(out)],
+                [M, N, K, K, N, N, batch, M * K, K * N, M * N, int(out_dt == np.float32), 0, 0],
+                note=f"tc {batch}x{M}x{N}x{K}",
+            )
+        else:
+            self.step(
+                "gemm_simt",
+                [self.bref(av), self.bref(bv), self.bref(out)],
+                [E.dt_code(av.dtype), E.dt_code(bv.dtype), E.dt_code(out_dt), M, N, K, batch, K, 1, N, 1, N, 1, M * K, K * N, M * N],
+                note=f"simt {batch}x{M}x{N}x{K}",
+            )
+        self.vals[("o", op.id)] = out
+
+    # ------------------------------------------------------------ data movement
+    def op_concatenate(self, op):
+        dim = op.attributes["dimension"]
+        out = self.tmp_view(op.result_shape, op.result_dtype)
+        pos = 0
+        for t in op.operands:
+            n = int(t.shape[dim])
+            starts = [0] * len(op.result_shape)
+            starts[dim] = pos
+            off, st = V.slice_view(out.offset, out.strides, starts, [1] * len(starts))
+            part = out.with_(offset=off, shape=tuple(t.shape), strides=st)
+            self.emit_ew(self.expr_of(self.get(t)), part)
+            pos += n
+        self.vals[("o", op.id)] = out
+
+    def op_pad(self, op):
+        x = op.operands[0]
+        xv = self.materialize(self.get(x), dense=True)
+        cfg = op.attributes["padding_config"]
+        if any(c[2] != 0 or c[0] < 0 or c[1] < 0 for c in cfg):
+            raise NotImplementedError("pad with interior or negative padding")
+        pv = op.operands[1].source_op.attributes["value"]
+        bits = int.from_bytes(np.asarray(pv, dtype=op.result_dtype).reshape(1).tobytes(), "little")
+        out = self.tmp_view(op.result_shape, op.result_dtype)
+        r = len(x.shape)
+        ints = [r, np.dtype(op.result_dtype).itemsize, out.size, bits]
+        ints += list(x.shape) + list(op.result_shape) + [c[0] for c in cfg]
+        self.step("pad", [self.bref(xv), self.bref(out)], ints)
+        self.vals[("o", op.id)] = out
+
+    def op_dynamic_update_slice(self, op):
+        base, upd = op.operands[0], op.operands[1]
+        starts = []
+        for t in op.operands[2:]:
+            sop = t.source_op
+            if sop is None or sop.op_name != "constant":
+                raise NotImplementedError("dynamic-update-slice with run-time start indices")
+            starts.append(int(np.asarray(sop.attributes["value"]).reshape(()).item()))
+        out = self.tmp_view(op.result_shape, op.result_dtype)
+        self.emit_ew(self.expr_of(self.get(base)), out)
+        starts = [max(0, min(s, int(n) - int(u))) for s, n, u in zip(starts, base.shape, upd.shape)]
+        off, st = V.slice_view(out.offset, out.strides, starts, [1] * len(starts))
+        self.emit_ew(self.expr_of(self.get(upd)), out.with_(offset=off, shape=tuple(upd.shape), strides=st))
+        self.vals[("o", op.id)] = out
+
+    def op_gather(self, op):
+        x, ind = op.operands
+        a = op.attributes
+        xv = self.materialize(self.get(x), dense=True)
+        iv = self.materialize(self.get(ind), dense=True)
+        out = self.tmp_view(op.result_shape, op.result_dtype)
+        r = len(x.shape)
+        es = np.dtype(op.result_dtype).itemsize
+        cs = list(a["collapsed_slice_dims"])
+        if len(cs) == 1 and list(a["start_index_map"]) == cs and a["index_vector_dim"] == len(ind.shape):
+            ax = cs[0]
+            pre = int(np.prod(x.shape[:ax])) if ax else 1
+            post = int(np.prod(x.shape[ax + 1 :])) if ax + 1 < r else 1
+            n_idx = int(np.prod(ind.shape)) if len(ind.shape) else 1
+            self.step(
+                "take",
+                [self.bref(xv), self.bref(iv), self.bref(out)],
+                [E.dt_code(iv.dtype), pre, int(x.shape[ax]), post * es, n_idx],
+                note=f"take axis {ax}",
+            )
+        elif not a["offset_dims"] and cs == list(range(r)) and a["index_vector_dim"] == len(ind.shape) - 1:
+            n = int(np.prod(op.result_shape)) if len(op.result_shape) else 1
+            ints = [E.dt_code(iv.dtype), r, es, n] + [int(s) for s in x.shape] + list(V.dense_strides(x.shape))
+            self.step("gather_pts", [self.bref(xv), self.bref(iv), self.bref(out)], ints, note="point gather")
+        else:
+            raise NotImplementedError("gather form outside take / take_along_axis")
+        self.vals[("o", op.id)] = out
+
+    def op_scatter(self, op):
+        x, ind, upd = op.operands
+        a = op.attributes
+        if a.get("update_computation", "assign") != "assign":
+            raise NotImplementedError("scatter with a combiner")
+        out = self.tmp_view(op.result_shape, op.result_dtype)
+        self.emit_ew(self.expr_of(self.get(x)), out)
+        iv = self.materialize(self.get(ind), dense=True)
+        uv = self.materialize(self.get(upd), dense=True)
+        r = len(x.shape)
+        es = np.dtype(op.result_dtype).itemsize
+        ins = list(a["inserted_window_dims"])
+        if len(ins) == 1 and list(a["update_window_dims"]) == [d for d in range(r) if d != ins[0]]:
+            ax = ins[0]
+            pre = int(np.prod(x.shape[:ax])) if ax else 1
+            post = int(np.prod(x.shape[ax + 1 :])) if ax + 1 < r else 1
+            n_idx = int(np.prod(ind.shape)) if len(ind.shape) else 1
+            if pre != 1:
+                raise NotImplementedError("window scatter on an inner axis")
+            self.step(
+                "scatter_rows",
+                [self.bref(out), self.bref(iv), self.bref(uv)],
+                [E.dt_code(iv.dtype), pre, int(x.shape[ax]), post * es, n_idx],
+            )
+        elif not a["update_window_dims"] and ins == list(range(r)):
+            n = int(np.prod(upd.shape)) if len(upd.shape) else 1
+            ints = [E.dt_code(iv.dtype), r, es, n] + [int(s) for s in x.shape] + list(V.dense_strides(x.shape))
+            self.step("scatter_pts", [self.bref(out), self.bref(iv), self.bref(uv)], ints)
+        else:
+            raise NotImplementedError("scatter form")
+        self.vals[("o", op.id)] = out
+
+    def op_all_reduce(self, op):
+        x = op.operands[0]
+        if op.attributes.get("reduce_op", "add") != "add":
+            raise NotImplementedError("all-reduce other than sum")
+        groups = op.attributes.get("replica_groups") or [[0]]
+        if len(groups[0]) != self.world:
+            raise ValueError(
+                f"all-reduce over {len(groups[0])} ranks but the kernel is planned for world size {self.world}"
+            )
+        if self.world == 1:
+            self.put(op, self.get(x))
+            return
+        xv = self.materialize(self.get(x), dense=True)
+        out = self.tmp_view(op.result_shape, op.result_dtype)
+        self.step("allreduce", [self.bref(xv), self.bref(out)], [xv.size, E.dt_code(xv.dtype)], note=f"nccl {xv.size}")
+        self.needs_comm = True
+        self.vals[("o", op.id)] = out
+
+
+def lower(graph, name=None, world: int = 1) -> Plan:
+    return Lowering(graph, world=world).run(name or graph.name)

@@ -1,0 +1,340 @@
+"""Recognisers that map decomposed NumPy compositions back onto fused kernels.
+
+The reference never emits ``softmax`` or ``rms_norm`` nodes (their ops are
+declared without an implementation, ``core/ops/nn.py:12-160``): a kernel body
+writes them as NumPy compositions, and the tracer records the primitive
+nodes plus reshape/broadcast noise.  Each recogniser here walks one such
+composition backwards from its last node and, when every interior value is
+used only inside the composition, claims the nodes for one fused launch:
+
+* row softmax      reduce-max, subtract, exponential, reduce-add, divide
+                   (``tests/kernels/softmax.py:7-10``), optional bf16<->f32
+                   converts around it (``qwen3_embedding/kernels/softmax.py``);
+* RMSNorm          square, mean (reduce-add / N), + eps, sqrt, divide, * w,
+                   optional residual add in front and dtype converts
+                   (``qwen3_embedding/kernels/rmsnorm.py:4-16``);
+* argmax / argmin  reduce-max, compare, float iota, select, reduce-min,
+                   convert to int32 (``core/ops/reduce.py:227-311``).
+"""
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import numpy as np
+
+NOISE = ("reshape", "broadcast")
+
+
+def tkey(t):
+    return ("p", t.parameter_id) if t.is_parameter else ("o", t.id)
+
+
+class GraphIndex:
+    def __init__(self, graph):
+        self.graph = graph
+        self.consumers: Dict[tuple, List] = {}
+        for op in graph.operations:
+            for t in op.operands:
+                self.consumers.setdefault(tkey(t), []).append(op)
+        self.results = {tkey(r) for r in graph.results}
+
+    def uses(self, t) -> int:
+        return len(self.consumers.get(tkey(t), [])) + (1 if tkey(t) in self.results else 0)
+
+    @staticmethod
+    def producer(t):
+        return None if t.is_parameter else t.source_op
+
+
+def strip(t, ops: list, allowed=NOISE):
+    """Follow reshape/broadcast producers back to the underlying value."""
+    while True:
+        p = GraphIndex.producer(t)
+        if p is None or p.op_name not in allowed:
+            return t
+        ops.append(p)
+        t = p.operands[0]
+
+
+def _is_float(dt) -> bool:
+    from nkipy_b200.planner.ewprog import kind
+
+    return kind(dt) == "F"
+
+
+def strip_copy(t, ops: list):
+    """Skip ``copy`` nodes and float -> float32 ``convert`` nodes."""
+    while True:
+        p = GraphIndex.producer(t)
+        if p is None:
+            return t
+        if p.op_name == "copy" or (
+            p.op_name == "convert" and np.dtype(p.result_dtype) == np.float32 and _is_float(p.operands[0].dtype)
+        ):
+            ops.append(p)
+            t = p.operands[0]
+            continue
+        return t
+
+
+def scalar_const(t, ops: list):
+    base = strip(t, ops)
+    p = GraphIndex.producer(base)
+    if p is None or p.op_name != "constant":
+        return None
+    v = p.attributes.get("value")
+    if isinstance(v, np.ndarray):
+        if v.size != 1:
+            return None
+        v = v.reshape(()).item()
+    ops.append(p)
+    return float(v)
+
+
+def is_row_bcast(t, full_shape, ops: list):
+    """t is a (rows,)-vector broadcast back over the last axis of full_shape."""
+    p = GraphIndex.producer(t)
+    if p is None or p.op_name != "broadcast" or tuple(p.result_shape) != tuple(full_shape):
+        return None
+    n = len(full_shape)
+    if list(p.attributes.get("broadcast_dimensions", [])) != list(range(n - 1)):
+        return None
+    ops.append(p)
+    return strip(p.operands[0], ops)
+
+
+def last_axis_reduce(t, computation, ops: list):
+    p = GraphIndex.producer(t)
+    if p is None or p.op_name != "reduce" or p.attributes.get("computation") != computation:
+        return None
+    x = p.operands[0]
+    if list(p.attributes.get("dimensions", [])) != [len(x.shape) - 1]:
+        return None
+    ops.append(p)
+    ops.append(GraphIndex.producer(p.operands[1]))  # init constant
+    return x
+
+
+@dataclass
+class Claim:
+    kind: str
+    root: object  # the op whose result the fused kernel produces
+    interior: List = field(default_factory=list)
+    params: dict = field(default_factory=dict)
+
+
+def _exclusive(gi: GraphIndex, ops, root) -> bool:
+    """Every value produced inside (except the root's) is consumed only inside."""
+    inside = {id(o) for o in ops if o is not None} | {id(root)}
+    for o in ops:
+        if o is None or o is root:
+            continue
+        t_key = ("o", o.id)
+        if t_key in gi.results:
+            return False
+        for c in gi.consumers.get(t_key, []):
+            if id(c) not in inside:
+                return False
+    return True
+
+
+def match_softmax(gi: GraphIndex, div_op) -> Optional[Claim]:
+    if div_op.op_name != "divide" or len(div_op.result_shape) < 1:
+        return None
+    shape = tuple(div_op.result_shape)
+    ops = []
+    e, bs = div_op.operands
+    pe = GraphIndex.producer(e)
+    if pe is None or pe.op_name != "exponential":
+        return None
+    ops.append(pe)
+    sub = GraphIndex.producer(pe.operands[0])
+    if sub is None or sub.op_name != "subtract":
+        return None
+    ops.append(sub)
+    x, bm = sub.operands
+    s_base = is_row_bcast(bs, shape, ops)
+    if s_base is None:
+        return None
+    e2 = last_axis_reduce(s_base, "add", ops)
+    if e2 is None or tkey(e2) != tkey(e):
+        return None
+    m_base = is_row_bcast(bm, shape, ops)
+    if m_base is None:
+        return None
+    x2 = last_axis_reduce(m_base, "maximum", ops)
+    if x2 is None or tkey(x2) != tkey(x):
+        return None
+    if np.dtype(div_op.result_dtype) != np.float32 or tuple(x.shape) != shape:
+        return None
+    if not _exclusive(gi, ops, div_op):
+        return None
+    # absorb a bf16 -> f32 convert feeding x, and an f32 -> bf16 convert after
+    src = x
+    px = GraphIndex.producer(x)
+    if px is not None and px.op_name == "convert" and str(np.dtype(px.operands[0].dtype)) == "bfloat16" and gi.uses(
+        x
+    ) == 2:
+        ops.append(px)
+        src = px.operands[0]
+    root = div_op
+    out_dtype = np.dtype(np.float32)
+    cons = gi.consumers.get(("o", div_op.id), [])
+    if len(cons) == 1 and ("o", div_op.id) not in gi.results and cons[0].op_name == "convert" and str(
+        np.dtype(cons[0].result_dtype)
+    ) == "bfloat16":
+        ops.append(div_op)
+        root = cons[0]
+        out_dtype = np.dtype(cons[0].result_dtype)
+    return Claim("softmax", root, [o for o in ops if o is not None and o is not root], {"x": src, "out_dtype": out_dtype})
+
+
+def match_rmsnorm(gi: GraphIndex, mul_op) -> Optional[Claim]:
+    if mul_op.op_name != "multiply" or len(mul_op.result_shape) < 1:
+        return None
+    shape = tuple(mul_op.result_shape)
+    cols = shape[-1]
+    for zz, wb in (mul_op.operands, mul_op.operands[::-1]):
+        ops = []
+        pzz = GraphIndex.producer(zz)
+        if pzz is None or pzz.op_name != "divide":
+            continue
+        ops.append(pzz)
+        x32, qb = pzz.operands
+        q = is_row_bcast(qb, shape, ops)
+        if q is None:
+            continue
+        psq = GraphIndex.producer(q)
+        if psq is None or psq.op_name != "sqrt":
+            continue
+        ops.append(psq)
+        pa = GraphIndex.producer(psq.operands[0])
+        if pa is None or pa.op_name != "add":
+            continue
+        ops.append(pa)
+        m, eb = pa.operands
+        eps = scalar_const(eb, ops)
+        if eps is None:
+            continue
+        pm = GraphIndex.producer(m)
+        if pm is None or pm.op_name != "divide":
+            continue
+        ops.append(pm)
+        s_keep, cb = pm.operands
+        n = scalar_const(cb, ops)
+        if n is None or int(round(n)) != cols:
+            continue
+        z = last_axis_reduce(strip(s_keep, ops), "add", ops)
+        if z is None:
+            continue
+        pz = GraphIndex.producer(z)
+        if pz is None or pz.op_name != "multiply" or tkey(pz.operands[0]) != tkey(pz.operands[1]) or tkey(
+            pz.operands[0]
+        ) != tkey(x32):
+            continue
+        ops.append(pz)
+        # weight: (cols,) broadcast along rows
+        pwb = GraphIndex.producer(wb)
+        if pwb is None or pwb.op_name != "broadcast" or list(pwb.attributes["broadcast_dimensions"]) != [len(shape) - 1]:
+            continue
+        ops.append(pwb)
+        w32 = strip(pwb.operands[0], ops)
+        if tuple(w32.shape) != (cols,):
+            continue
+        w = strip_copy(w32, ops)
+        if np.dtype(mul_op.result_dtype) != np.float32 or tuple(x32.shape) != shape:
+            continue
+        x = strip_copy(x32, ops)
+        if not _exclusive(gi, ops, mul_op):
+            continue
+        # residual add in front of the norm
+        res = None
+        px = GraphIndex.producer(x)
+        if px is not None and px.op_name == "add" and tuple(px.operands[0].shape) == shape and tuple(
+            px.operands[1].shape
+        ) == shape and np.dtype(px.operands[0].dtype) == np.dtype(px.operands[1].dtype) == np.dtype(px.result_dtype):
+            res = px
+        root = mul_op
+        out_dtype = np.dtype(np.float32)
+        cons = gi.consumers.get(("o", mul_op.id), [])
+        if len(cons) == 1 and ("o", mul_op.id) not in gi.results and cons[0].op_name in ("convert", "copy"):
+            ops.append(mul_op)
+            root = cons[0]
+            out_dtype = np.dtype(cons[0].result_dtype)
+        if out_dtype != np.dtype(x.dtype):
+            continue
+        params = {"x": x, "w": w, "eps": eps, "out_dtype": out_dtype, "residual": None, "sum_needed": False}
+        if res is not None:
+            params["residual"] = (res.operands[0], res.operands[1])
+            inside = {id(o) for o in ops if o is not None} | {id(root), id(mul_op)}
+            params["sum_needed"] = tkey(x) in gi.results or any(
+                id(c) not in inside for c in gi.consumers.get(tkey(x), [])
+            )
+            ops.append(res)
+            params["sum_tensor"] = x
+        return Claim("rmsnorm", root, [o for o in ops if o is not None and o is not root], params)
+    return None
+
+
+def match_argmax(gi: GraphIndex, cvt_op) -> Optional[Claim]:
+    if cvt_op.op_name != "convert" or np.dtype(cvt_op.result_dtype) != np.int32:
+        return None
+    ops = []
+    sel_t = last_axis_reduce(cvt_op.operands[0], "minimum", ops)
+    if sel_t is None:
+        return None
+    psel = GraphIndex.producer(sel_t)
+    if psel is None or psel.op_name != "select":
+        return None
+    ops.append(psel)
+    mask, io, big = psel.operands
+    pio = GraphIndex.producer(io)
+    n = len(sel_t.shape)
+    if pio is None or pio.op_name != "iota" or pio.attributes.get("iota_dimension") != n - 1:
+        return None
+    ops.append(pio)
+    if scalar_const(big, ops) is None:
+        return None
+    pm = GraphIndex.producer(mask)
+    if pm is None or pm.op_name != "compare" or pm.attributes.get("comparison_direction") != "EQ":
+        return None
+    ops.append(pm)
+    x, bx = pm.operands
+    ext = is_row_bcast(bx, tuple(x.shape), ops)
+    if ext is None:
+        return None
+    pr = GraphIndex.producer(ext)
+    if pr is None or pr.op_name != "reduce":
+        return None
+    comp = pr.attributes.get("computation")
+    if comp not in ("maximum", "minimum"):
+        return None
+    x2 = last_axis_reduce(ext, comp, ops)
+    if x2 is None or tkey(x2) != tkey(x):
+        return None
+    if not _exclusive(gi, ops, cvt_op):
+        return None
+    return Claim("argmax", cvt_op, [o for o in ops if o is not None], {"x": x, "is_max": comp == "maximum"})
+
+
+MATCHERS = (match_softmax, match_rmsnorm, match_argmax)
+
+
+def find_claims(graph) -> Dict[int, Claim]:
+    gi = GraphIndex(graph)
+    claims: Dict[int, Claim] = {}
+    taken = set()
+    for op in reversed(graph.operations):
+        if id(op) in taken:
+            continue
+        for m in MATCHERS:
+            c = m(gi, op)
+            if c is None:
+                continue
+            ids = {id(o) for o in c.interior} | {id(c.root)}
+            if ids & taken:
+                continue
+            taken |= ids
+            claims[c.root.id] = c
+            break
+    return claims, taken

@@ -1,0 +1,342 @@
+"""The ``Spike`` runtime object over libnkb (reference: ``spike/src/spike.cpp``,
+``spike/src/include/spike.h:28-86``, nanobind surface ``python_bindings.cpp``).
+
+Same method names and meanings as the reference's ``_spike.Spike``:
+``allocate_tensor`` / ``slice_from_tensor`` / ``free_tensor``,
+``tensor_write`` / ``tensor_read`` (+ ``_pybuffer`` variants, bounds-checked),
+``load_model`` / ``unload_model``, ``execute`` (name-keyed tensor dicts) and
+``get_tensor_info``.  A "model" is a launch plan file (``*.nkbplan``) instead
+of a NEFF; ``core_id`` is the CUDA device of this process.  One runtime per
+process, bound to one GPU (``NKB_DEVICE``, else ``LOCAL_RANK``, else 0).
+"""
+
+import ctypes
+import json
+import os
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import numpy as np
+
+from nkipy_b200.spike import _nkb
+from nkipy_b200.spike._nkb import NkbError, SpikeError
+
+COMM_ID_BYTES = 128
+
+
+def default_device() -> int:
+    for var in ("NKB_DEVICE", "LOCAL_RANK"):
+        v = os.environ.get(var)
+        if v is not None and v.strip().isdigit():
+            return int(v)
+    return 0
+
+
+@dataclass
+class TensorMetadata:
+    size: int
+    dtype: str
+    shape: List[int]
+
+
+@dataclass
+class ModelTensorInfo:
+    inputs: Dict[str, TensorMetadata] = field(default_factory=dict)
+    outputs: Dict[str, TensorMetadata] = field(default_factory=dict)
+
+
+class NkbTensor:
+    """A device buffer handle (reference ``NrtTensor``, tensor.h:14-53)."""
+
+    __slots__ = ("handle", "size", "core_id", "name", "_freed", "_keepalive", "__weakref__")
+
+    def __init__(self, handle, size, core_id, name=None, keepalive=None):
+        self.handle = handle
+        self.size = size
+        self.core_id = core_id
+        self.name = name
+        self._freed = False
+        self._keepalive = keepalive
+
+    @property
+    def va(self) -> int:
+        ptr = ctypes.c_void_p()
+        _nkb.call("nkb_buf_info", self.handle, None, None, ctypes.byref(ptr))
+        return ptr.value or 0
+
+    def __del__(self):
+        if not self._freed and self.handle and _nkb._lib is not None:
+            try:
+                _nkb.lib().nkb_free(self.handle)
+            except Exception:
+                pass
+            self._freed = True
+
+    def __repr__(self):
+        return f"NkbTensor(name={self.name}, size={self.size}, core_id={self.core_id})"
+
+
+class NkbModel:
+    """A loaded launch plan (reference ``NrtModel``, model.h:12-55)."""
+
+    def __init__(self, handle, core_id, path, io, rank_id=0, world_size=1, comm=None):
+        self.handle = handle
+        self.core_id = core_id
+        self.path = path
+        self.io = io
+        self.rank_id = rank_id
+        self.world_size = world_size
+        self.comm = comm
+        n = ctypes.c_int()
+        _nkb.call("nkb_plan_num_launches", handle, ctypes.byref(n))
+        self.num_launches = n.value
+        s = ctypes.c_size_t()
+        _nkb.call("nkb_plan_scratch_bytes", handle, ctypes.byref(s))
+        self.scratch_bytes = s.value
+
+    def __del__(self):
+        if self.handle and _nkb._lib is not None:
+            try:
+                _nkb.lib().nkb_plan_free(self.handle)
+            except Exception:
+                pass
+            self.handle = None
+
+    def __repr__(self):
+        return f"NkbModel({os.path.basename(self.path)}, core_id={self.core_id}, launches={self.num_launches})"
+
+
+_COMMS = {}
+
+
+def _communicator(rank: int, world: int, device: int):
+    """One NCCL communicator per (world, rank) and process.
+
+    The unique id is created on rank 0 and broadcast with torch.distributed --
+    the same control plane the reference uses to distribute its NEFF path
+    (runtime/device_kernel.py:142-197).
+    """
+    key = (world, rank)
+    if key in _COMMS:
+        return _COMMS[key]
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()):
+        raise ValueError("a collective plan needs torch.distributed to be initialised to exchange the NCCL id")
+    buf = (ctypes.c_uint8 * COMM_ID_BYTES)()
+    if rank == 0:
+        _nkb.call("nkb_comm_unique_id", ctypes.cast(buf, ctypes.c_void_p))
+    obj = [bytes(buf)]
+    dist.broadcast_object_list(obj, src=0)
+    ctypes.memmove(buf, obj[0], COMM_ID_BYTES)
+    comm = ctypes.c_void_p()
+    _nkb.call("nkb_comm_init", ctypes.cast(buf, ctypes.c_void_p), rank, world, device, ctypes.byref(comm))
+    _COMMS[key] = comm
+    return comm
+
+
+class Spike:
+    def __init__(self, verbose: int = 0, device: Optional[int] = None):
+        self.verbose = verbose
+        self.device = default_device() if device is None else device
+        _nkb.call("nkb_init", self.device)
+        self._closed = False
+
+    @staticmethod
+    def get_visible_neuron_core_count() -> int:
+        """Number of visible CUDA devices (name kept from the reference)."""
+        try:
+            n = ctypes.c_int()
+            _nkb.call("nkb_device_count", ctypes.byref(n))
+            return n.value
+        except (ImportError, NkbError, OSError):
+            return 0
+
+    get_visible_device_count = get_visible_neuron_core_count
+
+    def close(self) -> int:
+        if not self._closed:
+            for c in list(_COMMS.values()):
+                _nkb.lib().nkb_comm_free(c)
+            _COMMS.clear()
+            _nkb.call("nkb_shutdown")
+            self._closed = True
+        return 0
+
+    def is_closed(self) -> bool:
+        return self._closed
+
+    def _check_core(self, core_id):
+        if core_id != self.device:
+            raise SpikeError(f"core_id {core_id} is not this process's device {self.device}")
+
+    # -- tensors --------------------------------------------------------------
+    def allocate_tensor(self, size: int, core_id: Optional[int] = None, name: Optional[str] = None) -> NkbTensor:
+        core_id = self.device if core_id is None else core_id
+        self._check_core(core_id)
+        h = ctypes.c_void_p()
+        _nkb.call("nkb_alloc", int(size), core_id, ctypes.byref(h))
+        return NkbTensor(h, int(size), core_id, name)
+
+    def wrap_device_memory(self, ptr: int, size: int, name=None, keepalive=None) -> NkbTensor:
+        h = ctypes.c_void_p()
+        _nkb.call("nkb_wrap", ctypes.c_void_p(ptr), int(size), self.device, ctypes.byref(h))
+        return NkbTensor(h, int(size), self.device, name, keepalive=keepalive)
+
+    def slice_from_tensor(self, source: NkbTensor, offset: int = 0, size: int = 0, name: Optional[str] = None):
+        self._live(source)
+        h = ctypes.c_void_p()
+        _nkb.call("nkb_slice", source.handle, int(offset), int(size), ctypes.byref(h))
+        real = size if size else source.size - offset
+        return NkbTensor(h, int(real), source.core_id, name, keepalive=source)
+
+    def free_tensor(self, tensor: NkbTensor):
+        self._live(tensor)
+        _nkb.call("nkb_free", tensor.handle)
+        tensor._freed = True
+
+    @staticmethod
+    def _live(t: NkbTensor):
+        if t._freed:
+            raise SpikeError(f"tensor {t.name!r} has been freed")
+
+    def tensor_write(self, tensor: NkbTensor, data: bytes, offset: int = 0):
+        self._live(tensor)
+        buf = ctypes.create_string_buffer(bytes(data), len(data))
+        _nkb.call("nkb_h2d", tensor.handle, ctypes.cast(buf, ctypes.c_void_p), len(data), int(offset))
+
+    def tensor_read(self, tensor: NkbTensor, offset: int = 0, size: int = 0) -> bytes:
+        self._live(tensor)
+        size = size or tensor.size - offset
+        buf = ctypes.create_string_buffer(size)
+        _nkb.call("nkb_d2h", tensor.handle, ctypes.cast(buf, ctypes.c_void_p), int(size), int(offset))
+        return buf.raw
+
+    def tensor_write_from_pybuffer(self, tensor: NkbTensor, data, offset: int = 0):
+        self._live(tensor)
+        arr = np.ascontiguousarray(np.frombuffer(memoryview(data).cast("B"), dtype=np.uint8))
+        _nkb.call("nkb_h2d", tensor.handle, arr.ctypes.data_as(ctypes.c_void_p), arr.nbytes, int(offset))
+
+    def tensor_read_to_pybuffer(self, tensor: NkbTensor, data, offset: int = 0):
+        self._live(tensor)
+        mv = memoryview(data).cast("B")
+        if mv.readonly:
+            raise SpikeError("destination buffer is read-only")
+        c = (ctypes.c_uint8 * mv.nbytes).from_buffer(mv)
+        _nkb.call("nkb_d2h", tensor.handle, ctypes.cast(c, ctypes.c_void_p), mv.nbytes, int(offset))
+
+    # -- models -------------------------------------------------------------------
+    def load_model(self, plan_file: str, core_id: Optional[int] = None, cc_enabled: bool = False,
+                   rank_id: int = 0, world_size: int = 1) -> NkbModel:
+        core_id = self.device if core_id is None else core_id
+        self._check_core(core_id)
+        text, consts, io = read_plan_files(plan_file)
+        h = ctypes.c_void_p()
+        raw = text.encode()
+        _nkb.call("nkb_plan_load", raw, len(raw), core_id, ctypes.byref(h))
+        model = NkbModel(h, core_id, plan_file, io, rank_id, world_size)
+        for i, c in enumerate(consts):
+            c = np.ascontiguousarray(c)
+            _nkb.call("nkb_plan_set_const", h, i, c.ctypes.data_as(ctypes.c_void_p), c.nbytes)
+        if cc_enabled and world_size > 1:
+            model.comm = _communicator(rank_id, world_size, core_id)
+            _nkb.call("nkb_plan_bind_comm", h, model.comm)
+        elif io.get("needs_comm"):
+            raise ValueError("this plan contains collectives: load it with cc_enabled=True, rank_id and world_size")
+        return model
+
+    def unload_model(self, model: NkbModel):
+        if model.handle:
+            _nkb.call("nkb_plan_free", model.handle)
+            model.handle = None
+
+    def _io_lists(self, model, inputs, outputs):
+        ins, outs = [], []
+        for spec in model.io["inputs"]:
+            t = inputs.get(spec["name"])
+            if t is None:
+                raise SpikeError(f"missing input '{spec['name']}'")
+            self._live(t)
+            ins.append(t.handle)
+        for spec in model.io["outputs"]:
+            t = outputs.get(spec["name"])
+            if t is None:
+                raise SpikeError(f"missing output '{spec['name']}'")
+            self._live(t)
+            outs.append(t.handle)
+        extra = set(inputs) - {s["name"] for s in model.io["inputs"]}
+        if extra:
+            raise SpikeError(f"unknown inputs {sorted(extra)}")
+        extra = set(outputs) - {s["name"] for s in model.io["outputs"]}
+        if extra:
+            raise SpikeError(f"unknown outputs {sorted(extra)}")
+        I = (ctypes.c_void_p * max(1, len(ins)))(*[h.value for h in ins])
+        O = (ctypes.c_void_p * max(1, len(outs)))(*[h.value for h in outs])
+        return I, len(ins), O, len(outs)
+
+    def execute(self, model: NkbModel, inputs: Dict[str, NkbTensor], outputs: Dict[str, NkbTensor],
+                ntff_name: Optional[str] = None, save_trace: bool = False, use_graph: bool = False):
+        I, ni, O, no = self._io_lists(model, inputs, outputs)
+        _nkb.call("nkb_execute", model.handle, I, ni, O, no, None, int(use_graph))
+        _nkb.call("nkb_synchronize")
+        flag = ctypes.c_int()
+        _nkb.call("nkb_device_error", ctypes.byref(flag))
+        if flag.value:
+            raise NkbError(7, "a kernel's bounded wait expired; results are invalid")
+
+    def time_execute(self, model: NkbModel, inputs, outputs, warmup: int, iters: int, use_graph: bool = True):
+        I, ni, O, no = self._io_lists(model, inputs, outputs)
+        ms = (ctypes.c_float * iters)()
+        _nkb.call("nkb_time_execute", model.handle, I, ni, O, no, warmup, iters, int(use_graph), ms)
+        return [float(v) for v in ms]
+
+    def time_steps(self, model: NkbModel, inputs, outputs, iters: int):
+        """Mean device time of every launch of the plan (ms), in plan order."""
+        I, ni, O, no = self._io_lists(model, inputs, outputs)
+        ms = (ctypes.c_float * max(1, model.num_launches))()
+        _nkb.call("nkb_time_steps", model.handle, I, ni, O, no, iters, ms)
+        return [float(ms[i]) for i in range(model.num_launches)]
+
+    def get_tensor_info(self, model: NkbModel) -> ModelTensorInfo:
+        info = ModelTensorInfo()
+        for key, dst in (("inputs", info.inputs), ("outputs", info.outputs)):
+            for spec in model.io[key]:
+                dt = np.dtype(spec["dtype"]) if spec["dtype"] != "bfloat16" else None
+                size = int(np.prod(spec["shape"], dtype=np.int64)) * (2 if dt is None else dt.itemsize)
+                dst[spec["name"]] = TensorMetadata(size=size, dtype=spec["dtype"], shape=list(spec["shape"]))
+        return info
+
+
+# -- plan files ---------------------------------------------------------------------
+def write_plan_files(plan, path: str):
+    """``<path>`` (plan text), ``<path>.consts.npz`` and ``<path>.io.json``."""
+    os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
+    with open(path, "w") as f:
+        f.write(plan.to_text())
+    np.savez(path + ".consts.npz", **{f"c{i}": c.view(np.uint8).reshape(-1) for i, c in enumerate(plan.consts)})
+    io = {
+        "name": plan.name,
+        "inputs": [{"name": s.name, "shape": list(s.shape), "dtype": str(np.dtype(s.dtype))} for s in plan.inputs],
+        "outputs": [{"name": s.name, "shape": list(s.shape), "dtype": str(np.dtype(s.dtype))} for s in plan.outputs],
+        "aliases": plan.aliases,
+        "needs_comm": plan.needs_comm,
+        "launches": len(plan.steps),
+        "kernels": plan.kernel_counts(),
+    }
+    with open(path + ".io.json", "w") as f:
+        json.dump(io, f, indent=1)
+
+
+def read_plan_files(path: str):
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"plan file not found: {path}")
+    with open(path) as f:
+        text = f.read()
+    with open(path + ".io.json") as f:
+        io = json.load(f)
+    consts = []
+    cpath = path + ".consts.npz"
+    if os.path.exists(cpath):
+        with np.load(cpath) as z:
+            consts = [z[f"c{i}"] for i in range(len(z.files))]
+    return text, consts, io

@@ -1,0 +1,36 @@
+"""Import helper for the fixture generators in this folder.
+
+The reference package (shaojiex-aws/nkipy) imports two protobuf modules that
+its wheel build generates (``nkipy/setup.py:53-85``) and that are not present
+in a source checkout.  Stub modules stand in for them so that the tracer and
+the NumPy kernel bodies can be imported; nothing here serialises protobufs.
+Only the generator scripts use this, and only where the reference tree is
+available; tests read the committed fixtures instead.
+"""
+
+import os
+import sys
+import types
+
+REF_ROOT = os.environ.get("NKIPY_REFERENCE_ROOT", "/root/reference")
+
+
+def import_reference():
+    src = os.path.join(REF_ROOT, "nkipy", "src")
+    if not os.path.isdir(src):
+        raise RuntimeError(f"reference tree not found under {REF_ROOT}")
+    if src not in sys.path:
+        sys.path.insert(0, src)
+    for name in ("nkipy.third_party.xla.xla_data_pb2", "nkipy.third_party.xla.service.hlo_pb2"):
+        if name not in sys.modules:
+            mod = types.ModuleType(name)
+
+            def _missing(attr, _n=name):
+                return 0
+
+            mod.__getattr__ = _missing
+            sys.modules[name] = mod
+    import nkipy.core.trace as ref_trace  # noqa: F401
+    import nkipy.core.backend.hlo as ref_hlo  # noqa: F401
+
+    return ref_trace, ref_hlo
