@@ -233,9 +233,13 @@ def match_rmsnorm(gi: GraphIndex, mul_op) -> Optional[Claim]:
         ) != tkey(x32):
             continue
         ops.append(pz)
-        # weight: (cols,) broadcast along rows
+        # weight: a (cols,) vector broadcast along the rows
         pwb = GraphIndex.producer(wb)
-        if pwb is None or pwb.op_name != "broadcast" or list(pwb.attributes["broadcast_dimensions"]) != [len(shape) - 1]:
+        if pwb is None or pwb.op_name != "broadcast":
+            continue
+        bd = list(pwb.attributes["broadcast_dimensions"])
+        src_shape = tuple(pwb.operands[0].shape)
+        if not bd or bd[-1] != len(shape) - 1 or src_shape[-1] != cols or any(s_ != 1 for s_ in src_shape[:-1]):
             continue
         ops.append(pwb)
         w32 = strip(pwb.operands[0], ops)

@@ -212,18 +212,26 @@ class Spike:
         _nkb.call("nkb_d2h", tensor.handle, ctypes.cast(buf, ctypes.c_void_p), int(size), int(offset))
         return buf.raw
 
+    @staticmethod
+    def _bytes_view(data):
+        """A uint8 ndarray over ``data`` (ndarrays of any dtype, incl. bf16, or buffers)."""
+        if isinstance(data, np.ndarray):
+            if not data.flags.c_contiguous:
+                raise SpikeError("buffer must be C-contiguous")
+            return data.reshape(-1).view(np.uint8)
+        return np.frombuffer(memoryview(data).cast("B"), dtype=np.uint8)
+
     def tensor_write_from_pybuffer(self, tensor: NkbTensor, data, offset: int = 0):
         self._live(tensor)
-        arr = np.ascontiguousarray(np.frombuffer(memoryview(data).cast("B"), dtype=np.uint8))
+        arr = self._bytes_view(np.ascontiguousarray(data) if isinstance(data, np.ndarray) else data)
         _nkb.call("nkb_h2d", tensor.handle, arr.ctypes.data_as(ctypes.c_void_p), arr.nbytes, int(offset))
 
     def tensor_read_to_pybuffer(self, tensor: NkbTensor, data, offset: int = 0):
         self._live(tensor)
-        mv = memoryview(data).cast("B")
-        if mv.readonly:
+        arr = self._bytes_view(data)
+        if not arr.flags.writeable:
             raise SpikeError("destination buffer is read-only")
-        c = (ctypes.c_uint8 * mv.nbytes).from_buffer(mv)
-        _nkb.call("nkb_d2h", tensor.handle, ctypes.cast(c, ctypes.c_void_p), mv.nbytes, int(offset))
+        _nkb.call("nkb_d2h", tensor.handle, arr.ctypes.data_as(ctypes.c_void_p), arr.nbytes, int(offset))
 
     # -- models -------------------------------------------------------------------
     def load_model(self, plan_file: str, core_id: Optional[int] = None, cc_enabled: bool = False,

@@ -251,7 +251,9 @@ def shard_layer_weights(full, shape: LayerShape, rank, world):
 
 
 def layer_args(x, shard, shape: LayerShape, world):
-    cos, sin = rope_tables(x.shape[1], shape.head_dim, shape.theta)
+    # bf16 tables, as the reference's TP attention builds them
+    # (examples/models/qwen3/kernels/attention.py: compute_cos_sin_cache(..., dtype=bfloat16))
+    cos, sin = (t.astype(x.dtype) for t in rope_tables(x.shape[1], shape.head_dim, shape.theta))
     args = (x, shard["ln1"], shard["qkv"], shard["o"], shard["ln2"], shard["gate_up"], shard["down"], cos, sin)
     kwargs = dict(
         n_heads=shape.n_heads, n_kv_heads=shape.n_kv_heads, head_dim=shape.head_dim, eps=shape.eps, tp_world=world

@@ -81,10 +81,20 @@ def rope_tables(seq_len, head_dim, theta):
 
 
 def _rope(x, cos, sin):
-    """Half-split rotation of ``rope.py:34-57``; x (B,S,H,D), tables (S, D/2)."""
+    """Half-split rotation of ``rope.py:34-57``; x (B,S,H,D), tables (S, D/2).
+
+    With bf16 operands every product and sum is rounded to bf16, as the
+    NumPy/ml_dtypes direct call of the kernel body does.
+    """
     h = x.shape[-1] // 2
     c, s = cos[None, :, None, :], sin[None, :, None, :]
     x0, x1 = x[..., :h], x[..., h:]
+    if x.dtype == bfloat16 and cos.dtype == bfloat16:
+        f = lambda a: a.astype(np.float32)  # noqa: E731
+        r = lambda a: a.astype(bfloat16)  # noqa: E731
+        lo = r(f(r(f(x0) * f(c))) - f(r(f(x1) * f(s))))
+        hi = r(f(r(f(x0) * f(s))) + f(r(f(x1) * f(c))))
+        return np.concatenate([lo, hi], axis=-1)
     return np.concatenate([x0 * c - x1 * s, x0 * s + x1 * c], axis=-1)
 
 
@@ -110,7 +120,7 @@ def llama_layer(x, w, n_heads, n_kv_heads, head_dim, eps, theta, heads=None):
     q = qkv[..., :nq].reshape(B, S, n_heads, head_dim)
     k = qkv[..., nq : nq + nkv].reshape(B, S, n_kv_heads, head_dim)
     v = qkv[..., nq + nkv :].reshape(B, S, n_kv_heads, head_dim)
-    cos, sin = rope_tables(S, head_dim, theta)
+    cos, sin = (t.astype(bf) for t in rope_tables(S, head_dim, theta))
     q = _rope(q, cos, sin).astype(bf)
     k = _rope(k, cos, sin).astype(bf)
     rep = n_heads // n_kv_heads

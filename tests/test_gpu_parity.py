@@ -113,3 +113,16 @@ def test_reductions():
     assert_close(s, x.sum(0), 1e-5)
     np.testing.assert_array_equal(m, x.max(1))
     assert_close(mu, np.mean(x), 1e-5)
+
+
+@pytest.mark.parametrize("batch,seq", [(2, 128), (1, 512)])
+def test_llama_layer_tp1(batch, seq):
+    s = W.LayerShape(batch=batch, seq=seq, hidden=512, n_heads=8, n_kv_heads=2, head_dim=64, ffn=1024)
+    full = W.layer_weights(s, seed=1)
+    shard = W.shard_layer_weights(full, s, 0, 1)
+    x = np.random.default_rng(12).standard_normal((batch, seq, s.hidden), dtype=np.float32).astype(BF16)
+    args, kw = W.layer_args(x, shard, s, 1)
+    got = on_device(W.llama_decoder_layer_kernel, *args, **kw)
+    want = O.llama_layer(x, full, s.n_heads, s.n_kv_heads, s.head_dim, s.eps, s.theta)
+    assert got.dtype == BF16
+    assert_close(got, want, BF16_RTOL)

@@ -1,0 +1,90 @@
+"""The CPU oracle reproduces the reference's own NumPy kernel bodies.
+
+Golden vectors were produced by running the reference's functions
+(tests/kernels/softmax.py, examples/models/qwen3_embedding/kernels/*,
+core/ops/collectives.py cpu implementations) -- see tests/golden/make_golden.py.
+"""
+
+import os
+
+import ml_dtypes
+import numpy as np
+
+from nkipy_b200 import workloads as W
+from oracle import numpy_ref as O
+
+BF16 = np.dtype(ml_dtypes.bfloat16)
+_z = np.load(os.path.join(os.path.dirname(__file__), "golden", "vectors.npz"))
+_bf = set(_z["_bf16_keys"].tolist())
+
+
+def V(k):
+    a = _z[k]
+    return a.view(BF16) if k in _bf else a
+
+
+def test_softmax_vectors():
+    for i in range(3):
+        np.testing.assert_allclose(O.softmax(V(f"softmax{i}_x")), V(f"softmax{i}_y"), rtol=1e-6, atol=1e-7)
+        # the workload body traced by the bench is the same computation
+        np.testing.assert_allclose(W.softmax_kernel(V(f"softmax{i}_x")), V(f"softmax{i}_y"), rtol=1e-6, atol=1e-7)
+
+
+def test_rmsnorm_vectors():
+    got = O.residual_rmsnorm(V("rms_x"), V("rms_r"), V("rms_w"), 1e-6)
+    np.testing.assert_allclose(got, V("rms_y"), rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(W.residual_rmsnorm_kernel(V("rms_x"), V("rms_r"), V("rms_w")), V("rms_y"), rtol=1e-6, atol=1e-6)
+
+
+def test_rope_vectors():
+    cos, sin = O.rope_tables(64, 128, 500000.0)
+    np.testing.assert_allclose(cos, V("rope_cos"), rtol=1e-6)
+    np.testing.assert_allclose(sin, V("rope_sin"), rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(O._rope(V("rope_q"), cos, sin), V("rope_qo"), rtol=1e-5, atol=1e-6)
+    q, k = W.rope(V("rope_q"), V("rope_k"), cos, sin)
+    np.testing.assert_allclose(q, V("rope_qo"), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(k, V("rope_ko"), rtol=1e-5, atol=1e-6)
+
+
+def test_layer_vectors():
+    w = {
+        "qkv": V("layer_qkv"), "o": V("layer_o"), "gate": V("layer_gate"), "up": V("layer_up"), "down": V("layer_down"),
+        "ln1": np.ones(256, BF16), "ln2": np.ones(256, BF16),
+    }
+    got = O.llama_layer(V("layer_x"), w, n_heads=4, n_kv_heads=2, head_dim=64, eps=1e-6, theta=500000.0)
+    want = V("layer_y")
+    err = np.max(np.abs(got.astype(np.float32) - want)) / np.max(np.abs(want))
+    assert err < 2e-2, err
+    # the traced workload body (TP=1) computes the same layer
+    s = W.LayerShape(batch=1, seq=32, hidden=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=512)
+    shard = W.shard_layer_weights(w, s, 0, 1)
+    args, kw = W.layer_args(V("layer_x"), shard, s, 1)
+    y2 = W.llama_decoder_layer_kernel(*args, **kw)
+    err2 = np.max(np.abs(np.asarray(y2, np.float32) - want)) / np.max(np.abs(want))
+    assert err2 < 2e-2, err2
+
+
+def test_collective_cpu_semantics():
+    from nkipy_b200.core.ops import collectives as C
+
+    d = V("cc_in")
+    np.testing.assert_array_equal(C.all_reduce(d, replica_groups=[[0, 1, 2, 3]]), V("cc_all_reduce_w4"))
+    np.testing.assert_array_equal(C.all_gather(d, all_gather_dim=1, replica_groups=[[0, 1]]), V("cc_all_gather_w2"))
+    np.testing.assert_array_equal(
+        C.reduce_scatter(d, reduce_scatter_dim=0, replica_groups=[[0, 1]]), V("cc_reduce_scatter_w2")
+    )
+    np.testing.assert_array_equal(
+        C.all_to_all(d, split_dimension=1, concat_dimension=0, replica_groups=[[0, 1]]), V("cc_all_to_all_w2")
+    )
+    np.testing.assert_array_equal(O.all_reduce_identical(d, 4), V("cc_all_reduce_w4"))
+
+
+def test_linear_attention_forms_agree():
+    rng = np.random.default_rng(3)
+    q, k, v = (rng.standard_normal((1, 2, 256, 32), dtype=np.float32) for _ in range(3))
+    a = W.chunked_linear_attention_kernel(q, k, v, chunk=64)
+    b = O.linear_attention_recurrent(q, k, v, chunk=64)
+    np.testing.assert_allclose(a, b, rtol=2e-4, atol=1e-5)
+    # chunk size does not change the result (pure reassociation)
+    c = O.linear_attention_recurrent(q, k, v, chunk=16)
+    np.testing.assert_allclose(b, c, rtol=2e-4, atol=1e-5)

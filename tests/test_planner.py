@@ -1,0 +1,135 @@
+"""Planner unit tests (CPU): view algebra, fusion decisions, plan format."""
+
+import ml_dtypes
+import numpy as np
+import pytest
+
+from nkipy_b200 import workloads as W
+from nkipy_b200.core.trace import NKIPyKernel
+from nkipy_b200.planner import ewprog as E
+from nkipy_b200.planner import lower
+from nkipy_b200.planner import views as V
+
+BF16 = np.dtype(ml_dtypes.bfloat16)
+
+
+def plan_of(fn, *args, **kw):
+    return lower(NKIPyKernel.trace(fn).specialize(*args, **kw))
+
+
+@pytest.mark.parametrize(
+    "shape,perm_or_none,new_shape",
+    [((4, 6), None, (24,)), ((4, 6), None, (2, 2, 6)), ((2, 3, 4), (1, 0, 2), (6, 4)), ((3, 4), (1, 0), (12,))],
+)
+def test_reshape_strides_matches_numpy(shape, perm_or_none, new_shape):
+    a = np.arange(int(np.prod(shape))).reshape(shape)
+    st = V.dense_strides(shape)
+    if perm_or_none is not None:
+        a = a.transpose(perm_or_none)
+        st = V.transpose_strides(st, perm_or_none)
+    got = V.reshape_strides(a.shape, st, new_shape)
+    try:
+        r = a.view()
+        r.shape = new_shape  # numpy raises when a copy would be needed
+        want = tuple(s // a.itemsize for s in r.strides)
+    except AttributeError:
+        want = None
+    if want is None:
+        assert got is None
+    else:
+        flat = np.arange(int(np.prod(shape))).reshape(shape)
+        idx = np.indices(new_shape).reshape(len(new_shape), -1)
+        offs = sum(i * s for i, s in zip(idx, got))
+        np.testing.assert_array_equal(flat.reshape(-1)[offs], r.reshape(-1))
+
+
+def test_collapse_merges_contiguous_axes():
+    shp, sets = V.collapse((4, 5, 6), [(30, 6, 1), (0, 0, 1)])
+    assert shp == (20, 6) and sets == [(6, 1), (0, 1)]
+
+
+@pytest.mark.parametrize(
+    "name,args,kernels",
+    [
+        ("softmax", W.make_inputs("softmax", scale=1 / 512), {"softmax_rows": 1}),
+        ("rmsnorm", W.make_inputs("rmsnorm", scale=1 / 2048), {"rmsnorm_rows": 1}),
+        ("gemm", W.make_inputs("gemm", scale=1 / 64), {"gemm_bf16": 1}),
+        ("bmm", W.make_inputs("bmm", scale=1 / 32), {"gemm_bf16": 1}),
+    ],
+)
+def test_config_kernels_plan_to_one_fused_launch(name, args, kernels):
+    p = plan_of(W.KERNELS[name], *args)
+    assert p.kernel_counts() == kernels
+
+
+def test_elementwise_chain_is_one_launch():
+    def k(x, w):
+        return np.tanh(x * 2.0 + w[None, :]) - np.exp(-x)
+
+    p = plan_of(k, np.zeros((8, 16), np.float32), np.zeros(16, np.float32))
+    assert p.kernel_counts() == {"ew": 1}
+
+
+def test_plan_text_roundtrip_fields():
+    p = plan_of(W.softmax_kernel, np.zeros((4, 64), np.float32))
+    t = p.to_text()
+    assert t.startswith("NKBPLAN 1") and t.rstrip().endswith("end")
+    assert "step softmax_rows" in t
+
+
+def test_bool_output_is_bytes():
+    p = plan_of(lambda x: x > 0, np.zeros((3, 3), np.float32))
+    assert np.dtype(p.outputs[0].dtype) == np.uint8
+
+
+def test_unsupported_op_fails_loudly():
+    from nkipy_b200.core.ops import nn
+
+    def k(x):
+        v, i = nn.topk(x, 2, axis=-1)
+        return v
+
+    with pytest.raises(NotImplementedError):
+        plan_of(k, np.zeros((4, 8), np.float32))
+
+
+def test_ew_program_budget_split():
+    def k(x):
+        y = x
+        for i in range(40):
+            y = np.tanh(y * 1.01 + float(i))
+        return y
+
+    p = plan_of(k, np.zeros((4, 4), np.float32))
+    assert all(s.kernel == "ew" for s in p.steps)
+    assert len(p.steps) >= 2
+
+
+def test_ew_compile_bf16_rounding_inserted():
+    x = E.leaf(V.View(0, 0, (4,), (1,), BF16))
+    e = E.op("add", [x, x], (4,), BF16)
+    c = E.compile_ew(e, V.View(1, 0, (4,), (1,), BF16))
+    ops = c.ints[7 + 1 + 1 + 1 + (2 + 1) :]
+    assert E.OP["RBF"] in ops[0::6]
+
+
+def test_layer_plans(monkeypatch):
+    s = W.LayerShape(batch=1, seq=64, hidden=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=512)
+    full = W.layer_weights(s, seed=0)
+    shard = W.shard_layer_weights(full, s, 0, 1)
+    x = np.zeros((1, 64, 256), BF16)
+    args, kw = W.layer_args(x, shard, s, 1)
+    p = plan_of(W.llama_decoder_layer_kernel, *args, **kw)
+    counts = p.kernel_counts()
+    assert counts.get("gemm_bf16", 0) >= 4
+    assert counts.get("rmsnorm_rows", 0) == 2
+    assert "allreduce" not in counts
+
+
+def test_layer_tp2_has_two_allreduces():
+    s = W.LayerShape(batch=1, seq=64, hidden=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=512)
+    full = W.layer_weights(s, seed=0)
+    shard = W.shard_layer_weights(full, s, 1, 2)
+    args, kw = W.layer_args(np.zeros((1, 64, 256), BF16), shard, s, 2)
+    p = lower(NKIPyKernel.trace(W.llama_decoder_layer_kernel).specialize(*args, **kw), world=2)
+    assert p.kernel_counts()["allreduce"] == 2 and p.needs_comm
