@@ -65,12 +65,9 @@ __device__ __forceinline__ float rnd_bf16(float x) { return __bfloat162float(__f
 __device__ __forceinline__ float rnd_f16(float x) { return __half2float(__float2half_rn(x)); }
 __device__ __forceinline__ float fsignf(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : x); }
 
-// Executes the program for VEC lanes whose per-input element offsets and
-// per-axis indices are given.
-__device__ __forceinline__ void run_program(const Params &p, const int64_t (*off)[kVec], const int64_t (*idx)[kVec],
-                                            int nlanes, uint32_t (*r)[kVec]) {
-  for (int pc = 0; pc < p.n_instr; ++pc) {
-    const Instr I = p.prog[pc];
+// Executes one non-load instruction on VEC lanes.
+__device__ __forceinline__ void exec_one(const Instr I, const int64_t (*idx)[kVec], uint32_t (*r)[kVec]) {
+  {
     uint32_t *d = r[I.dst];
     const uint32_t *A = r[I.a];
     const uint32_t *B = r[I.b];
@@ -83,9 +80,6 @@ __device__ __forceinline__ void run_program(const Params &p, const int64_t (*off
 #define SETF(x) d[v] = __float_as_uint(x)
 #define SETI(x) d[v] = static_cast<uint32_t>(x)
     switch (I.op) {
-      case LD:
-        LANES if (v < nlanes) d[v] = load_as_reg(p.in[I.a], off[I.a][v], p.in_dtype[I.a]);
-        break;
       case CF: case CI: LANES d[v] = I.imm; break;
       case IOTA: LANES SETI(static_cast<int32_t>(idx[I.a][v])); break;
       case FADD: LANES SETF(FA + FB); break;
@@ -182,6 +176,21 @@ __device__ __forceinline__ void run_program(const Params &p, const int64_t (*off
   }
 }
 
+// Executes the program for VEC lanes whose per-input element offsets and
+// per-axis indices are given.
+__device__ __forceinline__ void run_program(const Params &p, const int64_t (*off)[kVec], const int64_t (*idx)[kVec],
+                                            int nlanes, uint32_t (*r)[kVec]) {
+  for (int pc = 0; pc < p.n_instr; ++pc) {
+    const Instr I = p.prog[pc];
+    if (I.op == LD) {
+      for (int v = 0; v < kVec; ++v)
+        if (v < nlanes) r[I.dst][v] = load_as_reg(p.in[I.a], off[I.a][v], p.in_dtype[I.a]);
+    } else {
+      exec_one(I, idx, r);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256) ew_kernel(const __grid_constant__ Params p) {
   uint32_t r[kRegs][kVec];
   int64_t off[kMaxIn][kVec];
@@ -235,6 +244,95 @@ __global__ void __launch_bounds__(256) ew_kernel(const __grid_constant__ Params 
 #pragma unroll
     for (int v = 0; v < kVec; ++v)
       if (v < nl) store_from_reg(p.out, oo[v], p.out_dtype, r[p.out_reg][v]);
+  }
+}
+
+// Row-run variant: the innermost (collapsed) axis has a multiple of kVec
+// elements, so each thread takes kVec consecutive elements of one row.  The
+// row index is decomposed once per run (32-bit math when every offset fits),
+// operands with unit inner stride are read with one 16-byte (fp32) or 8-byte
+// (bf16) load, broadcast operands (inner stride 0) with one scalar load.
+__device__ __forceinline__ void load_run(const void *p, int64_t off, int64_t st, int dt, uint32_t *d) {
+  if (st == 0) {
+    const uint32_t v = load_as_reg(p, off, dt);
+#pragma unroll
+    for (int k = 0; k < kVec; ++k) d[k] = v;
+    return;
+  }
+  if (st == 1 && dt == NKB_F32 && ((reinterpret_cast<uintptr_t>(static_cast<const float *>(p) + off) & 15) == 0)) {
+    const uint4 t = *reinterpret_cast<const uint4 *>(static_cast<const float *>(p) + off);
+    d[0] = t.x; d[1] = t.y; d[2] = t.z; d[3] = t.w;
+    return;
+  }
+  if (st == 1 && dt == NKB_BF16 &&
+      ((reinterpret_cast<uintptr_t>(static_cast<const __nv_bfloat16 *>(p) + off) & 7) == 0)) {
+    const uint2 t = *reinterpret_cast<const uint2 *>(static_cast<const __nv_bfloat16 *>(p) + off);
+    d[0] = t.x << 16; d[1] = t.x & 0xffff0000u; d[2] = t.y << 16; d[3] = t.y & 0xffff0000u;
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < kVec; ++k) d[k] = load_as_reg(p, off + k * st, dt);
+}
+
+__device__ __forceinline__ void store_run(void *p, int64_t off, int64_t st, int dt, const uint32_t *v) {
+  if (st == 1 && dt == NKB_F32 && ((reinterpret_cast<uintptr_t>(static_cast<float *>(p) + off) & 15) == 0)) {
+    *reinterpret_cast<uint4 *>(static_cast<float *>(p) + off) = make_uint4(v[0], v[1], v[2], v[3]);
+    return;
+  }
+  if (st == 1 && dt == NKB_BF16 && ((reinterpret_cast<uintptr_t>(static_cast<__nv_bfloat16 *>(p) + off) & 7) == 0)) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(__uint_as_float(v[0]), __uint_as_float(v[1]));
+    __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(v[2]), __uint_as_float(v[3]));
+    uint2 t;
+    t.x = *reinterpret_cast<uint32_t *>(&a);
+    t.y = *reinterpret_cast<uint32_t *>(&b);
+    *reinterpret_cast<uint2 *>(static_cast<__nv_bfloat16 *>(p) + off) = t;
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < kVec; ++k) store_from_reg(p, off + k * st, dt, v[k]);
+}
+
+template <typename IDX>
+__global__ void __launch_bounds__(256) ew_rows_kernel(const __grid_constant__ Params p) {
+  uint32_t r[kRegs][kVec];
+  const int last = p.rank - 1;
+  const IDX inner = (IDX)p.shape[last];
+  const IDX runs_per_row = inner / kVec;
+  const IDX runs = (IDX)(p.n / kVec);
+  bool uses_iota = false;
+  for (int pc = 0; pc < p.n_instr; ++pc) uses_iota |= (p.prog[pc].op == IOTA);
+  for (IDX c = (IDX)blockIdx.x * blockDim.x + threadIdx.x; c < runs; c += (IDX)gridDim.x * blockDim.x) {
+    const IDX row = c / runs_per_row;
+    const IDX col = (c - row * runs_per_row) * kVec;
+    int64_t oo = p.out_off + (int64_t)col * p.out_strides[last];
+    int64_t base[kMaxIn];
+    for (int k = 0; k < p.n_in; ++k) base[k] = p.in_off[k] + (int64_t)col * p.in_strides[k][last];
+    int64_t idx[kMaxRank][kVec];
+    IDX rem = row;
+    for (int d = last - 1; d >= 0; --d) {
+      const IDX s = (IDX)p.shape[d];
+      const IDX q = rem / s;
+      const IDX id = rem - q * s;
+      rem = q;
+      oo += (int64_t)id * p.out_strides[d];
+      for (int k = 0; k < p.n_in; ++k) base[k] += (int64_t)id * p.in_strides[k][d];
+      if (uses_iota)
+#pragma unroll
+        for (int v = 0; v < kVec; ++v) idx[d][v] = id;
+    }
+    if (uses_iota)
+#pragma unroll
+      for (int v = 0; v < kVec; ++v) idx[last][v] = col + v;
+    // program, with loads served by row runs
+    for (int pc = 0; pc < p.n_instr; ++pc) {
+      const Instr I = p.prog[pc];
+      if (I.op == LD) {
+        load_run(p.in[I.a], base[I.a], p.in_strides[I.a][last], p.in_dtype[I.a], r[I.dst]);
+      } else {
+        exec_one(I, idx, r);
+      }
+    }
+    store_run(p.out, oo, p.out_strides[last], p.out_dtype, r[p.out_reg]);
   }
 }
 
@@ -302,6 +400,18 @@ int launch(const LaunchArgs &a) {
   int64_t blocks = (p.n + (int64_t)threads * kVec - 1) / ((int64_t)threads * kVec);
   const int64_t cap = (int64_t)num_sms(a.device) * 16;
   if (blocks > cap) blocks = cap;
+  if (p.shape[p.rank - 1] % kVec == 0) {
+    // 32-bit index math when the element count and every offset fit
+    int64_t span = p.n;
+    for (int k = 0; k < p.n_in; ++k) {
+      int64_t hi = p.in_off[k];
+      for (int d = 0; d < p.rank; ++d) hi += (p.shape[d] - 1) * (p.in_strides[k][d] < 0 ? 0 : p.in_strides[k][d]);
+      span = span > hi ? span : hi;
+    }
+    if (span < INT32_MAX) ew_rows_kernel<int32_t><<<(unsigned)blocks, threads, 0, a.stream>>>(p);
+    else ew_rows_kernel<int64_t><<<(unsigned)blocks, threads, 0, a.stream>>>(p);
+    return launch_status("ew_rows_kernel");
+  }
   ew_kernel<<<(unsigned)blocks, threads, 0, a.stream>>>(p);
   return launch_status("ew_kernel");
 }

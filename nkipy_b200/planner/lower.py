@@ -232,6 +232,8 @@ class Lowering:
                     note=f"{rows}x{cols}",
                 )
             self.vals[("o", root.id)] = out
+        elif c.kind == "attention":
+            self.lower_attention(c)
         elif c.kind == "argmax":
             x = c.params["x"]
             xv, rows, cols = self.dense_rows(x)
@@ -245,6 +247,37 @@ class Lowering:
             self.vals[("o", root.id)] = out
         else:
             raise NotImplementedError(c.kind)
+
+    def lower_attention(self, c):
+        p = c.params
+        root = c.root
+
+        def strided(t, amap, heads_div=1):
+            v = self.get(t)
+            if not isinstance(v, V.View) or v.strides[amap[3]] != 1:
+                v = self.materialize(v, dense=True)
+            st = v.strides
+            return v, [st[amap[0]], st[amap[1]], st[amap[2]], st[amap[3]]]
+
+        qv, qs = strided(p["q"], p["q_map"])
+        kv, ks = strided(p["k"], p["k_map"])
+        vv, vs = strided(p["v"], p["v_map"])
+        B, H, S, D = p["batch"], p["heads"], p["sq"], p["d"]
+        k_heads = int(p["k"].shape[p["k_map"][1]])
+        if p["n_rep"] == 1 and k_heads != H:
+            raise NotImplementedError("attention with mismatched head counts")
+        # output stored (B, S, H, D): the traced transpose(0,2,1,3) after it is free
+        out = self.tmp_view((B, S, H, D), BF16)
+        ints = [B, H, k_heads, S, p["skv"], D, int(p["causal"])]
+        ints += qs[:3] + ks[:3] + vs[:3] + [S * H * D, D, H * D]
+        self.step(
+            "flash_attn",
+            [self.bref(qv), self.bref(kv), self.bref(vv), self.bref(out)],
+            ints,
+            [p["scale"]],
+            note=f"B{B} H{H}/{k_heads} S{S} D{D} causal={int(p['causal'])}",
+        )
+        self.vals[("o", root.id)] = out.with_(shape=(B, H, S, D), strides=(S * H * D, D, H * D, 1))
 
     # ------------------------------------------------------------ view ops
     def op_reshape(self, op):

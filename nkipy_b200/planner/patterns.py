@@ -14,7 +14,11 @@ used only inside the composition, claims the nodes for one fused launch:
                    optional residual add in front and dtype converts
                    (``qwen3_embedding/kernels/rmsnorm.py:4-16``);
 * argmax / argmin  reduce-max, compare, float iota, select, reduce-min,
-                   convert to int32 (``core/ops/reduce.py:227-311``).
+                   convert to int32 (``core/ops/reduce.py:227-311``);
+* attention        dot(q, k^T) -> / sqrt(d) -> + causal mask constant ->
+                   softmax -> dot(., v), with the transposes and the GQA
+                   ``np.repeat`` of k/v feeding it
+                   (``qwen3_embedding/kernels/attention.py:75-95``).
 """
 
 from dataclasses import dataclass, field
@@ -321,7 +325,154 @@ def match_argmax(gi: GraphIndex, cvt_op) -> Optional[Claim]:
     return Claim("argmax", cvt_op, [o for o in ops if o is not None], {"x": x, "is_max": comp == "maximum"})
 
 
-MATCHERS = (match_softmax, match_rmsnorm, match_argmax)
+def _trace_kv(t, ops: list):
+    """Follow transposes (and one GQA repeat) back from an attention operand.
+
+    Returns (source tensor, axis map, n_rep): operand axis i reads source axis
+    amap[i]; when a repeat (broadcast of a new axis after the head axis +
+    reshape merging it) is found, the head axis of the source is indexed by
+    head // n_rep.
+    """
+    amap = list(range(len(t.shape)))
+    cur = t
+    while True:
+        p = GraphIndex.producer(cur)
+        if p is not None and p.op_name == "transpose":
+            perm = list(p.attributes["permutation"])
+            amap = [perm[a] for a in amap]
+            ops.append(p)
+            cur = p.operands[0]
+            continue
+        break
+    n_rep = 1
+    p = GraphIndex.producer(cur)
+    if p is not None and p.op_name == "reshape":
+        pb = GraphIndex.producer(p.operands[0])
+        out_shape = tuple(p.result_shape)
+        if pb is not None and pb.op_name == "broadcast" and len(out_shape) == 4:
+            bshape = tuple(pb.result_shape)
+            bd = list(pb.attributes["broadcast_dimensions"])
+            src = pb.operands[0]
+            # (B, S, Hkv, D) -> (B, S, Hkv, rep, D) -> (B, S, Hkv*rep, D)
+            if (
+                len(bshape) == 5
+                and bd == [0, 1, 2, 4]
+                and tuple(src.shape) == (bshape[0], bshape[1], bshape[2], bshape[4])
+                and out_shape == (bshape[0], bshape[1], bshape[2] * bshape[3], bshape[4])
+            ):
+                n_rep = bshape[3]
+                ops += [p, pb]
+                cur = src
+    return cur, amap, n_rep
+
+
+def _is_causal_mask(arr, sq, skv) -> Optional[bool]:
+    a = np.asarray(arr).astype(np.float32)
+    a = a.reshape(a.shape[-2:]) if a.size == sq * skv else None
+    if a is None or a.shape != (sq, skv):
+        return None
+    shift = skv - sq
+    rows = np.arange(sq)[:, None]
+    cols = np.arange(skv)[None, :]
+    upper = cols > rows + shift
+    if np.all(a[~upper] == 0) and np.all(a[upper] <= -1000.0):
+        return True
+    if np.all(a == 0):
+        return False
+    return None
+
+
+def match_attention(gi: GraphIndex, dot2) -> Optional[Claim]:
+    if dot2.op_name != "dot" or len(dot2.result_shape) != 4:
+        return None
+    at = dot2.attributes
+    if at["lhs_batch_dimensions"] != [0, 1] or at["rhs_batch_dimensions"] != [0, 1]:
+        return None
+    if at["lhs_contracting_dimensions"] != [3] or at["rhs_contracting_dimensions"] != [2]:
+        return None
+    p_t, v_t = dot2.operands
+    pp = GraphIndex.producer(p_t)
+    if pp is None:
+        return None
+    div = GraphIndex.producer(pp.operands[0]) if pp.op_name == "convert" else pp
+    if div is None or div.op_name != "divide":
+        return None
+    sm = match_softmax(gi, div)
+    if sm is None or sm.root is not pp:
+        return None
+    ops = [pp] + list(sm.interior)
+    x = sm.params["x"]
+    sq, skv = int(x.shape[2]), int(x.shape[3])
+    causal = False
+    px = GraphIndex.producer(x)
+    scaled = x
+    if px is not None and px.op_name == "add":
+        for a, m in (px.operands, px.operands[::-1]):
+            tmp = []
+            base = strip(m, tmp)
+            pc = GraphIndex.producer(base)
+            if pc is not None and pc.op_name == "constant" and isinstance(pc.attributes.get("value"), np.ndarray):
+                c = _is_causal_mask(pc.attributes["value"], sq, skv)
+                if c is not None:
+                    causal = c
+                    ops += tmp + [pc, px]
+                    scaled = a
+                    break
+        if scaled is x:
+            return None
+    scale = 1.0
+    raw = scaled
+    ps = GraphIndex.producer(scaled)
+    if ps is not None and ps.op_name in ("divide", "multiply"):
+        tmp = []
+        c = scalar_const(ps.operands[1], tmp)
+        if c is not None and c != 0:
+            scale = 1.0 / c if ps.op_name == "divide" else c
+            ops += tmp + [ps]
+            raw = ps.operands[0]
+    pr = GraphIndex.producer(raw)
+    if pr is None or pr.op_name != "dot":
+        return None
+    a1 = pr.attributes
+    if a1["lhs_batch_dimensions"] != [0, 1] or a1["rhs_batch_dimensions"] != [0, 1]:
+        return None
+    if a1["lhs_contracting_dimensions"] != [3] or a1["rhs_contracting_dimensions"] != [2]:
+        return None
+    ops.append(pr)
+    q_t, kt_t = pr.operands
+    for t in (q_t, kt_t, v_t):
+        if str(np.dtype(t.dtype)) != "bfloat16":
+            return None
+    if str(np.dtype(dot2.result_dtype)) != "bfloat16" or str(np.dtype(x.dtype)) != "bfloat16":
+        return None
+    if not _exclusive(gi, ops, dot2):
+        return None
+    # operand paths: claimed only when they feed nothing else
+    qops, kops, vops = [], [], []
+    q_src, q_map, q_rep = _trace_kv(q_t, qops)
+    k_src, k_map, k_rep = _trace_kv(kt_t, kops)
+    v_src, v_map, v_rep = _trace_kv(v_t, vops)
+    if q_rep != 1 or k_rep != v_rep:
+        return None
+    d = int(q_t.shape[3])
+    if d not in (64, 128):
+        return None
+    path_ops = []
+    for po in (qops, kops, vops):
+        if po and _exclusive(gi, po + ops, dot2):
+            path_ops += po
+    params = dict(
+        q=q_src, q_map=q_map, k=k_src, k_map=[k_map[0], k_map[1], k_map[3], k_map[2]], v=v_src, v_map=v_map,
+        n_rep=k_rep, scale=scale, causal=causal, sq=sq, skv=skv, d=d, heads=int(q_t.shape[1]),
+        batch=int(q_t.shape[0]),
+    )
+    if not path_ops:
+        # the operand paths are shared: read the dot operands as they are
+        params.update(q=q_t, q_map=[0, 1, 2, 3], k=kt_t, k_map=[0, 1, 3, 2], v=v_t, v_map=[0, 1, 2, 3], n_rep=1)
+    return Claim("attention", dot2, ops + path_ops, params)
+
+
+MATCHERS = (match_attention, match_softmax, match_rmsnorm, match_argmax)
 
 
 def find_claims(graph) -> Dict[int, Claim]:

@@ -126,3 +126,41 @@ def test_llama_layer_tp1(batch, seq):
     want = O.llama_layer(x, full, s.n_heads, s.n_kv_heads, s.head_dim, s.eps, s.theta)
     assert got.dtype == BF16
     assert_close(got, want, BF16_RTOL)
+
+
+def _attention_body(q, k, v, n_rep):
+    B, S, H, D = q.shape
+    if n_rep > 1:
+        k = np.repeat(k, n_rep, axis=2)
+        v = np.repeat(v, n_rep, axis=2)
+    q, k, v = q.transpose(0, 2, 1, 3), k.transpose(0, 2, 1, 3), v.transpose(0, 2, 1, 3)
+    scores = (q @ k.transpose(0, 1, 3, 2)) / np.sqrt(D)
+    mask = np.triu(np.ones((S, S)) * -10000.0, k=1).astype(scores.dtype)
+    scores = scores + mask[None, None, :, :]
+    x = scores.astype(np.float32)
+    e = np.exp(x - np.max(x, axis=-1, keepdims=True))
+    p = (e / np.sum(e, axis=-1, keepdims=True)).astype(scores.dtype)
+    return (p @ v).transpose(0, 2, 1, 3)
+
+
+@pytest.mark.parametrize("B,S,H,Hkv,D", [(2, 256, 8, 2, 128), (1, 200, 4, 4, 64), (1, 1000, 2, 1, 128)])
+def test_flash_attention_gqa_causal(B, S, H, Hkv, D):
+    rng = np.random.default_rng(13)
+    q = rng.standard_normal((B, S, H, D), dtype=np.float32).astype(BF16)
+    k = rng.standard_normal((B, S, Hkv, D), dtype=np.float32).astype(BF16)
+    v = rng.standard_normal((B, S, Hkv, D), dtype=np.float32).astype(BF16)
+    n_rep = H // Hkv
+
+    def kern(q, k, v):
+        return _attention_body(q, k, v, n_rep)
+
+    got = on_device(kern, q, k, v)
+    # oracle: fp32 attention on the same bf16 inputs
+    qf, kf, vf = (t.astype(np.float32) for t in (q, k, v))
+    kf, vf = np.repeat(kf, n_rep, axis=2), np.repeat(vf, n_rep, axis=2)
+    s = np.einsum("bqhd,bkhd->bhqk", qf, kf) / np.sqrt(D)
+    s = s + np.triu(np.full((S, S), -np.inf, np.float32), k=1)
+    p = np.exp(s - s.max(-1, keepdims=True))
+    p /= p.sum(-1, keepdims=True)
+    want = np.einsum("bhqk,bkhd->bqhd", p, vf)
+    assert_close(got, want, BF16_RTOL)
