@@ -209,6 +209,36 @@ class Bmm(Gemm):
                 "l2": "operands 805 MB exceed L2; also flushed between steps"}
 
 
+class LinAttn(Workload):
+    name, metric, unit, bound, dtype, dominant = "linattn", "HBM GB/s (chunked causal linear attention)", "GB/s", "hbm", "bf16", "gemm_simt"
+    SHAPE = (8, 16, 4096, 128)
+
+    def kernel_and_args(self, rank, world):
+        from nkipy_b200 import workloads as W
+
+        q, k, v = W.make_inputs("linattn", seed=600 + rank)
+        return W.chunked_linear_attention_kernel, (q, k, v), {}
+
+    def units_per_step(self, world):
+        return 4 * int(np.prod(self.SHAPE)) * 2 / 1e9
+
+    def dominant_work(self):
+        return 4 * int(np.prod(self.SHAPE)) * 2
+
+    def cpu_step(self, threads):
+        from nkipy_b200 import workloads as W
+        from oracle import numpy_ref as O
+
+        q, k, v = W.make_inputs("linattn", seed=7, scale=1 / 8)
+        q, k, v = q[:, :2], k[:, :2], v[:, :2]
+        O.linear_attention_recurrent(q, k, v)
+        return 4 * q.size * 2 / 1e9, "1 x 2 of 8 x 16 (batch, head) pairs per step"
+
+    def config(self, world):
+        return {"workload": "chunked causal linear attention bf16 (8,16,4096,128), elu+1, chunk 64, fp32 state",
+                "shape": list(self.SHAPE), "l2": "inputs 403 MB exceed L2; also flushed between steps"}
+
+
 class Layer(Workload):
     name, metric, unit, bound, dtype, dominant = "layer", "TP decoder layer tokens/s", "tokens/s", "tensor", "bf16", "gemm_bf16"
     scaling = "strong"
@@ -260,7 +290,7 @@ class Layer(Workload):
                 "l2": "weights + activations exceed L2"}
 
 
-WORKLOADS = {w.name: w for w in (Softmax, RmsNorm, Gemm, Bmm, Layer)}
+WORKLOADS = {w.name: w for w in (Softmax, RmsNorm, Gemm, Bmm, LinAttn, Layer)}
 DEFAULT_WORKLOAD = "rmsnorm"
 
 

@@ -43,7 +43,10 @@ enum Opcode : uint8_t {
 };
 
 struct Instr {
-  uint8_t op, dst, a, b, c, pad0, pad1, pad2;
+  uint8_t op, dst, a, b, c;
+  uint8_t rnd;   // round the result: 1 = to bf16, 2 = to fp16
+  uint8_t bimm;  // 1 = operand b is the immediate `imm`
+  uint8_t pad;
   uint32_t imm;
 };
 
@@ -70,7 +73,11 @@ __device__ __forceinline__ void exec_one(const Instr I, const int64_t (*idx)[kVe
   {
     uint32_t *d = r[I.dst];
     const uint32_t *A = r[I.a];
-    const uint32_t *B = r[I.b];
+    uint32_t bimm[kVec];
+    if (I.bimm)
+#pragma unroll
+      for (int v = 0; v < kVec; ++v) bimm[v] = I.imm;
+    const uint32_t *B = I.bimm ? bimm : r[I.b];
     const uint32_t *C = r[I.c];
 #define LANES for (int v = 0; v < kVec; ++v)
 #define FA __uint_as_float(A[v])
@@ -165,6 +172,11 @@ __device__ __forceinline__ void exec_one(const Instr I, const int64_t (*idx)[kVe
       case INZ: LANES SETI(A[v] != 0u); break;
       case FNZ: LANES SETI(FA != 0.f); break;
       default: break;
+    }
+    if (I.rnd == 1) {
+      LANES d[v] = __float_as_uint(rnd_bf16(__uint_as_float(d[v])));
+    } else if (I.rnd == 2) {
+      LANES d[v] = __float_as_uint(rnd_f16(__uint_as_float(d[v])));
     }
 #undef LANES
 #undef FA
@@ -341,18 +353,18 @@ __global__ void __launch_bounds__(256) ew_rows_kernel(const __grid_constant__ Pa
 //   ints:  n_in rank n_instr out_dtype out_reg contig n
 //          shape[rank] out_off out_strides[rank]
 //          per input: dtype off strides[rank]
-//          per instr: op dst a b c imm_bits
+//          per instr: op dst a b c imm_bits round(0/1 bf16/2 fp16) b_is_imm
 int check(const Step &s) {
   if (s.ints.size() < 7) return fail(NKB_ERR_PLAN, "ew: short parameter list");
   const int64_t n_in = s.ints[0], rank = s.ints[1], n_instr = s.ints[2];
   if (n_in < 0 || n_in > kMaxIn) return fail(NKB_ERR_UNSUPPORTED, "ew: too many inputs");
   if (rank < 1 || rank > kMaxRank) return fail(NKB_ERR_UNSUPPORTED, "ew: rank out of range");
   if (n_instr < 1 || n_instr > kMaxInstr) return fail(NKB_ERR_UNSUPPORTED, "ew: program too long");
-  const size_t want = 7 + rank + 1 + rank + n_in * (2 + rank) + n_instr * 6;
+  const size_t want = 7 + rank + 1 + rank + n_in * (2 + rank) + n_instr * 8;
   if (s.ints.size() != want || s.buf_ids.size() != (size_t)(1 + n_in))
     return fail(NKB_ERR_PLAN, "ew: parameter count mismatch");
   const int64_t *q = s.ints.data() + 7 + rank + 1 + rank + n_in * (2 + rank);
-  for (int i = 0; i < n_instr; ++i, q += 6) {
+  for (int i = 0; i < n_instr; ++i, q += 8) {
     if (q[1] >= kRegs || q[2] >= kRegs || q[3] >= kRegs || q[4] >= kRegs || q[1] < 0)
       return fail(NKB_ERR_PLAN, "ew: register index out of range");
     if (q[0] == LD && (q[2] < 0 || q[2] >= n_in)) return fail(NKB_ERR_PLAN, "ew: load of a missing input");
@@ -393,7 +405,9 @@ int launch(const LaunchArgs &a) {
     I.b = (uint8_t)q[3];
     I.c = (uint8_t)q[4];
     I.imm = (uint32_t)q[5];
-    q += 6;
+    I.rnd = (uint8_t)q[6];
+    I.bimm = (uint8_t)q[7];
+    q += 8;
   }
   if (p.n == 0) return NKB_OK;
   const int threads = 256;

@@ -46,6 +46,11 @@ struct Args {
   int64_t M, N, K, ldc, sC, batch;
   int c_f32, a_mn_major, b_k_major;
   int tiles_m, tiles_n;
+  // epi == 1 (SwiGLU): B holds [gate | up] halves of width n_half; a CTA
+  // computes 128 gate + the matching 128 up columns and writes
+  // silu(gate) * up (N = n_half output columns).
+  int epi;
+  int64_t n_half;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -128,6 +133,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t *r) {
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 // Instruction descriptor, kind::f16: D fp32, A/B bf16, M=128, N=256.
 __host__ __device__ constexpr uint32_t make_idesc(int a_mn_major, int b_mn_major) {
@@ -218,6 +225,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           if (args.b_k_major) {
             tma_load_3d(b_dst, &map_b, &full[s], kb * BK, bn * BN, bb);
+          } else if (args.epi == 1) {
+            const int n0 = bn * (BN / 2);
+            for (int j = 0; j < BN / 64; ++j) {
+              const int col = (j < 2) ? n0 + j * 64 : (int)args.n_half + n0 + (j - 2) * 64;
+              tma_load_3d(b_dst + j * (64 * BK * 2), &map_b, &full[s], col, kb * BK, bb);
+            }
           } else {
             for (int j = 0; j < BN / 64; ++j)
               tma_load_3d(b_dst + j * (64 * BK * 2), &map_b, &full[s], bn * BN + j * 64, kb * BK, bb);
@@ -276,8 +289,49 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!mbar_wait(&acc_full[acc], acc_ph, abort_flag)) break;
       tc_fence_after();
       const int64_t row = (int64_t)bm * BM + row_in_tile;
-      const int64_t col0 = (int64_t)bn * BN;
       const bool row_ok = row < args.M;
+      if (args.epi == 1) {
+        const int64_t col0 = (int64_t)bn * (BN / 2);
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, g);
+          tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + BN / 2 + c * 32, u);
+          const int64_t col = col0 + c * 32;
+          if (!row_ok || col >= args.N) continue;
+          __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(args.C) + bb * args.sC + row * args.ldc + col;
+          uint32_t packed[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float o2[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              // silu(g) * u with the traced bf16 node sequence:
+              // negate, exponential, 1 + ., 1 / ., g * ., . * u (each rounded)
+              const float gv = bf16r(__uint_as_float(g[j + t]));
+              const float uv = bf16r(__uint_as_float(u[j + t]));
+              const float e = bf16r(expf(-gv));
+              const float d = bf16r(1.0f + e);
+              const float r = bf16r(1.0f / d);
+              const float sg = bf16r(gv * r);
+              o2[t] = sg * uv;
+            }
+            __nv_bfloat162 h = __floats2bfloat162_rn(o2[0], o2[1]);
+            packed[j / 2] = *reinterpret_cast<uint32_t *>(&h);
+          }
+          if (col + 32 <= args.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              *reinterpret_cast<uint4 *>(dst + 2 * j) = make_uint4(packed[j], packed[j + 1], packed[j + 2], packed[j + 3]);
+          } else {
+            for (int j = 0; j < 32 && col + j < args.N; ++j)
+              dst[j] = reinterpret_cast<__nv_bfloat16 *>(packed)[j];
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+        continue;
+      }
+      const int64_t col0 = (int64_t)bn * BN;
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
@@ -378,7 +432,7 @@ bool tc_eligible(const void *A, const void *B, int64_t lda, int64_t ldb, int64_t
 // that storage); b_k_major: B stored N x K.
 int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t N, int64_t K, int64_t lda,
             int64_t ldb, int64_t ldc, int64_t batch, int64_t sA, int64_t sB, int64_t sC, int a_mn_major, int b_k_major,
-            cudaStream_t st, int device) {
+            cudaStream_t st, int device, int epi = 0, int64_t n_half = 0) {
   if (M == 0 || N == 0 || batch == 0) return NKB_OK;
   if (K == 0) return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: K == 0 takes the strided path");
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(NKB_ERR_UNSUPPORTED, "gemm: dims exceed int32");
@@ -391,8 +445,11 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   if (!a_mn_major) s = make_map(&ma, A, K, M, ba, lda, sA, BK, BM);
   else s = make_map(&ma, A, M, K, ba, lda, sA, 64, BK);
   if (s) return s;
-  if (b_k_major) s = make_map(&mb, B, K, N, bb, ldb, sB, BK, BN);
-  else s = make_map(&mb, B, N, K, bb, ldb, sB, 64, BK);
+  if (epi == 1 && (b_k_major || c_f32 || n_half % 64 || N != n_half))
+    return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: SwiGLU epilogue needs N-major B, bf16 output and n_half % 64 == 0");
+  const int64_t bcols = epi == 1 ? 2 * n_half : N;
+  if (b_k_major) s = make_map(&mb, B, K, bcols, bb, ldb, sB, BK, BN);
+  else s = make_map(&mb, B, bcols, K, bb, ldb, sB, 64, BK);
   if (s) return s;
   Args args;
   args.C = C;
@@ -405,8 +462,10 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   args.c_f32 = c_f32;
   args.a_mn_major = a_mn_major;
   args.b_k_major = b_k_major;
+  args.epi = epi;
+  args.n_half = n_half;
   args.tiles_m = (int)((M + BM - 1) / BM);
-  args.tiles_n = (int)((N + BN - 1) / BN);
+  args.tiles_n = (int)((N + (epi == 1 ? BN / 2 : BN) - 1) / (epi == 1 ? BN / 2 : BN));
   const int64_t tiles = (int64_t)args.tiles_m * args.tiles_n * batch;
   if (tiles > INT32_MAX) return fail(NKB_ERR_UNSUPPORTED, "gemm: too many tiles");
   static bool attr_set[64] = {false};
@@ -487,15 +546,18 @@ int gemm_simt(const SimtArgs &p, cudaStream_t st) {
 }
 
 // ---- plan steps ---------------------------------------------------------------
-// "gemm_bf16": ptrs A B C; ints M N K lda ldb ldc batch sA sB sC c_f32 a_mn_major b_k_major
+// "gemm_bf16": ptrs A B C; ints M N K lda ldb ldc batch sA sB sC c_f32 a_mn_major b_k_major [epi n_half]
 int tc_check(const Step &s) {
-  if (s.buf_ids.size() != 3 || s.ints.size() != 13) return fail(NKB_ERR_PLAN, "gemm_bf16: bad parameters");
+  if (s.buf_ids.size() != 3 || (s.ints.size() != 13 && s.ints.size() != 15))
+    return fail(NKB_ERR_PLAN, "gemm_bf16: bad parameters");
   return NKB_OK;
 }
 int tc_launch(const LaunchArgs &a) {
   const auto &q = a.step->ints;
+  const int epi = q.size() == 15 ? (int)q[13] : 0;
+  const int64_t n_half = q.size() == 15 ? q[14] : 0;
   return gemm_tc(a.ptrs[0], a.ptrs[1], a.ptrs[2], (int)q[10], q[0], q[1], q[2], q[3], q[4], q[5], q[6], q[7], q[8],
-                 q[9], (int)q[11], (int)q[12], a.stream, a.device);
+                 q[9], (int)q[11], (int)q[12], a.stream, a.device, epi, n_half);
 }
 
 // "gemm_simt": ptrs A B C; ints adt bdt cdt M N K batch a_rs a_cs b_rs b_cs c_rs c_cs sA sB sC

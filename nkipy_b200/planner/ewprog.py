@@ -241,11 +241,20 @@ def _narrow(prog, reg, dt):
 
 
 def _round_float(prog, reg, dt):
+    """Round the value just written to ``reg`` to a narrow float type.
+
+    Folded into the producing instruction (its round field) when that
+    instruction wrote ``reg``; otherwise an explicit RBF/RF16.
+    """
     dt = np.dtype(dt)
-    if dt == np.dtype(ml_dtypes.bfloat16):
-        prog.emit("RBF", reg, reg)
-    elif dt == np.dtype(np.float16):
-        prog.emit("RF16", reg, reg)
+    code = 1 if dt == np.dtype(ml_dtypes.bfloat16) else (2 if dt == np.dtype(np.float16) else 0)
+    if not code:
+        return
+    last = prog.instrs[-1] if prog.instrs else None
+    if last is not None and last[1] == reg and last[6] == 0 and last[0] not in (OP["LD"], OP["CF"], OP["CI"]):
+        prog.instrs[-1] = last[:6] + (code,) + last[7:]
+    else:
+        prog.emit("RBF" if code == 1 else "RF16", reg, reg)
 
 
 class _Prog:
@@ -261,10 +270,10 @@ class _Prog:
     def release(self, r):
         self.free.append(r)
 
-    def emit(self, name, dst, a=0, b=0, c=0, imm=0):
+    def emit(self, name, dst, a=0, b=0, c=0, imm=0, bimm=0):
         if len(self.instrs) >= MAX_INSTR:
             raise TooBig("instructions")
-        self.instrs.append((OP[name], dst, a, b, c, imm))
+        self.instrs.append((OP[name], dst, a, b, c, imm, 0, bimm))
 
     def tmp_const_int(self, v):
         r = self.alloc()
@@ -403,7 +412,15 @@ def compile_ew(expr: Expr, out: V.View) -> CompiledEw:
             prog.emit("IOR", r, a, a)  # register move
             done(args[0])
             return r
-        regs = [value(a) for a in args]
+        imm_b = None
+        if name in ELEMENTWISE_BINARY and len(args) == 2:
+            if args[1].kind != "const" and args[0].kind == "const" and name in ("add", "multiply", "maximum", "minimum", "and", "or", "xor"):
+                args = [args[1], args[0]]
+            if args[1].kind == "const":
+                imm_b = _imm_bits(args[1])
+        regs = [value(a) for a in (args if imm_b is None else args[:1])]
+        if imm_b is not None:
+            regs.append(0)
         r = prog.alloc()
         if name == "convert":
             src = kind(args[0].dtype)
@@ -437,18 +454,19 @@ def compile_ew(expr: Expr, out: V.View) -> CompiledEw:
         elif name == "select":
             prog.emit("SEL", r, regs[0], regs[1], regs[2])
         elif name in ELEMENTWISE_BINARY:
+            bi = dict(imm=imm_b, bimm=1) if imm_b is not None else {}
             if k == "F":
                 if name not in _FBIN:
                     raise NotImplementedError(f"float {name}")
-                prog.emit(_FBIN[name], r, regs[0], regs[1])
+                prog.emit(_FBIN[name], r, regs[0], regs[1], **bi)
                 _round_float(prog, r, e.dtype)
             elif k == "B":
-                prog.emit(_IBIN[name], r, regs[0], regs[1])
+                prog.emit(_IBIN[name], r, regs[0], regs[1], **bi)
             else:
                 table = _UBIN if k == "U" else _IBIN
                 if name not in table:
                     raise NotImplementedError(f"integer {name}")
-                prog.emit(table[name], r, regs[0], regs[1])
+                prog.emit(table[name], r, regs[0], regs[1], **bi)
                 _narrow(prog, r, e.dtype)
         elif name == "not":
             if k == "B":
@@ -473,9 +491,20 @@ def compile_ew(expr: Expr, out: V.View) -> CompiledEw:
                 raise NotImplementedError(f"integer {name}")
         else:
             raise NotImplementedError(f"elementwise op {name}")
-        for a in args:
+        for a in e.args:
             done(a)
         return r
+
+    def _imm_bits(c):
+        kc = kind(c.dtype)
+        if kc == "F":
+            val = np.float32(c.value)
+            if np.dtype(c.dtype) != np.float32:
+                val = np.float32(np.array(val).astype(c.dtype).astype(np.float32))
+            return _f32_bits(val)
+        if kc == "B":
+            return 1 if bool(c.value) else 0
+        return _i32_bits(int(c.value))
 
     out_reg = value(expr)
     ints = [len(inputs), rank, len(prog.instrs), dt_code(out.dtype), out_reg]
@@ -488,6 +517,6 @@ def compile_ew(expr: Expr, out: V.View) -> CompiledEw:
     ints += [int(out.offset)] + list(out_st)
     for v, st in zip(inputs, in_st):
         ints += [dt_code(v.dtype), int(v.offset)] + list(st)
-    for (o, d, a, b, c, imm) in prog.instrs:
-        ints += [o, d, a, b, c, imm]
+    for (o, d, a, b, c, imm, rnd, bimm) in prog.instrs:
+        ints += [o, d, a, b, c, imm, rnd, bimm]
     return CompiledEw(ints=ints, in_views=inputs, n_instr=len(prog.instrs))

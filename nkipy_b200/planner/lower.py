@@ -234,6 +234,8 @@ class Lowering:
             self.vals[("o", root.id)] = out
         elif c.kind == "attention":
             self.lower_attention(c)
+        elif c.kind == "swiglu_gemm":
+            self.lower_swiglu(c)
         elif c.kind == "argmax":
             x = c.params["x"]
             xv, rows, cols = self.dense_rows(x)
@@ -278,6 +280,33 @@ class Lowering:
             note=f"B{B} H{H}/{k_heads} S{S} D{D} causal={int(p['causal'])}",
         )
         self.vals[("o", root.id)] = out.with_(shape=(B, H, S, D), strides=(S * H * D, D, H * D, 1))
+
+    def lower_swiglu(self, c):
+        """gate/up GEMM with silu(gate) * up in the epilogue; generic path otherwise."""
+        d = c.params["dot"]
+        F = c.params["n_half"]
+        root = c.root
+        ok = self.op_dot(d, epilogue=("swiglu", F, root))
+        if ok:
+            return
+        # fallback: the dot result exists in full; evaluate the activation as one ew group
+        full = self.expr_of(self.get(d))
+        n = len(d.result_shape)
+
+        def half(i):
+            starts = [0] * (n - 1) + [i * F]
+            limits = list(d.result_shape[:-1]) + [(i + 1) * F]
+            return E.t_slice(full, starts, limits, [1] * n)
+
+        g, u = half(0), half(1)
+        shape, bf = tuple(root.result_shape), BF16
+        one = E.const(1.0, bf, shape)
+        t = E.op("negate", [g], shape, bf)
+        t = E.op("exponential", [t], shape, bf)
+        t = E.op("add", [one, t], shape, bf)
+        t = E.op("divide", [one, t], shape, bf)
+        t = E.op("multiply", [g, t], shape, bf)
+        self.vals[("o", root.id)] = E.op("multiply", [t, u], shape, bf)
 
     # ------------------------------------------------------------ view ops
     def op_reshape(self, op):
@@ -396,7 +425,7 @@ class Lowering:
         self.vals[("o", op.id)] = out
 
     # ------------------------------------------------------------ dot
-    def op_dot(self, op):
+    def op_dot(self, op, epilogue=None):
         a_t, b_t = op.operands
         at = op.attributes
         lb, rb = list(at["lhs_batch_dimensions"]), list(at["rhs_batch_dimensions"])
@@ -421,7 +450,10 @@ class Lowering:
         a_bst = [av.strides[d] for d in lb]
         b_bst = [bv.strides[d] for d in rb]
         out_dt = np.dtype(op.result_dtype)
-        out = self.tmp_view(op.result_shape, out_dt)
+        if epilogue is not None:
+            out = self.tmp_view(epilogue[2].result_shape, out_dt)
+        else:
+            out = self.tmp_view(op.result_shape, out_dt)
         # fold a broadcast rhs (weights shared across the batch) into M
         if bshape and all(s == 0 for s in b_bst) and M > 0:
             shp, (st,) = V.collapse(bshape + [M], [tuple(a_bst + [a_ms])])
@@ -433,6 +465,9 @@ class Lowering:
         if len(bshape) > 1:
             shp, sts = V.collapse(bshape, [tuple(a_bst), tuple(b_bst), tuple(c_bst)])
             if len(shp) > 1:
+                if epilogue is not None:
+                    self.op_dot(op)
+                    return False
                 av = self.materialize(av, dense=True)
                 bv = self.materialize(bv, dense=True)
                 return self.op_dot_dense(op, av, bv, out)
@@ -463,6 +498,20 @@ class Lowering:
             and aligned(av, a_ks if a_mn else a_ms, sA)
             and aligned(bv, b_ks if b_n else b_ns, sB)
         )
+        if epilogue is not None:
+            F = epilogue[1]
+            if not (use_tc and b_n and out_dt == BF16 and F % 64 == 0 and N == 2 * F and batch == 1):
+                self.op_dot(op)
+                return False
+            lda = a_ms if a_k else a_ks
+            self.step(
+                "gemm_bf16",
+                [self.bref(av), self.bref(bv), self.bref(out)],
+                [M, F, K, lda, b_ks, F, 1, 0, 0, 0, 0, int(a_mn and not a_k), 0, 1, F],
+                note=f"tc {M}x{F}(x2)x{K} +swiglu",
+            )
+            self.vals[("o", epilogue[2].id)] = out
+            return True
         if use_tc:
             lda = a_ms if a_k else a_ks
             ldb = b_ks if b_n else b_ns

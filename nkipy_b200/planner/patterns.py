@@ -472,7 +472,82 @@ def match_attention(gi: GraphIndex, dot2) -> Optional[Claim]:
     return Claim("attention", dot2, ops + path_ops, params)
 
 
-MATCHERS = (match_attention, match_softmax, match_rmsnorm, match_argmax)
+def _const_value(t):
+    tmp = []
+    return scalar_const(t, tmp), tmp
+
+
+def _last_axis_half(t, which, ops):
+    """t = slice of a dot result selecting its first (0) / second (1) half along the last axis."""
+    p = GraphIndex.producer(t)
+    if p is None or p.op_name != "slice":
+        return None
+    src = p.operands[0]
+    n = len(src.shape)
+    full = int(src.shape[-1])
+    if full % 2:
+        return None
+    a = p.attributes
+    want_start = [0] * (n - 1) + [which * full // 2]
+    want_limit = list(src.shape[:-1]) + [(which + 1) * full // 2]
+    if list(a["start_indices"]) != want_start or list(a["limit_indices"]) != want_limit or set(a["strides"]) != {1}:
+        return None
+    ops.append(p)
+    return src
+
+
+def match_swiglu_gemm(gi: GraphIndex, mul_op) -> Optional[Claim]:
+    """gate, up = split(x @ W, 2, -1); silu(gate) * up  (``qwen3_embedding/kernels/ffn.py:4-46``)."""
+    if mul_op.op_name != "multiply" or str(np.dtype(mul_op.result_dtype)) != "bfloat16":
+        return None
+    for a_t, u_t in (mul_op.operands, mul_op.operands[::-1]):
+        ops = []
+        d_up = _last_axis_half(u_t, 1, ops)
+        if d_up is None:
+            continue
+        pa = GraphIndex.producer(a_t)
+        if pa is None or pa.op_name != "multiply":
+            continue
+        ops.append(pa)
+        for g_t, r_t in (pa.operands, pa.operands[::-1]):
+            o2 = list(ops)
+            d_g = _last_axis_half(g_t, 0, o2)
+            if d_g is None or tkey(d_g) != tkey(d_up):
+                continue
+            pr = GraphIndex.producer(r_t)
+            if pr is None or pr.op_name != "divide":
+                continue
+            one, t1 = _const_value(pr.operands[0])
+            if one != 1.0:
+                continue
+            o2 += t1 + [pr]
+            pd = GraphIndex.producer(pr.operands[1])
+            if pd is None or pd.op_name != "add":
+                continue
+            o2.append(pd)
+            ok = False
+            for c_t, e_t in (pd.operands, pd.operands[::-1]):
+                one2, t2 = _const_value(c_t)
+                pe = GraphIndex.producer(e_t)
+                if one2 == 1.0 and pe is not None and pe.op_name == "exponential":
+                    pn = GraphIndex.producer(pe.operands[0])
+                    if pn is not None and pn.op_name == "negate" and tkey(pn.operands[0]) == tkey(g_t):
+                        o2 += t2 + [pe, pn]
+                        ok = True
+                        break
+            if not ok:
+                continue
+            pdot = GraphIndex.producer(d_up)
+            if pdot is None or pdot.op_name != "dot" or str(np.dtype(pdot.result_dtype)) != "bfloat16":
+                continue
+            o2.append(pdot)
+            if not _exclusive(gi, o2, mul_op):
+                continue
+            return Claim("swiglu_gemm", mul_op, o2, {"dot": pdot, "gate": g_t, "up": u_t, "n_half": int(d_up.shape[-1]) // 2})
+    return None
+
+
+MATCHERS = (match_attention, match_swiglu_gemm, match_softmax, match_rmsnorm, match_argmax)
 
 
 def find_claims(graph) -> Dict[int, Claim]:

@@ -164,3 +164,23 @@ def test_flash_attention_gqa_causal(B, S, H, Hkv, D):
     p /= p.sum(-1, keepdims=True)
     want = np.einsum("bhqk,bkhd->bqhd", p, vf)
     assert_close(got, want, BF16_RTOL)
+
+
+@pytest.mark.parametrize("tokens,hidden,ffn", [(256, 512, 1024), (300, 256, 320)])
+def test_swiglu_ffn(tokens, hidden, ffn):
+    def ffn_kernel(x, gate_up, down):
+        gate, up = np.split(x @ gate_up, 2, axis=-1)
+        return (W.silu(gate) * up) @ down
+
+    rng = np.random.default_rng(14)
+    x = rng.standard_normal((tokens, hidden), dtype=np.float32).astype(BF16)
+    gu = (rng.standard_normal((hidden, 2 * ffn), dtype=np.float32) * 0.02).astype(BF16)
+    dn = (rng.standard_normal((ffn, hidden), dtype=np.float32) * 0.02).astype(BF16)
+    got = on_device(ffn_kernel, x, gu, dn)
+    f = lambda t: t.astype(np.float32)  # noqa: E731
+    r = lambda t: t.astype(BF16)  # noqa: E731
+    h = r(f(x) @ f(gu))
+    g, u = f(h[:, :ffn]), f(h[:, ffn:])
+    act = r(f(r(g * f(r(1.0 / f(r(1.0 + f(r(np.exp(-g))))))))) * u)
+    want = f(act) @ f(dn)
+    assert_close(got, want, BF16_RTOL)

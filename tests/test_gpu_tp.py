@@ -1,0 +1,32 @@
+"""Tensor-parallel decoder layer on 2 GPUs (NCCL all-reduce inside the plan)."""
+
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _gpus():
+    try:
+        import torch
+
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_tp2_layer_parity():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [
+        "timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+        "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533",
+        os.path.join(ROOT, "tests", "tp_layer_worker.py"),
+    ]
+    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

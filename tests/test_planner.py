@@ -109,8 +109,17 @@ def test_ew_compile_bf16_rounding_inserted():
     x = E.leaf(V.View(0, 0, (4,), (1,), BF16))
     e = E.op("add", [x, x], (4,), BF16)
     c = E.compile_ew(e, V.View(1, 0, (4,), (1,), BF16))
-    ops = c.ints[7 + 1 + 1 + 1 + (2 + 1) :]
-    assert E.OP["RBF"] in ops[0::6]
+    prog = c.ints[7 + 1 + 1 + 1 + (2 + 1) :]
+    instrs = [prog[i : i + 8] for i in range(0, len(prog), 8)]
+    add = [ins for ins in instrs if ins[0] == E.OP["FADD"]]
+    assert len(add) == 1 and add[0][6] == 1  # rounded to bf16 by the add itself
+
+
+def test_ew_constant_operand_is_immediate():
+    x = E.leaf(V.View(0, 0, (4,), (1,), np.dtype(np.float32)))
+    e = E.op("multiply", [E.const(2.0, np.float32, (4,)), x], (4,), np.float32)
+    c = E.compile_ew(e, V.View(1, 0, (4,), (1,), np.dtype(np.float32)))
+    assert c.n_instr == 2  # load + multiply-by-immediate
 
 
 def test_layer_plans(monkeypatch):
