@@ -571,6 +571,8 @@ def _plan_steps(path):
             flops = 0
             if kern == "gemm_bf16":
                 M, N, K, batch = ints[0], ints[1], ints[2], ints[6]
+                if len(ints) == 15 and ints[13] == 1:  # SwiGLU epilogue: gate and up halves
+                    N *= 2
                 flops = 2 * M * N * K * batch
             elif kern == "gemm_simt":
                 M, N, K, batch = ints[3], ints[4], ints[5], ints[6]

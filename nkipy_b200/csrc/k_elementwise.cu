@@ -68,18 +68,13 @@ __device__ __forceinline__ float rnd_bf16(float x) { return __bfloat162float(__f
 __device__ __forceinline__ float rnd_f16(float x) { return __half2float(__float2half_rn(x)); }
 __device__ __forceinline__ float fsignf(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : x); }
 
-// Executes one non-load instruction on VEC lanes.
-__device__ __forceinline__ void exec_one(const Instr I, const int64_t (*idx)[kVec], uint32_t (*r)[kVec]) {
+// One arithmetic instruction on VEC lanes held in (real) registers.  Loads
+// and iota are executed by the callers, which know the addressing.
+template <int VEC>
+__device__ __forceinline__ void compute(const Instr I, const uint32_t (&A)[VEC], const uint32_t (&B)[VEC],
+                                        const uint32_t (&C)[VEC], uint32_t (&d)[VEC]) {
   {
-    uint32_t *d = r[I.dst];
-    const uint32_t *A = r[I.a];
-    uint32_t bimm[kVec];
-    if (I.bimm)
-#pragma unroll
-      for (int v = 0; v < kVec; ++v) bimm[v] = I.imm;
-    const uint32_t *B = I.bimm ? bimm : r[I.b];
-    const uint32_t *C = r[I.c];
-#define LANES for (int v = 0; v < kVec; ++v)
+#define LANES _Pragma("unroll") for (int v = 0; v < VEC; ++v)
 #define FA __uint_as_float(A[v])
 #define FB __uint_as_float(B[v])
 #define IA static_cast<int32_t>(A[v])
@@ -88,7 +83,6 @@ __device__ __forceinline__ void exec_one(const Instr I, const int64_t (*idx)[kVe
 #define SETI(x) d[v] = static_cast<uint32_t>(x)
     switch (I.op) {
       case CF: case CI: LANES d[v] = I.imm; break;
-      case IOTA: LANES SETI(static_cast<int32_t>(idx[I.a][v])); break;
       case FADD: LANES SETF(FA + FB); break;
       case FSUB: LANES SETF(FA - FB); break;
       case FMUL: LANES SETF(FA * FB); break;
@@ -188,6 +182,24 @@ __device__ __forceinline__ void exec_one(const Instr I, const int64_t (*idx)[kVe
   }
 }
 
+__device__ __forceinline__ void exec_one(const Instr I, const int64_t (*idx)[kVec], uint32_t (*r)[kVec]) {
+  uint32_t A[kVec], B[kVec], C[kVec], d[kVec];
+#pragma unroll
+  for (int v = 0; v < kVec; ++v) {
+    A[v] = r[I.a][v];
+    B[v] = I.bimm ? I.imm : r[I.b][v];
+    C[v] = r[I.c][v];
+  }
+  if (I.op == IOTA) {
+#pragma unroll
+    for (int v = 0; v < kVec; ++v) d[v] = static_cast<uint32_t>(static_cast<int32_t>(idx[I.a][v]));
+  } else {
+    compute<kVec>(I, A, B, C, d);
+  }
+#pragma unroll
+  for (int v = 0; v < kVec; ++v) r[I.dst][v] = d[v];
+}
+
 // Executes the program for VEC lanes whose per-input element offsets and
 // per-axis indices are given.
 __device__ __forceinline__ void run_program(const Params &p, const int64_t (*off)[kVec], const int64_t (*idx)[kVec],
@@ -259,67 +271,82 @@ __global__ void __launch_bounds__(256) ew_kernel(const __grid_constant__ Params 
   }
 }
 
-// Row-run variant: the innermost (collapsed) axis has a multiple of kVec
-// elements, so each thread takes kVec consecutive elements of one row.  The
-// row index is decomposed once per run (32-bit math when every offset fits),
-// operands with unit inner stride are read with one 16-byte (fp32) or 8-byte
-// (bf16) load, broadcast operands (inner stride 0) with one scalar load.
-__device__ __forceinline__ void load_run(const void *p, int64_t off, int64_t st, int dt, uint32_t *d) {
+// Row-run variant: the innermost (collapsed) axis has a multiple of VEC
+// elements, so each thread takes VEC consecutive elements of one row.  The
+// row index is decomposed once per run (32-bit math when every offset fits);
+// operands with unit inner stride are read with 16-byte vector loads,
+// broadcast operands (inner stride 0) with one scalar load.  The program's
+// registers live in shared memory ([reg][lane][thread], bank-conflict free),
+// sized to the registers the program uses, so the interpreter state never
+// spills to local memory.
+template <int VEC>
+__device__ __forceinline__ void load_run(const void *p, int64_t off, int64_t st, int dt, uint32_t (&d)[VEC]) {
   if (st == 0) {
     const uint32_t v = load_as_reg(p, off, dt);
 #pragma unroll
-    for (int k = 0; k < kVec; ++k) d[k] = v;
+    for (int k = 0; k < VEC; ++k) d[k] = v;
     return;
   }
   if (st == 1 && dt == NKB_F32 && ((reinterpret_cast<uintptr_t>(static_cast<const float *>(p) + off) & 15) == 0)) {
-    const uint4 t = *reinterpret_cast<const uint4 *>(static_cast<const float *>(p) + off);
-    d[0] = t.x; d[1] = t.y; d[2] = t.z; d[3] = t.w;
+#pragma unroll
+    for (int k = 0; k < VEC; k += 4) {
+      const uint4 t = *reinterpret_cast<const uint4 *>(static_cast<const float *>(p) + off + k);
+      d[k] = t.x; d[k + 1] = t.y; d[k + 2] = t.z; d[k + 3] = t.w;
+    }
     return;
   }
   if (st == 1 && dt == NKB_BF16 &&
-      ((reinterpret_cast<uintptr_t>(static_cast<const __nv_bfloat16 *>(p) + off) & 7) == 0)) {
-    const uint2 t = *reinterpret_cast<const uint2 *>(static_cast<const __nv_bfloat16 *>(p) + off);
-    d[0] = t.x << 16; d[1] = t.x & 0xffff0000u; d[2] = t.y << 16; d[3] = t.y & 0xffff0000u;
+      ((reinterpret_cast<uintptr_t>(static_cast<const __nv_bfloat16 *>(p) + off) & (2 * VEC - 1)) == 0)) {
+#pragma unroll
+    for (int k = 0; k < VEC; k += 4) {
+      const uint2 t = *reinterpret_cast<const uint2 *>(static_cast<const __nv_bfloat16 *>(p) + off + k);
+      d[k] = t.x << 16; d[k + 1] = t.x & 0xffff0000u; d[k + 2] = t.y << 16; d[k + 3] = t.y & 0xffff0000u;
+    }
     return;
   }
 #pragma unroll
-  for (int k = 0; k < kVec; ++k) d[k] = load_as_reg(p, off + k * st, dt);
+  for (int k = 0; k < VEC; ++k) d[k] = load_as_reg(p, off + k * st, dt);
 }
 
-__device__ __forceinline__ void store_run(void *p, int64_t off, int64_t st, int dt, const uint32_t *v) {
+template <int VEC>
+__device__ __forceinline__ void store_run(void *p, int64_t off, int64_t st, int dt, const uint32_t (&v)[VEC]) {
   if (st == 1 && dt == NKB_F32 && ((reinterpret_cast<uintptr_t>(static_cast<float *>(p) + off) & 15) == 0)) {
-    *reinterpret_cast<uint4 *>(static_cast<float *>(p) + off) = make_uint4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+    for (int k = 0; k < VEC; k += 4)
+      *reinterpret_cast<uint4 *>(static_cast<float *>(p) + off + k) = make_uint4(v[k], v[k + 1], v[k + 2], v[k + 3]);
     return;
   }
   if (st == 1 && dt == NKB_BF16 && ((reinterpret_cast<uintptr_t>(static_cast<__nv_bfloat16 *>(p) + off) & 7) == 0)) {
-    __nv_bfloat162 a = __floats2bfloat162_rn(__uint_as_float(v[0]), __uint_as_float(v[1]));
-    __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(v[2]), __uint_as_float(v[3]));
-    uint2 t;
-    t.x = *reinterpret_cast<uint32_t *>(&a);
-    t.y = *reinterpret_cast<uint32_t *>(&b);
-    *reinterpret_cast<uint2 *>(static_cast<__nv_bfloat16 *>(p) + off) = t;
+#pragma unroll
+    for (int k = 0; k < VEC; k += 4) {
+      __nv_bfloat162 a = __floats2bfloat162_rn(__uint_as_float(v[k]), __uint_as_float(v[k + 1]));
+      __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(v[k + 2]), __uint_as_float(v[k + 3]));
+      uint2 t;
+      t.x = *reinterpret_cast<uint32_t *>(&a);
+      t.y = *reinterpret_cast<uint32_t *>(&b);
+      *reinterpret_cast<uint2 *>(static_cast<__nv_bfloat16 *>(p) + off + k) = t;
+    }
     return;
   }
 #pragma unroll
-  for (int k = 0; k < kVec; ++k) store_from_reg(p, off + k * st, dt, v[k]);
+  for (int k = 0; k < VEC; ++k) store_from_reg(p, off + k * st, dt, v[k]);
 }
 
-template <typename IDX>
+template <typename IDX, int VEC>
 __global__ void __launch_bounds__(256) ew_rows_kernel(const __grid_constant__ Params p) {
-  uint32_t r[kRegs][kVec];
+  extern __shared__ uint32_t sreg[];
+  const int T = blockDim.x;
+  uint32_t *R = sreg + threadIdx.x;  // register (g, lane v) at R[(g * VEC + v) * T]
   const int last = p.rank - 1;
   const IDX inner = (IDX)p.shape[last];
-  const IDX runs_per_row = inner / kVec;
-  const IDX runs = (IDX)(p.n / kVec);
-  bool uses_iota = false;
-  for (int pc = 0; pc < p.n_instr; ++pc) uses_iota |= (p.prog[pc].op == IOTA);
+  const IDX runs_per_row = inner / VEC;
+  const IDX runs = (IDX)(p.n / VEC);
   for (IDX c = (IDX)blockIdx.x * blockDim.x + threadIdx.x; c < runs; c += (IDX)gridDim.x * blockDim.x) {
     const IDX row = c / runs_per_row;
-    const IDX col = (c - row * runs_per_row) * kVec;
+    const IDX col = (c - row * runs_per_row) * VEC;
     int64_t oo = p.out_off + (int64_t)col * p.out_strides[last];
     int64_t base[kMaxIn];
     for (int k = 0; k < p.n_in; ++k) base[k] = p.in_off[k] + (int64_t)col * p.in_strides[k][last];
-    int64_t idx[kMaxRank][kVec];
     IDX rem = row;
     for (int d = last - 1; d >= 0; --d) {
       const IDX s = (IDX)p.shape[d];
@@ -328,23 +355,44 @@ __global__ void __launch_bounds__(256) ew_rows_kernel(const __grid_constant__ Pa
       rem = q;
       oo += (int64_t)id * p.out_strides[d];
       for (int k = 0; k < p.n_in; ++k) base[k] += (int64_t)id * p.in_strides[k][d];
-      if (uses_iota)
-#pragma unroll
-        for (int v = 0; v < kVec; ++v) idx[d][v] = id;
     }
-    if (uses_iota)
-#pragma unroll
-      for (int v = 0; v < kVec; ++v) idx[last][v] = col + v;
-    // program, with loads served by row runs
     for (int pc = 0; pc < p.n_instr; ++pc) {
       const Instr I = p.prog[pc];
+      uint32_t d[VEC];
       if (I.op == LD) {
-        load_run(p.in[I.a], base[I.a], p.in_strides[I.a][last], p.in_dtype[I.a], r[I.dst]);
+        load_run<VEC>(p.in[I.a], base[I.a], p.in_strides[I.a][last], p.in_dtype[I.a], d);
+      } else if (I.op == IOTA) {
+        int64_t id = 0;
+        if (I.a == last) {
+          id = col;
+        } else {
+          IDX r2 = row;
+          for (int dd = last - 1; dd >= 0; --dd) {
+            const IDX s = (IDX)p.shape[dd];
+            const IDX q = r2 / s;
+            if (dd == I.a) id = r2 - q * s;
+            r2 = q;
+          }
+        }
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) d[v] = (uint32_t)(int32_t)(id + (I.a == last ? v : 0));
       } else {
-        exec_one(I, idx, r);
+        uint32_t A[VEC], B[VEC], C[VEC];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          A[v] = R[(I.a * VEC + v) * T];
+          B[v] = I.bimm ? I.imm : R[(I.b * VEC + v) * T];
+          C[v] = R[(I.c * VEC + v) * T];
+        }
+        compute<VEC>(I, A, B, C, d);
       }
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) R[(I.dst * VEC + v) * T] = d[v];
     }
-    store_run(p.out, oo, p.out_strides[last], p.out_dtype, r[p.out_reg]);
+    uint32_t o[VEC];
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) o[v] = R[(p.out_reg * VEC + v) * T];
+    store_run<VEC>(p.out, oo, p.out_strides[last], p.out_dtype, o);
   }
 }
 
@@ -414,7 +462,7 @@ int launch(const LaunchArgs &a) {
   int64_t blocks = (p.n + (int64_t)threads * kVec - 1) / ((int64_t)threads * kVec);
   const int64_t cap = (int64_t)num_sms(a.device) * 16;
   if (blocks > cap) blocks = cap;
-  if (p.shape[p.rank - 1] % kVec == 0) {
+  if (p.shape[p.rank - 1] % 4 == 0) {
     // 32-bit index math when the element count and every offset fit
     int64_t span = p.n;
     for (int k = 0; k < p.n_in; ++k) {
@@ -422,8 +470,34 @@ int launch(const LaunchArgs &a) {
       for (int d = 0; d < p.rank; ++d) hi += (p.shape[d] - 1) * (p.in_strides[k][d] < 0 ? 0 : p.in_strides[k][d]);
       span = span > hi ? span : hi;
     }
-    if (span < INT32_MAX) ew_rows_kernel<int32_t><<<(unsigned)blocks, threads, 0, a.stream>>>(p);
-    else ew_rows_kernel<int64_t><<<(unsigned)blocks, threads, 0, a.stream>>>(p);
+    int nregs = p.out_reg + 1;
+    for (int i = 0; i < p.n_instr; ++i) {
+      const Instr &I = p.prog[i];
+      nregs = max(nregs, (int)I.dst + 1);
+      if (I.op != LD && I.op != IOTA && I.op != CF && I.op != CI) {
+        nregs = max(nregs, (int)I.a + 1);
+        if (!I.bimm) nregs = max(nregs, (int)I.b + 1);
+        if (I.op == SEL) nregs = max(nregs, (int)I.c + 1);
+      }
+    }
+    const bool v8 = p.shape[p.rank - 1] % 8 == 0;
+    const int vec = v8 ? 8 : 4;
+    const size_t smem = (size_t)nregs * vec * threads * 4;
+    int64_t blocks2 = (p.n / vec + threads - 1) / threads;
+    if (blocks2 > cap) blocks2 = cap;
+    if (blocks2 < 1) blocks2 = 1;
+    const bool small = span < INT32_MAX;
+#define EW_ROWS(IDXT, V)                                                                                  \
+  do {                                                                                                    \
+    auto kfn = ew_rows_kernel<IDXT, V>;                                                                    \
+    if (smem > 48 * 1024) NKB_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+    kfn<<<(unsigned)blocks2, threads, smem, a.stream>>>(p);                                                \
+  } while (0)
+    if (small && v8) EW_ROWS(int32_t, 8);
+    else if (small) EW_ROWS(int32_t, 4);
+    else if (v8) EW_ROWS(int64_t, 8);
+    else EW_ROWS(int64_t, 4);
+#undef EW_ROWS
     return launch_status("ew_rows_kernel");
   }
   ew_kernel<<<(unsigned)blocks, threads, 0, a.stream>>>(p);

@@ -184,3 +184,12 @@ def test_swiglu_ffn(tokens, hidden, ffn):
     act = r(f(r(g * f(r(1.0 / f(r(1.0 + f(r(np.exp(-g))))))))) * u)
     want = f(act) @ f(dn)
     assert_close(got, want, BF16_RTOL)
+
+
+@pytest.mark.parametrize("shape", [(1, 2, 256, 32), (2, 3, 512, 128)])
+def test_chunked_linear_attention(shape):
+    rng = np.random.default_rng(15)
+    q, k, v = (rng.standard_normal(shape, dtype=np.float32).astype(BF16) for _ in range(3))
+    got = on_device(W.chunked_linear_attention_kernel, q, k, v)
+    want = O.linear_attention_recurrent(q, k, v)
+    assert_close(got, want, BF16_RTOL)
