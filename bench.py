@@ -210,7 +210,7 @@ class Bmm(Gemm):
 
 
 class LinAttn(Workload):
-    name, metric, unit, bound, dtype, dominant = "linattn", "HBM GB/s (chunked causal linear attention)", "GB/s", "hbm", "bf16", "gemm_simt"
+    name, metric, unit, bound, dtype, dominant = "linattn", "HBM GB/s (chunked causal linear attention)", "GB/s", "hbm", "bf16", "linattn"
     SHAPE = (8, 16, 4096, 128)
 
     def kernel_and_args(self, rank, world):
@@ -291,7 +291,8 @@ class Layer(Workload):
 
 
 WORKLOADS = {w.name: w for w in (Softmax, RmsNorm, Gemm, Bmm, LinAttn, Layer)}
-DEFAULT_WORKLOAD = "rmsnorm"
+DEFAULT_WORKLOAD = "layer"
+SUITE = ("softmax", "rmsnorm", "gemm", "bmm", "linattn")
 
 
 def _parallel_rows(fn, arrays, threads):
@@ -552,7 +553,71 @@ def run_nkb(args, wl, rank, world, local_rank):
         "per_launch_ms": {f"{i}:{s['kernel']}": round(ms, 4) for i, (s, ms) in enumerate(zip(plan_steps, step_ms))}
         if len(step_ms) <= 64 else None,
     }
+    if world == 1 and not args.no_suite:
+        suite = {}
+        for name in SUITE:
+            if name == wl.name:
+                continue
+            try:
+                suite[name] = measure_quick(WORKLOADS[name](), 5, 2, local_rank, not args.no_cpu)
+            except Exception as e:  # report, never hide, a failing configuration
+                suite[name] = {"error": f"{type(e).__name__}: {e}"}
+        line["suite"] = suite
     print(json.dumps(line), flush=True)
+
+
+def measure_quick(wl, steps, warmup, local_rank, with_cpu):
+    """Single-GPU measurement of one workload for the suite object (same method, fewer steps)."""
+    import torch
+
+    from nkipy_b200.runtime import DeviceKernel, DeviceTensor
+    from nkipy_b200.spike import get_spike_singleton
+
+    spike = get_spike_singleton()
+    fn, np_args, kwargs = wl.kernel_and_args(0, 1)
+    kernel = DeviceKernel.compile_and_load(fn, *np_args, name=f"suite_{wl.name}", is_spmd=False, **kwargs)
+    names = [t["name"] for t in kernel.model_ref.io["inputs"]]
+    arrays = [a for a in np_args if isinstance(a, np.ndarray)]
+    ins = {n: DeviceTensor.from_numpy(a, name=n).tensor_ref for n, a in zip(names, arrays)}
+    outs = {t.name: t.tensor_ref for t in kernel.allocate_output_tensors()}
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=f"cuda:{local_rank}")
+    for _ in range(warmup):
+        spike.execute(kernel.model_ref, ins, outs, use_graph=True)
+    total = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        total += spike.time_execute(kernel.model_ref, ins, outs, warmup=0, iters=1, use_graph=True)[0]
+    ms = total / steps
+    step_ms = spike.time_steps(kernel.model_ref, ins, outs, iters=3)
+    plan_steps = _plan_steps(kernel.plan_path)
+    peaks, _ = load_peaks()
+    dom = [i for i, st in enumerate(plan_steps) if st["kernel"] == wl.dominant]
+    frac = achieved = None
+    if dom:
+        dur = sum(step_ms[i] for i in dom)
+        if wl.bound == "hbm":
+            achieved = wl.dominant_work() * len(dom) / (dur / 1e3) / 1e9
+            frac = achieved / float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+        else:
+            achieved = sum(plan_steps[i]["flops"] for i in dom) / (dur / 1e3) / 1e12
+            frac = achieved / float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+    out = {
+        "metric": wl.metric,
+        "value": wl.units_per_step(1) / (ms / 1e3),
+        "unit": wl.unit,
+        "ms_per_step": ms,
+        "launches_per_step": kernel.model_ref.num_launches,
+        "dominant_kernel": wl.dominant,
+        "dominant_achieved": achieved,
+        "roofline_frac": frac,
+        "bound": wl.bound,
+    }
+    if with_cpu:
+        cv, desc, _ = cpu_measure(wl, 1, 0, os.cpu_count() or 1)
+        out["cpu_baseline"] = {"value": cv, "unit": wl.unit, "cores": os.cpu_count() or 1, "kind": "port", "sample": desc}
+    del kernel, ins, outs
+    return out
 
 
 def _plan_steps(path):
@@ -589,6 +654,7 @@ def main():
     ap.add_argument("--impl", default="nkb", choices=["nkb", "reference"])
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-suite", action="store_true", help="at N=1, skip measuring the other configurations")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))
@@ -596,6 +662,8 @@ def main():
     wl = WORKLOADS[args.workload]()
     if args.impl == "reference":
         return run_reference(args, wl, rank, world)
+    # keep stdout to the one JSON line (NCCL prints a version banner at INFO/VERSION)
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
     if world > 1:
         import datetime
 

@@ -236,6 +236,8 @@ class Lowering:
             self.lower_attention(c)
         elif c.kind == "swiglu_gemm":
             self.lower_swiglu(c)
+        elif c.kind == "linattn":
+            self.lower_linattn(c)
         elif c.kind == "argmax":
             x = c.params["x"]
             xv, rows, cols = self.dense_rows(x)
@@ -280,6 +282,33 @@ class Lowering:
             note=f"B{B} H{H}/{k_heads} S{S} D{D} causal={int(p['causal'])}",
         )
         self.vals[("o", root.id)] = out.with_(shape=(B, H, S, D), strides=(S * H * D, D, H * D, 1))
+
+    def lower_linattn(self, c):
+        p = c.params
+        B, H, T, D = p["shape"]
+        views = []
+        for t in (p["q"], p["k"], p["v"]):
+            v = self.get(t)
+            if not isinstance(v, V.View) or v.strides[3] != 1 or any(st % 8 for st in v.strides[:3]):
+                v = self.materialize(v, dense=True)
+            views.append(v)
+        out = self.tmp_view((B, H, T, D), BF16)
+        # segments per (batch, head): enough CTAs for the 148 SMs, whole chunks each
+        chunks, G = T // 64, 1
+        while G * 2 <= chunks and B * H * G < 2 * 148 and chunks % (G * 2) == 0:
+            G *= 2
+        ws = self.new_buf("tmp", -1, B * H * G * (D * D + D) * 4)
+        ints = [B, H, T, D, G]
+        for v in views:
+            ints += list(v.strides[:3])
+        ints += list(out.strides[:3])
+        self.step(
+            "linattn",
+            [self.bref(views[0]), self.bref(views[1]), self.bref(views[2]), self.bref(out), (ws, 0)],
+            ints,
+            note=f"B{B} H{H} T{T} D{D} segments={G}",
+        )
+        self.vals[("o", c.root.id)] = out
 
     def lower_swiglu(self, c):
         """gate/up GEMM with silu(gate) * up in the epilogue; generic path otherwise."""

@@ -547,7 +547,171 @@ def match_swiglu_gemm(gi: GraphIndex, mul_op) -> Optional[Claim]:
     return None
 
 
-MATCHERS = (match_attention, match_swiglu_gemm, match_softmax, match_rmsnorm, match_argmax)
+def _prod(op_name, t, ops, n_args=None):
+    p = GraphIndex.producer(t)
+    if p is None or p.op_name != op_name or (n_args is not None and len(p.operands) != n_args):
+        return None
+    ops.append(p)
+    return p
+
+
+def _elu1_of(t, ops):
+    """t = select(x > 0, x + 1, exp(x)) with x = convert(src -> f32); returns src."""
+    sel = _prod("select", t, ops)
+    if sel is None:
+        return None
+    cond, a, b = sel.operands
+    pc = _prod("compare", cond, ops)
+    if pc is None or pc.attributes.get("comparison_direction") != "GT":
+        return None
+    x = pc.operands[0]
+    if scalar_const(pc.operands[1], ops) != 0.0:
+        return None
+    pa = _prod("add", a, ops)
+    pe = _prod("exponential", b, ops)
+    if pa is None or pe is None or tkey(pa.operands[0]) != tkey(x) or tkey(pe.operands[0]) != tkey(x):
+        return None
+    if scalar_const(pa.operands[1], ops) != 1.0:
+        return None
+    pcv = GraphIndex.producer(x)
+    if pcv is None or pcv.op_name != "convert":
+        return None
+    ops.append(pcv)
+    return pcv.operands[0]
+
+
+def _cumsum_of(t, ops):
+    """t = cumsum(x, axis) as core/ops/reduce.py:320-385 traces it; returns x."""
+    pt = _prod("transpose", t, ops)
+    if pt is None:
+        return None
+    pr = _prod("reshape", pt.operands[0], ops)
+    if pr is None:
+        return None
+    pd = _prod("dot", pr.operands[0], ops)
+    if pd is None:
+        return None
+    tri = GraphIndex.producer(pd.operands[1])
+    if tri is None or tri.op_name != "constant":
+        return None
+    val = np.asarray(tri.attributes.get("value"))
+    if val.ndim != 2 or not np.array_equal(val, np.triu(np.ones_like(val))):
+        return None
+    ops.append(tri)
+    pr2 = _prod("reshape", pd.operands[0], ops)
+    if pr2 is None:
+        return None
+    pt2 = _prod("transpose", pr2.operands[0], ops)
+    if pt2 is None or list(pt2.attributes["permutation"]) != list(pt.attributes["permutation"]):
+        return None
+    return pt2.operands[0]
+
+
+def match_linear_attention(gi: GraphIndex, root) -> Optional[Claim]:
+    """The chunked linear attention body of nkipy_b200/workloads.py (elu+1, causal, normalised)."""
+    if root.op_name != "convert" or len(root.result_shape) != 4:
+        return None
+    ops = []
+    rs = _prod("reshape", root.operands[0], ops)
+    if rs is None:
+        return None
+    dv = _prod("divide", rs.operands[0], ops)
+    if dv is None:
+        return None
+    num_t, den_b = dv.operands
+    den_t = strip(den_b, ops)
+    pnum = _prod("add", num_t, ops)
+    pden = _prod("add", den_t, ops)
+    if pnum is None or pden is None:
+        return None
+    # numerator: dot(Sm, V) + dot(Phi_q, State)
+    d1 = _prod("dot", pnum.operands[0], ops)
+    d2 = _prod("dot", pnum.operands[1], ops)
+    if d1 is None or d2 is None:
+        return None
+    sm_t, vc_t = d1.operands
+    phq_t, st_t = d2.operands
+    pm = _prod("multiply", sm_t, ops)
+    if pm is None:
+        return None
+    scores_t, mask_b = pm.operands
+    tri = GraphIndex.producer(strip(mask_b, ops))
+    if tri is None or tri.op_name != "constant":
+        return None
+    tv = np.asarray(tri.attributes.get("value"))
+    if tv.ndim != 2 or not np.array_equal(tv, np.tril(np.ones_like(tv))):
+        return None
+    ops.append(tri)
+    chunk = tv.shape[0]
+    psc = _prod("dot", scores_t, ops)
+    if psc is None or tkey(psc.operands[0]) != tkey(phq_t):
+        return None
+    ptk = _prod("transpose", psc.operands[1], ops)
+    if ptk is None:
+        return None
+    phk_t = ptk.operands[0]
+    # state = cumsum(KV) - KV, KV = Phi_k^T V
+    pst = _prod("subtract", st_t, ops)
+    if pst is None:
+        return None
+    pkv = _prod("dot", pst.operands[1], ops)
+    if pkv is None or tkey(pkv.operands[1]) != tkey(vc_t):
+        return None
+    ptk2 = _prod("transpose", pkv.operands[0], ops)
+    if ptk2 is None or tkey(ptk2.operands[0]) != tkey(phk_t):
+        return None
+    cs = _cumsum_of(pst.operands[0], ops)
+    if cs is None or tkey(cs) != tkey(pst.operands[1]):
+        return None
+    # denominator: rowsum(Sm) + rowsum(Phi_q * zsum)
+    r1 = last_axis_reduce(strip(pden.operands[0], ops), "add", ops)
+    r2 = last_axis_reduce(strip(pden.operands[1], ops), "add", ops)
+    if r1 is None or r2 is None or tkey(r1) != tkey(sm_t):
+        return None
+    pqz = _prod("multiply", r2, ops)
+    if pqz is None or tkey(pqz.operands[0]) != tkey(phq_t):
+        return None
+    pz = _prod("subtract", strip(pqz.operands[1], ops), ops)
+    if pz is None:
+        return None
+    ksum_t = pz.operands[1]
+    csz = _cumsum_of(pz.operands[0], ops)
+    if csz is None or tkey(csz) != tkey(ksum_t):
+        return None
+    pks = _prod("reshape", ksum_t, ops)
+    if pks is None:
+        return None
+    pkr = GraphIndex.producer(pks.operands[0])
+    if pkr is None or pkr.op_name != "reduce" or pkr.attributes.get("computation") != "add":
+        return None
+    ops += [pkr, GraphIndex.producer(pkr.operands[1])]
+    if tkey(pkr.operands[0]) != tkey(phk_t):
+        return None
+    # feature maps and value convert
+    pq_r = _prod("reshape", phq_t, ops)
+    pk_r = _prod("reshape", phk_t, ops)
+    pv_r = _prod("reshape", vc_t, ops)
+    if pq_r is None or pk_r is None or pv_r is None:
+        return None
+    q_src = _elu1_of(pq_r.operands[0], ops)
+    k_src = _elu1_of(pk_r.operands[0], ops)
+    pvc = _prod("convert", pv_r.operands[0], ops)
+    if q_src is None or k_src is None or pvc is None:
+        return None
+    v_src = pvc.operands[0]
+    shape = tuple(root.result_shape)
+    for t in (q_src, k_src, v_src):
+        if tuple(t.shape) != shape or str(np.dtype(t.dtype)) != "bfloat16":
+            return None
+    if str(np.dtype(root.result_dtype)) != "bfloat16" or shape[3] != 128 or chunk != 64 or shape[2] % chunk:
+        return None
+    ops = [o for o in ops if o is not None]
+    if not _exclusive(gi, ops, root):
+        return None
+    return Claim("linattn", root, ops, {"q": q_src, "k": k_src, "v": v_src, "shape": shape})
+
+
+MATCHERS = (match_attention, match_linear_attention, match_swiglu_gemm, match_softmax, match_rmsnorm, match_argmax)
 
 
 def find_claims(graph) -> Dict[int, Claim]:
