@@ -97,7 +97,7 @@ __device__ __forceinline__ float row_reduce_sum(float v, float *smem) {
 // THREADS threads per row (32 or 256); CHUNKS 4-element chunks per thread.
 // Rows per CTA = 256 / THREADS.  cols must be a multiple of 4 here.
 template <int THREADS, int CHUNKS, typename Tin, typename Tout>
-__global__ void __launch_bounds__(256) softmax_reg_kernel(const Tin *__restrict__ x, Tout *__restrict__ y,
+__global__ void __launch_bounds__(256, 6) softmax_reg_kernel(const Tin *__restrict__ x, Tout *__restrict__ y,
                                                           int64_t rows, int cols) {
   __shared__ float smem[32];
   constexpr int RPB = 256 / THREADS;
