@@ -154,6 +154,30 @@ NKB_API int nkb_gemm_bf16(const void *A, const void *B, void *C, int c_dtype, in
                   int64_t lda, int64_t ldb, int64_t ldc, int64_t batch, int64_t sA, int64_t sB, int64_t sC,
                   void *stream);
 
+/* Allocation-free chunked causal linear attention.  No counterpart in the
+ * reference: it serves callers that cannot allocate device memory when they
+ * run this kernel, such as a host that has reserved the whole GPU for its own
+ * caching allocator, or a latency-critical loop where cudaMalloc/cudaFree
+ * could block or synchronise the device.  Same computation as the planned
+ * "linattn" kernel (feature map elu + 1, chunk 64, fp32 running state); q, k,
+ * v and out are dense bf16 (B, H, T, 128) device arrays of the current device,
+ * T a multiple of 64, 16-byte aligned.  The caller passes inputs and the
+ * output; the kernel's segment-state workspace is a fixed device array of
+ * NKB_LINATTN_SCRATCH_BYTES inside libnkb, held by every GPU that loads the
+ * library until the process exits.  The workspace is B * H * ceil(T / 1024)
+ * * 66,048 bytes (one fp32 128 x 128 state and key sum per 1024-token
+ * segment; none for T <= 1024); sizes whose workspace would exceed the array
+ * are rejected with NKB_ERR_INVALID.  The function itself calls no cudaMalloc,
+ * cudaFree or allocating library routine; its first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress), so make that first call
+ * before any stream capture.  All calls share the one array: calls that
+ * overlap on the GPU (different streams, or several host threads) race and
+ * must be serialised by the caller.  Each call writes every workspace entry
+ * it reads, so the array needs no clearing between calls. */
+#define NKB_LINATTN_SCRATCH_BYTES (64u << 20)
+NKB_API int nkb_linear_attention_noalloc(const void *q, const void *k, const void *v, void *out, int64_t B, int64_t H,
+                                         int64_t T, int64_t D, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,15 +8,17 @@
 // One CTA per (batch*head, segment of the sequence); 8 warps.
 //   phase 0 (state): each segment's sum of phi(K)^T V and of phi(K) over its
 //                    chunks -> workspace (fp32, D x D + D per segment);
-//   phase 1 (output): the CTA seeds its running state with the sum of the
-//                    workspace entries of the earlier segments of its head,
-//                    then walks its chunks: intra-chunk masked scores, the
-//                    state product, the normaliser, and the state update.
+//   scan:             per head, the segment states become exclusive prefixes;
+//   phase 1 (output): the CTA seeds its running state with its segment's
+//                    prefix, then walks its chunks: intra-chunk masked scores,
+//                    the state product, the normaliser, and the state update.
 // Chunks of q/k/v are double-buffered in shared memory with cp.async; the
 // feature map is applied in place; products use bf16 mma.sync m16n8k16 with
 // fp32 accumulation; the running state S is kept in fp32 registers (16 rows of
 // S per warp) and mirrored to shared memory in bf16 as the operand of
 // phi(Q) S.  The workspace is the only memory beyond inputs and output.
+
+#include <mutex>
 
 #include "common.cuh"
 
@@ -122,25 +124,19 @@ __global__ void __launch_bounds__(THREADS, 1) linattn_kernel(const __grid_consta
   for (int j = 0; j < D / 8; ++j) S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.f;
   const int srow = warp * 16 + lane / 4;
   for (int i = threadIdx.x; i < D; i += THREADS) sZ[i] = 0.f;
-  if (out_phase) {
-    // seed with the earlier segments of this head (exclusive prefix)
-    for (int s2 = 0; s2 < seg; ++s2) {
-      const float *w = ws + (int64_t)s2 * (D * D + D);
+  if (out_phase && seg > 0) {
+    // seed with the exclusive prefix of the earlier segments of this head
+    const float *w = ws + (int64_t)seg * (D * D + D);
 #pragma unroll
-      for (int j = 0; j < D / 8; ++j) {
-        const int col = j * 8 + (lane % 4) * 2;
-        S[j][0] += w[srow * D + col];
-        S[j][1] += w[srow * D + col + 1];
-        S[j][2] += w[(srow + 8) * D + col];
-        S[j][3] += w[(srow + 8) * D + col + 1];
-      }
+    for (int j = 0; j < D / 8; ++j) {
+      const int col = j * 8 + (lane % 4) * 2;
+      S[j][0] = w[srow * D + col];
+      S[j][1] = w[srow * D + col + 1];
+      S[j][2] = w[(srow + 8) * D + col];
+      S[j][3] = w[(srow + 8) * D + col + 1];
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < D; i += THREADS) {
-      float z = 0.f;
-      for (int s2 = 0; s2 < seg; ++s2) z += ws[(int64_t)s2 * (D * D + D) + D * D + i];
-      sZ[i] = z;
-    }
+    for (int i = threadIdx.x; i < D; i += THREADS) sZ[i] = w[D * D + i];
   }
   // bf16 mirror of S for phi(Q) S
   auto publish_S = [&]() {
@@ -154,7 +150,7 @@ __global__ void __launch_bounds__(THREADS, 1) linattn_kernel(const __grid_consta
   if (out_phase) publish_S();
 
   const int c0 = seg * p.chunks_per_seg;
-  const int n = p.chunks_per_seg;
+  const int n = min(p.chunks_per_seg, p.T / C - c0);
   auto issue = [&](int ci, int stg) {
     uint8_t *base = stage0 + stg * 3 * TILE;
     const int t0 = (c0 + ci) * C;
@@ -329,6 +325,20 @@ __global__ void __launch_bounds__(THREADS, 1) linattn_kernel(const __grid_consta
 }
 
 constexpr int SMEM = 2 * 3 * TILE + D * D * 2 + C * C * 2 + (2 * D + 3 * C) * 4;
+constexpr int SEG_CHUNKS = 16;  // chunks (of 64 tokens) per segment
+
+// per head: segment states -> exclusive prefixes over the segments, in place
+__global__ void __launch_bounds__(256) linattn_scan_kernel(float *ws, int G) {
+  float *w = ws + (int64_t)blockIdx.x * G * (D * D + D);
+  for (int i = threadIdx.x; i < D * D + D; i += blockDim.x) {
+    float run = 0.f;
+    for (int g = 0; g < G; ++g) {
+      const float x = w[(int64_t)g * (D * D + D) + i];
+      w[(int64_t)g * (D * D + D) + i] = run;
+      run += x;
+    }
+  }
+}
 
 int run(const Params &base, cudaStream_t st) {
   static bool attr = false;
@@ -342,18 +352,20 @@ int run(const Params &base, cudaStream_t st) {
     p.phase = 0;
     linattn_kernel<<<grid, THREADS, SMEM, st>>>(p);
     if (int s = launch_status("linattn_kernel(state)")) return s;
+    linattn_scan_kernel<<<p.BH, 256, 0, st>>>(p.ws, p.G);
+    if (int s = launch_status("linattn_scan_kernel")) return s;
   }
   p.phase = 1;
   linattn_kernel<<<grid, THREADS, SMEM, st>>>(p);
   return launch_status("linattn_kernel(output)");
 }
 
-// segments per head: enough CTAs to fill the GPU, whole chunks per segment
+// segments per head: SEG_CHUNKS chunks each (the last one may be shorter)
 int pick_segments(int BH, int T, int device) {
+  (void)BH;
+  (void)device;
   const int chunks = T / C;
-  int g = 1;
-  while (g * 2 <= chunks && BH * g < 2 * num_sms(device) && chunks % (g * 2) == 0) g *= 2;
-  return g;
+  return chunks <= SEG_CHUNKS ? 1 : (chunks + SEG_CHUNKS - 1) / SEG_CHUNKS;
 }
 
 size_t workspace_bytes(int BH, int G) { return (size_t)BH * G * (D * D + D) * sizeof(float); }
@@ -363,6 +375,9 @@ int check(const Step &s) {
   if (s.buf_ids.size() != 5 || s.ints.size() != 17) return fail(NKB_ERR_PLAN, "linattn: bad parameters");
   if (s.ints[3] != D) return fail(NKB_ERR_UNSUPPORTED, "linattn: head_dim must be 128");
   if (s.ints[2] % C) return fail(NKB_ERR_UNSUPPORTED, "linattn: length must be a multiple of 64");
+  const int64_t chunks = s.ints[2] / C;
+  const int64_t G = chunks <= SEG_CHUNKS ? 1 : (chunks + SEG_CHUNKS - 1) / SEG_CHUNKS;
+  if (s.ints[4] != G) return fail(NKB_ERR_PLAN, "linattn: segment count does not match the kernel's segmentation");
   for (int i = 5; i < 17; ++i)
     if (s.ints[i] % 8) return fail(NKB_ERR_UNSUPPORTED, "linattn: strides must be multiples of 8");
   return NKB_OK;
@@ -381,7 +396,7 @@ int launch(const LaunchArgs &a) {
   p.BH = B * p.H;
   p.T = (int)q[2];
   p.G = (int)q[4];
-  p.chunks_per_seg = p.T / C / p.G;
+  p.chunks_per_seg = p.G > 1 ? SEG_CHUNKS : p.T / C;
   p.qb = q[5]; p.qh = q[6]; p.qs = q[7];
   p.kb = q[8]; p.kh = q[9]; p.ks = q[10];
   p.vb = q[11]; p.vh = q[12]; p.vs = q[13];
@@ -399,4 +414,81 @@ NKB_REGISTER_KERNEL("linattn", linattn::launch, linattn::check);
 int linattn_segments(int BH, int T, int device) { return linattn::pick_segments(BH, T, device); }
 size_t linattn_workspace_bytes(int BH, int G) { return linattn::workspace_bytes(BH, G); }
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant
+// ---------------------------------------------------------------------------
+// The planned path gets its segment-state workspace from the plan's scratch
+// arena, which the runtime allocates when the plan is loaded.  Some callers
+// cannot allocate device memory at the point where they run this kernel: a
+// host process that has handed the whole GPU to its own caching allocator up
+// front, or a latency-critical loop in which a cudaMalloc/cudaFree could
+// block or synchronise the device.  For them the workspace lives in a fixed,
+// file-scope device array of NKB_LINATTN_SCRATCH_BYTES: every GPU that loads
+// this library holds it until the process exits, and every call shares it.
+namespace linattn {
+
+static __device__ __align__(256) unsigned char g_scratch[NKB_LINATTN_SCRATCH_BYTES];
+
+static void *g_scratch_addr[64];
+static std::mutex g_scratch_mu;
+
+// Device address of the fixed workspace on the current device.  In host code
+// `g_scratch` only names a host-side stand-in, so the address is looked up
+// once per device with that device current.
+static int scratch_address(int device, void **out) {
+  if (device < 0 || device >= 64) return fail(NKB_ERR_INVALID, "device index out of range");
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_addr[device]) {
+    void *ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(NKB_ERR_CUDA, std::string("cudaGetSymbolAddress(linear-attention scratch): ") + cudaGetErrorString(e));
+    g_scratch_addr[device] = ptr;
+  }
+  *out = g_scratch_addr[device];
+  return NKB_OK;
+}
+
+}  // namespace linattn
 }  // namespace nkb
+
+extern "C" int nkb_linear_attention_noalloc(const void *q, const void *k, const void *v, void *out, int64_t B,
+                                            int64_t H, int64_t T, int64_t D, void *stream) {
+  using namespace nkb;
+  using namespace nkb::linattn;
+  if (!q || !k || !v || !out) return fail(NKB_ERR_INVALID, "linear attention: NULL pointer");
+  if (D != linattn::D) return fail(NKB_ERR_UNSUPPORTED, "linear attention: head_dim must be 128");
+  if (B < 0 || H < 0 || T < 0 || T % C) return fail(NKB_ERR_UNSUPPORTED, "linear attention: length must be a multiple of 64");
+  if (B * H > INT32_MAX / 2 || T > INT32_MAX / 2) return fail(NKB_ERR_INVALID, "linear attention: sizes too large");
+  const uintptr_t al = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                       reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out);
+  if (al & 15) return fail(NKB_ERR_UNSUPPORTED, "linear attention: pointers must be 16-byte aligned");
+  if (B == 0 || H == 0 || T == 0) return NKB_OK;
+  int dev = 0;
+  NKB_CUDA_TRY(cudaGetDevice(&dev));
+  const int BH = (int)(B * H);
+  const int G = pick_segments(BH, (int)T, dev);
+  const size_t need = G > 1 ? workspace_bytes(BH, G) : 0;
+  if (need > (size_t)NKB_LINATTN_SCRATCH_BYTES)
+    return fail(NKB_ERR_INVALID, "linear attention: " + std::to_string(B) + "x" + std::to_string(H) +
+                                     " heads need " + std::to_string(need) + " bytes of workspace, more than the fixed " +
+                                     std::to_string((size_t)NKB_LINATTN_SCRATCH_BYTES) + " bytes of the allocation-free entry point");
+  void *ws = nullptr;
+  if (int s = scratch_address(dev, &ws)) return s;
+  Params p;
+  p.q = static_cast<const __nv_bfloat16 *>(q);
+  p.k = static_cast<const __nv_bfloat16 *>(k);
+  p.v = static_cast<const __nv_bfloat16 *>(v);
+  p.o = static_cast<__nv_bfloat16 *>(out);
+  p.ws = static_cast<float *>(ws);
+  p.H = (int)H;
+  p.BH = BH;
+  p.T = (int)T;
+  p.G = G;
+  p.chunks_per_seg = G > 1 ? SEG_CHUNKS : (int)(T / C);
+  const int64_t sb = H * T * D, sh = T * D, ss = D;
+  p.qb = p.kb = p.vb = p.ob = sb;
+  p.qh = p.kh = p.vh = p.oh = sh;
+  p.qs = p.ks = p.vs = p.os = ss;
+  return run(p, static_cast<cudaStream_t>(stream));
+}

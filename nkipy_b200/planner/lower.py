@@ -293,11 +293,10 @@ class Lowering:
                 v = self.materialize(v, dense=True)
             views.append(v)
         out = self.tmp_view((B, H, T, D), BF16)
-        # segments per (batch, head): enough CTAs for the 148 SMs, whole chunks each
-        chunks, G = T // 64, 1
-        while G * 2 <= chunks and B * H * G < 2 * 148 and chunks % (G * 2) == 0:
-            G *= 2
-        ws = self.new_buf("tmp", -1, B * H * G * (D * D + D) * 4)
+        # segments of 16 chunks (1024 tokens) per (batch, head); one fp32 state each
+        chunks = T // 64
+        G = 1 if chunks <= 16 else -(-chunks // 16)
+        ws = self.new_buf("tmp", -1, max(1, B * H * G * (D * D + D) * 4) if G > 1 else 256)
         ints = [B, H, T, D, G]
         for v in views:
             ints += list(v.strides[:3])

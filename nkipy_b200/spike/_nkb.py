@@ -90,6 +90,7 @@ def _declare(lib):
         "nkb_softmax_rows": [vp, i32, vp, i32, i64, i64, vp],
         "nkb_rmsnorm_rows": [vp, vp, vp, vp, vp, i32, i32, i64, i64, ctypes.c_float, vp],
         "nkb_gemm_bf16": [vp, vp, vp, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64, i64, vp],
+        "nkb_linear_attention_noalloc": [vp, vp, vp, vp, i64, i64, i64, i64, vp],
     }
     for name, args in sig.items():
         fn = getattr(lib, name)

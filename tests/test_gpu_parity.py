@@ -186,7 +186,7 @@ def test_swiglu_ffn(tokens, hidden, ffn):
     assert_close(got, want, BF16_RTOL)
 
 
-@pytest.mark.parametrize("shape", [(1, 2, 256, 32), (2, 3, 512, 128)])
+@pytest.mark.parametrize("shape", [(1, 2, 256, 32), (2, 3, 512, 128), (1, 2, 3072, 128), (1, 1, 2560, 128)])
 def test_chunked_linear_attention(shape):
     rng = np.random.default_rng(15)
     q, k, v = (rng.standard_normal(shape, dtype=np.float32).astype(BF16) for _ in range(3))
