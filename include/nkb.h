@@ -166,8 +166,9 @@ NKB_API int nkb_gemm_bf16(const void *A, const void *B, void *C, int c_dtype, in
  * NKB_LINATTN_SCRATCH_BYTES inside libnkb, held by every GPU that loads the
  * library until the process exits.  The workspace is B * H * ceil(T / 1024)
  * * 66,048 bytes (one fp32 128 x 128 state and key sum per 1024-token
- * segment; none for T <= 1024); sizes whose workspace would exceed the array
- * are rejected with NKB_ERR_INVALID.  The function itself calls no cudaMalloc,
+ * segment) when B * H < 96 and T > 1024, and none otherwise (each head is
+ * then one segment); sizes whose workspace would exceed the array are
+ * rejected with NKB_ERR_INVALID.  The function itself calls no cudaMalloc,
  * cudaFree or allocating library routine; its first call on a device looks up
  * the array's device address (cudaGetSymbolAddress), so make that first call
  * before any stream capture.  All calls share the one array: calls that

@@ -184,12 +184,17 @@ extern "C" int nkb_version(int *major, int *minor) {
 
 namespace nkb {
 int gemm_read_and_clear_error(int *flag);
+int linattn_read_and_clear_error(int *flag);
 }
 
 extern "C" int nkb_device_error(int *flag) {
   if (int s = ensure_init()) return s;
   if (!flag) return fail(NKB_ERR_INVALID, "flag is NULL");
-  return nkb::gemm_read_and_clear_error(flag);
+  int g = 0, l = 0;
+  if (int s = nkb::gemm_read_and_clear_error(&g)) return s;
+  if (int s = nkb::linattn_read_and_clear_error(&l)) return s;
+  *flag = g | l;
+  return NKB_OK;
 }
 
 extern "C" int nkb_synchronize(void) {

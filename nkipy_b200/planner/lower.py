@@ -43,6 +43,16 @@ def _nbytes(shape, dtype) -> int:
     return n * np.dtype(dtype).itemsize
 
 
+def linattn_segments(heads, T):
+    """Segments per (batch, head) of the linear-attention kernel: one, unless the
+    heads alone cannot fill the GPU (fewer than 96) and the sequence is longer
+    than one segment of 8 blocks of 128 tokens.  Mirrors the kernel's rule."""
+    blocks = -(-T // 128)
+    if blocks <= 8 or heads >= 96:
+        return 1
+    return -(-blocks // 8)
+
+
 class Lowering:
     def __init__(self, graph, world: int = 1):
         self.g = graph
@@ -293,9 +303,7 @@ class Lowering:
                 v = self.materialize(v, dense=True)
             views.append(v)
         out = self.tmp_view((B, H, T, D), BF16)
-        # segments of 16 chunks (1024 tokens) per (batch, head); one fp32 state each
-        chunks = T // 64
-        G = 1 if chunks <= 16 else -(-chunks // 16)
+        G = linattn_segments(B * H, T)
         ws = self.new_buf("tmp", -1, max(1, B * H * G * (D * D + D) * 4) if G > 1 else 256)
         ints = [B, H, T, D, G]
         for v in views:

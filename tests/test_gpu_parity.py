@@ -186,7 +186,14 @@ def test_swiglu_ffn(tokens, hidden, ffn):
     assert_close(got, want, BF16_RTOL)
 
 
-@pytest.mark.parametrize("shape", [(1, 2, 256, 32), (2, 3, 512, 128), (1, 2, 3072, 128), (1, 1, 2560, 128)])
+# head_dim 32 takes the generic lowering; the others the tensor-core kernel:
+# one segment, a 64-token tail block, a single partial block, several segments
+# (with a tail segment of one partial block), and 96 heads (one segment each).
+@pytest.mark.parametrize(
+    "shape",
+    [(1, 2, 256, 32), (2, 3, 512, 128), (1, 2, 320, 128), (1, 1, 64, 128), (1, 2, 3072, 128),
+     (1, 1, 2560, 128), (1, 1, 1088, 128), (2, 48, 256, 128)],
+)
 def test_chunked_linear_attention(shape):
     rng = np.random.default_rng(15)
     q, k, v = (rng.standard_normal(shape, dtype=np.float32).astype(BF16) for _ in range(3))

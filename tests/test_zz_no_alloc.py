@@ -60,9 +60,9 @@ def test_noalloc_rejects_oversized_workspace():
 
     lib = _nkb.lib()
     get_spike_singleton()
-    # 8 x 16 heads of 16384 tokens need 16 segment states each (135 MB), more
+    # 4 heads of 262144 tokens need 256 segment states each (67.6 MB), more
     # than the fixed array; the size check happens before any memory is touched.
     fake = ctypes.c_void_p(256)
-    st = lib.nkb_linear_attention_noalloc(fake, fake, fake, fake, 8, 16, 16384, 128, None)
+    st = lib.nkb_linear_attention_noalloc(fake, fake, fake, fake, 1, 4, 262144, 128, None)
     assert st == 1 and b"workspace" in lib.nkb_last_error()
     torch.cuda.synchronize()
