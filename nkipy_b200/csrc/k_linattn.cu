@@ -365,39 +365,49 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_before();
           mbar_arrive(sa_ready);
         }
-        // output rows 64*team .. 64*team+63 of this block, 32 tokens per TMA store
+        // output rows 64*team .. 64*team+63 of this block: O^T and the
+        // denominators are read into registers first, so the accumulator is
+        // released before the (slower) staging and TMA stores
         if (!team_and(bar_id, wait_warp(o_full, c & 1, abort_flag) && wait_warp(p_ready, c & 1, abort_flag))) break;
         tc_fence_after();
         const int t0 = (blk0 + c) * TB;
-#pragma unroll 1
-        for (int g = team * 2; g < team * 2 + 2; ++g) {
+        // tokens j and j+4 in one step: the even lane of a pair keeps token j,
+        // the odd lane token j+4, each as the two adjacent columns dcol, dcol+1
+        uint32_t w[2][16];
+#pragma unroll
+        for (int gi = 0; gi < 2; ++gi) {
+          const int g = team * 2 + gi;
           uint32_t r[32];
           tmem_ld32(lane_base + T_OT + g * 32, r);
-          if (leader) bulk_wait_read<0>();  // the previous store has read the staging buffer
-          team_sync(bar_id);
-          // tokens j and j+4 in one step: the even lane of a pair stores token j,
-          // the odd lane token j+4, each as the two adjacent columns dcol, dcol+1
 #pragma unroll
           for (int jj = 0; jj < 16; ++jj) {
             const int j = (jj & 3) + (jj >> 2) * 8;
-            const int t = g * 32 + j;
-            const float a = __uint_as_float(r[j]) * sInv[t];
-            const float a4 = __uint_as_float(r[j + 4]) * sInv[t + 4];
+            const float a = __uint_as_float(r[j]) * sInv[g * 32 + j];
+            const float a4 = __uint_as_float(r[j + 4]) * sInv[g * 32 + j + 4];
             const float recv = __shfl_xor_sync(0xffffffffu, odd ? a : a4, 1);
-            const int tl = odd ? j + 4 : j;
-            const uint32_t w = odd ? pack_bf16(recv, a4) : pack_bf16(a, recv);
-            *reinterpret_cast<uint32_t *>(stg + swz_off(tl, dcol, 32)) = w;
-          }
-          fence_proxy_async_smem();
-          team_sync(bar_id);
-          if (leader) {
-            tma_store_4d(&mo, stg, 0, t0 + g * 32, h, b);
-            tma_store_4d(&mo, stg + OBOX, 64, t0 + g * 32, h, b);
-            bulk_commit();
+            w[gi][jj] = odd ? pack_bf16(recv, a4) : pack_bf16(a, recv);
           }
         }
         tc_fence_before();
         mbar_arrive(o_free);
+#pragma unroll
+        for (int gi = 0; gi < 2; ++gi) {
+          if (leader) bulk_wait_read<0>();  // the previous store has read the staging buffer
+          team_sync(bar_id);
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = (jj & 3) + (jj >> 2) * 8;
+            *reinterpret_cast<uint32_t *>(stg + swz_off(odd ? j + 4 : j, dcol, 32)) = w[gi][jj];
+          }
+          fence_proxy_async_smem();
+          team_sync(bar_id);
+          if (leader) {
+            const int tok = t0 + (team * 2 + gi) * 32;
+            tma_store_4d(&mo, stg, 0, tok, h, b);
+            tma_store_4d(&mo, stg + OBOX, 64, tok, h, b);
+            bulk_commit();
+          }
+        }
       }
       if (leader) bulk_wait<0>();
     } else if (wait_warp(s_full, 0, abort_flag)) {
