@@ -123,6 +123,20 @@ NKB_API int nkb_comm_init(const void *id, int rank, int world, int device, nkb_c
 NKB_API int nkb_comm_free(nkb_comm comm);
 NKB_API int nkb_plan_bind_comm(nkb_plan plan, nkb_comm comm);
 NKB_API int nkb_comm_all_reduce(nkb_comm comm, nkb_buf buf, size_t count, int dtype, void *stream);
+/* Binds a symmetric region to the communicator: `bytes` at `local` on this
+ * rank, the same region through an NVLink multicast object at `multicast`,
+ * and every rank's region as mapped in this process (`peers`, one per rank).
+ * Afterwards bf16/fp32 sum all-reduces whose slices are whole 16-byte
+ * vectors and that fit the region run as one kernel reducing inside NVSwitch
+ * (multimem); the others keep using NCCL.  The last nkb_comm_symm_flag_bytes()
+ * bytes of the region hold barrier flags: this call zeroes this rank's, and
+ * the caller synchronises the ranks before the next all-reduce.  No
+ * counterpart in the reference, whose collectives run inside NRT; the
+ * allocation itself is the caller's (PyTorch symmetric memory in the Python
+ * layer). */
+NKB_API int nkb_comm_bind_symm(nkb_comm comm, void *local, void *multicast, void *const *peers, int n_peers,
+                               size_t bytes);
+NKB_API size_t nkb_comm_symm_flag_bytes(void);
 
 /* dtype codes used by plans and nkb_comm_all_reduce */
 enum nkb_dtype {

@@ -126,5 +126,8 @@ int num_sms(int device);
 
 // NCCL all-reduce entry (implemented in the runtime, which owns the dlopen).
 int comm_all_reduce(void *comm, const void *src, void *dst, size_t count, int dtype, cudaStream_t stream);
+// dst = res + all-reduce(buf) (buf keeps the sum)
+int comm_all_reduce_add(void *comm, void *buf, const void *res, void *dst, size_t count, int dtype,
+                        cudaStream_t stream);
 
 }  // namespace nkb

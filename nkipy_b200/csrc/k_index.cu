@@ -9,7 +9,9 @@
 //  scatter     HLO scatter with update_computation "assign" of whole windows
 //              along one axis (indexing.py:360-433) or of points
 //              (indexing.py:771-862);
-//  allreduce   HLO all-reduce (collectives.py:87-110) -> ncclAllReduce sum.
+//  allreduce   HLO all-reduce (collectives.py:87-110), sum: inside NVSwitch when the
+//              payload sits in the communicator's symmetric region, else NCCL;
+//  allreduce_add  the same followed by the residual add of a row-parallel block.
 // Indices are clamped into range like XLA gather/scatter start indices, so no
 // index value can address memory outside the operand.
 
@@ -249,6 +251,17 @@ int ar_launch(const LaunchArgs &a) {
   return comm_all_reduce(a.comm, a.ptrs[0], a.ptrs[1], (size_t)a.step->ints[0], (int)a.step->ints[1], a.stream);
 }
 
+// "allreduce_add": ptrs buf res dst; ints count dtype -- dst = res + all-reduce(buf), buf keeps the sum
+int ara_check(const Step &s) {
+  if (s.buf_ids.size() != 3 || s.ints.size() != 2) return fail(NKB_ERR_PLAN, "allreduce_add: bad parameters");
+  if (s.ints[1] != NKB_BF16 && s.ints[1] != NKB_F32) return fail(NKB_ERR_UNSUPPORTED, "allreduce_add: bf16 or fp32");
+  return NKB_OK;
+}
+int ara_launch(const LaunchArgs &a) {
+  return comm_all_reduce_add(a.comm, a.ptrs[0], a.ptrs[1], a.ptrs[2], (size_t)a.step->ints[0], (int)a.step->ints[1],
+                             a.stream);
+}
+
 }  // namespace idx
 
 NKB_REGISTER_KERNEL("take", idx::take_launch, idx::take_check);
@@ -258,5 +271,6 @@ NKB_REGISTER_KERNEL("scatter_rows", idx::srows_launch, idx::srows_check);
 NKB_REGISTER_KERNEL("scatter_pts", idx::spts_launch, idx::spts_check);
 NKB_REGISTER_KERNEL("copy_bytes", idx::copy_launch, idx::copy_check);
 NKB_REGISTER_KERNEL("allreduce", idx::ar_launch, idx::ar_check);
+NKB_REGISTER_KERNEL("allreduce_add", idx::ara_launch, idx::ara_check);
 
 }  // namespace nkb

@@ -185,15 +185,17 @@ extern "C" int nkb_version(int *major, int *minor) {
 namespace nkb {
 int gemm_read_and_clear_error(int *flag);
 int linattn_read_and_clear_error(int *flag);
+int nvls_read_and_clear_error(int *flag);
 }
 
 extern "C" int nkb_device_error(int *flag) {
   if (int s = ensure_init()) return s;
   if (!flag) return fail(NKB_ERR_INVALID, "flag is NULL");
-  int g = 0, l = 0;
+  int g = 0, l = 0, n = 0;
   if (int s = nkb::gemm_read_and_clear_error(&g)) return s;
   if (int s = nkb::linattn_read_and_clear_error(&l)) return s;
-  *flag = g | l;
+  if (int s = nkb::nvls_read_and_clear_error(&n)) return s;
+  *flag = g | l | n;
   return NKB_OK;
 }
 
@@ -382,9 +384,27 @@ int nccl_dtype(int dt) {
 
 }  // namespace
 
+namespace nkb {
+size_t nvls_flag_bytes();
+bool nvls_eligible(size_t count, int dtype, int world);
+int nvls_all_reduce(void *buf, void *mc_buf, const void *res, void *dst, size_t count, int dtype, uint32_t *flags,
+                    uint32_t *const *peer_flags, uint32_t *epochs, int rank, int world, int device,
+                    cudaStream_t stream);
+int add_elementwise(const void *a, const void *b, void *out, size_t count, int dtype, cudaStream_t stream);
+}  // namespace nkb
+
 struct nkb_comm_s {
   ncclComm_t_ comm;
   int rank, world, device;
+  // symmetric region bound with nkb_comm_bind_symm (NVLS all-reduce); unset -> NCCL
+  void *symm_local = nullptr, *symm_mc = nullptr;
+  size_t symm_data = 0;                 // bytes of the data area (the flags follow it)
+  uint32_t **symm_peer_flags = nullptr;  // device array [world]
+  uint32_t *symm_epochs = nullptr;       // device array, per-CTA launch counters
+  ~nkb_comm_s() {
+    if (symm_peer_flags) cudaFree(symm_peer_flags);
+    if (symm_epochs) cudaFree(symm_epochs);
+  }
 };
 
 extern "C" int nkb_comm_unique_id(void *id_out) {
@@ -411,6 +431,40 @@ extern "C" int nkb_comm_init(const void *id, int rank, int world, int device, nk
   return NKB_OK;
 }
 
+extern "C" int nkb_comm_bind_symm(nkb_comm comm, void *local, void *multicast, void *const *peers, int n_peers,
+                                  size_t bytes) {
+  if (int s = ensure_init()) return s;
+  if (!comm || !local || !multicast || !peers) return fail(NKB_ERR_INVALID, "NULL argument");
+  if (n_peers != comm->world) return fail(NKB_ERR_INVALID, "one peer pointer per rank is needed");
+  if (comm->world > 16) return fail(NKB_ERR_UNSUPPORTED, "symmetric all-reduce supports at most 16 ranks");
+  const size_t fb = nkb::nvls_flag_bytes();
+  if (bytes <= fb + 16) return fail(NKB_ERR_INVALID, "symmetric region too small");
+  if ((reinterpret_cast<uintptr_t>(local) | reinterpret_cast<uintptr_t>(multicast) | bytes) & 15)
+    return fail(NKB_ERR_INVALID, "symmetric region must be 16-byte aligned");
+  const size_t data = (bytes - fb) & ~size_t(15);
+  NKB_CUDA_TRY(cudaSetDevice(comm->device));
+  std::vector<uint32_t *> pf(comm->world);
+  for (int r = 0; r < comm->world; ++r) {
+    if (!peers[r]) return fail(NKB_ERR_INVALID, "NULL peer pointer");
+    pf[r] = reinterpret_cast<uint32_t *>(static_cast<char *>(peers[r]) + data);
+  }
+  if (!comm->symm_peer_flags) NKB_CUDA_TRY(cudaMalloc(&comm->symm_peer_flags, 16 * sizeof(uint32_t *)));
+  if (!comm->symm_epochs) {
+    NKB_CUDA_TRY(cudaMalloc(&comm->symm_epochs, 1024 * sizeof(uint32_t)));
+    NKB_CUDA_TRY(cudaMemset(comm->symm_epochs, 0, 1024 * sizeof(uint32_t)));
+  }
+  NKB_CUDA_TRY(cudaMemcpy(comm->symm_peer_flags, pf.data(), pf.size() * sizeof(uint32_t *), cudaMemcpyHostToDevice));
+  // this rank's flags start at zero; the caller synchronises the ranks before the first all-reduce
+  NKB_CUDA_TRY(cudaMemset(static_cast<char *>(local) + data, 0, fb));
+  NKB_CUDA_TRY(cudaDeviceSynchronize());
+  comm->symm_local = local;
+  comm->symm_mc = multicast;
+  comm->symm_data = data;
+  return NKB_OK;
+}
+
+extern "C" size_t nkb_comm_symm_flag_bytes(void) { return nkb::nvls_flag_bytes(); }
+
 extern "C" int nkb_comm_free(nkb_comm comm) {
   if (!comm) return NKB_OK;
   if (g_nccl.loaded && comm->comm) g_nccl.CommDestroy(comm->comm);
@@ -419,6 +473,22 @@ extern "C" int nkb_comm_free(nkb_comm comm) {
 }
 
 namespace nkb {
+// The payload lies inside the bound symmetric data area and can be reduced
+// there inside NVSwitch.
+static bool symm_payload(const nkb_comm_s *c, const void *p, size_t count, int dtype) {
+  if (!c->symm_local || !nvls_eligible(count, dtype, c->world)) return false;
+  const char *lo = static_cast<const char *>(c->symm_local), *q = static_cast<const char *>(p);
+  const size_t bytes = count * dtype_size(dtype);
+  return q >= lo && q + bytes <= lo + c->symm_data && ((q - lo) & 15) == 0;
+}
+
+static int nvls_on(nkb_comm_s *c, void *buf, const void *res, void *dst, size_t count, int dtype, cudaStream_t stream) {
+  const size_t off = static_cast<char *>(buf) - static_cast<char *>(c->symm_local);
+  return nvls_all_reduce(buf, static_cast<char *>(c->symm_mc) + off, res, dst, count, dtype,
+                         reinterpret_cast<uint32_t *>(static_cast<char *>(c->symm_local) + c->symm_data),
+                         c->symm_peer_flags, c->symm_epochs, c->rank, c->world, c->device, stream);
+}
+
 int comm_all_reduce(void *comm, const void *src, void *dst, size_t count, int dtype, cudaStream_t stream) {
   auto *c = static_cast<nkb_comm_s *>(comm);
   if (!c) return fail(NKB_ERR_STATE, "all-reduce step but no communicator is bound to the plan");
@@ -428,9 +498,20 @@ int comm_all_reduce(void *comm, const void *src, void *dst, size_t count, int dt
     if (src != dst) NKB_CUDA_TRY(cudaMemcpyAsync(dst, src, count * dtype_size(dtype), cudaMemcpyDeviceToDevice, stream));
     return NKB_OK;
   }
+  if (src == dst && symm_payload(c, dst, count, dtype)) return nvls_on(c, dst, nullptr, nullptr, count, dtype, stream);
   int r = g_nccl.AllReduce(src, dst, count, nd, /*ncclSum*/ 0, c->comm, stream);
   if (r) return fail(NKB_ERR_NCCL, std::string("ncclAllReduce: ") + g_nccl.GetErrorString(r));
   return NKB_OK;
+}
+
+// dst = res + (sum over the ranks of buf); buf holds the sum afterwards
+int comm_all_reduce_add(void *comm, void *buf, const void *res, void *dst, size_t count, int dtype,
+                        cudaStream_t stream) {
+  auto *c = static_cast<nkb_comm_s *>(comm);
+  if (!c) return fail(NKB_ERR_STATE, "all-reduce step but no communicator is bound to the plan");
+  if (c->world > 1 && symm_payload(c, buf, count, dtype)) return nvls_on(c, buf, res, dst, count, dtype, stream);
+  if (int s = comm_all_reduce(comm, buf, buf, count, dtype, stream)) return s;
+  return add_elementwise(res, buf, dst, count, dtype, stream);
 }
 }  // namespace nkb
 
@@ -447,12 +528,12 @@ extern "C" int nkb_comm_all_reduce(nkb_comm comm, nkb_buf buf, size_t count, int
 // ---------------------------------------------------------------------------
 namespace {
 
-enum BufKind { BK_IN = 0, BK_OUT = 1, BK_CONST = 2, BK_TMP = 3 };
+enum BufKind { BK_IN = 0, BK_OUT = 1, BK_CONST = 2, BK_TMP = 3, BK_SYMM = 4 };
 
 struct PlanBuffer {
   BufKind kind;
   int index;        // io / const index
-  size_t offset;    // arena offset (tmp)
+  size_t offset;    // arena offset (tmp) or offset in the symmetric region (symm)
   size_t bytes;
 };
 
@@ -465,6 +546,8 @@ struct nkb_plan_s {
   std::vector<void *> const_ptrs;
   size_t scratch = 0;
   void *arena = nullptr;
+  size_t symm = 0;                // bytes of the symmetric region the plan's symm buffers need
+  void *symm_fallback = nullptr;  // used for them while no large-enough region is bound
   std::vector<PlanBuffer> buffers;
   std::vector<nkb::Step> steps;
   std::vector<const nkb::KernelEntry *> entries;
@@ -478,6 +561,7 @@ struct nkb_plan_s {
     for (void *p : const_ptrs)
       if (p) cudaFree(p);
     if (arena) cudaFree(arena);
+    if (symm_fallback) cudaFree(symm_fallback);
   }
 };
 
@@ -515,6 +599,8 @@ int parse_plan(const std::string &text, nkb_plan_s *p) {
       p->const_bytes.assign(n, 0);
     } else if (tok == "scratch") {
       in >> p->scratch;
+    } else if (tok == "symm") {
+      in >> p->symm;
     } else if (tok == "buffers") {
       size_t n;
       in >> n;
@@ -535,6 +621,10 @@ int parse_plan(const std::string &text, nkb_plan_s *p) {
         b.kind = BK_TMP;
         in >> b.offset >> b.bytes;
         if (b.offset + b.bytes > p->scratch) return fail(NKB_ERR_PLAN, "tmp buffer exceeds scratch arena");
+      } else if (kind == "symm") {
+        b.kind = BK_SYMM;
+        in >> b.offset >> b.bytes;
+        if (b.offset + b.bytes > p->symm) return fail(NKB_ERR_PLAN, "symm buffer exceeds the plan's symmetric region");
       } else {
         return fail(NKB_ERR_PLAN, "unknown buffer kind " + kind);
       }
@@ -693,6 +783,25 @@ int resolve_io(nkb_plan plan, const nkb_buf *ins, int n_in, const nkb_buf *outs,
       case BK_OUT: h = outs[b.index]; break;
       case BK_CONST: base[i] = plan->const_ptrs[b.index]; continue;
       case BK_TMP: base[i] = static_cast<char *>(plan->arena) + b.offset; continue;
+      case BK_SYMM: {
+        // the communicator's symmetric region when one large enough is bound
+        // (all-reduces then run inside NVSwitch), else a region of the plan's own
+        nkb_comm c = plan->comm;
+        if (c && c->symm_local && plan->symm <= c->symm_data) {
+          base[i] = static_cast<char *>(c->symm_local) + b.offset;
+        } else {
+          if (!plan->symm_fallback) {
+            cudaError_t e = cudaMalloc(&plan->symm_fallback, plan->symm);
+            if (e != cudaSuccess) {
+              cudaGetLastError();
+              plan->symm_fallback = nullptr;
+              return fail(NKB_ERR_CUDA, std::string("symm buffer cudaMalloc: ") + cudaGetErrorString(e));
+            }
+          }
+          base[i] = static_cast<char *>(plan->symm_fallback) + b.offset;
+        }
+        continue;
+      }
     }
     if (!buf_ok(h)) return fail(NKB_ERR_STATE, "plan io buffer " + std::to_string(i) + " is invalid or freed");
     if (h->bytes < b.bytes)

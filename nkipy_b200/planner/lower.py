@@ -31,7 +31,7 @@ import numpy as np
 from nkipy_b200.planner import ewprog as E
 from nkipy_b200.planner import views as V
 from nkipy_b200.planner.patterns import find_claims, tkey
-from nkipy_b200.planner.plan import BufDecl, IoSpec, Plan, StepRec, pack_arena
+from nkipy_b200.planner.plan import BufDecl, IoSpec, Plan, StepRec, pack_arena, pack_symmetric
 
 Value = Union[V.View, E.Expr]
 
@@ -67,7 +67,12 @@ class Lowering:
                 self.uses[tkey(t)] = self.uses.get(tkey(t), 0) + 1
         for r in graph.results:
             self.uses[tkey(r)] = self.uses.get(tkey(r), 0) + 1
+        self.consumers: Dict[tuple, list] = {}
+        for op in graph.operations:
+            for t in op.operands:
+                self.consumers.setdefault(tkey(t), []).append(op)
         self.claims, self.claimed = find_claims(graph)
+        self.fused = set()  # ids of ops already lowered as part of an earlier step
         self.needs_comm = False
 
     # ------------------------------------------------------------ buffers
@@ -145,6 +150,8 @@ class Lowering:
             b = self.new_buf("in", p.parameter_id, max(1, spec.nbytes))
             self.vals[("p", p.parameter_id)] = V.View(b, 0, tuple(p.shape), V.dense_strides(p.shape), np.dtype(p.dtype))
         for op in g.operations:
+            if op.id in self.fused:
+                continue
             if id(op) in self.claimed and op.id not in self.claims:
                 continue
             if op.id in self.claims:
@@ -165,8 +172,10 @@ class Lowering:
             self.bind_output(i, r, spec)
         lifetimes = self.lifetimes()
         scratch = pack_arena(self.buffers, lifetimes)
+        symm = pack_symmetric(self.buffers)
         aliases = [(a.output_index, a.param_index) for a in g.aliases]
-        return Plan(name, inputs, outputs, self.consts, self.buffers, self.steps, scratch, aliases, self.needs_comm)
+        return Plan(name, inputs, outputs, self.consts, self.buffers, self.steps, scratch, aliases, self.needs_comm,
+                    symm)
 
     def bind_output(self, i, r, spec):
         val = self.vals[tkey(r)]
@@ -696,6 +705,15 @@ class Lowering:
         self.vals[("o", op.id)] = out
 
     def op_all_reduce(self, op):
+        """Sum over the ranks, in place in symmetric memory.
+
+        The partial sum is produced straight into a "symm" buffer (one region
+        that every rank maps, bound to the communicator when the plan is
+        loaded), where the runtime reduces it inside NVSwitch, or with NCCL
+        when no such region is bound.  An add of the reduced value to one
+        other tensor of its shape (the residual after a row-parallel block) is
+        folded into the same step.
+        """
         x = op.operands[0]
         if op.attributes.get("reduce_op", "add") != "add":
             raise NotImplementedError("all-reduce other than sum")
@@ -708,10 +726,50 @@ class Lowering:
             self.put(op, self.get(x))
             return
         xv = self.materialize(self.get(x), dense=True)
-        out = self.tmp_view(op.result_shape, op.result_dtype)
-        self.step("allreduce", [self.bref(xv), self.bref(out)], [xv.size, E.dt_code(xv.dtype)], note=f"nccl {xv.size}")
+        esize = np.dtype(xv.dtype).itemsize
+        b = self.buffers[xv.buf]
+        if (b.kind == "tmp" and xv.offset == 0 and b.nbytes == xv.size * esize
+                and self.uses.get(tkey(x), 0) == 1 and tkey(x) not in self.result_keys):
+            b.kind = "symm"  # the producer writes into the symmetric region
+        else:
+            sb = self.new_buf("symm", -1, max(1, xv.size * esize))
+            sv = V.View(sb, 0, tuple(op.result_shape), V.dense_strides(op.result_shape), np.dtype(xv.dtype))
+            self.emit_ew(self.expr_of(xv), sv)
+            xv = sv
+        dt = E.dt_code(xv.dtype)
         self.needs_comm = True
-        self.vals[("o", op.id)] = out
+        add = self._residual_add(op)
+        if add is not None:
+            add_op, other = add
+            rv = self.materialize(self.get(other), dense=True)
+            out = self.tmp_view(add_op.result_shape, add_op.result_dtype)
+            self.step("allreduce_add", [self.bref(xv), self.bref(rv), self.bref(out)], [xv.size, dt],
+                      note=f"{xv.size} + residual")
+            self.vals[("o", add_op.id)] = out
+            self.fused.add(add_op.id)
+            return
+        self.step("allreduce", [self.bref(xv), self.bref(xv)], [xv.size, dt], note=f"{xv.size} in place")
+        self.vals[("o", op.id)] = xv
+
+    def _residual_add(self, op):
+        """(add op, other operand) when the all-reduce result's only use is an
+        unclaimed add with a same-shape, same-dtype tensor; else None."""
+        key = ("o", op.id)
+        users = self.consumers.get(key, [])
+        if self.uses.get(key, 0) != 1 or len(users) != 1 or key in self.result_keys:
+            return None
+        u = users[0]
+        if u.op_name != "add" or id(u) in self.claimed or u.id in self.claims or len(u.operands) != 2:
+            return None
+        a, c = u.operands
+        other = c if tkey(a) == key else a
+        if tkey(other) == key or tuple(other.shape) != tuple(op.result_shape):
+            return None
+        if np.dtype(other.dtype) != np.dtype(op.result_dtype) or np.dtype(u.result_dtype) != np.dtype(op.result_dtype):
+            return None
+        if np.dtype(op.result_dtype) not in (np.dtype(np.float32), BF16):
+            return None
+        return u, other
 
 
 def lower(graph, name=None, world: int = 1) -> Plan:

@@ -18,10 +18,10 @@ ALIGN = 256
 
 @dataclass
 class BufDecl:
-    kind: str  # "in" | "out" | "const" | "tmp"
-    index: int  # io / const index (tmp: -1)
+    kind: str  # "in" | "out" | "const" | "tmp" | "symm"
+    index: int  # io / const index (tmp, symm: -1)
     nbytes: int
-    offset: int = 0  # arena offset for tmp
+    offset: int = 0  # arena offset (tmp) or offset in the symmetric region (symm)
 
 
 @dataclass
@@ -55,6 +55,7 @@ class Plan:
     scratch: int = 0
     aliases: list = field(default_factory=list)  # (output index, input index)
     needs_comm: bool = False
+    symm: int = 0  # bytes of the symmetric region the "symm" buffers need
 
     def to_text(self) -> str:
         lines = ["NKBPLAN 1", f"name {self.name or 'kernel'}"]
@@ -68,10 +69,12 @@ class Plan:
         for i, c in enumerate(self.consts):
             lines.append(f"const {i} {c.nbytes}")
         lines.append(f"scratch {self.scratch}")
+        if self.symm:
+            lines.append(f"symm {self.symm}")
         lines.append(f"buffers {len(self.buffers)}")
         for i, b in enumerate(self.buffers):
-            if b.kind == "tmp":
-                lines.append(f"buffer {i} tmp {b.offset} {b.nbytes}")
+            if b.kind in ("tmp", "symm"):
+                lines.append(f"buffer {i} {b.kind} {b.offset} {b.nbytes}")
             else:
                 lines.append(f"buffer {i} {b.kind} {b.index}")
         lines.append(f"steps {len(self.steps)}")
@@ -104,6 +107,20 @@ class Plan:
         for s in self.steps:
             rows.append(f"  {s.kernel:<14} {s.note}")
         return "\n".join(rows)
+
+
+SYMM_ALIGN = 4096
+
+
+def pack_symmetric(buffers: List[BufDecl]) -> int:
+    """Give every "symm" buffer its own offset in the symmetric region (they are
+    few and large: the operands of all-reduces); returns the region size."""
+    top = 0
+    for b in buffers:
+        if b.kind == "symm":
+            b.offset = top
+            top += (b.nbytes + SYMM_ALIGN - 1) // SYMM_ALIGN * SYMM_ALIGN
+    return top
 
 
 def pack_arena(buffers: List[BufDecl], lifetimes) -> int:

@@ -87,6 +87,7 @@ def _declare(lib):
         "nkb_comm_free": [c_comm],
         "nkb_plan_bind_comm": [c_plan, c_comm],
         "nkb_comm_all_reduce": [c_comm, c_buf, sz, i32, vp],
+        "nkb_comm_bind_symm": [c_comm, vp, vp, pp, i32, sz],
         "nkb_softmax_rows": [vp, i32, vp, i32, i64, i64, vp],
         "nkb_rmsnorm_rows": [vp, vp, vp, vp, vp, i32, i32, i64, i64, ctypes.c_float, vp],
         "nkb_gemm_bf16": [vp, vp, vp, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64, i64, vp],
@@ -100,7 +101,9 @@ def _declare(lib):
     lib.nkb_last_error.restype = ctypes.c_char_p
     lib.nkb_status_str.argtypes = [ctypes.c_int]
     lib.nkb_status_str.restype = ctypes.c_char_p
-    return sorted(sig) + ["nkb_last_error", "nkb_status_str"]
+    lib.nkb_comm_symm_flag_bytes.argtypes = []
+    lib.nkb_comm_symm_flag_bytes.restype = ctypes.c_size_t
+    return sorted(sig) + ["nkb_last_error", "nkb_status_str", "nkb_comm_symm_flag_bytes"]
 
 
 EXPORTED = None

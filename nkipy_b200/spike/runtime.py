@@ -87,6 +87,7 @@ class NkbModel:
         self.rank_id = rank_id
         self.world_size = world_size
         self.comm = comm
+        self.symmetric = False  # all-reduces run inside NVSwitch (bound symmetric region)
         n = ctypes.c_int()
         _nkb.call("nkb_plan_num_launches", handle, ctypes.byref(n))
         self.num_launches = n.value
@@ -133,6 +134,60 @@ def _communicator(rank: int, world: int, device: int):
     _nkb.call("nkb_comm_init", ctypes.cast(buf, ctypes.c_void_p), rank, world, device, ctypes.byref(comm))
     _COMMS[key] = comm
     return comm
+
+
+_SYMM: Dict[tuple, list] = {}  # (world, rank) -> [capacity bytes, tensors kept alive]
+
+
+def _symm_bytes(plan_text: str) -> int:
+    """Bytes of the symmetric region a plan's all-reduce operands need (its "symm" line)."""
+    for line in plan_text.splitlines():
+        if line.startswith("symm "):
+            return int(line.split()[1])
+        if line.startswith("steps "):
+            break
+    return 0
+
+
+def _bind_symmetric(comm, rank: int, world: int, device: int, need: int) -> bool:
+    """Give the communicator a symmetric region for all-reduces inside NVSwitch.
+
+    The region is a PyTorch symmetric-memory allocation (every rank maps every
+    other rank's copy, plus an NVLink multicast object over all of them); all
+    ranks take the same decision, and a rank without multicast support makes
+    every rank keep NCCL.  NKB_SYMM: "auto" (default) binds it from 4 ranks up,
+    where reducing inside NVSwitch beats NCCL's ring on B200 (at 2 ranks NCCL
+    is faster); "force" binds it at any size; "0" never.  Regions are never
+    freed: plans captured into CUDA graphs keep their addresses.
+    """
+    mode = os.environ.get("NKB_SYMM", "auto")
+    if need <= 0 or mode == "0" or (mode == "auto" and world < 4):
+        return False
+    entry = _SYMM.get((world, rank))
+    if entry is not None and entry[0] >= need:
+        return True
+    import torch
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm_mem
+
+    flag = int(_nkb.lib().nkb_comm_symm_flag_bytes())
+    cap = max(need, 64 << 20)
+    nbytes = cap + flag
+    t = symm_mem.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", device))
+    h = symm_mem.rendezvous(t, dist.group.WORLD)
+    peers = [int(x) for x in h.buffer_ptrs]
+    ok = int(h.multicast_ptr) != 0 and len(peers) == world and peers[rank] == t.data_ptr()
+    votes = [None] * world
+    dist.all_gather_object(votes, bool(ok))
+    if not all(votes):
+        return False
+    arr = (ctypes.c_void_p * world)(*peers)
+    _nkb.call("nkb_comm_bind_symm", comm, t.data_ptr(), int(h.multicast_ptr), arr, world, nbytes)
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    kept = (entry[1] if entry else []) + [t, h]
+    _SYMM[(world, rank)] = [cap, kept]
+    return True
 
 
 class Spike:
@@ -249,6 +304,7 @@ class Spike:
         if cc_enabled and world_size > 1:
             model.comm = _communicator(rank_id, world_size, core_id)
             _nkb.call("nkb_plan_bind_comm", h, model.comm)
+            model.symmetric = _bind_symmetric(model.comm, rank_id, world_size, core_id, _symm_bytes(text))
         elif io.get("needs_comm"):
             raise ValueError("this plan contains collectives: load it with cc_enabled=True, rank_id and world_size")
         return model

@@ -1,4 +1,4 @@
-"""Tensor-parallel decoder layer on 2 GPUs (NCCL all-reduce inside the plan)."""
+"""Tensor-parallel decoder layer on 2 GPUs, all-reduce inside NVSwitch (own kernel) and through NCCL."""
 
 import os
 import subprocess
@@ -21,8 +21,9 @@ def _gpus():
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
-def test_tp2_layer_parity():
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+@pytest.mark.parametrize("symm", ["force", "0"], ids=["nvswitch", "nccl"])
+def test_tp2_layer_parity(symm):
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", NKB_SYMM=symm)
     cmd = [
         "timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
         "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533",

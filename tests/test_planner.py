@@ -141,4 +141,13 @@ def test_layer_tp2_has_two_allreduces():
     shard = W.shard_layer_weights(full, s, 1, 2)
     args, kw = W.layer_args(np.zeros((1, 64, 256), BF16), shard, s, 2)
     p = lower(NKIPyKernel.trace(W.llama_decoder_layer_kernel).specialize(*args, **kw), world=2)
-    assert p.kernel_counts()["allreduce"] == 2 and p.needs_comm
+    kc = p.kernel_counts()
+    # one all-reduce per block: the second carries the final residual add
+    assert kc["allreduce"] == 1 and kc["allreduce_add"] == 1 and p.needs_comm
+    assert p.steps[-1].kernel == "allreduce_add"
+    # both partial sums are written by their GEMM straight into the symmetric region
+    symm = [i for i, b in enumerate(p.buffers) if b.kind == "symm"]
+    assert len(symm) == 2 and p.symm >= sum(p.buffers[i].nbytes for i in symm)
+    for i in symm:
+        assert any(s.kernel == "gemm_bf16" and s.bufs[2][0] == i for s in p.steps)
+    assert "symm %d" % p.symm in p.to_text()

@@ -1,8 +1,11 @@
 """One rank of the tensor-parallel decoder-layer parity check (launched by torchrun).
 
 Each rank plans its shard of the layer with the collective world size, runs it
-through DeviceKernel (NCCL all-reduce inside the plan) and rank 0 compares the
-result with the TP=1 oracle.  Exit status 0 = parity within 2e-2.
+through DeviceKernel (all-reduce inside the plan: inside NVSwitch when a
+symmetric region could be bound, NCCL otherwise, or NCCL only with
+NKB_SYMM=0) and rank 0 compares the result with the TP=1 oracle.  Before
+that, the plan's communicator all-reduces a buffer of small integers whose sum
+is exact in bf16.  Exit status 0 = both checks pass.
 """
 
 import datetime
@@ -19,11 +22,47 @@ import torch.distributed as dist  # noqa: E402
 from nkipy_b200 import workloads as W  # noqa: E402
 
 
+def check_all_reduce(model, rank, world):
+    """The communicator bound to the plan sums exactly representable bf16 values
+    (in the bound symmetric region when there is one, so inside NVSwitch)."""
+    import ctypes
+
+    from nkipy_b200.spike import _nkb
+    from nkipy_b200.spike import runtime as R
+
+    n = 1 << 20
+    i = np.arange(n)
+    x = ((i % 64) + rank).astype(W.bfloat16)
+    h = ctypes.c_void_p()
+    if model.symmetric:
+        region = R._SYMM[(world, rank)][1][-2]  # the bound symmetric tensor
+        _nkb.call("nkb_wrap", ctypes.c_void_p(region.data_ptr()), n * 2, local_device(), ctypes.byref(h))
+    else:
+        _nkb.call("nkb_alloc", n * 2, local_device(), ctypes.byref(h))
+    _nkb.call("nkb_h2d", h, x.ctypes.data_as(ctypes.c_void_p), n * 2, 0)
+    _nkb.call("nkb_comm_all_reduce", model.comm, h, n, 1, None)
+    _nkb.call("nkb_synchronize")
+    got = np.empty_like(x)
+    _nkb.call("nkb_d2h", h, got.ctypes.data_as(ctypes.c_void_p), n * 2, 0)
+    _nkb.call("nkb_free", h)
+    want = (world * (i % 64) + world * (world - 1) // 2).astype(np.float32)
+    flag = ctypes.c_int()
+    _nkb.call("nkb_device_error", ctypes.byref(flag))
+    ok = bool(np.array_equal(got.astype(np.float32), want)) and flag.value == 0
+    print(f"rank {rank}: all-reduce {'NVLS' if model.symmetric else 'NCCL'} exact={ok}", flush=True)
+    return ok
+
+
+def local_device():
+    return int(os.environ.get("LOCAL_RANK", os.environ["RANK"]))
+
+
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
-    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    dist.init_process_group("cpu:gloo,cuda:nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
     from nkipy_b200.runtime import DeviceKernel, DeviceTensor
     from oracle import numpy_ref as O
 
@@ -34,16 +73,17 @@ def main():
     args, kw = W.layer_args(x, shard, s, world)
     k = DeviceKernel.compile_and_load(W.llama_decoder_layer_kernel, *args, name="tp_layer", is_spmd=False,
                                       cc_enabled=True, rank_id=rank, world_size=world, **kw)
-    names = [t["name"] for t in k.model_ref.io["inputs"]]
+    model = k.model_ref
+    ok = check_all_reduce(model, rank, world)
+    names = [t["name"] for t in model.io["inputs"]]
     ins = {n: DeviceTensor.from_numpy(a, name=n) for n, a in zip(names, args)}
     outs = k(inputs=ins)
     y = next(iter(outs.values())).numpy().astype(np.float32)
-    ok = True
     if rank == 0:
         want = O.llama_layer(x, full, s.n_heads, s.n_kv_heads, s.head_dim, s.eps, s.theta).astype(np.float32)
         err = float(np.max(np.abs(y - want)) / np.max(np.abs(want)))
         print(f"tp{world} layer rel err {err:.3e}", flush=True)
-        ok = err < 2e-2
+        ok = ok and err < 2e-2
     flag = torch.tensor([1 if ok else 0])
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     dist.destroy_process_group()
