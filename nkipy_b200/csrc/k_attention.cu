@@ -19,6 +19,12 @@
 #include "common.cuh"
 
 namespace nkb {
+
+bool fa_tc_eligible(int D, int64_t qs, int64_t ks, int64_t vs, int64_t os);
+int fa_tc_launch(const void *q, const void *k, const void *v, void *o, int B, int H, int Hkv, int Sq, int Skv,
+                 int causal, float scale, const int64_t *qst, const int64_t *kst, const int64_t *vst,
+                 const int64_t *ost, cudaStream_t st, int device);
+
 namespace attn {
 
 constexpr int BM = 128, BN = 64, WARPS = 8;
@@ -309,6 +315,10 @@ int launch(const LaunchArgs &a) {
   for (int i = 0; i < 4; ++i)
     if (reinterpret_cast<uintptr_t>(a.ptrs[i]) & 15) return fail(NKB_ERR_UNSUPPORTED, "flash_attn: unaligned base");
   if (p.B == 0 || p.H == 0 || p.Sq == 0) return NKB_OK;
+  // head_dim 128: tcgen05 kernel (k_flash_sm100.cu); head_dim 64: mma.sync kernel below
+  if (fa_tc_eligible((int)q[5], p.qs, p.ks, p.vs, p.os))
+    return fa_tc_launch(p.q, p.k, p.v, p.o, p.B, p.H, p.Hkv, p.Sq, p.Skv, p.causal, a.step->floats[0], &q[7], &q[10],
+                        &q[13], &q[16], a.stream, a.device);
   return q[5] == 128 ? launch_d<128>(p, a.stream) : launch_d<64>(p, a.stream);
 }
 

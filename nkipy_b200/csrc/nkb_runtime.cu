@@ -186,16 +186,18 @@ namespace nkb {
 int gemm_read_and_clear_error(int *flag);
 int linattn_read_and_clear_error(int *flag);
 int nvls_read_and_clear_error(int *flag);
+int fa_read_and_clear_error(int *flag);
 }
 
 extern "C" int nkb_device_error(int *flag) {
   if (int s = ensure_init()) return s;
   if (!flag) return fail(NKB_ERR_INVALID, "flag is NULL");
-  int g = 0, l = 0, n = 0;
+  int g = 0, l = 0, n = 0, f = 0;
   if (int s = nkb::gemm_read_and_clear_error(&g)) return s;
   if (int s = nkb::linattn_read_and_clear_error(&l)) return s;
   if (int s = nkb::nvls_read_and_clear_error(&n)) return s;
-  *flag = g | l | n;
+  if (int s = nkb::fa_read_and_clear_error(&f)) return s;
+  *flag = g | l | n | f;
   return NKB_OK;
 }
 

@@ -143,10 +143,18 @@ def _attention_body(q, k, v, n_rep):
     return (p @ v).transpose(0, 2, 1, 3)
 
 
-@pytest.mark.parametrize("B,S,H,Hkv,D", [(2, 256, 8, 2, 128), (1, 200, 4, 4, 64), (1, 1000, 2, 1, 128)])
-def test_flash_attention_gqa_causal(B, S, H, Hkv, D):
+# head_dim 128 runs the tcgen05 kernel (two 128-row tiles per CTA): full tiles,
+# a ragged last pair, a second tile with 2 valid rows, an empty second tile, and
+# a long sequence with widely spread scores (qscale) so the running maximum is
+# raised and O rescaled; head_dim 64 the mma.sync kernel.
+@pytest.mark.parametrize(
+    "B,S,H,Hkv,D,qscale",
+    [(2, 256, 8, 2, 128, 1.0), (1, 200, 4, 4, 64, 1.0), (1, 1000, 2, 1, 128, 1.0), (4, 130, 2, 2, 128, 1.0),
+     (1, 64, 2, 1, 128, 1.0), (1, 2048, 4, 1, 128, 4.0)],
+)
+def test_flash_attention_gqa_causal(B, S, H, Hkv, D, qscale):
     rng = np.random.default_rng(13)
-    q = rng.standard_normal((B, S, H, D), dtype=np.float32).astype(BF16)
+    q = (qscale * rng.standard_normal((B, S, H, D), dtype=np.float32)).astype(BF16)
     k = rng.standard_normal((B, S, Hkv, D), dtype=np.float32).astype(BF16)
     v = rng.standard_normal((B, S, Hkv, D), dtype=np.float32).astype(BF16)
     n_rep = H // Hkv
