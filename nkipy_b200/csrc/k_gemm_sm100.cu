@@ -45,6 +45,15 @@ struct Args {
   // silu(gate) * up (N = n_half output columns).
   int epi;
   int64_t n_half;
+  // epi == 2 (residual): C = bf16(bf16(A @ B) + R), R bf16 with row stride ldr
+  const __nv_bfloat16 *res;
+  int64_t ldr;
+  // epi == 3 (rotary embedding): columns [rope_r0[i], rope_r1[i]) are heads of
+  // rope_hd columns rotated in place; position = row % rope_seq; cos/sin are
+  // bf16 tables [rope_seq][rope_hd / 2]
+  const __nv_bfloat16 *rope_cos, *rope_sin;
+  int64_t rope_r0[2], rope_r1[2];
+  int rope_hd, rope_seq;
 };
 
 using namespace sm100;
@@ -249,6 +258,63 @@ __global__ void __launch_bounds__(THREADS, 1)
         continue;
       }
       const int64_t col0 = (int64_t)bn * BN;
+      if (args.epi == 3) {
+        // the traced rotation of rope.py:34-57 on bf16 values, each node rounded:
+        //   lo = x0 * cos - x1 * sin,  hi = x0 * sin + x1 * cos  (x0 = column d, x1 = d + hd/2)
+        const int hd = args.rope_hd, half = hd / 2;
+        const int64_t pos = row % args.rope_seq;
+        const uint32_t lane_acc = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+        for (int c = 0; c < BN / 32; ++c) {
+          const int64_t col = col0 + c * 32;
+          int rr = -1;
+          for (int i = 0; i < 2; ++i)
+            if (col >= args.rope_r0[i] && col < args.rope_r1[i]) rr = i;
+          const int d = rr < 0 ? 0 : (int)((col - args.rope_r0[rr]) % hd);
+          if (rr >= 0 && d >= half) continue;  // written together with its partner chunk
+          uint32_t x0[32], x1[32];
+          tmem_ld32(lane_acc + c * 32, x0);
+          if (rr >= 0) tmem_ld32(lane_acc + (c + half / 32) * 32, x1);
+          if (!row_ok || col >= args.N) continue;
+          __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(args.C) + bb * args.sC + row * args.ldc + col;
+          uint32_t lo[16], hi[16];
+          if (rr < 0) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) lo[j] = pack_bf16(__uint_as_float(x0[2 * j]), __uint_as_float(x0[2 * j + 1]));
+          } else {
+            const __nv_bfloat16 *cs = args.rope_cos + pos * half + d, *sn = args.rope_sin + pos * half + d;
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              float l2[2], h2[2];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const float a = bf16r(__uint_as_float(x0[j + e])), b = bf16r(__uint_as_float(x1[j + e]));
+                const float co = __bfloat162float(cs[j + e]), si = __bfloat162float(sn[j + e]);
+                l2[e] = bf16r(bf16r(a * co) - bf16r(b * si));
+                h2[e] = bf16r(a * si) + bf16r(b * co);
+              }
+              lo[j / 2] = pack_bf16(l2[0], l2[1]);
+              hi[j / 2] = pack_bf16(h2[0], h2[1]);
+            }
+          }
+          const bool vec = col + 32 <= args.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
+#pragma unroll
+          for (int w = 0; w < 2; ++w) {
+            if (w == 1 && rr < 0) break;
+            const uint32_t *src = w ? hi : lo;
+            __nv_bfloat16 *o = dst + w * half;
+            if (vec) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<uint4 *>(o + 2 * j) = make_uint4(src[j], src[j + 1], src[j + 2], src[j + 3]);
+            } else {
+              for (int j = 0; j < 32 && col + w * half + j < args.N; ++j) o[j] = reinterpret_cast<const __nv_bfloat16 *>(src)[j];
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+        continue;
+      }
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
@@ -272,13 +338,34 @@ __global__ void __launch_bounds__(THREADS, 1)
             __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
             packed[j] = *reinterpret_cast<uint32_t *>(&h);
           }
+          if (args.epi == 2) {
+            // the traced add after the product: both operands bf16, the sum rounded once more
+            const __nv_bfloat16 *src = args.res + row * args.ldr + col;
+            if (full_chunk && ((reinterpret_cast<uintptr_t>(src) & 15) == 0)) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                const uint4 rv = *reinterpret_cast<const uint4 *>(src + 2 * j);
+                const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&packed[j + i]));
+                  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&rw[i]));
+                  packed[j + i] = pack_bf16(a.x + b.x, a.y + b.y);
+                }
+              }
+            } else {
+              for (int j = 0; j < 32 && col + j < args.N; ++j) {
+                const float a = __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(packed)[j]);
+                reinterpret_cast<__nv_bfloat16 *>(packed)[j] = __float2bfloat16_rn(a + __bfloat162float(src[j]));
+              }
+            }
+          }
           if (full_chunk && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
 #pragma unroll
             for (int j = 0; j < 16; j += 4)
               *reinterpret_cast<uint4 *>(dst + 2 * j) = make_uint4(packed[j], packed[j + 1], packed[j + 2], packed[j + 3]);
           } else {
-            for (int j = 0; j < 32 && col + j < args.N; ++j)
-              dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+            for (int j = 0; j < 32 && col + j < args.N; ++j) dst[j] = reinterpret_cast<const __nv_bfloat16 *>(packed)[j];
           }
         }
       }
@@ -329,7 +416,8 @@ bool tc_eligible(const void *A, const void *B, int64_t lda, int64_t ldb, int64_t
 // that storage); b_k_major: B stored N x K.
 int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t N, int64_t K, int64_t lda,
             int64_t ldb, int64_t ldc, int64_t batch, int64_t sA, int64_t sB, int64_t sC, int a_mn_major, int b_k_major,
-            cudaStream_t st, int device, int epi = 0, int64_t n_half = 0) {
+            cudaStream_t st, int device, int epi = 0, int64_t n_half = 0, const void *res = nullptr, int64_t ldr = 0,
+            const Args *rope = nullptr) {
   if (M == 0 || N == 0 || batch == 0) return NKB_OK;
   if (K == 0) return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: K == 0 takes the strided path");
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(NKB_ERR_UNSUPPORTED, "gemm: dims exceed int32");
@@ -342,6 +430,8 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   if (!a_mn_major) s = make_map(&ma, A, K, M, ba, lda, sA, BK, BM);
   else s = make_map(&ma, A, M, K, ba, lda, sA, 64, BK);
   if (s) return s;
+  if (epi == 2 && (c_f32 || batch != 1 || !res || ldr < N))
+    return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: residual epilogue needs bf16 output, one batch and a residual of N columns");
   if (epi == 1 && (b_k_major || c_f32 || n_half % 64 || N != n_half))
     return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: SwiGLU epilogue needs N-major B, bf16 output and n_half % 64 == 0");
   const int64_t bcols = epi == 1 ? 2 * n_half : N;
@@ -361,6 +451,23 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   args.b_k_major = b_k_major;
   args.epi = epi;
   args.n_half = n_half;
+  args.res = static_cast<const __nv_bfloat16 *>(res);
+  args.ldr = ldr;
+  if (epi == 3) {
+    if (!rope || c_f32 || batch != 1 || (rope->rope_hd != 64 && rope->rope_hd != 128) || rope->rope_seq <= 0)
+      return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: rotary epilogue needs bf16 output, one batch, head_dim 64 or 128");
+    for (int i = 0; i < 2; ++i)
+      if (rope->rope_r0[i] % rope->rope_hd || rope->rope_r1[i] % rope->rope_hd || rope->rope_r1[i] > N)
+        return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: rotary column ranges must be whole heads");
+    args.rope_cos = rope->rope_cos;
+    args.rope_sin = rope->rope_sin;
+    for (int i = 0; i < 2; ++i) {
+      args.rope_r0[i] = rope->rope_r0[i];
+      args.rope_r1[i] = rope->rope_r1[i];
+    }
+    args.rope_hd = rope->rope_hd;
+    args.rope_seq = rope->rope_seq;
+  }
   args.tiles_m = (int)((M + BM - 1) / BM);
   args.tiles_n = (int)((N + (epi == 1 ? BN / 2 : BN) - 1) / (epi == 1 ? BN / 2 : BN));
   const int64_t tiles = (int64_t)args.tiles_m * args.tiles_n * batch;
@@ -443,18 +550,40 @@ int gemm_simt(const SimtArgs &p, cudaStream_t st) {
 }
 
 // ---- plan steps ---------------------------------------------------------------
-// "gemm_bf16": ptrs A B C; ints M N K lda ldb ldc batch sA sB sC c_f32 a_mn_major b_k_major [epi n_half]
+// "gemm_bf16": ptrs A B C [R | COS SIN]; ints M N K lda ldb ldc batch sA sB sC c_f32 a_mn_major b_k_major
+//              [epi n_half]  (epi 1: SwiGLU over [gate | up] halves of n_half columns)
+//              [epi ldr]     (epi 2, fourth pointer R: C = A @ B + R, R row stride ldr)
+//              [epi hd seq q0 q1 k0 k1]  (epi 3, pointers COS SIN: rotary embedding of
+//                            the heads in columns [q0, q1) and [k0, k1))
 int tc_check(const Step &s) {
-  if (s.buf_ids.size() != 3 || (s.ints.size() != 13 && s.ints.size() != 15))
-    return fail(NKB_ERR_PLAN, "gemm_bf16: bad parameters");
+  const size_t n = s.ints.size();
+  if (n != 13 && n != 15 && n != 20) return fail(NKB_ERR_PLAN, "gemm_bf16: bad parameters");
+  const int epi = n > 13 ? (int)s.ints[13] : 0;
+  if ((epi == 3) != (n == 20)) return fail(NKB_ERR_PLAN, "gemm_bf16: bad epilogue parameters");
+  const size_t ptrs = epi == 2 ? 4u : epi == 3 ? 5u : 3u;
+  if (s.buf_ids.size() != ptrs) return fail(NKB_ERR_PLAN, "gemm_bf16: bad pointer count");
+  if (epi < 0 || epi > 3) return fail(NKB_ERR_PLAN, "gemm_bf16: unknown epilogue");
   return NKB_OK;
 }
 int tc_launch(const LaunchArgs &a) {
   const auto &q = a.step->ints;
-  const int epi = q.size() == 15 ? (int)q[13] : 0;
-  const int64_t n_half = q.size() == 15 ? q[14] : 0;
+  const int epi = q.size() > 13 ? (int)q[13] : 0;
+  const int64_t n_half = epi == 1 ? q[14] : 0;
+  const int64_t ldr = epi == 2 ? q[14] : 0;
+  Args rope;
+  if (epi == 3) {
+    rope.rope_cos = static_cast<const __nv_bfloat16 *>(a.ptrs[3]);
+    rope.rope_sin = static_cast<const __nv_bfloat16 *>(a.ptrs[4]);
+    rope.rope_hd = (int)q[14];
+    rope.rope_seq = (int)q[15];
+    rope.rope_r0[0] = q[16];
+    rope.rope_r1[0] = q[17];
+    rope.rope_r0[1] = q[18];
+    rope.rope_r1[1] = q[19];
+  }
   return gemm_tc(a.ptrs[0], a.ptrs[1], a.ptrs[2], (int)q[10], q[0], q[1], q[2], q[3], q[4], q[5], q[6], q[7], q[8],
-                 q[9], (int)q[11], (int)q[12], a.stream, a.device, epi, n_half);
+                 q[9], (int)q[11], (int)q[12], a.stream, a.device, epi, n_half, epi == 2 ? a.ptrs[3] : nullptr, ldr,
+                 epi == 3 ? &rope : nullptr);
 }
 
 // "gemm_simt": ptrs A B C; ints adt bdt cdt M N K batch a_rs a_cs b_rs b_cs c_rs c_cs sA sB sC

@@ -73,6 +73,7 @@ class Lowering:
                 self.consumers.setdefault(tkey(t), []).append(op)
         self.claims, self.claimed = find_claims(graph)
         self.fused = set()  # ids of ops already lowered as part of an earlier step
+        self.alias_ops: Dict[int, object] = {}  # op id -> op whose value it takes (rotated in place)
         self.needs_comm = False
 
     # ------------------------------------------------------------ buffers
@@ -151,6 +152,9 @@ class Lowering:
             self.vals[("p", p.parameter_id)] = V.View(b, 0, tuple(p.shape), V.dense_strides(p.shape), np.dtype(p.dtype))
         for op in g.operations:
             if op.id in self.fused:
+                continue
+            if op.id in self.alias_ops:
+                self.vals[("o", op.id)] = self.vals[("o", self.alias_ops[op.id].id)]
                 continue
             if id(op) in self.claimed and op.id not in self.claims:
                 continue
@@ -255,6 +259,10 @@ class Lowering:
             self.lower_attention(c)
         elif c.kind == "swiglu_gemm":
             self.lower_swiglu(c)
+        elif c.kind == "residual_gemm":
+            self.lower_residual_gemm(c)
+        elif c.kind == "rope_gemm":
+            self.lower_rope_gemm(c)
         elif c.kind == "linattn":
             self.lower_linattn(c)
         elif c.kind == "argmax":
@@ -325,6 +333,25 @@ class Lowering:
             note=f"B{B} H{H} T{T} D{D} segments={G}",
         )
         self.vals[("o", c.root.id)] = out
+
+    def lower_rope_gemm(self, c):
+        """q, k, v = split(x @ Wqkv) with the rotary embedding of q and k in the
+        GEMM epilogue: the rotated heads stay in place in the product, and each
+        traced concatenate of rotated halves takes the view of its heads."""
+        if self.op_dot(c.params["dot"], epilogue=("rope", c, c.root)):
+            for cat_id, rs in c.params["aliases"].items():
+                self.alias_ops[cat_id] = rs
+            return
+        # the plain product was emitted: the rotations lower op by op where they stand
+        self.claimed -= {id(o) for o in c.interior}
+
+    def lower_residual_gemm(self, c):
+        """x @ W + R with the add in the GEMM epilogue; the generic path otherwise."""
+        root = c.root
+        if self.op_dot(c.params["dot"], epilogue=("add", c.params["res"], root)):
+            return
+        a, b = (self.expr_of(self.get(t)) for t in root.operands)
+        self.put(root, E.op("add", [a, b], tuple(root.result_shape), np.dtype(root.result_dtype)))
 
     def lower_swiglu(self, c):
         """gate/up GEMM with silu(gate) * up in the epilogue; generic path otherwise."""
@@ -543,6 +570,42 @@ class Lowering:
             and aligned(av, a_ks if a_mn else a_ms, sA)
             and aligned(bv, b_ks if b_n else b_ns, sB)
         )
+        if epilogue is not None and epilogue[0] == "rope":
+            cl = epilogue[1]
+            cosv = self.materialize(self.get(cl.params["cos"]), dense=True)
+            sinv = self.materialize(self.get(cl.params["sin"]), dense=True)
+            ok = (use_tc and out_dt == BF16 and batch == 1 and N % 8 == 0
+                  and all(np.dtype(v.dtype) == BF16 and (v.offset * eb) % 16 == 0 for v in (cosv, sinv)))
+            if not ok:
+                self.op_dot(op)
+                return False
+            rngs = list(cl.params["ranges"]) + [(0, 0)] * (2 - len(cl.params["ranges"]))
+            lda = a_ms if a_k else a_ks
+            ldb = b_ks if b_n else b_ns
+            self.step(
+                "gemm_bf16",
+                [self.bref(av), self.bref(bv), self.bref(out), self.bref(cosv), self.bref(sinv)],
+                [M, N, K, lda, ldb, N, 1, 0, 0, 0, 0, int(a_mn and not a_k), int(b_k and not b_n), 3,
+                 cl.params["hd"], cl.params["seq"], rngs[0][0], rngs[0][1], rngs[1][0], rngs[1][1]],
+                note=f"tc {M}x{N}x{K} +rope",
+            )
+            self.vals[("o", op.id)] = out
+            return True
+        if epilogue is not None and epilogue[0] == "add":
+            rv = self.materialize(self.get(epilogue[1]), dense=True)
+            if not (use_tc and out_dt == BF16 and batch == 1 and (rv.offset * eb) % 16 == 0 and N % 8 == 0):
+                self.op_dot(op)
+                return False
+            lda = a_ms if a_k else a_ks
+            ldb = b_ks if b_n else b_ns
+            self.step(
+                "gemm_bf16",
+                [self.bref(av), self.bref(bv), self.bref(out), self.bref(rv)],
+                [M, N, K, lda, ldb, N, 1, 0, 0, 0, 0, int(a_mn and not a_k), int(b_k and not b_n), 2, N],
+                note=f"tc {M}x{N}x{K} +residual",
+            )
+            self.vals[("o", epilogue[2].id)] = out
+            return True
         if epilogue is not None:
             F = epilogue[1]
             if not (use_tc and b_n and out_dt == BF16 and F % 64 == 0 and N == 2 * F and batch == 1):

@@ -711,7 +711,170 @@ def match_linear_attention(gi: GraphIndex, root) -> Optional[Claim]:
     return Claim("linattn", root, ops, {"q": q_src, "k": k_src, "v": v_src, "shape": shape})
 
 
-MATCHERS = (match_attention, match_linear_attention, match_swiglu_gemm, match_softmax, match_rmsnorm, match_argmax)
+def match_residual_gemm(gi: GraphIndex, add_op) -> Optional[Claim]:
+    """h + x @ W with the product used only by the add (the residual after the
+    FFN down projection, ``qwen3_embedding/kernels/transformer_layer.py:60-83``):
+    the add becomes the GEMM's epilogue."""
+    if add_op.op_name != "add" or len(add_op.operands) != 2 or str(np.dtype(add_op.result_dtype)) != "bfloat16":
+        return None
+    for d_t, r_t in (add_op.operands, add_op.operands[::-1]):
+        pd = GraphIndex.producer(d_t)
+        if pd is None or pd.op_name != "dot" or str(np.dtype(pd.result_dtype)) != "bfloat16":
+            continue
+        if tuple(r_t.shape) != tuple(add_op.result_shape) or tuple(d_t.shape) != tuple(add_op.result_shape):
+            continue
+        if str(np.dtype(r_t.dtype)) != "bfloat16" or tkey(r_t) == tkey(d_t):
+            continue
+        if not _exclusive(gi, [pd], add_op):
+            continue
+        return Claim("residual_gemm", add_op, [pd], {"dot": pd, "res": r_t})
+    return None
+
+
+def _view_base(t, ops):
+    """Strip reshape/broadcast ops (appending them to ops); the underlying tensor."""
+    while True:
+        p = GraphIndex.producer(t)
+        if p is None or p.op_name not in ("reshape", "broadcast"):
+            return t
+        ops.append(p)
+        t = p.operands[0]
+
+
+def _last_axis_slice(op, n_axes):
+    """(start, limit) of a slice that only narrows the last of n_axes axes, else None."""
+    if op.op_name != "slice" or len(op.operands[0].shape) != n_axes:
+        return None
+    st, lim = list(op.attributes["start_indices"]), list(op.attributes["limit_indices"])
+    strides = op.attributes.get("strides") or [1] * n_axes
+    full = op.operands[0].shape
+    if any(int(x) != 1 for x in strides):
+        return None
+    if any(st[i] != 0 or lim[i] != full[i] for i in range(n_axes - 1)):
+        return None
+    return int(st[-1]), int(lim[-1])
+
+
+def _rotation_of(gi: GraphIndex, heads_op):
+    """heads_op's result (B, S, H, hd): the traced half-split rotation of
+    rope.py:34-57, concatenate([x0 * cos - x1 * sin, x0 * sin + x1 * cos], -1)
+    with x0, x1 its halves.  Returns (concat op, interior ops, cos, sin) or None."""
+    hd = int(heads_op.result_shape[-1])
+    half = hd // 2
+    key = ("o", heads_op.id)
+    users = gi.consumers.get(key, [])
+    if len(users) != 2 or key in gi.results:
+        return None
+    halves = {}
+    for u in users:
+        rng = _last_axis_slice(u, 4)
+        if rng == (0, half):
+            halves[0] = u
+        elif rng == (half, hd):
+            halves[1] = u
+    if len(halves) != 2:
+        return None
+    ops = [halves[0], halves[1]]
+    prods = {}  # (half, base tensor key) -> (multiply op, base tensor)
+    for i in (0, 1):
+        mults = gi.consumers.get(("o", halves[i].id), [])
+        if len(mults) != 2 or any(m.op_name != "multiply" for m in mults):
+            return None
+        for m in mults:
+            a, b = m.operands
+            other = b if tkey(a) == ("o", halves[i].id) else a
+            base = _view_base(other, [])  # the table's reshape/broadcast views stay outside the claim
+            ops.append(m)
+            prods[(i, tkey(base))] = (m, base)
+    # lo = x0*cos - x1*sin and hi = x0*sin + x1*cos: find the subtract and the add
+    outs = {}
+    for (i, bk), (m, base) in prods.items():
+        for c in gi.consumers.get(("o", m.id), []):
+            if c.op_name in ("subtract", "add"):
+                outs.setdefault(c.id, c)
+    if len(outs) != 2:
+        return None
+    sub = next((c for c in outs.values() if c.op_name == "subtract"), None)
+    add = next((c for c in outs.values() if c.op_name == "add"), None)
+    if sub is None or add is None:
+        return None
+    def src(c, j):
+        p = GraphIndex.producer(c.operands[j])
+        for (i, bk), (m, base) in prods.items():
+            if p is m:
+                return i, bk, base
+        return None
+    s0, s1, a0, a1 = src(sub, 0), src(sub, 1), src(add, 0), src(add, 1)
+    if None in (s0, s1, a0, a1):
+        return None
+    # subtract: x0*cos - x1*sin; add: x0*sin + x1*cos (in either operand order)
+    if not (s0[0] == 0 and s1[0] == 1):
+        return None
+    cos_k, sin_k = s0[1], s1[1]
+    if {(a0[0], a0[1]), (a1[0], a1[1])} != {(0, sin_k), (1, cos_k)} or cos_k == sin_k:
+        return None
+    cons = gi.consumers.get(("o", sub.id), [])
+    if len(cons) != 1 or cons[0].op_name != "concatenate":
+        return None
+    cat = cons[0]
+    if len(cat.operands) != 2 or tkey(cat.operands[0]) != ("o", sub.id) or tkey(cat.operands[1]) != ("o", add.id):
+        return None
+    if int(cat.attributes.get("dimension", -1)) != 3:
+        return None
+    cos_t, sin_t = s0[2], s1[2]
+    ops += [sub, add, cat]
+    if not _exclusive(gi, ops, cat):
+        return None
+    return cat, ops, cos_t, sin_t
+
+
+def match_rope_gemm(gi: GraphIndex, dot) -> Optional[Claim]:
+    """x @ Wqkv split into q, k, v heads with the half-split rotary embedding on q
+    and k (qwen3_embedding/kernels/attention.py + rope.py): the rotation becomes
+    the GEMM's epilogue and the rotated heads stay in place in its output."""
+    if dot.op_name != "dot" or str(np.dtype(dot.result_dtype)) != "bfloat16" or len(dot.result_shape) != 3:
+        return None
+    if ("o", dot.id) in gi.results:
+        return None
+    B, S, N = (int(x) for x in dot.result_shape)
+    ranges, interior, aliases, tables = [], [], {}, None
+    for sl in gi.consumers.get(("o", dot.id), []):
+        rng = _last_axis_slice(sl, 3)
+        if rng is None:
+            return None  # every use of the product must be a column slice
+        users = gi.consumers.get(("o", sl.id), [])
+        if len(users) != 1 or users[0].op_name != "reshape" or ("o", sl.id) in gi.results:
+            continue
+        rs = users[0]
+        shp = tuple(int(x) for x in rs.result_shape)
+        if len(shp) != 4 or shp[:2] != (B, S) or shp[2] * shp[3] != rng[1] - rng[0]:
+            continue
+        rot = _rotation_of(gi, rs)
+        if rot is None:
+            continue
+        cat, ops, cos_t, sin_t = rot
+        hd = shp[3]
+        if tables is not None and (tkey(cos_t), tkey(sin_t), tables[2]) != (tkey(tables[0]), tkey(tables[1]), hd):
+            continue
+        if tuple(int(x) for x in cos_t.shape) != (S, hd // 2) or tuple(int(x) for x in sin_t.shape) != (S, hd // 2):
+            continue
+        if rng[0] % hd or hd not in (64, 128):
+            continue
+        tables = (cos_t, sin_t, hd)
+        ranges.append(rng)
+        interior += ops
+        aliases[cat.id] = rs
+    if not ranges or len(ranges) > 2:
+        return None
+    return Claim("rope_gemm", dot, interior, {"dot": dot, "ranges": ranges, "hd": tables[2], "cos": tables[0],
+                                                 "sin": tables[1], "aliases": aliases, "seq": S})
+
+
+# rmsnorm before residual_gemm: a residual add that feeds an RMSNorm belongs to the fused norm kernel
+MATCHERS = (
+    match_attention, match_linear_attention, match_swiglu_gemm, match_softmax, match_rmsnorm, match_argmax,
+    match_residual_gemm, match_rope_gemm,
+)
 
 
 def find_claims(graph) -> Dict[int, Claim]:

@@ -130,9 +130,12 @@ def test_layer_plans(monkeypatch):
     args, kw = W.layer_args(x, shard, s, 1)
     p = plan_of(W.llama_decoder_layer_kernel, *args, **kw)
     counts = p.kernel_counts()
-    assert counts.get("gemm_bf16", 0) >= 4
-    assert counts.get("rmsnorm_rows", 0) == 2
-    assert "allreduce" not in counts
+    # RoPE in the QKV GEMM epilogue, SwiGLU in the gate/up epilogue, the last
+    # residual add in the down projection's epilogue: no elementwise launch left
+    assert counts == {"rmsnorm_rows": 2, "gemm_bf16": 4, "flash_attn": 1}
+    notes = [s.note for s in p.steps if s.kernel == "gemm_bf16"]
+    assert any("+rope" in n for n in notes) and any("+swiglu" in n for n in notes)
+    assert any("+residual" in n for n in notes)
 
 
 def test_layer_tp2_has_two_allreduces():
@@ -142,6 +145,7 @@ def test_layer_tp2_has_two_allreduces():
     args, kw = W.layer_args(np.zeros((1, 64, 256), BF16), shard, s, 2)
     p = lower(NKIPyKernel.trace(W.llama_decoder_layer_kernel).specialize(*args, **kw), world=2)
     kc = p.kernel_counts()
+    assert "ew" not in kc and any("+rope" in s.note for s in p.steps)
     # one all-reduce per block: the second carries the final residual add
     assert kc["allreduce"] == 1 and kc["allreduce_add"] == 1 and p.needs_comm
     assert p.steps[-1].kernel == "allreduce_add"
