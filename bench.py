@@ -13,7 +13,9 @@ line.  Workloads (``--workload``):
   layer    Llama decoder layer, batch 4 x 2048, TP = N       tokens/s
 
 Timing: W untimed warm-up steps, then K steps each preceded by an L2 flush
-(a 256 MiB device write outside the timed events) and timed with CUDA events
+(256 MiB written, then read back, outside the timed events: the lines it
+leaves in L2 are clean, so no write-back of the flush falls inside the timed
+step) and timed with CUDA events
 on the plan's stream; barrier + synchronize on both sides; the max over
 ranks is reported.  ``e2e`` repeats the K steps through the public API with
 pinned host buffers (H2D of every input, execute, D2H of the result).
@@ -39,6 +41,16 @@ import ml_dtypes  # noqa: E402
 
 BF16 = np.dtype(ml_dtypes.bfloat16)
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def flush_l2(buf):
+    """Evict L2: write a buffer larger than L2, then read it back so that the
+    lines left behind are clean (no write-back of the flush inside the next
+    timed step)."""
+    import torch
+
+    buf.zero_()
+    buf.view(torch.int32).sum()
 
 
 def load_peaks():
@@ -106,7 +118,7 @@ class Softmax(Workload):
 
     def config(self, world):
         return {"workload": "softmax fp32 (4096, 4096) last axis", "shape": [self.ROWS, self.COLS],
-                "l2": "flushed between steps (256 MiB write)"}
+                "l2": "flushed between steps (256 MiB written, then read back)"}
 
 
 class RmsNorm(Workload):
@@ -451,7 +463,7 @@ def run_nkb(args, wl, rank, world, local_rank):
     barrier()
     total_ms = 0.0
     for _ in range(args.steps):
-        flush.zero_()
+        flush_l2(flush)
         torch.cuda.synchronize()
         total_ms += spike.time_execute(kernel.model_ref, in_refs, out_refs, warmup=0, iters=1, use_graph=True)[0]
     barrier()
@@ -585,7 +597,7 @@ def measure_quick(wl, steps, warmup, local_rank, with_cpu):
         spike.execute(kernel.model_ref, ins, outs, use_graph=True)
     total = 0.0
     for _ in range(steps):
-        flush.zero_()
+        flush_l2(flush)
         torch.cuda.synchronize()
         total += spike.time_execute(kernel.model_ref, ins, outs, warmup=0, iters=1, use_graph=True)[0]
     ms = total / steps

@@ -104,7 +104,8 @@ NKB_API int nkb_synchronize(void);
 
 /* Per-launch device time: runs the plan `iters` times with CUDA events
  * between consecutive kernel launches and writes the mean duration of each
- * launch (milliseconds) into step_ms[0..n_launches-1]. */
+ * launch (milliseconds) into step_ms[0..n_launches-1].  Each run is preceded
+ * by an L2 flush (256 MiB written, then read back) in a temporary buffer. */
 NKB_API int nkb_time_steps(nkb_plan plan, const nkb_buf *ins, int n_in, const nkb_buf *outs, int n_out, int iters,
                            float *step_ms);
 

@@ -94,55 +94,111 @@ __device__ __forceinline__ float row_reduce_sum(float v, float *smem) {
 // ---------------------------------------------------------------------------
 // softmax
 // ---------------------------------------------------------------------------
-// THREADS threads per row (32 or 256); CHUNKS 4-element chunks per thread.
-// Rows per CTA = 256 / THREADS.  cols must be a multiple of 4 here.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Row softmax held in registers: THREADS threads per row (32 or 256), CHUNKS
+// 4-element chunks per thread, 256 / THREADS rows per CTA.  Persistent: a grid
+// of MINB CTAs per SM walks the rows, and the loads of a thread's next row are
+// issued before the current row is reduced, so about MINB x 256 x CHUNKS x 16
+// bytes per SM stay in flight from HBM across the reductions.  exp is
+// ex2.approx of (x - max)·log2(e) and the division a multiply by the rounded
+// reciprocal of the sum: within a few ulp of exp(x - max) / sum, far inside
+// the fp32 tolerance of the path.  cols must be a multiple of 4 here.
+template <int CHUNKS>
+constexpr int softmax_minb() {
+  return CHUNKS <= 1 ? 8 : CHUNKS <= 2 ? 6 : CHUNKS <= 4 ? 5 : 2;
+}
+
 template <int THREADS, int CHUNKS, typename Tin, typename Tout>
-__global__ void __launch_bounds__(256, 6) softmax_reg_kernel(const Tin *__restrict__ x, Tout *__restrict__ y,
-                                                          int64_t rows, int cols) {
-  __shared__ float smem[32];
+__global__ void __launch_bounds__(256, softmax_minb<CHUNKS>())
+    softmax_reg_kernel(const Tin *__restrict__ x, Tout *__restrict__ y, int64_t rows, int cols) {
+  // [0]: per-warp maxima, [1]: per-warp sums (256-thread rows only); one
+  // buffer each, so a row needs two CTA barriers
+  __shared__ float red[2][8];
   constexpr int RPB = 256 / THREADS;
+  constexpr float LOG2E = 1.4426950408889634f;
   const int sub = threadIdx.x / THREADS;
   const int t = threadIdx.x % THREADS;
-  for (int64_t row = (int64_t)blockIdx.x * RPB + sub; row - sub < rows; row += (int64_t)gridDim.x * RPB) {
-    const bool active = row < rows;
-    const Tin *xr = x + (active ? row : 0) * cols;
-    float v[CHUNKS][4];
-    float m = -INFINITY;
+  const int64_t stride = (int64_t)gridDim.x * RPB;
+  float nx[CHUNKS][4];
+  auto fetch = [&](int64_t r) {
 #pragma unroll
     for (int c = 0; c < CHUNKS; ++c) {
       const int col = (c * THREADS + t) * 4;
-      if (active && col < cols) {
-        load4(xr + col, v[c]);
+      if (r < rows && col < cols) {
+        load4(x + r * cols + col, nx[c]);
       } else {
-        v[c][0] = v[c][1] = v[c][2] = v[c][3] = -INFINITY;
+        nx[c][0] = nx[c][1] = nx[c][2] = nx[c][3] = -INFINITY;
       }
+    }
+  };
+  int64_t row = (int64_t)blockIdx.x * RPB + sub;
+  fetch(row);
+  // 256-thread rows: the CTA walks rows together (row is CTA-uniform)
+  for (; row < rows; row += stride) {
+    float v[CHUNKS][4];
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[c][j] = nx[c][j];
+    fetch(row + stride);
+    float m = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c)
 #pragma unroll
       for (int j = 0; j < 4; ++j) m = fmaxf(m, v[c][j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (THREADS > 32) {
+      if (t % 32 == 0) red[0][t / 32] = m;
+      __syncthreads();
+      m = red[0][t % 8];
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     }
-    m = row_reduce_max<THREADS>(m, smem);
     float s = 0.f;
 #pragma unroll
     for (int c = 0; c < CHUNKS; ++c)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        v[c][j] = expf(v[c][j] - m);
+        v[c][j] = ex2_approx((v[c][j] - m) * LOG2E);
         s += v[c][j];
       }
-    s = row_reduce_sum<THREADS>(s, smem);
-    if (active) {
-      Tout *yr = y + row * cols;
 #pragma unroll
-      for (int c = 0; c < CHUNKS; ++c) {
-        const int col = (c * THREADS + t) * 4;
-        if (col < cols) {
-          float o[4];
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (THREADS > 32) {
+      if (t % 32 == 0) red[1][t / 32] = s;
+      __syncthreads();
+      s = red[1][t % 8];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) o[j] = __fdiv_rn(v[c][j], s);
-          store4(yr + col, o);
-        }
+      for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    }
+    const float inv = __frcp_rn(s);
+    Tout *yr = y + row * cols;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+      const int col = (c * THREADS + t) * 4;
+      if (col < cols) {
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = v[c][j] * inv;
+        store4(yr + col, o);
       }
     }
   }
+}
+
+template <int THREADS, int CHUNKS, typename Tin, typename Tout>
+int softmax_reg_launch(const Tin *x, Tout *y, int64_t rows, int cols, cudaStream_t st, int device) {
+  constexpr int RPB = 256 / THREADS;
+  const unsigned grid = (unsigned)std::min<int64_t>((rows + RPB - 1) / RPB,
+                                                    (int64_t)num_sms(device) * softmax_minb<CHUNKS>());
+  softmax_reg_kernel<THREADS, CHUNKS, Tin, Tout><<<grid, 256, 0, st>>>(x, y, rows, cols);
+  return launch_status("softmax_rows");
 }
 
 // Rows too long for registers (or cols % 4 != 0): online max/sum pass, then
@@ -182,16 +238,16 @@ int softmax_dispatch(const void *x, void *y, int64_t rows, int64_t cols, cudaStr
   auto grid = [&](int rpb) { return (unsigned)std::min<int64_t>((rows + rpb - 1) / rpb, cap); };
   if (aligned && cols <= 1024) {
     const int chunks = (int)((cols + 127) / 128);
-    if (chunks <= 1) softmax_reg_kernel<32, 1, Tin, Tout><<<grid(8), 256, 0, st>>>(xi, yo, rows, (int)cols);
-    else if (chunks <= 2) softmax_reg_kernel<32, 2, Tin, Tout><<<grid(8), 256, 0, st>>>(xi, yo, rows, (int)cols);
-    else if (chunks <= 4) softmax_reg_kernel<32, 4, Tin, Tout><<<grid(8), 256, 0, st>>>(xi, yo, rows, (int)cols);
-    else softmax_reg_kernel<32, 8, Tin, Tout><<<grid(8), 256, 0, st>>>(xi, yo, rows, (int)cols);
+    if (chunks <= 1) return softmax_reg_launch<32, 1>(xi, yo, rows, (int)cols, st, device);
+    if (chunks <= 2) return softmax_reg_launch<32, 2>(xi, yo, rows, (int)cols, st, device);
+    if (chunks <= 4) return softmax_reg_launch<32, 4>(xi, yo, rows, (int)cols, st, device);
+    return softmax_reg_launch<32, 8>(xi, yo, rows, (int)cols, st, device);
   } else if (aligned && cols <= 8192) {
     const int chunks = (int)((cols + 1023) / 1024);
-    if (chunks <= 1) softmax_reg_kernel<256, 1, Tin, Tout><<<grid(1), 256, 0, st>>>(xi, yo, rows, (int)cols);
-    else if (chunks <= 2) softmax_reg_kernel<256, 2, Tin, Tout><<<grid(1), 256, 0, st>>>(xi, yo, rows, (int)cols);
-    else if (chunks <= 4) softmax_reg_kernel<256, 4, Tin, Tout><<<grid(1), 256, 0, st>>>(xi, yo, rows, (int)cols);
-    else softmax_reg_kernel<256, 8, Tin, Tout><<<grid(1), 256, 0, st>>>(xi, yo, rows, (int)cols);
+    if (chunks <= 1) return softmax_reg_launch<256, 1>(xi, yo, rows, (int)cols, st, device);
+    if (chunks <= 2) return softmax_reg_launch<256, 2>(xi, yo, rows, (int)cols, st, device);
+    if (chunks <= 4) return softmax_reg_launch<256, 4>(xi, yo, rows, (int)cols, st, device);
+    return softmax_reg_launch<256, 8>(xi, yo, rows, (int)cols, st, device);
   } else {
     softmax_stream_kernel<Tin, Tout><<<grid(1), 256, 0, st>>>(xi, yo, rows, cols);
   }

@@ -19,7 +19,9 @@ BF16 = np.dtype(ml_dtypes.bfloat16)
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("shape", [(4096, 4096), (7, 1000), (33, 128), (3, 9000), (2, 130), (1, 1)])
+@pytest.mark.parametrize(
+    "shape", [(4096, 4096), (7, 1000), (33, 128), (3, 9000), (2, 130), (1, 1), (5, 2000), (2000, 6000), (300, 8192)]
+)
 def test_softmax(shape):
     x = np.random.default_rng(1).standard_normal(shape, dtype=np.float32)
     got = on_device(W.softmax_kernel, x)
