@@ -464,7 +464,9 @@ def run_nkb(args, wl, rank, world, local_rank):
     total_ms = 0.0
     for _ in range(args.steps):
         flush_l2(flush)
-        torch.cuda.synchronize()
+        # every rank's flush is done before any rank starts the step, so the
+        # collectives inside it do not time another rank's flush
+        barrier()
         total_ms += spike.time_execute(kernel.model_ref, in_refs, out_refs, warmup=0, iters=1, use_graph=True)[0]
     barrier()
     t = torch.tensor([total_ms], dtype=torch.float64, device=f"cuda:{local_rank}")
@@ -529,7 +531,8 @@ def run_nkb(args, wl, rank, world, local_rank):
             unit = "TFLOP/s"
             work = work / len(dom)
             dur = dur / len(dom)
-        traffic = profile_traffic(wl)
+        # the committed ncu summaries are single-GPU captures
+        traffic = profile_traffic(wl) if world == 1 else None
         roof = {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
                 "traffic": traffic, "peak_source": f"{peak_kind} ({key if wl.bound != 'hbm' else 'hbm_gbs'})",
                 "kernel": wl.dominant, "launch_ms": dur, "work_per_launch": work}

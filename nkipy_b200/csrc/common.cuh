@@ -126,6 +126,21 @@ int num_sms(int device);
 
 // NCCL all-reduce entry (implemented in the runtime, which owns the dlopen).
 int comm_all_reduce(void *comm, const void *src, void *dst, size_t count, int dtype, cudaStream_t stream);
+// Fused GEMM + all-reduce: per-step flag slots after the all-reduce flags at
+// the end of the bound symmetric region.  A slot holds SYMM_AR_CHUNKS arrival
+// counts (one per 128-row block of the output), then a count of this rank's
+// finished CTAs and a count of finished ranks.
+constexpr int SYMM_AR_SLOTS = 4, SYMM_AR_CHUNKS = 1022, SYMM_AR_SLOT_BYTES = 4096;
+struct SymmAr {
+  uint64_t mc_payload;  // the payload through the multicast object
+  uint32_t *flags;      // this rank's slot
+  uint64_t mc_flags;    // the slot through the multicast object
+  int rank, world;
+};
+// Fills `out` when `payload` (bytes) lies in the communicator's bound
+// symmetric data area (16-byte aligned) and slot is valid; false otherwise.
+bool comm_symm_ar(void *comm, const void *payload, size_t bytes, int slot, SymmAr *out);
+
 // dst = res + all-reduce(buf) (buf keeps the sum)
 int comm_all_reduce_add(void *comm, void *buf, const void *res, void *dst, size_t count, int dtype,
                         cudaStream_t stream);

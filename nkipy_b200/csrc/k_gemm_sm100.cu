@@ -15,6 +15,17 @@
 // fetches its own tiles and L2 provides the reuse, so the same kernel is safe
 // on multi-GPU runs.
 //
+// Fused all-reduce (row-parallel GEMMs under tensor parallelism): C is this
+// rank's copy of a symmetric region; tiles are taken row block by row block,
+// and after the epilogue stores a tile one thread adds 1 to that row block's
+// arrival count on every rank (multimem.red through the multicast object).
+// Two more warps per CTA (warps 6-7) reduce, as soon as a row block's count
+// shows every rank's tiles, this CTA's share of this rank's part of the block
+// (multimem.ld_reduce with fp32 accumulation, optionally + a residual, then
+// multimem.st to every rank), while later tiles are still computing.  The last
+// CTA of a rank clears the arrival counts and adds 1 to a done count on every
+// rank, then waits until every rank is done.  Every wait is bounded.
+//
 // A may be K-major (row-major M x K) or M-major (stored K x M); B may be
 // N-major (row-major K x N) or K-major (stored N x K).  Tensor maps are 3-D
 // (inner, outer, batch).  Every mbarrier wait is bounded by a clock budget;
@@ -54,7 +65,15 @@ struct Args {
   const __nv_bfloat16 *rope_cos, *rope_sin;
   int64_t rope_r0[2], rope_r1[2];
   int rope_hd, rope_seq;
+  // fused all-reduce (gemm_bf16_tcgen05<true>): C dense bf16 with N columns
+  uint64_t ar_mc;               // C through the multicast object
+  uint32_t *ar_flags;           // this rank's flag slot
+  uint64_t ar_mc_flags;         // the slot through the multicast object
+  const __nv_bfloat16 *ar_res;  // optional residual (dense, N columns): C = res + sum
+  int ar_rank, ar_world;
 };
+
+constexpr int AR_THREADS = 256;  // 192 + two all-reduce warps
 
 using namespace sm100;
 
@@ -70,7 +89,14 @@ __host__ __device__ constexpr uint32_t make_idesc(int a_mn_major, int b_mn_major
   return idesc_bf16(BM, BN, a_mn_major, b_mn_major);
 }
 
+template <bool AR>
 __device__ __forceinline__ void tile_coords(int t, const Args &a, int &bm, int &bn, int &bb) {
+  if (AR) {  // row block by row block, so blocks complete (and are reduced) in order
+    bb = 0;
+    bm = t / a.tiles_n;
+    bn = t - bm * a.tiles_n;
+    return;
+  }
   const int per_batch = a.tiles_m * a.tiles_n;
   bb = t / per_batch;
   int r = t - bb * per_batch;
@@ -85,7 +111,163 @@ __device__ __forceinline__ void tile_coords(int t, const Args &a, int &bm, int &
   bn = within / gsize;
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+// ---- fused all-reduce helpers ------------------------------------------------
+constexpr long long AR_WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// +v on every rank's copy of a multicast address, ordered after this thread's
+// (and, through a preceding barrier, its CTA's) earlier writes
+__device__ __forceinline__ void mc_red_add_release(uint64_t addr, uint32_t v) {
+  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+// sum over all ranks of 16 bytes of bf16 pairs at a multicast address (fp32
+// accumulation inside the switch, one bf16 rounding)
+__device__ __forceinline__ void mc_ld_reduce_bf16(uint64_t addr, uint32_t *r) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "l"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void mc_st16(uint64_t addr, const uint32_t *r) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+__device__ __forceinline__ void named_bar(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+// barrier over `threads` threads that returns the AND of `pred` (uniform exits)
+__device__ __forceinline__ bool named_bar_and(int id, int threads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(threads)
+      : "memory");
+  return r != 0;
+}
+
+// Vectors (16 bytes) [lo, hi) of row block cc that this CTA reduces on this rank.
+__device__ __forceinline__ void ar_piece(const Args &a, int cc, int64_t &lo, int64_t &hi) {
+  const int64_t row_vecs = a.N / 8;
+  const int64_t r0 = (int64_t)cc * BM;
+  const int64_t nv = min((int64_t)BM, a.M - r0) * row_vecs;
+  const int64_t rlo = nv * a.ar_rank / a.ar_world, rn = nv * (a.ar_rank + 1) / a.ar_world - rlo;
+  lo = r0 * row_vecs + rlo + rn * blockIdx.x / gridDim.x;
+  hi = r0 * row_vecs + rlo + rn * (blockIdx.x + 1) / gridDim.x;
+}
+
+// Warps 6-7 of the fused kernel (64 threads, ct = 0..63).
+__device__ void ar_comm(const Args &a, int ct, volatile int *abort_flag) {
+  const int lane = ct % 32;
+  uint32_t *const cnt = a.ar_flags + SYMM_AR_CHUNKS;  // this rank's finished CTAs
+  uint32_t *const done = cnt + 1;                     // finished ranks (every rank adds 1)
+  const uint64_t mc_done = a.ar_mc_flags + 4ull * (SYMM_AR_CHUNKS + 1);
+  // done counts of earlier launches: no rank can finish this launch before this
+  // CTA has stored its tiles, which it does after this read
+  const uint32_t d0 = ld_acquire_sys(done);
+  const uint32_t need = (uint32_t)(a.tiles_n * a.ar_world);
+  auto ready = [&](int cc) { return (int)(ld_acquire_sys(a.ar_flags + cc) - need) >= 0; };
+  bool ok = true;
+  int c = 0;
+  while (c < a.tiles_m) {
+    // warp-uniform: wait for row block c, then take the run of ready blocks after it (at most 8)
+    int ce = c;
+    if (lane == 0) {
+      const long long t0 = clock64();
+      while (!ready(c)) {
+        if (*abort_flag || clock64() - t0 > AR_WAIT_CYCLES) {
+          ok = false;
+          break;
+        }
+        __nanosleep(256);
+      }
+      if (ok)
+        for (ce = c + 1; ce < a.tiles_m && ce < c + 8 && ready(ce);) ++ce;
+    }
+    ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
+    ce = __shfl_sync(0xffffffffu, ce, 0);
+    if (!ok) break;
+    // this thread's vectors of blocks [c, ce), eight reductions in flight at a time
+    int cc = c;
+    int64_t lo, hi;
+    ar_piece(a, cc, lo, hi);
+    int64_t v = lo + ct;
+    while (true) {
+      int64_t addr[8];
+      bool valid[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        while (v >= hi && cc + 1 < ce) {
+          ++cc;
+          ar_piece(a, cc, lo, hi);
+          v = lo + ct;
+        }
+        valid[i] = v < hi;
+        addr[i] = v;
+        if (valid[i]) v += 64;
+      }
+      if (!valid[0]) break;
+      uint32_t r[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (valid[i]) mc_ld_reduce_bf16(a.ar_mc + 16ull * addr[i], r[i]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (!valid[i]) continue;
+        if (a.ar_res) {
+          // the traced add after the all-reduce: bf16 + bf16, rounded once
+          const uint4 x = *reinterpret_cast<const uint4 *>(a.ar_res + 8 * addr[i]);
+          const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 p = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&r[i][j]));
+            const float2 q = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&xw[j]));
+            r[i][j] = pack_bf16(p.x + q.x, p.y + q.y);
+          }
+        }
+        mc_st16(a.ar_mc + 16ull * addr[i], r[i]);
+      }
+    }
+    __syncwarp();
+    c = ce;
+  }
+  if (!ok) {
+    atomicExch(&g_device_error, 1);
+    *abort_flag = 1;
+  }
+  named_bar(2, 64);  // both warps are past their last store
+  if (ct == 0) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    const uint32_t prev = atomicAdd(cnt, 1u);
+    if (prev == gridDim.x - 1) {
+      // last CTA of this rank: every CTA has read its counts; clear them for the
+      // next launch before telling the other ranks (whose next launch starts
+      // only after they see every rank done)
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
+      *cnt = 0;
+      for (int i = 0; i < a.tiles_m; ++i) a.ar_flags[i] = 0;
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      mc_red_add_release(mc_done, 1);
+      const uint32_t target = d0 - d0 % (uint32_t)a.ar_world + (uint32_t)a.ar_world;
+      const long long t0 = clock64();
+      while ((int)(ld_acquire_sys(done) - target) < 0) {
+        if (clock64() - t0 > AR_WAIT_CYCLES) {
+          atomicExch(&g_device_error, 1);
+          break;
+        }
+        __nanosleep(256);
+      }
+    }
+  }
+}
+
+template <bool AR>
+__global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Args args) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -132,7 +314,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int bm, bn, bb;
-        tile_coords(t, args, bm, bn, bb);
+        tile_coords<AR>(t, args, bm, bn, bb);
         for (int kb = 0; kb < k_blocks; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -202,6 +384,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         umma_commit(&acc_full[acc]);  // accumulator ready for the epilogue
       }
     }
+  } else if (AR && warp >= 6) {
+    // ---------------- all-reduce (warps 6..7) ----------------
+    ar_comm(args, threadIdx.x - 192, abort_flag);
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int quad = warp % 4;  // TMEM lane quadrant this warp may access
@@ -209,10 +394,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       int bm, bn, bb;
-      tile_coords(t, args, bm, bn, bb);
+      tile_coords<AR>(t, args, bm, bn, bb);
       const int acc = local & 1;
       const uint32_t acc_ph = (local >> 1) & 1;
-      if (!mbar_wait(&acc_full[acc], acc_ph, abort_flag)) break;
+      bool got = mbar_wait(&acc_full[acc], acc_ph, abort_flag);
+      if (AR) got = named_bar_and(1, 128, got);  // the four warps leave together
+      if (!got) break;
       tc_fence_after();
       const int64_t row = (int64_t)bm * BM + row_in_tile;
       const bool row_ok = row < args.M;
@@ -371,6 +558,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
+      if (AR) {
+        named_bar(1, 128);  // the tile is stored by all four warps
+        if (warp == 2 && lane == 0) {
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
+          mc_red_add_release(args.ar_mc_flags + 4ull * bm, 1);
+        }
+      }
     }
   }
 
@@ -417,7 +611,7 @@ bool tc_eligible(const void *A, const void *B, int64_t lda, int64_t ldb, int64_t
 int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t N, int64_t K, int64_t lda,
             int64_t ldb, int64_t ldc, int64_t batch, int64_t sA, int64_t sB, int64_t sC, int a_mn_major, int b_k_major,
             cudaStream_t st, int device, int epi = 0, int64_t n_half = 0, const void *res = nullptr, int64_t ldr = 0,
-            const Args *rope = nullptr) {
+            const Args *rope = nullptr, const SymmAr *ar = nullptr, const void *ar_res = nullptr) {
   if (M == 0 || N == 0 || batch == 0) return NKB_OK;
   if (K == 0) return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: K == 0 takes the strided path");
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(NKB_ERR_UNSUPPORTED, "gemm: dims exceed int32");
@@ -474,11 +668,27 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   if (tiles > INT32_MAX) return fail(NKB_ERR_UNSUPPORTED, "gemm: too many tiles");
   static bool attr_set[64] = {false};
   if (device >= 0 && device < 64 && !attr_set[device]) {
-    NKB_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    NKB_CUDA_TRY(
+        cudaFuncSetAttribute(gemm_bf16_tcgen05<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    NKB_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tcgen05<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     attr_set[device] = true;
   }
+  // one CTA per SM: every CTA of the fused kernel is resident at once, so its
+  // all-reduce warps can wait for tiles of other CTAs
   const int grid = (int)std::min<int64_t>(tiles, num_sms(device));
-  gemm_bf16_tcgen05<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, args);
+  if (ar) {
+    if (epi != 0 || c_f32 || batch != 1 || ldc != N || N % 8 || args.tiles_m > SYMM_AR_CHUNKS)
+      return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: fused all-reduce needs a dense bf16 C, one batch, no epilogue");
+    args.ar_mc = ar->mc_payload;
+    args.ar_flags = ar->flags;
+    args.ar_mc_flags = ar->mc_flags;
+    args.ar_res = static_cast<const __nv_bfloat16 *>(ar_res);
+    args.ar_rank = ar->rank;
+    args.ar_world = ar->world;
+    gemm_bf16_tcgen05<true><<<grid, AR_THREADS, SMEM_BYTES, st>>>(ma, mb, args);
+  } else {
+    gemm_bf16_tcgen05<false><<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, args);
+  }
   return launch_status("gemm_bf16_tcgen05");
 }
 
@@ -586,6 +796,38 @@ int tc_launch(const LaunchArgs &a) {
                  epi == 3 ? &rope : nullptr);
 }
 
+// "gemm_bf16_ar": ptrs A B C [R]; ints M N K lda ldb ldc batch sA sB sC c_f32 a_mn_major b_k_major slot.
+// C (bf16, dense) lies in the plan's symmetric region; afterwards it holds the
+// sum over the ranks of A @ B (+ R when given, R dense with N columns).  With a
+// bound symmetric region the reduction runs inside the GEMM kernel (flag slot
+// `slot`); otherwise the GEMM is followed by the communicator's all-reduce.
+int ar_check(const Step &s) {
+  if (s.ints.size() != 14 || (s.buf_ids.size() != 3 && s.buf_ids.size() != 4))
+    return fail(NKB_ERR_PLAN, "gemm_bf16_ar: bad parameters");
+  if (s.ints[13] < 0 || s.ints[13] >= SYMM_AR_SLOTS) return fail(NKB_ERR_PLAN, "gemm_bf16_ar: bad flag slot");
+  if (s.ints[10] != 0 || s.ints[6] != 1 || s.ints[5] != s.ints[1])
+    return fail(NKB_ERR_PLAN, "gemm_bf16_ar: C must be dense bf16, one batch");
+  return NKB_OK;
+}
+int ar_launch(const LaunchArgs &a) {
+  const auto &q = a.step->ints;
+  const void *res = a.step->buf_ids.size() == 4 ? a.ptrs[3] : nullptr;
+  const int64_t M = q[0], N = q[1];
+  const size_t count = (size_t)M * N;
+  SymmAr ar;
+  const bool fused = a.comm && M > 0 && N % 8 == 0 && (M + BM - 1) / BM <= SYMM_AR_CHUNKS &&
+                     ((reinterpret_cast<uintptr_t>(res) & 15) == 0) &&
+                     comm_symm_ar(a.comm, a.ptrs[2], count * 2, (int)q[13], &ar);
+  if (int s = gemm_tc(a.ptrs[0], a.ptrs[1], a.ptrs[2], 0, M, N, q[2], q[3], q[4], q[5], 1, q[7], q[8], q[9],
+                      (int)q[11], (int)q[12], a.stream, a.device, 0, 0, nullptr, 0, nullptr, fused ? &ar : nullptr,
+                      res))
+    return s;
+  if (fused) return NKB_OK;
+  if (!a.comm) return fail(NKB_ERR_STATE, "gemm_bf16_ar: no communicator is bound to the plan");
+  if (res) return comm_all_reduce_add(a.comm, a.ptrs[2], res, a.ptrs[2], count, NKB_BF16, a.stream);
+  return comm_all_reduce(a.comm, a.ptrs[2], a.ptrs[2], count, NKB_BF16, a.stream);
+}
+
 // "gemm_simt": ptrs A B C; ints adt bdt cdt M N K batch a_rs a_cs b_rs b_cs c_rs c_cs sA sB sC
 int simt_check(const Step &s) {
   if (s.buf_ids.size() != 3 || s.ints.size() != 16) return fail(NKB_ERR_PLAN, "gemm_simt: bad parameters");
@@ -620,6 +862,7 @@ int simt_launch(const LaunchArgs &a) {
 
 NKB_REGISTER_KERNEL("gemm_bf16", gemm::tc_launch, gemm::tc_check);
 NKB_REGISTER_KERNEL("gemm_simt", gemm::simt_launch, gemm::simt_check);
+NKB_REGISTER_KERNEL("gemm_bf16_ar", gemm::ar_launch, gemm::ar_check);
 
 // Device error flag of the bounded waits (read by nkb_check_device_error).
 int gemm_read_and_clear_error(int *flag) {

@@ -433,13 +433,19 @@ extern "C" int nkb_comm_init(const void *id, int rank, int world, int device, nk
   return NKB_OK;
 }
 
+// flags at the end of a bound region: the all-reduce barrier flags, then the
+// fused GEMM + all-reduce slots
+extern "C" size_t nkb_comm_symm_flag_bytes(void) {
+  return nkb::nvls_flag_bytes() + (size_t)nkb::SYMM_AR_SLOTS * nkb::SYMM_AR_SLOT_BYTES;
+}
+
 extern "C" int nkb_comm_bind_symm(nkb_comm comm, void *local, void *multicast, void *const *peers, int n_peers,
                                   size_t bytes) {
   if (int s = ensure_init()) return s;
   if (!comm || !local || !multicast || !peers) return fail(NKB_ERR_INVALID, "NULL argument");
   if (n_peers != comm->world) return fail(NKB_ERR_INVALID, "one peer pointer per rank is needed");
   if (comm->world > 16) return fail(NKB_ERR_UNSUPPORTED, "symmetric all-reduce supports at most 16 ranks");
-  const size_t fb = nkb::nvls_flag_bytes();
+  const size_t fb = nkb_comm_symm_flag_bytes();
   if (bytes <= fb + 16) return fail(NKB_ERR_INVALID, "symmetric region too small");
   if ((reinterpret_cast<uintptr_t>(local) | reinterpret_cast<uintptr_t>(multicast) | bytes) & 15)
     return fail(NKB_ERR_INVALID, "symmetric region must be 16-byte aligned");
@@ -465,7 +471,7 @@ extern "C" int nkb_comm_bind_symm(nkb_comm comm, void *local, void *multicast, v
   return NKB_OK;
 }
 
-extern "C" size_t nkb_comm_symm_flag_bytes(void) { return nkb::nvls_flag_bytes(); }
+
 
 extern "C" int nkb_comm_free(nkb_comm comm) {
   if (!comm) return NKB_OK;
@@ -482,6 +488,20 @@ static bool symm_payload(const nkb_comm_s *c, const void *p, size_t count, int d
   const char *lo = static_cast<const char *>(c->symm_local), *q = static_cast<const char *>(p);
   const size_t bytes = count * dtype_size(dtype);
   return q >= lo && q + bytes <= lo + c->symm_data && ((q - lo) & 15) == 0;
+}
+
+bool comm_symm_ar(void *comm, const void *payload, size_t bytes, int slot, SymmAr *out) {
+  const auto *c = static_cast<const nkb_comm_s *>(comm);
+  if (!c || c->world < 2 || !c->symm_local || slot < 0 || slot >= SYMM_AR_SLOTS) return false;
+  const char *lo = static_cast<const char *>(c->symm_local), *q = static_cast<const char *>(payload);
+  if (q < lo || q + bytes > lo + c->symm_data || ((q - lo) & 15)) return false;
+  const size_t flag_off = c->symm_data + nvls_flag_bytes() + (size_t)slot * SYMM_AR_SLOT_BYTES;
+  out->mc_payload = reinterpret_cast<uint64_t>(static_cast<char *>(c->symm_mc) + (q - lo));
+  out->flags = reinterpret_cast<uint32_t *>(static_cast<char *>(c->symm_local) + flag_off);
+  out->mc_flags = reinterpret_cast<uint64_t>(static_cast<char *>(c->symm_mc) + flag_off);
+  out->rank = c->rank;
+  out->world = c->world;
+  return true;
 }
 
 static int nvls_on(nkb_comm_s *c, void *buf, const void *res, void *dst, size_t count, int dtype, cudaStream_t stream) {

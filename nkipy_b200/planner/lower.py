@@ -802,6 +802,23 @@ class Lowering:
         dt = E.dt_code(xv.dtype)
         self.needs_comm = True
         add = self._residual_add(op)
+        gemm = self._fusable_gemm(xv)
+        if gemm is not None:
+            # the GEMM that produced the partial sum reduces it itself, tile
+            # row block by row block, as its tiles are stored
+            gemm.kernel = "gemm_bf16_ar"
+            gemm.ints.append(0)  # flag slot (launches of the plan are ordered, so they share one)
+            gemm.note += " +all-reduce"
+            if add is not None:
+                add_op, other = add
+                rv = self.materialize(self.get(other), dense=True)
+                gemm.bufs.append(self.bref(rv))
+                gemm.note += " +residual"
+                self.vals[("o", add_op.id)] = xv
+                self.fused.add(add_op.id)
+                return
+            self.vals[("o", op.id)] = xv
+            return
         if add is not None:
             add_op, other = add
             rv = self.materialize(self.get(other), dense=True)
@@ -813,6 +830,21 @@ class Lowering:
             return
         self.step("allreduce", [self.bref(xv), self.bref(xv)], [xv.size, dt], note=f"{xv.size} in place")
         self.vals[("o", op.id)] = xv
+
+    def _fusable_gemm(self, xv):
+        """The step that just wrote ``xv`` when it is a plain bf16 GEMM whose
+        dense output is exactly ``xv`` (one batch, no epilogue); else None."""
+        if not self.steps:
+            return None
+        s = self.steps[-1]
+        if s.kernel != "gemm_bf16" or len(s.ints) != 13 or len(s.bufs) != 3:
+            return None
+        M, N, _K, _lda, _ldb, ldc, batch = s.ints[:7]
+        if s.bufs[2] != self.bref(xv) or s.ints[10] != 0 or batch != 1 or ldc != N or N % 8:
+            return None
+        if np.dtype(xv.dtype).itemsize != 2 or xv.size != M * N:
+            return None
+        return s
 
     def _residual_add(self, op):
         """(add op, other operand) when the all-reduce result's only use is an

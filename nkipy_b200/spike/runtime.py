@@ -155,13 +155,15 @@ def _bind_symmetric(comm, rank: int, world: int, device: int, need: int) -> bool
     The region is a PyTorch symmetric-memory allocation (every rank maps every
     other rank's copy, plus an NVLink multicast object over all of them); all
     ranks take the same decision, and a rank without multicast support makes
-    every rank keep NCCL.  NKB_SYMM: "auto" (default) binds it from 4 ranks up,
-    where reducing inside NVSwitch beats NCCL's ring on B200 (at 2 ranks NCCL
-    is faster); "force" binds it at any size; "0" never.  Regions are never
-    freed: plans captured into CUDA graphs keep their addresses.
+    every rank keep NCCL.  NKB_SYMM: "auto" (default) and "force" bind it at
+    any world size ("force" fails loudly when it cannot); "0" never.  With a
+    region bound, a row-parallel GEMM reduces its output inside its own kernel
+    (multimem through NVSwitch) while its later tiles compute, which beats the
+    GEMM followed by NCCL's all-reduce from 2 ranks up on B200.  Regions are
+    never freed: plans captured into CUDA graphs keep their addresses.
     """
     mode = os.environ.get("NKB_SYMM", "auto")
-    if need <= 0 or mode == "0" or (mode == "auto" and world < 4):
+    if need <= 0 or mode == "0":
         return False
     entry = _SYMM.get((world, rank))
     if entry is not None and entry[0] >= need:

@@ -138,20 +138,31 @@ def test_layer_plans(monkeypatch):
     assert any("+residual" in n for n in notes)
 
 
-def test_layer_tp2_has_two_allreduces():
+def test_layer_tp2_fuses_allreduces_into_gemms():
     s = W.LayerShape(batch=1, seq=64, hidden=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=512)
     full = W.layer_weights(s, seed=0)
     shard = W.shard_layer_weights(full, s, 1, 2)
     args, kw = W.layer_args(np.zeros((1, 64, 256), BF16), shard, s, 2)
     p = lower(NKIPyKernel.trace(W.llama_decoder_layer_kernel).specialize(*args, **kw), world=2)
     kc = p.kernel_counts()
-    assert "ew" not in kc and any("+rope" in s.note for s in p.steps)
-    # one all-reduce per block: the second carries the final residual add
-    assert kc["allreduce"] == 1 and kc["allreduce_add"] == 1 and p.needs_comm
-    assert p.steps[-1].kernel == "allreduce_add"
-    # both partial sums are written by their GEMM straight into the symmetric region
+    assert any("+rope" in s.note for s in p.steps) and p.needs_comm
+    # each row-parallel GEMM reduces its own partial sum; the second also adds the residual
+    assert kc["gemm_bf16_ar"] == 2 and "allreduce" not in kc and "allreduce_add" not in kc
+    ar = [s for s in p.steps if s.kernel == "gemm_bf16_ar"]
+    assert [len(s.bufs) for s in ar] == [3, 4] and all(len(s.ints) == 14 for s in ar)
+    # both partial sums live in the symmetric region; the layer output is copied out of it
     symm = [i for i, b in enumerate(p.buffers) if b.kind == "symm"]
-    assert len(symm) == 2 and p.symm >= sum(p.buffers[i].nbytes for i in symm)
-    for i in symm:
-        assert any(s.kernel == "gemm_bf16" and s.bufs[2][0] == i for s in p.steps)
+    assert sorted(s.bufs[2][0] for s in ar) == symm and p.symm >= sum(p.buffers[i].nbytes for i in symm)
+    assert kc.get("ew") == 1 and p.steps[-1].kernel == "ew" and p.steps[-1].bufs[1][0] == ar[1].bufs[2][0]
     assert "symm %d" % p.symm in p.to_text()
+
+
+def test_allreduce_without_gemm_stays_a_step():
+    from nkipy_b200.core.ops import collectives as cc
+
+    def k(x, r):
+        return r + cc.all_reduce(x * 2.0, replica_groups=[[0, 1]], reduce_op=np.add)
+
+    x = np.zeros((64, 256), BF16)
+    p = lower(NKIPyKernel.trace(k).specialize(x, x), world=2)
+    assert p.kernel_counts().get("allreduce_add") == 1 and "gemm_bf16_ar" not in p.kernel_counts()

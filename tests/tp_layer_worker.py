@@ -5,9 +5,11 @@ through DeviceKernel (all-reduce inside the plan: inside NVSwitch when a
 symmetric region could be bound, NCCL otherwise, or NCCL only with
 NKB_SYMM=0) and rank 0 compares the result with the TP=1 oracle.  Before
 that, the plan's communicator all-reduces a buffer of small integers whose sum
-is exact in bf16.  Exit status 0 = both checks pass.
+is exact in bf16, and a GEMM + all-reduce + residual plan on small integers
+is compared exactly with NumPy.  Exit status 0 = all checks pass.
 """
 
+import ctypes
 import datetime
 import os
 import sys
@@ -20,13 +22,12 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 from nkipy_b200 import workloads as W  # noqa: E402
+from nkipy_b200.core.ops import collectives as cc  # noqa: E402
 
 
 def check_all_reduce(model, rank, world):
     """The communicator bound to the plan sums exactly representable bf16 values
     (in the bound symmetric region when there is one, so inside NVSwitch)."""
-    import ctypes
-
     from nkipy_b200.spike import _nkb
     from nkipy_b200.spike import runtime as R
 
@@ -53,6 +54,47 @@ def check_all_reduce(model, rank, world):
     return ok
 
 
+def gemm_all_reduce_kernel(a, b, r, world=2):
+    """A row-parallel GEMM, its all-reduce and the residual add after it."""
+    p = a @ b
+    s = cc.all_reduce(p, replica_groups=[list(range(world))], reduce_op=np.add)
+    return r + s
+
+
+def gemm_ar_inputs(rank, M=1000, K=384, N=520):
+    """Small integers whose products, sums over the ranks and residual add are exact in bf16."""
+    g = np.random.default_rng(100 + rank)
+    a = g.integers(-1, 2, (M, K)) * (g.random((M, K)) < 1 / 16)
+    b = g.integers(-1, 2, (K, N))
+    r = np.random.default_rng(99).integers(-32, 33, (M, N))
+    return [x.astype(np.float32).astype(W.bfloat16) for x in (a, b, r)]
+
+
+def check_gemm_all_reduce(rank, world):
+    """gemm_bf16_ar (fused in the GEMM when a symmetric region is bound) over a
+    ragged shape: 8 row blocks, the last of 104 rows, and a partial last column tile."""
+    from nkipy_b200.runtime import DeviceKernel, DeviceTensor
+
+    a, b, r = gemm_ar_inputs(rank)
+    k = DeviceKernel.compile_and_load(gemm_all_reduce_kernel, a, b, r, world=world, name="tp_gemm_ar", is_spmd=False,
+                                      cc_enabled=True, rank_id=rank, world_size=world)
+    kinds = k.model_ref.io["kernels"]
+    names = [t["name"] for t in k.model_ref.io["inputs"]]
+    outs = k(inputs={n: DeviceTensor.from_numpy(x, name=n) for n, x in zip(names, (a, b, r))})
+    got = next(iter(outs.values())).numpy().astype(np.float32)
+    want = r.astype(np.float32).copy()
+    for q in range(world):
+        aq, bq, _ = gemm_ar_inputs(q)
+        want += aq.astype(np.float32) @ bq.astype(np.float32)
+    flag = ctypes.c_int()
+    from nkipy_b200.spike import _nkb
+
+    _nkb.call("nkb_device_error", ctypes.byref(flag))
+    ok = kinds.get("gemm_bf16_ar") == 1 and bool(np.array_equal(got, want)) and flag.value == 0
+    print(f"rank {rank}: gemm + all-reduce + residual exact={ok} ({kinds})", flush=True)
+    return ok
+
+
 def local_device():
     return int(os.environ.get("LOCAL_RANK", os.environ["RANK"]))
 
@@ -75,6 +117,7 @@ def main():
                                       cc_enabled=True, rank_id=rank, world_size=world, **kw)
     model = k.model_ref
     ok = check_all_reduce(model, rank, world)
+    ok = check_gemm_all_reduce(rank, world) and ok
     names = [t["name"] for t in model.io["inputs"]]
     ins = {n: DeviceTensor.from_numpy(a, name=n) for n, a in zip(names, args)}
     outs = k(inputs=ins)
