@@ -64,7 +64,7 @@ def gemm_all_reduce_kernel(a, b, r, world=2):
 def gemm_ar_inputs(rank, M=1000, K=384, N=520):
     """Small integers whose products, sums over the ranks and residual add are exact in bf16."""
     g = np.random.default_rng(100 + rank)
-    a = g.integers(-1, 2, (M, K)) * (g.random((M, K)) < 1 / 16)
+    a = g.integers(-1, 2, (M, K)) * (g.random((M, K)) < 1 / 64)
     b = g.integers(-1, 2, (K, N))
     r = np.random.default_rng(99).integers(-32, 33, (M, N))
     return [x.astype(np.float32).astype(W.bfloat16) for x in (a, b, r)]
@@ -108,7 +108,8 @@ def main():
     from nkipy_b200.runtime import DeviceKernel, DeviceTensor
     from oracle import numpy_ref as O
 
-    s = W.LayerShape(batch=2, seq=128, hidden=512, n_heads=8, n_kv_heads=4, head_dim=64, ffn=1024)
+    kv = max(4, world)  # whole kv heads per rank
+    s = W.LayerShape(batch=2, seq=128, hidden=128 * kv, n_heads=2 * kv, n_kv_heads=kv, head_dim=64, ffn=256 * kv)
     full = W.layer_weights(s, seed=5)
     x = np.random.default_rng(6).standard_normal((s.batch, s.seq, s.hidden), dtype=np.float32).astype(W.bfloat16)
     shard = W.shard_layer_weights(full, s, rank, world)
