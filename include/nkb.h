@@ -169,6 +169,27 @@ NKB_API int nkb_gemm_bf16(const void *A, const void *B, void *C, int c_dtype, in
                   int64_t lda, int64_t ldb, int64_t ldc, int64_t batch, int64_t sA, int64_t sB, int64_t sC,
                   void *stream);
 
+/* Top-k along the last axis of dense (rows, cols) x: values (rows, k) in x's
+ * dtype, largest first, and their column indices (rows, k) as uint32; ties
+ * keep the lower column first.  The reference's topk op (core/ops/nn.py:65-152,
+ * HLO TopK largest=true; is_ascend traces as negate -> topk -> negate), used
+ * by greedy sampling (examples/models/qwen3/kernels/sampling.py:113-147). */
+NKB_API int nkb_topk_rows(const void *x, int dtype, void *values, uint32_t *indices, int64_t rows, int64_t cols,
+                          int64_t k, void *stream);
+
+/* All-gather / reduce-scatter (sum) of `count` elements per rank on the
+ * leading axis, rank-major (core/ops/collectives.py:34-53,148-178; HLO
+ * all-gather / reduce-scatter run by NRT in the reference).  `send` holds
+ * this rank's count elements (all-gather) or world * count (reduce-scatter),
+ * `recv` the other size.  NCCL. */
+NKB_API int nkb_comm_all_gather(nkb_comm comm, const void *send, void *recv, size_t count, int dtype, void *stream);
+NKB_API int nkb_comm_reduce_scatter(nkb_comm comm, const void *send, void *recv, size_t count, int dtype,
+                                    void *stream);
+/* All-to-all (core/ops/collectives.py:217-233): send and recv hold world
+ * blocks of `count` elements, rank-major; block j of send goes to rank j and
+ * block i of recv comes from rank i.  NCCL grouped send/recv. */
+NKB_API int nkb_comm_all_to_all(nkb_comm comm, const void *send, void *recv, size_t count, int dtype, void *stream);
+
 /* Allocation-free chunked causal linear attention.  No counterpart in the
  * reference: it serves callers that cannot allocate device memory when they
  * run this kernel, such as a host that has reserved the whole GPU for its own

@@ -141,6 +141,13 @@ struct SymmAr {
 // symmetric data area (16-byte aligned) and slot is valid; false otherwise.
 bool comm_symm_ar(void *comm, const void *payload, size_t bytes, int slot, SymmAr *out);
 
+// NCCL all-gather (recv = world * count, rank-major) and sum reduce-scatter
+// (send = world * count); count is per rank.
+int comm_all_gather(void *comm, const void *send, void *recv, size_t count, int dtype, cudaStream_t stream);
+int comm_reduce_scatter(void *comm, const void *send, void *recv, size_t count, int dtype, cudaStream_t stream);
+// all-to-all of (world, count) rank-major blocks (count per block)
+int comm_all_to_all(void *comm, const void *send, void *recv, size_t count, int dtype, cudaStream_t stream);
+
 // dst = res + all-reduce(buf) (buf keeps the sum)
 int comm_all_reduce_add(void *comm, void *buf, const void *res, void *dst, size_t count, int dtype,
                         cudaStream_t stream);

@@ -262,8 +262,27 @@ int ara_launch(const LaunchArgs &a) {
                              a.stream);
 }
 
+// "allgather" / "reducescatter" / "alltoall": ptrs send recv; ints count (per rank / block) dtype
+int coll_check(const Step &s) {
+  if (s.buf_ids.size() != 2 || s.ints.size() != 2) return fail(NKB_ERR_PLAN, "allgather/reducescatter: bad parameters");
+  return NKB_OK;
+}
+int ag_launch(const LaunchArgs &a) {
+  return comm_all_gather(a.comm, a.ptrs[0], a.ptrs[1], (size_t)a.step->ints[0], (int)a.step->ints[1], a.stream);
+}
+int rs_launch(const LaunchArgs &a) {
+  return comm_reduce_scatter(a.comm, a.ptrs[0], a.ptrs[1], (size_t)a.step->ints[0], (int)a.step->ints[1], a.stream);
+}
+
+int a2a_launch(const LaunchArgs &a) {
+  return comm_all_to_all(a.comm, a.ptrs[0], a.ptrs[1], (size_t)a.step->ints[0], (int)a.step->ints[1], a.stream);
+}
+
 }  // namespace idx
 
+NKB_REGISTER_KERNEL("alltoall", idx::a2a_launch, idx::coll_check);
+NKB_REGISTER_KERNEL("allgather", idx::ag_launch, idx::coll_check);
+NKB_REGISTER_KERNEL("reducescatter", idx::rs_launch, idx::coll_check);
 NKB_REGISTER_KERNEL("take", idx::take_launch, idx::take_check);
 NKB_REGISTER_KERNEL("gather_pts", idx::pts_launch, idx::pts_check);
 NKB_REGISTER_KERNEL("pad", idx::pad_launch, idx::pad_check);

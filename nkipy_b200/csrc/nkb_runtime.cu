@@ -344,6 +344,12 @@ struct NcclApi {
   ncclResult_t_ (*CommInitRank)(ncclComm_t_ *, int, ncclUniqueId_, int) = nullptr;
   ncclResult_t_ (*CommDestroy)(ncclComm_t_) = nullptr;
   ncclResult_t_ (*AllReduce)(const void *, void *, size_t, int, int, ncclComm_t_, cudaStream_t) = nullptr;
+  ncclResult_t_ (*AllGather)(const void *, void *, size_t, int, ncclComm_t_, cudaStream_t) = nullptr;
+  ncclResult_t_ (*ReduceScatter)(const void *, void *, size_t, int, int, ncclComm_t_, cudaStream_t) = nullptr;
+  ncclResult_t_ (*Send)(const void *, size_t, int, int, ncclComm_t_, cudaStream_t) = nullptr;
+  ncclResult_t_ (*Recv)(void *, size_t, int, int, ncclComm_t_, cudaStream_t) = nullptr;
+  ncclResult_t_ (*GroupStart)() = nullptr;
+  ncclResult_t_ (*GroupEnd)() = nullptr;
   const char *(*GetErrorString)(ncclResult_t_) = nullptr;
   bool loaded = false;
 };
@@ -364,6 +370,12 @@ int load_nccl() {
   g_nccl.CommDestroy = reinterpret_cast<decltype(g_nccl.CommDestroy)>(dlsym(g_nccl.handle, "ncclCommDestroy"));
   g_nccl.AllReduce = reinterpret_cast<decltype(g_nccl.AllReduce)>(dlsym(g_nccl.handle, "ncclAllReduce"));
   g_nccl.GetErrorString = reinterpret_cast<decltype(g_nccl.GetErrorString)>(dlsym(g_nccl.handle, "ncclGetErrorString"));
+  g_nccl.AllGather = reinterpret_cast<decltype(g_nccl.AllGather)>(dlsym(g_nccl.handle, "ncclAllGather"));
+  g_nccl.ReduceScatter = reinterpret_cast<decltype(g_nccl.ReduceScatter)>(dlsym(g_nccl.handle, "ncclReduceScatter"));
+  g_nccl.Send = reinterpret_cast<decltype(g_nccl.Send)>(dlsym(g_nccl.handle, "ncclSend"));
+  g_nccl.Recv = reinterpret_cast<decltype(g_nccl.Recv)>(dlsym(g_nccl.handle, "ncclRecv"));
+  g_nccl.GroupStart = reinterpret_cast<decltype(g_nccl.GroupStart)>(dlsym(g_nccl.handle, "ncclGroupStart"));
+  g_nccl.GroupEnd = reinterpret_cast<decltype(g_nccl.GroupEnd)>(dlsym(g_nccl.handle, "ncclGroupEnd"));
   if (!g_nccl.GetUniqueId || !g_nccl.CommInitRank || !g_nccl.CommDestroy || !g_nccl.AllReduce)
     return fail(NKB_ERR_NCCL, "NCCL library lacks required symbols");
   g_nccl.loaded = true;
@@ -526,6 +538,61 @@ int comm_all_reduce(void *comm, const void *src, void *dst, size_t count, int dt
   return NKB_OK;
 }
 
+// recv (world * count) = the ranks' send (count each), rank-major
+int comm_all_gather(void *comm, const void *send, void *recv, size_t count, int dtype, cudaStream_t stream) {
+  auto *c = static_cast<nkb_comm_s *>(comm);
+  if (!c) return fail(NKB_ERR_STATE, "all-gather step but no communicator is bound to the plan");
+  const size_t bytes = count * dtype_size(dtype);
+  if (c->world == 1) {
+    if (send != recv && bytes) NKB_CUDA_TRY(cudaMemcpyAsync(recv, send, bytes, cudaMemcpyDeviceToDevice, stream));
+    return NKB_OK;
+  }
+  if (!g_nccl.AllGather) return fail(NKB_ERR_NCCL, "NCCL library lacks ncclAllGather");
+  // NCCL takes bytes as uint8 so every dtype (bool, fp8 included) gathers
+  int r = g_nccl.AllGather(send, recv, bytes, /*ncclUint8*/ 1, c->comm, stream);
+  if (r) return fail(NKB_ERR_NCCL, std::string("ncclAllGather: ") + g_nccl.GetErrorString(r));
+  return NKB_OK;
+}
+
+// recv (count) = sum over the ranks of their send block `rank` (send holds world * count)
+int comm_reduce_scatter(void *comm, const void *send, void *recv, size_t count, int dtype, cudaStream_t stream) {
+  auto *c = static_cast<nkb_comm_s *>(comm);
+  if (!c) return fail(NKB_ERR_STATE, "reduce-scatter step but no communicator is bound to the plan");
+  int nd = nccl_dtype(dtype);
+  if (nd < 0) return fail(NKB_ERR_UNSUPPORTED, "dtype not supported by NCCL reduce-scatter");
+  if (c->world == 1) {
+    if (send != recv && count)
+      NKB_CUDA_TRY(cudaMemcpyAsync(recv, send, count * dtype_size(dtype), cudaMemcpyDeviceToDevice, stream));
+    return NKB_OK;
+  }
+  if (!g_nccl.ReduceScatter) return fail(NKB_ERR_NCCL, "NCCL library lacks ncclReduceScatter");
+  int r = g_nccl.ReduceScatter(send, recv, count, nd, /*ncclSum*/ 0, c->comm, stream);
+  if (r) return fail(NKB_ERR_NCCL, std::string("ncclReduceScatter: ") + g_nccl.GetErrorString(r));
+  return NKB_OK;
+}
+
+// send and recv are (world, count) rank-major: block j of send goes to rank j,
+// block i of recv comes from rank i
+int comm_all_to_all(void *comm, const void *send, void *recv, size_t count, int dtype, cudaStream_t stream) {
+  auto *c = static_cast<nkb_comm_s *>(comm);
+  if (!c) return fail(NKB_ERR_STATE, "all-to-all step but no communicator is bound to the plan");
+  const size_t bytes = count * dtype_size(dtype);
+  if (c->world == 1) {
+    if (send != recv && bytes) NKB_CUDA_TRY(cudaMemcpyAsync(recv, send, bytes, cudaMemcpyDeviceToDevice, stream));
+    return NKB_OK;
+  }
+  if (!g_nccl.Send || !g_nccl.Recv || !g_nccl.GroupStart || !g_nccl.GroupEnd)
+    return fail(NKB_ERR_NCCL, "NCCL library lacks point-to-point calls");
+  int r = g_nccl.GroupStart();
+  for (int p = 0; !r && p < c->world; ++p) {
+    r = g_nccl.Send(static_cast<const char *>(send) + p * bytes, bytes, /*ncclUint8*/ 1, p, c->comm, stream);
+    if (!r) r = g_nccl.Recv(static_cast<char *>(recv) + p * bytes, bytes, /*ncclUint8*/ 1, p, c->comm, stream);
+  }
+  int r2 = g_nccl.GroupEnd();
+  if (r || r2) return fail(NKB_ERR_NCCL, std::string("all-to-all: ") + g_nccl.GetErrorString(r ? r : r2));
+  return NKB_OK;
+}
+
 // dst = res + (sum over the ranks of buf); buf holds the sum afterwards
 int comm_all_reduce_add(void *comm, void *buf, const void *res, void *dst, size_t count, int dtype,
                         cudaStream_t stream) {
@@ -543,6 +610,28 @@ extern "C" int nkb_comm_all_reduce(nkb_comm comm, nkb_buf buf, size_t count, int
   if (count * nkb::dtype_size(dtype) > buf->bytes) return fail(NKB_ERR_INVALID, "all-reduce count exceeds buffer");
   return nkb::comm_all_reduce(comm, buf->ptr, buf->ptr, count, dtype,
                               stream ? static_cast<cudaStream_t>(stream) : g_rt.stream);
+}
+
+extern "C" int nkb_comm_all_gather(nkb_comm comm, const void *send, void *recv, size_t count, int dtype,
+                                   void *stream) {
+  if (int s = ensure_init()) return s;
+  if (!comm) return fail(NKB_ERR_STATE, "no communicator");
+  return nkb::comm_all_gather(comm, send, recv, count, dtype, stream ? static_cast<cudaStream_t>(stream) : g_rt.stream);
+}
+
+extern "C" int nkb_comm_all_to_all(nkb_comm comm, const void *send, void *recv, size_t count, int dtype,
+                                   void *stream) {
+  if (int s = ensure_init()) return s;
+  if (!comm) return fail(NKB_ERR_STATE, "no communicator");
+  return nkb::comm_all_to_all(comm, send, recv, count, dtype, stream ? static_cast<cudaStream_t>(stream) : g_rt.stream);
+}
+
+extern "C" int nkb_comm_reduce_scatter(nkb_comm comm, const void *send, void *recv, size_t count, int dtype,
+                                       void *stream) {
+  if (int s = ensure_init()) return s;
+  if (!comm) return fail(NKB_ERR_STATE, "no communicator");
+  return nkb::comm_reduce_scatter(comm, send, recv, count, dtype,
+                                  stream ? static_cast<cudaStream_t>(stream) : g_rt.stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -75,6 +75,11 @@ class Lowering:
         self.fused = set()  # ids of ops already lowered as part of an earlier step
         self.alias_ops: Dict[int, object] = {}  # op id -> op whose value it takes (rotated in place)
         self.needs_comm = False
+        self.pos = {op.id: i for i, op in enumerate(graph.operations)}
+        self.cur = -1  # position of the op being lowered
+        self.mutated_params = {a.param_index for a in graph.aliases}
+        self.updatable = set()  # tmp buffers written by a scatter / update-slice chain
+        self.tuples: Dict[int, tuple] = {}  # op id -> views of a tuple-valued node
 
     # ------------------------------------------------------------ buffers
     def new_buf(self, kind, index, nbytes) -> int:
@@ -110,6 +115,66 @@ class Lowering:
         if out is None:
             out = self.tmp_view(val.shape, val.dtype)
         self.emit_ew(self.expr_of(val), out)
+        return out
+
+    # ------------------------------------------------------------ in-place updates
+    def _whole(self, v) -> bool:
+        return (
+            isinstance(v, V.View) and v.offset == 0 and v.is_dense()
+            and self.buffers[v.buf].nbytes == max(1, _nbytes(v.shape, v.dtype))
+        )
+
+    def _refs_buf(self, val, b) -> bool:
+        if isinstance(val, V.View):
+            return val.buf == b
+        return any(l.view.buf == b for l in val.leaves())
+
+    def _pending(self, key) -> bool:
+        """Is the value under ``key`` still read by an op after the current one?"""
+        if key in self.result_keys:
+            return True
+        return any(self.pos[c.id] > self.cur for c in self.consumers.get(key, ()))
+
+    def mutable_base(self, t, op) -> V.View:
+        """A whole dense buffer holding the value of ``t`` that ``op`` (a scatter or
+        dynamic-update-slice) may overwrite.
+
+        The reference traces ``a[i] = v`` with a tensor ``i`` as ``copy(a)`` and a
+        scatter (``core/ops/indexing.py:359-433``), and ``a[0:n] = v`` as a
+        dynamic-update-slice of ``a`` itself (``indexing.py:692-760``,
+        ``core/tensor.py:627-815``).  With ``t`` (or the tensor it copies):
+
+        * an update result read by nothing else: the update runs in place in that
+          buffer (successive ``a[...] = v`` cost no copies);
+        * a parameter that the kernel mutates (its output is
+          bound to the ``<name>.must_alias_input`` input): a ``copy_bytes`` step,
+          which does nothing when the caller binds the same device memory to both
+          (the reference's KV-cache decode, ``examples/models/qwen3/qwen3.py:289-301``).
+          Values still to be read that depend on the parameter's old contents
+          are materialised first, since the update may overwrite them;
+        * otherwise: a copy into a new buffer.
+        """
+        prev = t
+        src = t.source_op
+        if src is not None and src.op_name == "copy" and self.uses.get(tkey(t), 0) == 1 and tkey(t) not in self.result_keys:
+            prev = src.operands[0]
+        pv = self.get(prev)
+        sole = self.uses.get(tkey(prev), 0) == 1 and tkey(prev) not in self.result_keys
+        if self._whole(pv) and self.buffers[pv.buf].kind == "tmp" and pv.buf in self.updatable and sole:
+            return pv.with_(shape=tuple(op.result_shape), strides=V.dense_strides(op.result_shape))
+        if self._whole(pv) and self.buffers[pv.buf].kind == "in" and self.buffers[pv.buf].index in self.mutated_params:
+            b = pv.buf
+            for key, val in list(self.vals.items()):
+                if self._refs_buf(val, b) and self._pending(key):
+                    self.vals[key] = self.materialize(val, out=self.tmp_view(val.shape, val.dtype))
+            out = self.tmp_view(op.result_shape, op.result_dtype)
+            self.step("copy_bytes", [self.bref(pv), self.bref(out)], [max(1, _nbytes(t.shape, t.dtype))],
+                      note="mutated parameter (no-op when bound in place)")
+            self.updatable.add(out.buf)
+            return out
+        out = self.tmp_view(op.result_shape, op.result_dtype)
+        self.emit_ew(self.expr_of(self.get(t)), out)
+        self.updatable.add(out.buf)
         return out
 
     def emit_ew(self, expr: E.Expr, out: V.View, depth=0):
@@ -151,6 +216,7 @@ class Lowering:
             b = self.new_buf("in", p.parameter_id, max(1, spec.nbytes))
             self.vals[("p", p.parameter_id)] = V.View(b, 0, tuple(p.shape), V.dense_strides(p.shape), np.dtype(p.dtype))
         for op in g.operations:
+            self.cur = self.pos[op.id]
             if op.id in self.fused:
                 continue
             if op.id in self.alias_ops:
@@ -700,8 +766,7 @@ class Lowering:
             if sop is None or sop.op_name != "constant":
                 raise NotImplementedError("dynamic-update-slice with run-time start indices")
             starts.append(int(np.asarray(sop.attributes["value"]).reshape(()).item()))
-        out = self.tmp_view(op.result_shape, op.result_dtype)
-        self.emit_ew(self.expr_of(self.get(base)), out)
+        out = self.mutable_base(base, op)
         starts = [max(0, min(s, int(n) - int(u))) for s, n, u in zip(starts, base.shape, upd.shape)]
         off, st = V.slice_view(out.offset, out.strides, starts, [1] * len(starts))
         self.emit_ew(self.expr_of(self.get(upd)), out.with_(offset=off, shape=tuple(upd.shape), strides=st))
@@ -740,32 +805,166 @@ class Lowering:
         a = op.attributes
         if a.get("update_computation", "assign") != "assign":
             raise NotImplementedError("scatter with a combiner")
-        out = self.tmp_view(op.result_shape, op.result_dtype)
-        self.emit_ew(self.expr_of(self.get(x)), out)
         iv = self.materialize(self.get(ind), dense=True)
-        uv = self.materialize(self.get(upd), dense=True)
+        ue = self.get(upd)
+        if np.dtype(upd.dtype) != np.dtype(op.result_dtype):
+            # NumPy casts the assigned values to the array's dtype; the kernels copy bytes
+            ue = E.op("convert", [self.expr_of(ue)], tuple(upd.shape), np.dtype(op.result_dtype))
+        uv = self.materialize(ue, dense=True)
         r = len(x.shape)
         es = np.dtype(op.result_dtype).itemsize
         ins = list(a["inserted_window_dims"])
-        if len(ins) == 1 and list(a["update_window_dims"]) == [d for d in range(r) if d != ins[0]]:
+        xs, us = tuple(int(d) for d in x.shape), tuple(int(d) for d in upd.shape)
+        window = (
+            len(ins) == 1
+            and list(a["update_window_dims"]) == [d for d in range(r) if d != ins[0]]
+            and len(us) == r
+            and len(ind.shape) <= 1
+            and us[: ins[0]] == xs[: ins[0]]
+            and us[ins[0] + 1 :] == xs[ins[0] + 1 :]
+        )
+        points = not a["update_window_dims"] and ins == list(range(r))
+        if not (window or points):
+            raise NotImplementedError("scatter form")
+        out = self.mutable_base(x, op)
+        if window:
+            # whole windows along one axis: updates are (pre, n_idx, post), dense
             ax = ins[0]
             pre = int(np.prod(x.shape[:ax])) if ax else 1
             post = int(np.prod(x.shape[ax + 1 :])) if ax + 1 < r else 1
             n_idx = int(np.prod(ind.shape)) if len(ind.shape) else 1
-            if pre != 1:
-                raise NotImplementedError("window scatter on an inner axis")
             self.step(
                 "scatter_rows",
                 [self.bref(out), self.bref(iv), self.bref(uv)],
                 [E.dt_code(iv.dtype), pre, int(x.shape[ax]), post * es, n_idx],
             )
-        elif not a["update_window_dims"] and ins == list(range(r)):
+        else:
             n = int(np.prod(upd.shape)) if len(upd.shape) else 1
             ints = [E.dt_code(iv.dtype), r, es, n] + [int(s) for s in x.shape] + list(V.dense_strides(x.shape))
             self.step("scatter_pts", [self.bref(out), self.bref(iv), self.bref(uv)], ints)
-        else:
-            raise NotImplementedError("scatter form")
         self.vals[("o", op.id)] = out
+
+    def op_topk(self, op):
+        """Last-axis top-k (``core/ops/nn.py:65-152``): one ``topk_rows`` launch
+        writing the values and the uint32 indices; the two ``get-tuple-element``
+        nodes that follow take them."""
+        x = op.operands[0]
+        k = int(op.attributes["k"])
+        if not op.attributes.get("largest", True):
+            raise NotImplementedError("topk with largest = false")
+        xv, rows, cols = self.dense_rows(x)
+        shape = tuple(op.result_shape)
+        vals = self.tmp_view(shape, x.dtype)
+        idx = self.tmp_view(shape, np.uint32)
+        self.step("topk_rows", [self.bref(xv), self.bref(vals), self.bref(idx)],
+                  [rows, cols, k, E.dt_code(xv.dtype)], note=f"{rows}x{cols} k={k}")
+        self.tuples[op.id] = (vals, idx)
+
+    def op_get_tuple_element(self, op):
+        src = op.operands[0].source_op
+        if src is None or src.id not in self.tuples:
+            raise NotImplementedError("get-tuple-element of a node without a tuple lowering")
+        self.vals[("o", op.id)] = self.tuples[src.id][int(op.attributes["tuple_index"])]
+
+    def _gather_dim(self, op, key):
+        groups = op.attributes.get("replica_groups") or [[0]]
+        if len(groups) != 1 or len(groups[0]) != self.world:
+            raise ValueError(
+                f"{op.op_name} over groups {groups} but the kernel is planned for world size {self.world}"
+            )
+        return int(op.attributes[key]) % max(1, len(op.operands[0].shape))
+
+    def op_all_gather(self, op):
+        """Concatenation of every rank's tensor along ``all_gather_dim``
+        (``core/ops/collectives.py:34-53``): NCCL gathers rank-major into a
+        (world, *shape) buffer; the concatenation is a view of it (a move to
+        the gather axis when it is not the leading one)."""
+        x = op.operands[0]
+        d = self._gather_dim(op, "all_gather_dim")
+        if self.world == 1:
+            self.put(op, self.get(x))
+            return
+        xv = self.materialize(self.get(x), dense=True)
+        shp = tuple(int(s) for s in x.shape)
+        g = self.tmp_view((self.world,) + shp, x.dtype)
+        self.needs_comm = True
+        self.step("allgather", [self.bref(xv), self.bref(g)], [xv.size, E.dt_code(xv.dtype)],
+                  note=f"{xv.size} x {self.world}")
+        self._concat_ranks(op, g, d)
+
+    def _rank_blocks(self, x, d):
+        """``x`` split into world blocks along axis ``d``, laid out rank-major as
+        a dense (world, *block) buffer (a view when ``d`` is the leading axis)."""
+        shp = tuple(int(s) for s in x.shape)
+        if shp[d] % self.world:
+            raise ValueError(f"axis {d} of {shp} does not split over {self.world} ranks")
+        blk = shp[:d] + (shp[d] // self.world,) + shp[d + 1:]
+        src = self.get(x)
+        if d == 0:
+            return self.materialize(src, dense=True), blk
+        split = shp[:d] + (self.world, shp[d] // self.world) + shp[d + 1:]
+        perm = [d] + [i for i in range(len(split)) if i != d]
+        e = E.t_reshape(self.expr_of(src), split)
+        if e is None:
+            m = self.materialize(src)
+            e = E.leaf(m.with_(shape=split, strides=V.dense_strides(split)))
+        sv = self.tmp_view((self.world,) + blk, x.dtype)
+        self.emit_ew(E.t_transpose(e, perm), sv)
+        return sv, blk
+
+    def _concat_ranks(self, op, g, d):
+        """Bind a (world, *block) buffer as the concatenation of its blocks along ``d``."""
+        n = len(g.shape) - 1
+        perm = list(range(1, d + 1)) + [0] + list(range(d + 1, n + 1))
+        moved = g.with_(shape=tuple(g.shape[p] for p in perm), strides=V.transpose_strides(g.strides, perm))
+        self.op_reshape_value(op, moved)
+
+    def op_reduce_scatter(self, op):
+        """Sum over the ranks, each keeping its block of ``reduce_scatter_dim``
+        (``core/ops/collectives.py:148-178``): the blocks laid out rank-major,
+        then one NCCL reduce-scatter."""
+        x = op.operands[0]
+        if op.attributes.get("reduce_op", "add") not in ("add", np.add):
+            raise NotImplementedError("reduce-scatter other than sum")
+        d = self._gather_dim(op, "reduce_scatter_dim")
+        if self.world == 1:
+            self.put(op, self.get(x))
+            return
+        sv, blk = self._rank_blocks(x, d)
+        out = self.tmp_view(blk, x.dtype)
+        self.needs_comm = True
+        n = int(np.prod(blk)) if blk else 1
+        self.step("reducescatter", [self.bref(sv), self.bref(out)], [n, E.dt_code(out.dtype)], note=f"{n} per rank")
+        self.vals[("o", op.id)] = out
+
+    def op_all_to_all(self, op):
+        """Block j of ``split_dimension`` goes to rank j; the blocks received
+        are concatenated in rank order (``core/ops/collectives.py:217-233``,
+        whose traced result keeps the input shape, so the split and concat
+        axes must agree)."""
+        x = op.operands[0]
+        a = op.attributes
+        d = self._gather_dim(op, "split_dimension")
+        if int(a["concat_dimension"]) % max(1, len(x.shape)) != d:
+            raise NotImplementedError("all-to-all with different split and concat axes")
+        if self.world == 1:
+            self.put(op, self.get(x))
+            return
+        sv, blk = self._rank_blocks(x, d)
+        g = self.tmp_view((self.world,) + blk, x.dtype)
+        self.needs_comm = True
+        n = int(np.prod(blk)) if blk else 1
+        self.step("alltoall", [self.bref(sv), self.bref(g)], [n, E.dt_code(g.dtype)], note=f"{n} per block")
+        self._concat_ranks(op, g, d)
+
+    def op_reshape_value(self, op, v):
+        """Bind ``v`` reshaped to ``op``'s result shape (a view when possible)."""
+        shape = tuple(op.result_shape)
+        st = V.reshape_strides(v.shape, v.strides, shape)
+        if st is None:
+            v = self.materialize(v)
+            st = V.dense_strides(shape)
+        self.put(op, v.with_(shape=shape, strides=st))
 
     def op_all_reduce(self, op):
         """Sum over the ranks, in place in symmetric memory.

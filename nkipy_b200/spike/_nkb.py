@@ -91,6 +91,10 @@ def _declare(lib):
         "nkb_softmax_rows": [vp, i32, vp, i32, i64, i64, vp],
         "nkb_rmsnorm_rows": [vp, vp, vp, vp, vp, i32, i32, i64, i64, ctypes.c_float, vp],
         "nkb_gemm_bf16": [vp, vp, vp, i32, i64, i64, i64, i64, i64, i64, i64, i64, i64, i64, vp],
+        "nkb_topk_rows": [vp, i32, vp, vp, i64, i64, i64, vp],
+        "nkb_comm_all_gather": [c_comm, vp, vp, sz, i32, vp],
+        "nkb_comm_reduce_scatter": [c_comm, vp, vp, sz, i32, vp],
+        "nkb_comm_all_to_all": [c_comm, vp, vp, sz, i32, vp],
         "nkb_linear_attention_noalloc": [vp, vp, vp, vp, i64, i64, i64, i64, vp],
     }
     for name, args in sig.items():

@@ -176,6 +176,115 @@ def llama_decoder_layer_kernel(
     return h1 + d
 
 
+# ---------------------------------------------------------------------------
+# 6. Qwen3 attention with a KV cache (prefill and one-token decode)
+# ---------------------------------------------------------------------------
+def qk_rmsnorm(x, weight, eps):
+    """``examples/models/qwen3/kernels/rmsnorm.py:4-21`` (fp32 compute)."""
+    original_dtype = x.dtype
+    x = x.astype(np.float32)
+    weight = weight.astype(np.float32)
+    z = np.mean(np.square(x), axis=-1, keepdims=True)
+    z = (z + eps).astype(x.dtype)
+    return (x / np.sqrt(z) * weight).astype(original_dtype)
+
+
+def qwen3_rope_cache(head_dim, max_seq_len, base=1000000.0, dtype=bfloat16):
+    """cos/sin tables (max_seq_len, head_dim/2) of the Qwen3 example
+    (``examples/models/qwen3/kernels/rope.py:4-21``): inverse frequencies in
+    float64, positions in float32, cos/sin evaluated in float32, then cast."""
+    inv = 1.0 / (base ** (np.arange(0, head_dim, 2)[: head_dim // 2] / head_dim))
+    ang = np.outer(np.arange(max_seq_len, dtype=np.float32), inv)
+    return np.cos(ang, dtype=np.float32).astype(dtype), np.sin(ang, dtype=np.float32).astype(dtype)
+
+
+def cached_attention_kernel(
+    x, qkv_weight, q_norm_weight, k_norm_weight, cache_k, cache_v, start_pos, o_weight,
+    n_heads=4, head_dim=128, n_kv_heads=2, norm_eps=1e-6, rope_base=1000000.0, tp_world=1,
+):
+    """One attention block of the reference's Qwen3 decode loop
+    (``examples/models/qwen3/kernels/attention.py:25-156``): QKV projection,
+    q/k RMSNorm, RoPE, KV-cache update (``cache[:, :S] = k`` at prefill,
+    ``cache[:, start_pos] = k`` at decode), GQA repeat, causal scores, softmax,
+    PV, o-projection (+ all-reduce under TP).  ``start_pos`` is None for the
+    prefill, else a (1,) int32 tensor; the caches are mutated in place (the
+    traced kernel returns them as aliased outputs).  The rotary and mask
+    tables are trace-time constants, as in the reference."""
+    from nkipy_b200.core import tensor_apis
+
+    is_prefill = start_pos is None
+    B, S, _ = x.shape
+    nq = n_heads // tp_world
+    nkv = max(1, n_kv_heads // tp_world)
+    n_rep = nq // nkv
+    s0, s1 = nq * head_dim, (nq + nkv) * head_dim
+    xq, xk, xv = np.split(np.matmul(x, qkv_weight), [s0, s1], axis=x.ndim - 1)
+    xq = qk_rmsnorm(xq.reshape(B, S, nq, head_dim), q_norm_weight, norm_eps)
+    xk = qk_rmsnorm(xk.reshape(B, S, nkv, head_dim), k_norm_weight, norm_eps)
+    xv = xv.reshape(B, S, nkv, head_dim)
+
+    L = cache_k.shape[1]
+    cos_t, sin_t = qwen3_rope_cache(head_dim, L, rope_base)
+    if is_prefill:
+        cos, sin = cos_t[0:S], sin_t[0:S]
+    else:
+        cos = tensor_apis.constant(cos_t)[start_pos]
+        sin = tensor_apis.constant(sin_t)[start_pos]
+    xq, xk = rope(xq, xk, cos, sin)
+
+    if is_prefill:
+        cache_k[:, :S] = xk
+        cache_v[:, :S] = xv
+    else:
+        cache_k[:, start_pos] = xk
+        cache_v[:, start_pos] = xv
+
+    keys = np.repeat(cache_k, n_rep, axis=2) if n_rep > 1 else cache_k
+    values = np.repeat(cache_v, n_rep, axis=2) if n_rep > 1 else cache_v
+    xq = xq.transpose(0, 2, 1, 3)
+    keys = keys.transpose(0, 2, 1, 3)
+    values = values.transpose(0, 2, 1, 3)
+    scores = (xq @ keys.transpose(0, 1, 3, 2)) / np.float32(np.sqrt(head_dim))
+    scores = scores.astype(bfloat16)
+    mask = np.triu(np.ones((L, L)) * -100000, k=1).astype(scores.dtype)
+    mask = tensor_apis.constant(mask)
+    if is_prefill:
+        scores = scores + np.expand_dims(mask[:S, :L], axis=[0, 1])
+    else:
+        scores = scores + np.expand_dims(mask[start_pos, :L], axis=[0, 1])
+    exp_s = np.exp(scores - np.max(scores, axis=-1, keepdims=True))
+    probs = exp_s / np.sum(exp_s, axis=-1, keepdims=True)
+    out = (probs @ values).transpose(0, 2, 1, 3).reshape(B, S, -1)
+    out = np.matmul(out, o_weight)
+    if tp_world > 1:
+        out = cc.all_reduce(out, replica_groups=[list(range(tp_world))], reduce_op=np.add)
+    return out
+
+
+def greedy_sampling_kernel(h, norm_weight, lm_head_weight, max_batch_size=1, norm_eps=1e-6, tp_world=1):
+    """Greedy next-token choice over a vocabulary split across ranks, as the
+    reference's ``greedy_sampling`` (``examples/models/qwen3/kernels/
+    sampling.py:113-147``): RMSNorm, last-position logits of this rank's
+    vocabulary shard, top-1 per rank, all-gather of the ranks' maxima and ids,
+    top-1 over the ranks, global id = rank * shard + local id."""
+    from nkipy_b200.core import tensor_apis
+
+    h = qk_rmsnorm(h, norm_weight, norm_eps)
+    logits = h[:, -1, :] @ lm_head_weight
+    logits, next_id = tensor_apis.topk(logits, k=1, axis=1)
+    group = [list(range(tp_world))]
+    logits_all = cc.all_gather(logits, all_gather_dim=1, replica_groups=group)
+    next_id_all = cc.all_gather(next_id, all_gather_dim=1, replica_groups=group)
+    _, top_index = tensor_apis.topk(logits_all, k=1, axis=1)
+    final_next_id = np.empty_like(next_id)
+    vocab_per_device = lm_head_weight.shape[1]
+    for b in range(max_batch_size):
+        device_idx = top_index[b]
+        local_idx = next_id_all[b, device_idx]
+        final_next_id[b] = device_idx * vocab_per_device + local_idx
+    return final_next_id
+
+
 def rope_tables(seq_len, head_dim, theta=500000.0):
     """cos/sin tables (S, head_dim/2), as ``qwen3_embedding/kernels/rope.py:4-31``."""
     inv_freq = 1.0 / (theta ** (np.arange(0, head_dim, 2, dtype=np.float32) / head_dim))

@@ -156,3 +156,31 @@ def all_reduce_identical(data, world, reduce_op=np.add):
     if reduce_op is np.multiply:
         return data**world
     return data.copy()
+
+
+def all_gather_identical(data, world, dim):
+    """Reference CPU semantics (``core/ops/collectives.py:17-31``): tile along ``dim``."""
+    return np.tile(data, tuple(world if i == dim else 1 for i in range(data.ndim)))
+
+
+def reduce_scatter_identical(data, world, dim):
+    """Reference CPU semantics (``core/ops/collectives.py:120-145``): sum, then rank 0's block."""
+    return np.take(data * world, range(data.shape[dim] // world), axis=dim)
+
+
+# -- top-k ---------------------------------------------------------------------
+def topk(x, k, is_ascend=False):
+    """Last-axis top-k with a total order: values largest first (smallest first
+    when ``is_ascend``), ties by the lower index, indices as uint32.
+
+    The reference's CPU implementation (``core/ops/nn.py:22-62``) selects the
+    same set with ``np.argpartition`` and orders it with ``np.argsort``, whose
+    default sort leaves the order of equal values unspecified; its device path
+    is the HLO TopK (``nn.py:65-152``), which keeps equal values in index order.
+    This restatement fixes that order, so that it agrees with the reference
+    CPU result wherever the values are distinct, and states the tie order the
+    device kernel must reproduce bit for bit (NaN and the sign of zero are
+    outside it: the kernel orders those by bit pattern)."""
+    wide = x.astype(np.float64) if (x.dtype.kind == "f" or x.dtype == bfloat16) else x.astype(np.int64)
+    idx = np.argsort(wide if is_ascend else -wide, axis=-1, kind="stable")[..., :k]
+    return np.take_along_axis(x, idx, axis=-1), idx.astype(np.uint32)

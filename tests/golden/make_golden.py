@@ -12,8 +12,9 @@ Writes:
   vectors.npz     outputs of the reference's own NumPy kernel bodies
                   (tests/kernels/softmax.py; examples/models/qwen3_embedding
                   kernels rmsnorm, softmax, rope, ffn; a Llama layer composed
-                  from them) and of its CPU collective semantics, on seeded
-                  inputs
+                  from them; the Qwen3 attention kernel with its KV cache,
+                  prefill and decode), of its CPU collective semantics and
+                  of its CPU top-k, on seeded inputs
 The tests only read these files.
 """
 
@@ -24,6 +25,7 @@ import sys
 
 import ml_dtypes
 import numpy as np
+import torch.distributed  # noqa: F401  (before the protobuf stubs, which confuse torch's import-time inspection)
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
@@ -152,7 +154,61 @@ def vectors():
     v["cc_all_gather_w2"] = C.all_gather(d, all_gather_dim=1, replica_groups=[[0, 1]])
     v["cc_reduce_scatter_w2"] = C.reduce_scatter(d, reduce_scatter_dim=0, replica_groups=[[0, 1]])
     v["cc_all_to_all_w2"] = C.all_to_all(d, split_dimension=1, concat_dimension=0, replica_groups=[[0, 1]])
+    v["cc_all_gather_w2_d0"] = C.all_gather(d, all_gather_dim=0, replica_groups=[[0, 1]])
+    v["cc_reduce_scatter_w2_d1"] = C.reduce_scatter(d, reduce_scatter_dim=1, replica_groups=[[0, 1]])
+    v["cc_all_to_all_w2_d1"] = C.all_to_all(d, split_dimension=1, concat_dimension=1, replica_groups=[[0, 1]])
+
+    # top-k (reference core/ops/nn.py:22-62, CPU implementation) on distinct values
+    from nkipy.core.ops import nn as NN
+
+    tx = (rng.permutation(6 * 300).reshape(6, 300).astype(np.float32) - 900.0) / 7.0
+    v["topk_x"] = tx
+    for kk in (1, 5, 17):
+        for asc in (False, True):
+            vals, ids = NN.topk(tx, kk, axis=-1, is_ascend=asc)
+            v[f"topk_k{kk}_a{int(asc)}_v"], v[f"topk_k{kk}_a{int(asc)}_i"] = vals, ids
+
+    v.update(qwen3_cached_attention(rng))
     return {k: (a.view(np.uint16) if a.dtype == BF16 else a) for k, a in v.items()}, [k for k, a in v.items() if a.dtype == BF16]
+
+
+def qwen3_cached_attention(rng):
+    """The reference's Qwen3 attention kernel (examples/models/qwen3/kernels/
+    attention.py:25-156) called directly on NumPy arrays: a prefill of 8 tokens
+    then two one-token decode steps on the same KV cache, world size 1.  Its
+    imports of neuronxcc (nki.language.bfloat16, nki.typing) are stubbed with
+    ml_dtypes' bfloat16 and placeholders; torch.distributed reports world 1."""
+    import types
+
+    for name in ("neuronxcc", "neuronxcc.nki"):
+        sys.modules.setdefault(name, types.ModuleType(name))
+    lang = types.ModuleType("neuronxcc.nki.language")
+    lang.bfloat16 = BF16
+    typ = types.ModuleType("neuronxcc.nki.typing")
+    typ.tensor = typ.mutable_tensor = typ.mutable = typ.immutable = object
+    sys.modules["neuronxcc.nki.language"] = lang
+    sys.modules["neuronxcc.nki.typing"] = typ
+    sys.path.insert(0, os.path.join(REF_ROOT, "examples", "models", "qwen3"))
+    from kernels import attention as A
+
+    A.dist.get_world_size = lambda *a, **k: 1
+    B, L, nq, nkv, hd, D, S = 2, 16, 4, 2, 64, 256, 8
+    x = rng.standard_normal((B, S, D), dtype=np.float32).astype(BF16)
+    wqkv = (rng.standard_normal((D, (nq + 2 * nkv) * hd), dtype=np.float32) * 0.05).astype(BF16)
+    wo = (rng.standard_normal((nq * hd, D), dtype=np.float32) * 0.05).astype(BF16)
+    qn = rng.uniform(0.5, 1.5, hd).astype(BF16)
+    kn = rng.uniform(0.5, 1.5, hd).astype(BF16)
+    ck = np.zeros((B, L, nkv, hd), BF16)
+    cv = np.zeros((B, L, nkv, hd), BF16)
+    v = dict(qa_x=x, qa_wqkv=wqkv, qa_wo=wo, qa_qn=qn, qa_kn=kn)
+    v["qa_y0"] = A.attention_kernel(x, wqkv, qn, kn, 1e-6, nq, hd, nkv, ck, cv, None, wo)
+    for i in range(2):
+        t = rng.standard_normal((B, 1, D), dtype=np.float32).astype(BF16)
+        v[f"qa_t{i + 1}"] = t
+        v[f"qa_y{i + 1}"] = A.attention_kernel(t, wqkv, qn, kn, 1e-6, nq, hd, nkv, ck, cv,
+                                               np.array([S + i], np.int32), wo)
+    v["qa_cache_k"], v["qa_cache_v"] = ck.copy(), cv.copy()
+    return v
 
 
 def main():

@@ -210,3 +210,47 @@ def test_chunked_linear_attention(shape):
     got = on_device(W.chunked_linear_attention_kernel, q, k, v)
     want = O.linear_attention_recurrent(q, k, v)
     assert_close(got, want, BF16_RTOL)
+
+
+@pytest.mark.parametrize(
+    "shape,k,dtype,asc",
+    [
+        ((64, 1000), 1, np.float32, False),
+        ((64, 1000), 8, np.float32, True),
+        ((3, 151936), 4, BF16, False),  # a Qwen3 vocabulary row: longer than the shared-memory stage
+        ((17, 49152), 3, np.float32, False),  # the longest staged row
+        ((2, 4096), 64, np.float32, False),
+        ((5, 7), 7, np.int32, False),
+        ((1, 1), 1, np.float32, False),
+        ((300, 130), 5, np.float16, True),
+    ],
+)
+def test_topk_exact(shape, k, dtype, asc):
+    from nkipy_b200.core.ops import nn
+
+    def kern(x):
+        return nn.topk(x, k, axis=-1, is_ascend=asc)
+
+    rng = np.random.default_rng(13)
+    if np.dtype(dtype).kind == "i":
+        x = rng.integers(-50, 50, shape).astype(dtype)  # many ties: lower index first
+    else:
+        x = rng.standard_normal(shape, dtype=np.float32).astype(dtype)  # bf16/f16 rounding makes ties too
+    vals, idx = on_device(kern, x)
+    want_v, want_i = O.topk(x, k, is_ascend=asc)
+    np.testing.assert_array_equal(idx, want_i)
+    np.testing.assert_array_equal(vals.view(np.uint8), want_v.view(np.uint8))
+
+
+def test_greedy_sampling_single_device():
+    B, S, H, V = 4, 8, 512, 32000
+    rng = np.random.default_rng(14)
+    h = rng.standard_normal((B, S, H), dtype=np.float32).astype(BF16)
+    nw = rng.uniform(0.5, 1.5, H).astype(BF16)
+    lm = (rng.standard_normal((H, V), dtype=np.float32) * 0.05).astype(BF16)
+    ids = on_device(W.greedy_sampling_kernel, h, nw, lm, max_batch_size=B).reshape(-1).astype(np.int64)
+    logits = W.qk_rmsnorm(h, nw, 1e-6)[:, -1, :].astype(np.float32) @ lm.astype(np.float32)
+    best = logits.max(axis=1)
+    assert np.all((ids >= 0) & (ids < V))
+    # the chosen token holds the largest logit, up to the bf16 rounding of the device's logits
+    assert np.all(logits[np.arange(B), ids] >= best - (2.0**-7 * np.abs(best) + 1e-6))

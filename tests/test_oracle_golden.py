@@ -8,6 +8,7 @@ core/ops/collectives.py cpu implementations) -- see tests/golden/make_golden.py.
 import os
 
 import ml_dtypes
+import pytest
 import numpy as np
 
 from nkipy_b200 import workloads as W
@@ -77,6 +78,48 @@ def test_collective_cpu_semantics():
         C.all_to_all(d, split_dimension=1, concat_dimension=0, replica_groups=[[0, 1]]), V("cc_all_to_all_w2")
     )
     np.testing.assert_array_equal(O.all_reduce_identical(d, 4), V("cc_all_reduce_w4"))
+    np.testing.assert_array_equal(C.all_gather(d, all_gather_dim=0, replica_groups=[[0, 1]]), V("cc_all_gather_w2_d0"))
+    np.testing.assert_array_equal(O.all_gather_identical(d, 2, 0), V("cc_all_gather_w2_d0"))
+    np.testing.assert_array_equal(O.all_gather_identical(d, 2, 1), V("cc_all_gather_w2"))
+    np.testing.assert_array_equal(
+        C.reduce_scatter(d, reduce_scatter_dim=1, replica_groups=[[0, 1]]), V("cc_reduce_scatter_w2_d1")
+    )
+    np.testing.assert_array_equal(O.reduce_scatter_identical(d, 2, 1), V("cc_reduce_scatter_w2_d1"))
+    np.testing.assert_array_equal(O.reduce_scatter_identical(d, 2, 0), V("cc_reduce_scatter_w2"))
+    np.testing.assert_array_equal(
+        C.all_to_all(d, split_dimension=1, concat_dimension=1, replica_groups=[[0, 1]]), V("cc_all_to_all_w2_d1")
+    )
+
+
+@pytest.mark.parametrize("k", [1, 5, 17])
+@pytest.mark.parametrize("asc", [False, True])
+def test_topk_vectors(k, asc):
+    """The oracle's top-k equals the reference CPU top-k on distinct values."""
+    from nkipy_b200.core.ops import nn as NN
+
+    x = V("topk_x")
+    vals, ids = O.topk(x, k, is_ascend=asc)
+    np.testing.assert_array_equal(vals, V(f"topk_k{k}_a{int(asc)}_v"))
+    np.testing.assert_array_equal(ids, V(f"topk_k{k}_a{int(asc)}_i"))
+    v2, i2 = NN.topk(x, k, axis=-1, is_ascend=asc)  # this package's CPU op
+    np.testing.assert_array_equal(i2, ids)
+
+
+def test_qwen3_cached_attention_vectors():
+    """The cached-attention kernel body reproduces the reference's Qwen3
+    attention kernel, prefill then two decode steps on one KV cache."""
+    B, L, nq, nkv, hd, D, S = 2, 16, 4, 2, 64, 256, 8
+    kw = dict(n_heads=nq, head_dim=hd, n_kv_heads=nkv)
+    args = [V("qa_wqkv"), V("qa_qn"), V("qa_kn")]
+    ck = np.zeros((B, L, nkv, hd), W.bfloat16)
+    cv = np.zeros((B, L, nkv, hd), W.bfloat16)
+    y0 = W.cached_attention_kernel(V("qa_x"), *args, ck, cv, None, V("qa_wo"), **kw)
+    np.testing.assert_array_equal(np.asarray(y0, np.float32), V("qa_y0"))
+    for i in range(2):
+        y = W.cached_attention_kernel(V(f"qa_t{i + 1}"), *args, ck, cv, np.array([S + i], np.int32), V("qa_wo"), **kw)
+        np.testing.assert_array_equal(np.asarray(y, np.float32), V(f"qa_y{i + 1}"))
+    np.testing.assert_array_equal(ck.view(np.uint16), V("qa_cache_k").view(np.uint16))
+    np.testing.assert_array_equal(cv.view(np.uint16), V("qa_cache_v").view(np.uint16))
 
 
 def test_linear_attention_forms_agree():

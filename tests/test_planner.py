@@ -5,6 +5,7 @@ import numpy as np
 import pytest
 
 from nkipy_b200 import workloads as W
+from nkipy_b200.core.ops import collectives as cc
 from nkipy_b200.core.trace import NKIPyKernel
 from nkipy_b200.planner import ewprog as E
 from nkipy_b200.planner import lower
@@ -83,14 +84,115 @@ def test_bool_output_is_bytes():
 
 
 def test_unsupported_op_fails_loudly():
+    def k(x):
+        return cc.all_to_all(x, split_dimension=0, concat_dimension=1, replica_groups=[[0, 1]])
+
+    with pytest.raises(NotImplementedError):
+        lower(NKIPyKernel.trace(k).specialize(np.zeros((4, 8), np.float32)), world=2)
+
+
+def test_topk_is_one_launch_with_two_results():
     from nkipy_b200.core.ops import nn
 
     def k(x):
-        v, i = nn.topk(x, 2, axis=-1)
-        return v
+        v, i = nn.topk(x, 5, axis=-1)
+        return v, i
 
-    with pytest.raises(NotImplementedError):
-        plan_of(k, np.zeros((4, 8), np.float32))
+    p = plan_of(k, np.zeros((4, 100), np.float32))
+    assert p.kernel_counts() == {"topk_rows": 1}
+    assert [np.dtype(o.dtype) for o in p.outputs] == [np.dtype(np.float32), np.dtype(np.uint32)]
+    # both results are written straight into the output buffers
+    assert [p.buffers[b].kind for b, _ in p.steps[0].bufs[1:]] == ["out", "out"]
+
+
+def _ag0(x):
+    return cc.all_gather(x, all_gather_dim=0, replica_groups=[[0, 1]])
+
+
+def _ag1(x):
+    return cc.all_gather(x, all_gather_dim=1, replica_groups=[[0, 1]])
+
+
+def _rs0(x):
+    return cc.reduce_scatter(x, reduce_scatter_dim=0, replica_groups=[[0, 1]])
+
+
+def _rs1(x):
+    return cc.reduce_scatter(x, reduce_scatter_dim=1, replica_groups=[[0, 1]])
+
+
+def _a2a1(x):
+    return cc.all_to_all(x, split_dimension=1, concat_dimension=1, replica_groups=[[0, 1]])
+
+
+@pytest.mark.parametrize(
+    "fn,kernels",
+    [
+        (_ag0, ["allgather"]),  # rank-major gather is the concatenation itself
+        (_ag1, ["allgather", "ew"]),  # ... moved to the gather axis
+        (_rs0, ["reducescatter"]),
+        (_rs1, ["ew", "reducescatter"]),  # blocks laid out rank-major first
+        (_a2a1, ["ew", "alltoall", "ew"]),
+    ],
+)
+def test_collective_plans_world2(fn, kernels):
+    p = lower(NKIPyKernel.trace(fn).specialize(np.zeros((8, 16), np.float32)), world=2)
+    assert [s.kernel for s in p.steps] == kernels and p.needs_comm
+
+
+def _cache_decode_plan():
+    B, L, nq, nkv, hd, D = 2, 64, 4, 2, 128, 512
+    kw = dict(n_heads=nq, head_dim=hd, n_kv_heads=nkv)
+    z = np.zeros((B, L, nkv, hd), BF16)
+    args = (np.zeros((B, 1, D), BF16), np.zeros((D, (nq + 2 * nkv) * hd), BF16), np.ones(hd, BF16), np.ones(hd, BF16),
+            z, z, np.array([3], np.int32), np.zeros((nq * hd, D), BF16))
+    return plan_of(W.cached_attention_kernel, *args, **kw), z.nbytes
+
+
+def test_kv_cache_decode_updates_caches_in_place():
+    p, cache_bytes = _cache_decode_plan()
+    assert sorted(p.aliases) == [(1, 4), (2, 5)]
+    copies = [s for s in p.steps if s.kernel == "copy_bytes"]
+    # one copy per cache, from the mutated input into its output (a no-op when bound in place)
+    assert [(p.buffers[s.bufs[0][0]].kind, p.buffers[s.bufs[0][0]].index) for s in copies] == [("in", 4), ("in", 5)]
+    assert [(p.buffers[s.bufs[1][0]].kind, p.buffers[s.bufs[1][0]].index) for s in copies] == [("out", 1), ("out", 2)]
+    assert all(s.ints == [cache_bytes] for s in copies)
+    # the new token's row is scattered into the output buffer; no other step writes a whole cache
+    sc = [s for s in p.steps if s.kernel == "scatter_rows"]
+    assert [p.buffers[s.bufs[0][0]].kind for s in sc] == ["out", "out"]
+    cache_ins = {i for i, b in enumerate(p.buffers) if b.kind == "in" and b.index in (4, 5)}
+    assert not any(s.kernel == "ew" and s.bufs[1][0] in cache_ins for s in p.steps)
+
+
+def test_readers_of_a_mutated_parameter_run_before_its_update():
+    def k(a, idx, v):
+        old = a * 2.0
+        a[:, idx] = v
+        return old + a
+
+    a = np.zeros((6, 10, 5), np.float32)
+    p = plan_of(k, a, np.array([7], np.int32), np.zeros((6, 1, 5), np.float32))
+    kinds = [s.kernel for s in p.steps]
+    first_write = kinds.index("copy_bytes")
+    reads_a = [i for i, s in enumerate(p.steps) if any(p.buffers[b].kind == "in" and p.buffers[b].index == 0
+                                                       for b, _ in s.bufs)]
+    assert reads_a and all(i <= first_write for i in reads_a)
+
+
+def test_successive_updates_share_one_buffer():
+    def k(a, i, j, v, w):
+        a[i] = v
+        a[j] = w
+        a[0:2] = 0.0
+        return a.sum(axis=1)
+
+    a = np.zeros((9, 33), np.float32)
+    r = np.zeros((1, 33), np.float32)
+    p = plan_of(k, a, np.array([4], np.int32), np.array([7], np.int32), r, r)
+    assert p.kernel_counts()["copy_bytes"] == 1
+    writes = {s.bufs[0][0] for s in p.steps if s.kernel in ("scatter_rows", "copy_bytes")}
+    dst = {s.bufs[1][0] for s in p.steps if s.kernel == "copy_bytes"}
+    assert writes - {b for b, _ in [s.bufs[0] for s in p.steps if s.kernel == "copy_bytes"]} == dst
 
 
 def test_ew_program_budget_split():
@@ -158,8 +260,6 @@ def test_layer_tp2_fuses_allreduces_into_gemms():
 
 
 def test_allreduce_without_gemm_stays_a_step():
-    from nkipy_b200.core.ops import collectives as cc
-
     def k(x, r):
         return r + cc.all_reduce(x * 2.0, replica_groups=[[0, 1]], reduce_op=np.add)
 

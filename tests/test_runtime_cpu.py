@@ -169,3 +169,88 @@ def test_tensor_parallel_decomposition_gloo_world2():
     res = dict(q.get(timeout=5) for _ in range(2))
     assert all(p.exitcode == 0 for p in procs)
     assert res[0] < 2e-2 and res[1] < 2e-2, res
+
+
+def _decode_worker(rank, world, port, q):
+    """Vocabulary-parallel greedy sampling and a head-parallel KV-cache decode,
+    the collectives done by gloo, against the single-rank direct calls."""
+    import torch
+    import torch.distributed as dist
+
+    from nkipy_b200 import workloads as W
+    from nkipy_b200.core.ops import collectives as cc
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        def gloo_all_gather(data, all_gather_dim, replica_groups, **_):
+            a = np.asarray(data)
+            wide = np.float64 if a.dtype.kind == "f" or a.dtype == W.bfloat16 else np.int64
+            t = torch.from_numpy(a.astype(wide))
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t)
+            return np.concatenate([p.numpy() for p in parts], axis=all_gather_dim).astype(a.dtype)
+
+        def gloo_all_reduce(data, replica_groups, reduce_op=np.add, **_):
+            t = torch.from_numpy(np.asarray(data, np.float32).copy())
+            dist.all_reduce(t)
+            return t.numpy().astype(data.dtype)
+
+        rng = np.random.default_rng(21)
+        B, S, H, V = 3, 4, 128, 600
+        h = rng.standard_normal((B, S, H), dtype=np.float32).astype(W.bfloat16)
+        nw = np.ones(H, W.bfloat16)
+        lm = (rng.standard_normal((H, V), dtype=np.float32) * 0.05).astype(W.bfloat16)
+        shard = lm[:, rank * (V // world):(rank + 1) * (V // world)]
+        with mock.patch.object(cc, "all_gather", gloo_all_gather):
+            ids = W.greedy_sampling_kernel(h, nw, shard, max_batch_size=B, tp_world=world)
+        full = W.greedy_sampling_kernel(h, nw, lm, max_batch_size=B, tp_world=1)
+        same_ids = bool(np.array_equal(np.asarray(ids).reshape(-1), np.asarray(full).reshape(-1)))
+
+        B, L, nq, nkv, hd, D, S = 1, 16, 4, 2, 32, 128, 4
+        x = rng.standard_normal((B, S, D), dtype=np.float32).astype(W.bfloat16)
+        wqkv = (rng.standard_normal((D, (nq + 2 * nkv) * hd), dtype=np.float32) * 0.05).astype(W.bfloat16)
+        wo = (rng.standard_normal((nq * hd, D), dtype=np.float32) * 0.05).astype(W.bfloat16)
+        qn = np.ones(hd, W.bfloat16)
+        t1 = rng.standard_normal((B, 1, D), dtype=np.float32).astype(W.bfloat16)
+        kw = dict(n_heads=nq, head_dim=hd, n_kv_heads=nkv)
+        ck, cv = np.zeros((B, L, nkv, hd), W.bfloat16), np.zeros((B, L, nkv, hd), W.bfloat16)
+        W.cached_attention_kernel(x, wqkv, qn, qn, ck, cv, None, wo, **kw)
+        want = np.asarray(W.cached_attention_kernel(t1, wqkv, qn, qn, ck, cv, np.array([S], np.int32), wo, **kw),
+                          np.float32)
+        lq, lkv = nq // world, nkv // world
+        cols = np.r_[rank * lq * hd:(rank + 1) * lq * hd,
+                     nq * hd + rank * lkv * hd:nq * hd + (rank + 1) * lkv * hd,
+                     (nq + nkv) * hd + rank * lkv * hd:(nq + nkv) * hd + (rank + 1) * lkv * hd]
+        wr, wor = wqkv[:, cols], wo[rank * lq * hd:(rank + 1) * lq * hd]
+        ckr, cvr = np.zeros((B, L, lkv, hd), W.bfloat16), np.zeros((B, L, lkv, hd), W.bfloat16)
+        with mock.patch.object(cc, "all_reduce", gloo_all_reduce):
+            W.cached_attention_kernel(x, wr, qn, qn, ckr, cvr, None, wor, tp_world=world, **kw)
+            got = np.asarray(W.cached_attention_kernel(t1, wr, qn, qn, ckr, cvr, np.array([S], np.int32), wor,
+                                                       tp_world=world, **kw), np.float32)
+        err = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
+        cache_ok = bool(np.array_equal(ckr.view(np.uint16), ck[:, :, rank * lkv:(rank + 1) * lkv].view(np.uint16)))
+        q.put((rank, (same_ids, err, cache_ok)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_vocab_and_head_parallel_decode_gloo_world2():
+    """Greedy sampling over a vocabulary split in two (top-1 per rank, all-gather,
+    top-1 over ranks) picks the same tokens as one rank; the KV-cache decode
+    split by heads (+ all-reduce) matches one rank (CPU, gloo)."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_decode_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    res = dict(q.get(timeout=5) for _ in range(2))
+    assert all(p.exitcode == 0 for p in procs)
+    for rank in (0, 1):
+        same_ids, err, cache_ok = res[rank]
+        assert same_ids and cache_ok and err < 2e-2, res
