@@ -177,6 +177,28 @@ class Lowering:
         self.updatable.add(out.buf)
         return out
 
+    def copy_view(self, src: V.View, dst: V.View):
+        """dst = src for two strided views of one shape; views of more axes than
+        the ``ew`` kernel takes (after merging) are copied in slices along
+        their shortest axis."""
+        try:
+            self.emit_ew(E.leaf(src), dst)
+            return
+        except E.TooBig:
+            pass
+        axes = [d for d in range(len(src.shape)) if src.shape[d] > 1]
+        if not axes:
+            raise NotImplementedError("copy of a view the elementwise kernel cannot take")
+        d = min(axes, key=lambda i: src.shape[i])
+        keep = [i for i in range(len(src.shape)) if i != d]
+        for i in range(int(src.shape[d])):
+            self.copy_view(
+                src.with_(offset=src.offset + i * src.strides[d], shape=tuple(src.shape[k] for k in keep),
+                          strides=tuple(src.strides[k] for k in keep)),
+                dst.with_(offset=dst.offset + i * dst.strides[d], shape=tuple(dst.shape[k] for k in keep),
+                          strides=tuple(dst.strides[k] for k in keep)),
+            )
+
     def emit_ew(self, expr: E.Expr, out: V.View, depth=0):
         try:
             c = E.compile_ew(expr, out)
@@ -757,6 +779,75 @@ class Lowering:
         ints += list(x.shape) + list(op.result_shape) + [c[0] for c in cfg]
         self.step("pad", [self.bref(xv), self.bref(out)], ints)
         self.vals[("o", op.id)] = out
+
+    def op_convolution(self, op):
+        """``conv2d`` / ``conv3d`` (``core/ops/conv.py:230-312``) as one GEMM.
+
+        The zero-padded input (one ``pad`` launch when the padding is not 0) is
+        read through a strided view of its kernel windows, ordered (batch,
+        output position, channel, kernel offset); one ``ew`` launch writes it
+        dense, so the correlation is cols (B*P x C*prod(k)) @ W^T (C*prod(k) x
+        OC): the weight, row-major (OC, C, *k), is a K-major right operand as
+        it lies.  The (B, P, OC) product is then moved to the (B, OC, *out)
+        result layout.  bf16 runs on ``gemm_bf16`` (fp32 accumulation), other
+        dtypes on ``gemm_simt``.
+        """
+        x, w = op.operands
+        a = op.attributes
+        n = len(x.shape) - 2
+        sp = list(range(2, 2 + n))
+        std = (
+            a.get("input_batch_dimension", 0) == 0 and a.get("input_feature_dimension", 1) == 1
+            and list(a.get("input_spatial_dimensions", sp)) == sp
+            and a.get("kernel_output_feature_dimension", 0) == 0 and a.get("kernel_input_feature_dimension", 1) == 1
+            and list(a.get("kernel_spatial_dimensions", sp)) == sp
+            and a.get("output_batch_dimension", 0) == 0 and a.get("output_feature_dimension", 1) == 1
+            and list(a.get("output_spatial_dimensions", sp)) == sp
+        )
+        if not std or a.get("feature_group_count", 1) != 1 or a.get("batch_group_count", 1) != 1:
+            raise NotImplementedError("convolution outside NC-spatial layout with one feature group")
+        if any(int(d) != 1 for d in a.get("lhs_dilation", [1] * n)):
+            raise NotImplementedError("convolution with input dilation")
+        stride = [int(s) for s in a["window_strides"]]
+        pads = [(int(lo), int(hi)) for lo, hi in a["padding"]]
+        dil = [int(d) for d in a.get("rhs_dilation", [1] * n)]
+        B, C = int(x.shape[0]), int(x.shape[1])
+        OC, ks = int(w.shape[0]), tuple(int(k) for k in w.shape[2:])
+        out_sp = tuple(int(s) for s in op.result_shape[2:])
+        dt = np.dtype(op.result_dtype)
+        xv = self.materialize(self.get(x), dense=True)
+        if any(lo or hi for lo, hi in pads):
+            pshape = (B, C) + tuple(int(x.shape[2 + i]) + pads[i][0] + pads[i][1] for i in range(n))
+            pv = self.tmp_view(pshape, x.dtype)
+            ints = [n + 2, np.dtype(x.dtype).itemsize, pv.size, 0] + [int(s) for s in x.shape] + list(pshape)
+            ints += [0, 0] + [lo for lo, _ in pads]
+            self.step("pad", [self.bref(xv), self.bref(pv)], ints, note="convolution padding")
+            xv = pv
+        xs = xv.strides
+        win = xv.with_(
+            shape=(B,) + out_sp + (C,) + ks,
+            strides=(xs[0],) + tuple(xs[2 + i] * stride[i] for i in range(n)) + (xs[1],)
+            + tuple(xs[2 + i] * dil[i] for i in range(n)),
+        )
+        P, KK = int(np.prod(out_sp)), C * int(np.prod(ks))
+        cols = self.tmp_view((B * P, KK), x.dtype)
+        self.copy_view(win, cols.with_(shape=win.shape, strides=V.dense_strides(win.shape)))
+        wv = self.materialize(self.get(w), dense=True)
+        M, N, K = B * P, OC, KK
+        prod = self.tmp_view((B, P, OC), dt)
+        eb = np.dtype(BF16).itemsize
+        if (np.dtype(cols.dtype) == BF16 and np.dtype(wv.dtype) == BF16 and dt == BF16 and K % 8 == 0
+                and N % 8 == 0 and (wv.offset * eb) % 16 == 0):
+            self.step("gemm_bf16", [self.bref(cols), self.bref(wv), self.bref(prod)],
+                      [M, N, K, K, K, N, 1, 0, 0, 0, 0, 0, 1], note=f"tc {M}x{N}x{K} convolution")
+        else:
+            self.step("gemm_simt", [self.bref(cols), self.bref(wv), self.bref(prod)],
+                      [E.dt_code(cols.dtype), E.dt_code(wv.dtype), E.dt_code(dt), M, N, K, 1, K, 1, 1, K, N, 1, 0, 0, 0],
+                      note=f"simt {M}x{N}x{K} convolution")
+        # (B, P, OC) -> (B, OC, *out)
+        moved = prod.with_(shape=(B, OC) + out_sp,
+                           strides=(P * OC, 1) + tuple(s * OC for s in V.dense_strides(out_sp)))
+        self.put(op, moved)
 
     def op_dynamic_update_slice(self, op):
         base, upd = op.operands[0], op.operands[1]

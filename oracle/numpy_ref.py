@@ -184,3 +184,27 @@ def topk(x, k, is_ascend=False):
     wide = x.astype(np.float64) if (x.dtype.kind == "f" or x.dtype == bfloat16) else x.astype(np.int64)
     idx = np.argsort(wide if is_ascend else -wide, axis=-1, kind="stable")[..., :k]
     return np.take_along_axis(x, idx, axis=-1), idx.astype(np.uint32)
+
+
+# -- convolution ------------------------------------------------------------------
+def conv_nd(x, w, bias=None, stride=1, padding=0, dilation=1):
+    """N-d cross-correlation, NC-spatial layout (reference ``core/ops/conv.py``:
+    CPU ``:133-228``, traced attributes ``:230-312``).  Accumulated in float64
+    as a sum over kernel offsets of shifted, strided input slices times the
+    weight; returns float32 (what the reference's fp32 direct call returns)."""
+    n = x.ndim - 2
+    st = (stride,) * n if np.isscalar(stride) else tuple(stride)
+    pd = (padding,) * n if np.isscalar(padding) else tuple(padding)
+    dl = (dilation,) * n if np.isscalar(dilation) else tuple(dilation)
+    xf = np.pad(x.astype(np.float64), ((0, 0), (0, 0)) + tuple((p, p) for p in pd))
+    wf = w.astype(np.float64)
+    ks = w.shape[2:]
+    out_sp = tuple((xf.shape[2 + i] - dl[i] * (ks[i] - 1) - 1) // st[i] + 1 for i in range(n))
+    y = np.zeros((x.shape[0], w.shape[0]) + out_sp)
+    for off in np.ndindex(*ks):
+        sl = tuple(slice(off[i] * dl[i], off[i] * dl[i] + st[i] * (out_sp[i] - 1) + 1, st[i]) for i in range(n))
+        patch = xf[(slice(None), slice(None)) + sl]  # (B, C, *out)
+        y += np.einsum("bc...,oc->bo...", patch, wf[(slice(None), slice(None)) + off])
+    if bias is not None:
+        y += bias.astype(np.float64).reshape((1, -1) + (1,) * n)
+    return y.astype(np.float32)

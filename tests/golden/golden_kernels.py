@@ -85,6 +85,24 @@ def tril_mask(x):
     return np.tril(x) + np.triu(x, k=1) * 0.0
 
 
+# Op library of the tracer in use, for kernels calling NKIPy ops that are not
+# NumPy functions (conv2d / conv3d): set by make_golden.py to the reference's
+# ``nkipy.core.ops`` and by the tests to ``nkipy_b200.core.ops``.
+OPS = None
+
+
+def conv2d_bias(x, w, b):
+    return OPS.conv2d(x, w, b, stride=(2, 1), padding=(1, 2))
+
+
+def conv2d_dilated(x, w):
+    return OPS.conv2d(x, w, stride=1, padding=2, dilation=2)
+
+
+def conv3d_bias(x, w, b):
+    return OPS.conv3d(x, w, b, stride=1, padding=1)
+
+
 def _rng(seed):
     return np.random.default_rng(seed)
 
@@ -120,6 +138,19 @@ CASES = [
     ("silu_mul", silu_mul, lambda: (np.zeros((4, 8), BF16), np.zeros((4, 8), BF16)), {}),
     ("repeat_kv", repeat_kv, lambda: (np.zeros((1, 5, 2, 4), BF16),), {}),
     ("tril_mask", tril_mask, lambda: (np.zeros((2, 5, 5), np.float32),), {}),
+    (
+        "conv2d_bias",
+        conv2d_bias,
+        lambda: (np.zeros((2, 3, 9, 11), BF16), np.zeros((4, 3, 3, 2), BF16), np.zeros((4,), BF16)),
+        {},
+    ),
+    ("conv2d_dilated", conv2d_dilated, lambda: (np.zeros((1, 2, 8, 8), np.float32), np.zeros((3, 2, 3, 3), np.float32)), {}),
+    (
+        "conv3d_bias",
+        conv3d_bias,
+        lambda: (np.zeros((1, 2, 5, 6, 7), np.float32), np.zeros((3, 2, 2, 3, 2), np.float32), np.zeros((3,), np.float32)),
+        {},
+    ),
 ]
 
 

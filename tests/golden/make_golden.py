@@ -47,6 +47,9 @@ def oplists():
     import golden_kernels as G
 
     ref_trace, _ = import_reference()
+    import nkipy.core.ops as ref_ops
+
+    G.OPS = ref_ops
     out = {}
     for name, fn, make, kw in G.CASES:
         k = ref_trace.NKIPyKernel.trace(fn, backend="hlo")
@@ -167,6 +170,17 @@ def vectors():
         for asc in (False, True):
             vals, ids = NN.topk(tx, kk, axis=-1, is_ascend=asc)
             v[f"topk_k{kk}_a{int(asc)}_v"], v[f"topk_k{kk}_a{int(asc)}_i"] = vals, ids
+
+    # convolutions (reference core/ops/conv.py CPU implementations)
+    from nkipy.core.ops import conv as CV
+
+    cx = rng.standard_normal((2, 3, 9, 11), dtype=np.float32)
+    cw = rng.standard_normal((4, 3, 3, 2), dtype=np.float32)
+    cb = rng.standard_normal((4,), dtype=np.float32)
+    v.update(conv2_x=cx, conv2_w=cw, conv2_b=cb, conv2_y=CV.conv2d(cx, cw, cb, stride=(2, 1), padding=(1, 2)))
+    cx3 = rng.standard_normal((1, 2, 5, 6, 7), dtype=np.float32)
+    cw3 = rng.standard_normal((3, 2, 2, 3, 2), dtype=np.float32)
+    v.update(conv3_x=cx3, conv3_w=cw3, conv3_y=CV.conv3d(cx3, cw3, None, stride=(1, 2, 1), padding=1))
 
     v.update(qwen3_cached_attention(rng))
     return {k: (a.view(np.uint16) if a.dtype == BF16 else a) for k, a in v.items()}, [k for k, a in v.items() if a.dtype == BF16]

@@ -254,3 +254,29 @@ def test_greedy_sampling_single_device():
     assert np.all((ids >= 0) & (ids < V))
     # the chosen token holds the largest logit, up to the bf16 rounding of the device's logits
     assert np.all(logits[np.arange(B), ids] >= best - (2.0**-7 * np.abs(best) + 1e-6))
+
+
+
+@pytest.mark.parametrize(
+    "n,x_shape,w_shape,kw,dtype,bias",
+    [
+        (2, (2, 16, 20, 24), (32, 16, 3, 3), dict(stride=1, padding=1), BF16, True),  # tensor-core GEMM
+        (2, (3, 3, 17, 13), (5, 3, 4, 2), dict(stride=(2, 1), padding=(1, 3)), np.float32, True),
+        (2, (1, 2, 9, 9), (3, 2, 3, 3), dict(stride=1, padding=2, dilation=2), np.float32, False),
+        (3, (1, 2, 6, 7, 8), (4, 2, 2, 3, 2), dict(stride=(1, 2, 1), padding=1), np.float32, True),
+    ],
+)
+def test_convolution(n, x_shape, w_shape, kw, dtype, bias):
+    from nkipy_b200.core import ops as OPS
+
+    conv = OPS.conv2d if n == 2 else OPS.conv3d
+    rng = np.random.default_rng(16)
+    x = rng.standard_normal(x_shape, dtype=np.float32).astype(dtype)
+    w = (rng.standard_normal(w_shape, dtype=np.float32) * 0.1).astype(dtype)
+    b = rng.standard_normal(w_shape[0], dtype=np.float32).astype(dtype)
+    if bias:
+        got = on_device(lambda x, w, b: conv(x, w, b, **kw), x, w, b)
+    else:
+        got = on_device(lambda x, w: conv(x, w, **kw), x, w)
+    want = O.conv_nd(x, w, b if bias else None, **kw)
+    assert_close(got, want, BF16_RTOL if dtype == BF16 else FP32_RTOL)

@@ -131,3 +131,18 @@ def test_linear_attention_forms_agree():
     # chunk size does not change the result (pure reassociation)
     c = O.linear_attention_recurrent(q, k, v, chunk=16)
     np.testing.assert_allclose(b, c, rtol=2e-4, atol=1e-5)
+
+
+def test_convolution_vectors():
+    """The oracle's convolution and this package's CPU conv ops equal the
+    reference's CPU conv2d / conv3d (core/ops/conv.py)."""
+    from nkipy_b200.core.ops import conv as CV
+
+    y2 = O.conv_nd(V("conv2_x"), V("conv2_w"), V("conv2_b"), stride=(2, 1), padding=(1, 2))
+    np.testing.assert_allclose(y2, V("conv2_y"), rtol=1e-5, atol=1e-5)
+    y3 = O.conv_nd(V("conv3_x"), V("conv3_w"), None, stride=(1, 2, 1), padding=1)
+    np.testing.assert_allclose(y3, V("conv3_y"), rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(CV.conv2d(V("conv2_x"), V("conv2_w"), V("conv2_b"), stride=(2, 1), padding=(1, 2)),
+                               V("conv2_y"), rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(CV.conv3d(V("conv3_x"), V("conv3_w"), None, stride=(1, 2, 1), padding=1), V("conv3_y"),
+                               rtol=1e-6, atol=1e-6)

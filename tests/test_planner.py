@@ -5,6 +5,7 @@ import numpy as np
 import pytest
 
 from nkipy_b200 import workloads as W
+from nkipy_b200.core import ops as cc_ops
 from nkipy_b200.core.ops import collectives as cc
 from nkipy_b200.core.trace import NKIPyKernel
 from nkipy_b200.planner import ewprog as E
@@ -266,3 +267,18 @@ def test_allreduce_without_gemm_stays_a_step():
     x = np.zeros((64, 256), BF16)
     p = lower(NKIPyKernel.trace(k).specialize(x, x), world=2)
     assert p.kernel_counts().get("allreduce_add") == 1 and "gemm_bf16_ar" not in p.kernel_counts()
+
+
+def test_convolution_plans():
+    def c2(x, w, b):
+        return cc_ops.conv2d(x, w, b, stride=1, padding=1)
+
+    def c3(x, w):
+        return cc_ops.conv3d(x, w, stride=(1, 2, 1), padding=1, dilation=(2, 1, 1))
+
+    p = plan_of(c2, np.zeros((2, 16, 12, 12), BF16), np.zeros((32, 16, 3, 3), BF16), np.zeros(32, BF16))
+    # pad, im2col copy, tensor-core GEMM, layout move fused with the bias add
+    assert [s.kernel for s in p.steps] == ["pad", "ew", "gemm_bf16", "ew"]
+    p = plan_of(c3, np.zeros((1, 2, 6, 7, 8), np.float32), np.zeros((3, 2, 2, 3, 2), np.float32))
+    kinds = p.kernel_counts()
+    assert kinds["gemm_simt"] == 1 and kinds["pad"] == 1

@@ -16,6 +16,10 @@ sys.path.insert(0, os.path.join(HERE, "golden"))
 
 import golden_kernels as G  # noqa: E402
 
+import nkipy_b200.core.ops as _ops  # noqa: E402
+
+G.OPS = _ops
+
 from nkipy_b200.core import graph as GR  # noqa: E402
 from nkipy_b200.core.trace import NKIPyKernel  # noqa: E402
 
