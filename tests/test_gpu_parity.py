@@ -49,6 +49,24 @@ def test_matmul_bf16(m, k, n):
     assert_close(got, O.matmul(a, b), BF16_RTOL)
 
 
+@pytest.mark.parametrize("layout", ["a_t", "b_t", "both_t"])
+@pytest.mark.parametrize("m,k,n", [(1000, 512, 776), (4096, 1024, 2048), (200, 64, 128)])
+def test_matmul_bf16_transposed_operands(layout, m, k, n):
+    """M-major A (A stored K x M) and K-major B (B stored N x K) on the tensor cores."""
+    rng = np.random.default_rng(17)
+    a = (rng.standard_normal((m, k), dtype=np.float32) * 0.05).astype(BF16)
+    b = (rng.standard_normal((k, n), dtype=np.float32) * 0.05).astype(BF16)
+    at, bt = np.ascontiguousarray(a.T), np.ascontiguousarray(b.T)
+    kern = {
+        "a_t": lambda x, y: x.T @ y,
+        "b_t": lambda x, y: x @ y.T,
+        "both_t": lambda x, y: x.T @ y.T,
+    }[layout]
+    args = {"a_t": (at, b), "b_t": (a, bt), "both_t": (at, bt)}[layout]
+    got = on_device(kern, *args)
+    assert_close(got, O.matmul(a, b), BF16_RTOL)
+
+
 @pytest.mark.parametrize("b,m,k,n", [(32, 2048, 2048, 2048), (3, 130, 72, 200)])
 def test_bmm_bf16(b, m, k, n):
     rng = np.random.default_rng(6)
