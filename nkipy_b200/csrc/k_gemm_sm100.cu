@@ -19,7 +19,7 @@
 // rank's copy of a symmetric region; tiles are taken row block by row block,
 // and after the epilogue stores a tile one thread adds 1 to that row block's
 // arrival count on every rank (multimem.red through the multicast object).
-// Two more warps per CTA (warps 6-7) reduce, as soon as a row block's count
+// Four more warps per CTA (warps 6-9) reduce, as soon as a row block's count
 // shows every rank's tiles, this CTA's share of this rank's part of the block
 // (multimem.ld_reduce with fp32 accumulation, optionally + a residual, then
 // multimem.st to every rank), while later tiles are still computing.  The last
@@ -73,7 +73,8 @@ struct Args {
   int ar_rank, ar_world;
 };
 
-constexpr int AR_THREADS = 256;  // 192 + two all-reduce warps
+constexpr int AR_WARPS = 4, AR_T = AR_WARPS * 32;  // all-reduce warps per CTA
+constexpr int AR_THREADS = 192 + AR_T;
 
 using namespace sm100;
 
@@ -161,7 +162,7 @@ __device__ __forceinline__ void ar_piece(const Args &a, int cc, int64_t &lo, int
   hi = r0 * row_vecs + rlo + rn * (blockIdx.x + 1) / gridDim.x;
 }
 
-// Warps 6-7 of the fused kernel (64 threads, ct = 0..63).
+// Warps 6.. of the fused kernel (AR_T threads, ct = 0..AR_T-1).
 __device__ void ar_comm(const Args &a, int ct, volatile int *abort_flag) {
   const int lane = ct % 32;
   uint32_t *const cnt = a.ar_flags + SYMM_AR_CHUNKS;  // this rank's finished CTAs
@@ -209,7 +210,7 @@ __device__ void ar_comm(const Args &a, int ct, volatile int *abort_flag) {
         }
         valid[i] = v < hi;
         addr[i] = v;
-        if (valid[i]) v += 64;
+        if (valid[i]) v += AR_T;
       }
       if (!valid[0]) break;
       uint32_t r[8][4];
@@ -240,7 +241,7 @@ __device__ void ar_comm(const Args &a, int ct, volatile int *abort_flag) {
     atomicExch(&g_device_error, 1);
     *abort_flag = 1;
   }
-  named_bar(2, 64);  // both warps are past their last store
+  named_bar(2, AR_T);  // every all-reduce warp is past its last store
   if (ct == 0) {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
     const uint32_t prev = atomicAdd(cnt, 1u);
@@ -385,7 +386,7 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
       }
     }
   } else if (AR && warp >= 6) {
-    // ---------------- all-reduce (warps 6..7) ----------------
+    // ---------------- all-reduce (warps 6..) ----------------
     ar_comm(args, threadIdx.x - 192, abort_flag);
   } else {
     // ---------------- epilogue (warps 2..5) ----------------

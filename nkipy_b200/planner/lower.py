@@ -280,6 +280,10 @@ class Lowering:
                 return
         ob = self.new_buf("out", i, max(1, spec.nbytes))
         out_view = V.View(ob, 0, tuple(r.shape), V.dense_strides(r.shape), out_dt)
+        if isinstance(val, V.View) and val.is_dense() and np.dtype(val.dtype) == out_dt and spec.nbytes > 0:
+            # a dense result held elsewhere (the symmetric region of a fused all-reduce)
+            self.step("copy_bytes", [self.bref(val), self.bref(out_view)], [spec.nbytes], note="result copy")
+            return
         self.emit_ew(self.expr_of(val), out_view)
 
     def lifetimes(self):
@@ -1144,7 +1148,10 @@ class Lowering:
         if self.uses.get(key, 0) != 1 or len(users) != 1 or key in self.result_keys:
             return None
         u = users[0]
-        if u.op_name != "add" or id(u) in self.claimed or u.id in self.claims or len(u.operands) != 2:
+        if u.op_name != "add" or len(u.operands) != 2:
+            return None
+        rms = self._rmsnorm_of_residual(u)
+        if (id(u) in self.claimed or u.id in self.claims) and rms is None:
             return None
         a, c = u.operands
         other = c if tkey(a) == key else a
@@ -1154,7 +1161,22 @@ class Lowering:
             return None
         if np.dtype(op.result_dtype) not in (np.dtype(np.float32), BF16):
             return None
+        if rms is not None:
+            # the residual + RMSNorm recogniser claimed this add: the all-reduce
+            # applies it, and the norm reads the sum (one read and one write of
+            # the activations less)
+            rms.params["residual"] = None
+            rms.params["x"] = rms.params["sum_tensor"]
         return u, other
+
+    def _rmsnorm_of_residual(self, add_op):
+        """The residual + RMSNorm claim whose residual sum is ``add_op``, or None."""
+        for c in self.claims.values():
+            if c.kind == "rmsnorm" and c.params.get("residual") is not None:
+                st = c.params.get("sum_tensor")
+                if st is not None and st.source_op is add_op:
+                    return c
+        return None
 
 
 def lower(graph, name=None, world: int = 1) -> Plan:

@@ -249,14 +249,19 @@ def test_layer_tp2_fuses_allreduces_into_gemms():
     p = lower(NKIPyKernel.trace(W.llama_decoder_layer_kernel).specialize(*args, **kw), world=2)
     kc = p.kernel_counts()
     assert any("+rope" in s.note for s in p.steps) and p.needs_comm
-    # each row-parallel GEMM reduces its own partial sum; the second also adds the residual
+    # each row-parallel GEMM reduces its own partial sum and adds the residual after it (the
+    # first one's add is also the residual of the post-attention RMSNorm, which then reads the sum)
     assert kc["gemm_bf16_ar"] == 2 and "allreduce" not in kc and "allreduce_add" not in kc
     ar = [s for s in p.steps if s.kernel == "gemm_bf16_ar"]
-    assert [len(s.bufs) for s in ar] == [3, 4] and all(len(s.ints) == 14 for s in ar)
+    assert [len(s.bufs) for s in ar] == [4, 4] and all(len(s.ints) == 14 for s in ar)
+    norms = [s for s in p.steps if s.kernel == "rmsnorm_rows"]
+    assert norms[1].ints[4] == 0 and norms[1].bufs[0][0] == ar[0].bufs[2][0]
+    # the second all-reduce's residual is the first one's result, in the symmetric region
+    assert ar[1].bufs[3][0] == ar[0].bufs[2][0]
     # both partial sums live in the symmetric region; the layer output is copied out of it
     symm = [i for i, b in enumerate(p.buffers) if b.kind == "symm"]
     assert sorted(s.bufs[2][0] for s in ar) == symm and p.symm >= sum(p.buffers[i].nbytes for i in symm)
-    assert kc.get("ew") == 1 and p.steps[-1].kernel == "ew" and p.steps[-1].bufs[1][0] == ar[1].bufs[2][0]
+    assert "ew" not in kc and p.steps[-1].kernel == "copy_bytes" and p.steps[-1].bufs[0][0] == ar[1].bufs[2][0]
     assert "symm %d" % p.symm in p.to_text()
 
 
