@@ -74,6 +74,7 @@ struct Args {
 };
 
 constexpr int AR_WARPS = 4, AR_T = AR_WARPS * 32;  // all-reduce warps per CTA
+constexpr int AR_RUN = 64;                         // most row blocks reduced in one pass
 constexpr int AR_THREADS = 192 + AR_T;
 
 using namespace sm100;
@@ -176,7 +177,9 @@ __device__ void ar_comm(const Args &a, int ct, volatile int *abort_flag) {
   bool ok = true;
   int c = 0;
   while (c < a.tiles_m) {
-    // warp-uniform: wait for row block c, then take the run of ready blocks after it (at most 8)
+    // warp-uniform: wait for row block c, then take the run of ready blocks after it (at most
+    // AR_RUN: one block gives a thread less than one vector at 8 ranks, so a run of many blocks
+    // is what keeps eight reductions in flight per thread)
     int ce = c;
     if (lane == 0) {
       const long long t0 = clock64();
@@ -188,7 +191,7 @@ __device__ void ar_comm(const Args &a, int ct, volatile int *abort_flag) {
         __nanosleep(256);
       }
       if (ok)
-        for (ce = c + 1; ce < a.tiles_m && ce < c + 8 && ready(ce);) ++ce;
+        for (ce = c + 1; ce < a.tiles_m && ce < c + AR_RUN && ready(ce);) ++ce;
     }
     ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
     ce = __shfl_sync(0xffffffffu, ce, 0);
@@ -469,7 +472,18 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) lo[j] = pack_bf16(__uint_as_float(x0[2 * j]), __uint_as_float(x0[2 * j + 1]));
           } else {
-            const __nv_bfloat16 *cs = args.rope_cos + pos * half + d, *sn = args.rope_sin + pos * half + d;
+            // the 32 cos / sin values of this row's position, 16 bytes at a time (the
+            // planner passes 16-byte aligned tables and d is a multiple of 32)
+            const uint4 *cs4 = reinterpret_cast<const uint4 *>(args.rope_cos + pos * half + d);
+            const uint4 *sn4 = reinterpret_cast<const uint4 *>(args.rope_sin + pos * half + d);
+            uint4 cv[4], sv[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              cv[q] = cs4[q];
+              sv[q] = sn4[q];
+            }
+            const __nv_bfloat16 *cs = reinterpret_cast<const __nv_bfloat16 *>(cv);
+            const __nv_bfloat16 *sn = reinterpret_cast<const __nv_bfloat16 *>(sv);
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
               float l2[2], h2[2];
@@ -651,6 +665,8 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   if (epi == 3) {
     if (!rope || c_f32 || batch != 1 || (rope->rope_hd != 64 && rope->rope_hd != 128) || rope->rope_seq <= 0)
       return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: rotary epilogue needs bf16 output, one batch, head_dim 64 or 128");
+    if ((reinterpret_cast<uintptr_t>(rope->rope_cos) | reinterpret_cast<uintptr_t>(rope->rope_sin)) & 15)
+      return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: rotary tables must be 16-byte aligned");
     for (int i = 0; i < 2; ++i)
       if (rope->rope_r0[i] % rope->rope_hd || rope->rope_r1[i] % rope->rope_hd || rope->rope_r1[i] > N)
         return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: rotary column ranges must be whole heads");
