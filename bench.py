@@ -311,9 +311,131 @@ class Layer(Workload):
                 "l2": "weights + activations exceed L2"}
 
 
-WORKLOADS = {w.name: w for w in (Softmax, RmsNorm, Gemm, Bmm, LinAttn, Layer)}
+class Decode(Workload):
+    """One decode step of the Qwen3 attention block with its KV cache resident
+    and updated in place (examples/models/qwen3/kernels/attention.py:25-156,
+    qwen3.py:280-336): 8 sequences, cache length 2048, hidden 4096, 32 query /
+    8 KV heads of 128.  Bound by HBM: the step reads the projection weights
+    and both caches once; the roofline is taken over the whole step."""
+
+    name, metric, unit, bound, dtype, dominant = "decode", "decode tokens/s (KV-cache attention step)", "tokens/s", "hbm", "bf16", "*step*"
+    B, L, H, NQ, NKV, HD = 8, 2048, 4096, 32, 8, 128
+
+    def _args(self, B, seed):
+        from nkipy_b200 import workloads as W
+
+        rng = np.random.default_rng(seed)
+        x = rng.standard_normal((B, 1, self.H), dtype=np.float32).astype(BF16)
+        wqkv = (rng.standard_normal((self.H, (self.NQ + 2 * self.NKV) * self.HD), dtype=np.float32) * 0.02).astype(BF16)
+        wo = (rng.standard_normal((self.NQ * self.HD, self.H), dtype=np.float32) * 0.02).astype(BF16)
+        qn = rng.uniform(0.5, 1.5, self.HD).astype(BF16)
+        kn = rng.uniform(0.5, 1.5, self.HD).astype(BF16)
+        ck = rng.standard_normal((B, self.L, self.NKV, self.HD), dtype=np.float32).astype(BF16)
+        cv = rng.standard_normal((B, self.L, self.NKV, self.HD), dtype=np.float32).astype(BF16)
+        pos = np.array([self.L - 1], np.int32)
+        kw = dict(n_heads=self.NQ, head_dim=self.HD, n_kv_heads=self.NKV)
+        return W.cached_attention_kernel, (x, wqkv, qn, kn, ck, cv, pos, wo), kw
+
+    def kernel_and_args(self, rank, world):
+        return self._args(self.B, 700 + rank)
+
+    def units_per_step(self, world):
+        return self.B
+
+    def dominant_work(self):
+        # projection weights + both caches read once, the new token's cache rows written
+        w = self.H * (self.NQ + 2 * self.NKV) * self.HD * 2 + self.NQ * self.HD * self.H * 2
+        return w + 2 * self.B * self.L * self.NKV * self.HD * 2
+
+    def cpu_step(self, threads):
+        fn, args, kw = self._args(1, 11)
+        fn(*args, **kw)
+        return 1, f"1 of {self.B} sequences per step (NumPy direct call)"
+
+    def config(self, world):
+        return {"workload": "Qwen3 attention decode step bf16, KV cache 2048 resident and updated in place, "
+                            "hidden 4096, 32q/8kv x 128", "batch": self.B, "cache_len": self.L,
+                "l2": "weights + caches 149 MB exceed L2; also flushed between steps"}
+
+
+class TopK(Workload):
+    """Last-axis top-8 of 128 rows of a Qwen3 vocabulary (151936) in bf16: the
+    sampling step (core/ops/nn.py:65-152).  Bound by HBM on the logits read."""
+
+    name, metric, unit, bound, dtype, dominant = "topk", "HBM GB/s (top-8 over a vocabulary)", "GB/s", "hbm", "bf16", "topk_rows"
+    ROWS, COLS, K = 128, 151936, 8
+
+    def kernel_and_args(self, rank, world):
+        from nkipy_b200.core.ops import nn
+
+        x = np.random.default_rng(800 + rank).standard_normal((self.ROWS, self.COLS), dtype=np.float32).astype(BF16)
+
+        def topk_kernel(logits):
+            return nn.topk(logits, self.K, axis=-1)
+
+        return topk_kernel, (x,), {}
+
+    def units_per_step(self, world):
+        return self.ROWS * self.COLS * 2 / 1e9
+
+    def dominant_work(self):
+        return self.ROWS * self.COLS * 2
+
+    def cpu_step(self, threads):
+        from oracle import numpy_ref as O
+
+        rows = 16
+        x = np.random.default_rng(12).standard_normal((rows, self.COLS), dtype=np.float32).astype(BF16)
+        O.topk(x, self.K)
+        return rows * self.COLS * 2 / 1e9, f"{rows} of {self.ROWS} rows per step"
+
+    def config(self, world):
+        return {"workload": "top-8 bf16 (128, 151936) last axis", "shape": [self.ROWS, self.COLS], "k": self.K,
+                "l2": "flushed between steps"}
+
+
+class Conv(Workload):
+    """conv2d bf16, batch 16, 128 -> 128 channels, 3x3, padding 1 on 56x56
+    (core/ops/conv.py): pad, kernel windows written dense, one GEMM."""
+
+    name, metric, unit, bound, dtype, dominant = "conv", "bf16 TFLOP/s (conv2d 3x3)", "TFLOP/s", "tensor", "bf16", "gemm_bf16"
+    B, C, OC, HW = 16, 128, 128, 56
+
+    def kernel_and_args(self, rank, world):
+        from nkipy_b200.core import ops as OPS
+
+        rng = np.random.default_rng(900 + rank)
+        x = rng.standard_normal((self.B, self.C, self.HW, self.HW), dtype=np.float32).astype(BF16)
+        w = (rng.standard_normal((self.OC, self.C, 3, 3), dtype=np.float32) * 0.05).astype(BF16)
+
+        def conv_kernel(x, w):
+            return OPS.conv2d(x, w, stride=1, padding=1)
+
+        return conv_kernel, (x, w), {}
+
+    def units_per_step(self, world):
+        return 2 * self.B * self.OC * self.C * 9 * self.HW * self.HW / 1e12
+
+    def dominant_work(self):
+        return 2 * self.B * self.OC * self.C * 9 * self.HW * self.HW
+
+    def cpu_step(self, threads):
+        from oracle import numpy_ref as O
+
+        rng = np.random.default_rng(13)
+        x = rng.standard_normal((1, self.C, self.HW, self.HW), dtype=np.float32).astype(BF16)
+        w = (rng.standard_normal((self.OC, self.C, 3, 3), dtype=np.float32) * 0.05).astype(BF16)
+        O.conv_nd(x, w, padding=1)
+        return 2 * self.OC * self.C * 9 * self.HW * self.HW / 1e12, f"1 of {self.B} images per step"
+
+    def config(self, world):
+        return {"workload": "conv2d bf16 x(16,128,56,56) w(128,128,3,3) padding 1",
+                "l2": "flushed between steps"}
+
+
+WORKLOADS = {w.name: w for w in (Softmax, RmsNorm, Gemm, Bmm, LinAttn, Layer, Decode, TopK, Conv)}
 DEFAULT_WORKLOAD = "layer"
-SUITE = ("softmax", "rmsnorm", "gemm", "bmm", "linattn")
+SUITE = ("softmax", "rmsnorm", "gemm", "bmm", "linattn", "decode", "topk", "conv")
 
 
 def _parallel_rows(fn, arrays, threads):
@@ -609,7 +731,8 @@ def measure_quick(wl, steps, warmup, local_rank, with_cpu):
     names = [t["name"] for t in kernel.model_ref.io["inputs"]]
     arrays = [a for a in np_args if isinstance(a, np.ndarray)]
     ins = {n: DeviceTensor.from_numpy(a, name=n).tensor_ref for n, a in zip(names, arrays)}
-    outs = {t.name: t.tensor_ref for t in kernel.allocate_output_tensors()}
+    # a mutated input (``<name>.must_alias_input``) is bound in place as its output
+    outs = {t.name: ins.get(f"{t.name}.must_alias_input", t.tensor_ref) for t in kernel.allocate_output_tensors()}
     flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=f"cuda:{local_rank}")
     for _ in range(warmup):
         spike.execute(kernel.model_ref, ins, outs, use_graph=True)
@@ -624,7 +747,10 @@ def measure_quick(wl, steps, warmup, local_rank, with_cpu):
     peaks, _ = load_peaks()
     dom = [i for i, st in enumerate(plan_steps) if st["kernel"] == wl.dominant]
     frac = achieved = None
-    if dom:
+    if wl.dominant == "*step*":  # whole-step roofline (no single dominant launch)
+        achieved = wl.dominant_work() / (ms / 1e3) / 1e9
+        frac = achieved / float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    elif dom:
         dur = sum(step_ms[i] for i in dom)
         if wl.bound == "hbm":
             achieved = wl.dominant_work() * len(dom) / (dur / 1e3) / 1e9

@@ -95,17 +95,18 @@ __global__ void pad_kernel(const __grid_constant__ PadParams p) {
 }
 
 // Window scatter along `axis` of a (pre, axis_len, post) operand; updates are
-// (pre, n_idx, post).  Duplicate indices: the last writer wins in an
+// (pre, n_idx, post), dense within each of the `pre` blocks, blocks
+// `upd_pre_bytes` apart.  Duplicate indices: the last writer wins in an
 // unspecified order, as for XLA with unique_indices = false.
 __global__ void scatter_rows_kernel(uint8_t *__restrict__ out, const void *__restrict__ ind, int ind_dt,
                                     const uint8_t *__restrict__ upd, int64_t pre, int64_t axis_len, int64_t post_bytes,
-                                    int64_t n_idx) {
+                                    int64_t n_idx, int64_t upd_pre_bytes) {
   for (int64_t r = blockIdx.x; r < pre * n_idx; r += gridDim.x) {
     const int64_t p = r / n_idx, j = r - p * n_idx;
     const int64_t dst_row = load_index(ind, j, ind_dt);
     if (dst_row < 0 || dst_row >= axis_len) continue;  // out-of-range updates are skipped
     uint8_t *dst = out + (p * axis_len + dst_row) * post_bytes;
-    const uint8_t *src = upd + r * post_bytes;
+    const uint8_t *src = upd + p * upd_pre_bytes + j * post_bytes;
     for (int64_t b = threadIdx.x; b < post_bytes; b += blockDim.x) dst[b] = src[b];
   }
 }
@@ -202,15 +203,20 @@ int pad_launch(const LaunchArgs &a) {
 }
 
 // "scatter_rows": ptrs out idx upd; ints ind_dtype pre axis_len post_bytes n_idx
+// [upd_pre_bytes] (absent: the updates are dense)
 int srows_check(const Step &s) {
-  if (s.buf_ids.size() != 3 || s.ints.size() != 5) return fail(NKB_ERR_PLAN, "scatter_rows: bad parameters");
+  if (s.buf_ids.size() != 3 || (s.ints.size() != 5 && s.ints.size() != 6))
+    return fail(NKB_ERR_PLAN, "scatter_rows: bad parameters");
+  if (s.ints.size() == 6 && s.ints[5] < s.ints[4] * s.ints[3])
+    return fail(NKB_ERR_PLAN, "scatter_rows: update blocks overlap");
   return NKB_OK;
 }
 int srows_launch(const LaunchArgs &a) {
   const auto &q = a.step->ints;
   if (q[1] * q[4] == 0 || q[3] == 0) return NKB_OK;
+  const int64_t upd_pre = q.size() == 6 ? q[5] : q[4] * q[3];
   scatter_rows_kernel<<<grid_for(q[1] * q[4], a.device, 32), 128, 0, a.stream>>>(
-      (uint8_t *)a.ptrs[0], a.ptrs[1], (int)q[0], (const uint8_t *)a.ptrs[2], q[1], q[2], q[3], q[4]);
+      (uint8_t *)a.ptrs[0], a.ptrs[1], (int)q[0], (const uint8_t *)a.ptrs[2], q[1], q[2], q[3], q[4], upd_pre);
   return launch_status("scatter_rows_kernel");
 }
 

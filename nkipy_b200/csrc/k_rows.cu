@@ -269,7 +269,8 @@ int softmax_any(const void *x, int xdt, void *y, int ydt, int64_t rows, int64_t 
 template <int THREADS, int CHUNKS, typename T, typename TW, bool RES, bool SUM_OUT>
 __global__ void __launch_bounds__(256) rmsnorm_reg_kernel(const T *__restrict__ x, const T *__restrict__ r,
                                                           const TW *__restrict__ w, T *__restrict__ y,
-                                                          T *__restrict__ hsum, int64_t rows, int cols, float eps) {
+                                                          T *__restrict__ hsum, int64_t rows, int cols, float eps,
+                                                          int64_t xin, int64_t xos) {
   __shared__ float smem[32];
   constexpr int RPB = 256 / THREADS;
   const int sub = threadIdx.x / THREADS;
@@ -277,17 +278,19 @@ __global__ void __launch_bounds__(256) rmsnorm_reg_kernel(const T *__restrict__ 
   const float inv_n = (float)cols;
   for (int64_t row = (int64_t)blockIdx.x * RPB + sub; row - sub < rows; row += (int64_t)gridDim.x * RPB) {
     const bool active = row < rows;
-    const int64_t base = (active ? row : 0) * cols;
+    const int64_t arow = active ? row : 0;
+    const int64_t base = arow * cols;
+    const int64_t ibase = (arow / xin) * xos + (arow % xin) * cols;  // input rows: blocks of xin rows
     float v[CHUNKS][4];
     float ss = 0.f;
 #pragma unroll
     for (int c = 0; c < CHUNKS; ++c) {
       const int col = (c * THREADS + t) * 4;
       if (active && col < cols) {
-        load4(x + base + col, v[c]);
+        load4(x + ibase + col, v[c]);
         if (RES) {
           float rv[4];
-          load4(r + base + col, rv);
+          load4(r + ibase + col, rv);
 #pragma unroll
           for (int j = 0; j < 4; ++j) v[c][j] += rv[j];
           if (sizeof(T) == 2) {
@@ -325,15 +328,16 @@ template <typename T, typename TW, bool RES, bool SUM_OUT>
 __global__ void __launch_bounds__(256) rmsnorm_stream_kernel(const T *__restrict__ x, const T *__restrict__ r,
                                                              const TW *__restrict__ w, T *__restrict__ y,
                                                              T *__restrict__ hsum, int64_t rows, int64_t cols,
-                                                             float eps) {
+                                                             float eps, int64_t xin, int64_t xos) {
   __shared__ float smem[32];
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const int64_t base = row * cols;
+    const int64_t ibase = (row / xin) * xos + (row % xin) * cols;
     float ss = 0.f;
     for (int64_t c = threadIdx.x; c < cols; c += 256) {
-      float h = load1(x + base + c);
+      float h = load1(x + ibase + c);
       if (RES) {
-        h += load1(r + base + c);
+        h += load1(r + ibase + c);
         if (sizeof(T) == 2) h = __bfloat162float(__float2bfloat16_rn(h));
       }
       ss += h * h;
@@ -341,9 +345,9 @@ __global__ void __launch_bounds__(256) rmsnorm_stream_kernel(const T *__restrict
     ss = row_reduce_sum<256>(ss, smem);
     const float denom = sqrtf(__fdiv_rn(ss, (float)cols) + eps);
     for (int64_t c = threadIdx.x; c < cols; c += 256) {
-      float h = load1(x + base + c);
+      float h = load1(x + ibase + c);
       if (RES) {
-        h += load1(r + base + c);
+        h += load1(r + ibase + c);
         if (sizeof(T) == 2) h = __bfloat162float(__float2bfloat16_rn(h));
       }
       if (SUM_OUT) store1(hsum + base + c, h);
@@ -355,19 +359,20 @@ __global__ void __launch_bounds__(256) rmsnorm_stream_kernel(const T *__restrict
 
 template <typename T, typename TW, bool RES, bool SUM_OUT>
 int rmsnorm_dispatch3(const void *x, const void *r, const void *w, void *y, void *hs, int64_t rows, int64_t cols,
-                      float eps, cudaStream_t st, int device) {
+                      float eps, int64_t xin, int64_t xos, cudaStream_t st, int device) {
   const T *xi = static_cast<const T *>(x);
   const T *ri = static_cast<const T *>(r);
   const TW *wi = static_cast<const TW *>(w);
   T *yo = static_cast<T *>(y);
   T *ho = static_cast<T *>(hs);
-  const bool aligned = (cols % 4 == 0) && ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) &&
+  const bool aligned = (cols % 4 == 0) && (xos % 4 == 0) && ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) &&
                        ((uintptr_t)w % 16 == 0) && (!RES || (uintptr_t)r % 16 == 0) &&
                        (!SUM_OUT || (uintptr_t)hs % 16 == 0);
   const int64_t cap = (int64_t)num_sms(device) * 32;
   auto grid = [&](int rpb) { return (unsigned)std::min<int64_t>((rows + rpb - 1) / rpb, cap); };
 #define RMS_LAUNCH(TH, CH, RPB) \
-  rmsnorm_reg_kernel<TH, CH, T, TW, RES, SUM_OUT><<<grid(RPB), 256, 0, st>>>(xi, ri, wi, yo, ho, rows, (int)cols, eps)
+  rmsnorm_reg_kernel<TH, CH, T, TW, RES, SUM_OUT><<<grid(RPB), 256, 0, st>>>(xi, ri, wi, yo, ho, rows, (int)cols, eps, \
+                                                                       xin, xos)
   if (aligned && cols <= 1024) {
     const int ch = (int)((cols + 127) / 128);
     if (ch <= 1) RMS_LAUNCH(32, 1, 8);
@@ -381,7 +386,7 @@ int rmsnorm_dispatch3(const void *x, const void *r, const void *w, void *y, void
     else if (ch <= 4) RMS_LAUNCH(256, 4, 1);
     else RMS_LAUNCH(256, 8, 1);
   } else {
-    rmsnorm_stream_kernel<T, TW, RES, SUM_OUT><<<grid(1), 256, 0, st>>>(xi, ri, wi, yo, ho, rows, cols, eps);
+    rmsnorm_stream_kernel<T, TW, RES, SUM_OUT><<<grid(1), 256, 0, st>>>(xi, ri, wi, yo, ho, rows, cols, eps, xin, xos);
   }
 #undef RMS_LAUNCH
   return launch_status("rmsnorm_rows");
@@ -389,21 +394,25 @@ int rmsnorm_dispatch3(const void *x, const void *r, const void *w, void *y, void
 
 template <typename T, typename TW>
 int rmsnorm_dispatch2(const void *x, const void *r, const void *w, void *y, void *hs, int64_t rows, int64_t cols,
-                      float eps, cudaStream_t st, int dev) {
-  if (r && hs) return rmsnorm_dispatch3<T, TW, true, true>(x, r, w, y, hs, rows, cols, eps, st, dev);
-  if (r) return rmsnorm_dispatch3<T, TW, true, false>(x, r, w, y, hs, rows, cols, eps, st, dev);
-  return rmsnorm_dispatch3<T, TW, false, false>(x, r, w, y, hs, rows, cols, eps, st, dev);
+                      float eps, int64_t xin, int64_t xos, cudaStream_t st, int dev) {
+  if (r && hs) return rmsnorm_dispatch3<T, TW, true, true>(x, r, w, y, hs, rows, cols, eps, xin, xos, st, dev);
+  if (r) return rmsnorm_dispatch3<T, TW, true, false>(x, r, w, y, hs, rows, cols, eps, xin, xos, st, dev);
+  return rmsnorm_dispatch3<T, TW, false, false>(x, r, w, y, hs, rows, cols, eps, xin, xos, st, dev);
 }
 
+// Input rows (x and the residual) come in blocks of ``xin`` consecutive rows,
+// blocks ``xos`` elements apart (xin = rows: dense); output rows are dense.
 int rmsnorm_any(const void *x, const void *r, const void *w, void *y, void *hs, int dt, int wdt, int64_t rows,
-                int64_t cols, float eps, cudaStream_t st, int dev) {
+                int64_t cols, float eps, cudaStream_t st, int dev, int64_t xin, int64_t xos) {
   if (rows == 0 || cols == 0) return NKB_OK;
   if (!r && hs) return fail(NKB_ERR_INVALID, "rmsnorm_rows: sum output requires a residual input");
-  if (dt == NKB_F32 && wdt == NKB_F32) return rmsnorm_dispatch2<float, float>(x, r, w, y, hs, rows, cols, eps, st, dev);
+  if (xin <= 0 || rows % xin || xos < xin * cols) return fail(NKB_ERR_INVALID, "rmsnorm_rows: bad input row blocks");
+  if (dt == NKB_F32 && wdt == NKB_F32)
+    return rmsnorm_dispatch2<float, float>(x, r, w, y, hs, rows, cols, eps, xin, xos, st, dev);
   if (dt == NKB_BF16 && wdt == NKB_BF16)
-    return rmsnorm_dispatch2<__nv_bfloat16, __nv_bfloat16>(x, r, w, y, hs, rows, cols, eps, st, dev);
+    return rmsnorm_dispatch2<__nv_bfloat16, __nv_bfloat16>(x, r, w, y, hs, rows, cols, eps, xin, xos, st, dev);
   if (dt == NKB_BF16 && wdt == NKB_F32)
-    return rmsnorm_dispatch2<__nv_bfloat16, float>(x, r, w, y, hs, rows, cols, eps, st, dev);
+    return rmsnorm_dispatch2<__nv_bfloat16, float>(x, r, w, y, hs, rows, cols, eps, xin, xos, st, dev);
   return fail(NKB_ERR_UNSUPPORTED, "rmsnorm_rows: dtype combination not supported");
 }
 
@@ -574,16 +583,19 @@ int softmax_launch(const LaunchArgs &a) {
 }
 
 // "rmsnorm_rows": ptrs x r w y hsum (r/hsum may be unused per flags);
-// ints rows cols dtype w_dtype has_res has_sum; floats eps
+// ints rows cols dtype w_dtype has_res has_sum [in_block_rows in_block_stride];
+// floats eps.  Without the last two the input rows are dense.
 int rmsnorm_check(const Step &s) {
-  if (s.buf_ids.size() != 5 || s.ints.size() != 6 || s.floats.size() != 1)
+  if (s.buf_ids.size() != 5 || (s.ints.size() != 6 && s.ints.size() != 8) || s.floats.size() != 1)
     return fail(NKB_ERR_PLAN, "rmsnorm_rows: bad parameters");
   return NKB_OK;
 }
 int rmsnorm_launch(const LaunchArgs &a) {
   const auto &q = a.step->ints;
+  const bool blocks = q.size() == 8;
   return rmsnorm_any(a.ptrs[0], q[4] ? a.ptrs[1] : nullptr, a.ptrs[2], a.ptrs[3], q[5] ? a.ptrs[4] : nullptr,
-                     (int)q[2], (int)q[3], q[0], q[1], a.step->floats[0], a.stream, a.device);
+                     (int)q[2], (int)q[3], q[0], q[1], a.step->floats[0], a.stream, a.device,
+                     blocks ? q[6] : q[0], blocks ? q[7] : q[0] * q[1]);
 }
 
 // "argmax_rows": ptrs x out; ints rows cols dtype is_max
@@ -659,5 +671,5 @@ extern "C" int nkb_rmsnorm_rows(const void *x, const void *r, const void *w, voi
   int dev = 0;
   cudaGetDevice(&dev);
   return nkb::rows::rmsnorm_any(x, r, w, out, sum_out, dtype, w_dtype, rows, cols, eps,
-                                static_cast<cudaStream_t>(stream), dev);
+                                static_cast<cudaStream_t>(stream), dev, rows, rows * cols);
 }

@@ -301,6 +301,21 @@ class Lowering:
         rows = int(np.prod(t.shape[:-1])) if len(t.shape) > 1 else 1
         return v, rows, cols
 
+    def row_blocks(self, t):
+        """``(view, rows, cols, block_rows, block_stride)`` for a row kernel's
+        input: its rows read in place when they come in equally spaced blocks
+        of dense rows (per-head rows of a fused projection's output), else a
+        dense copy (one block)."""
+        val = self.get(t)
+        cols = int(t.shape[-1]) if t.shape else 1
+        rows = int(np.prod(t.shape[:-1])) if len(t.shape) > 1 else 1
+        if isinstance(val, V.View) and not val.is_dense() and rows > 0 and cols > 0:
+            shp, (st,) = V.collapse(val.shape, [val.strides])
+            if len(shp) == 2 and st[1] == 1 and shp[1] % cols == 0 and st[0] >= shp[1]:
+                return val, rows, cols, shp[1] // cols, int(st[0])
+        v, rows, cols = self.dense_rows(t)
+        return v, rows, cols, rows, rows * cols
+
     def lower_claim(self, c):
         root = c.root
         if c.kind == "softmax":
@@ -337,14 +352,17 @@ class Lowering:
                 if hs is not None:
                     self.vals[tkey(p["sum_tensor"])] = hs
             else:
-                xv, rows, cols = self.dense_rows(p["x"])
+                xv, rows, cols, blk, bstride = self.row_blocks(p["x"])
                 bufs = [self.bref(xv), self.bref(xv), self.bref(wv), self.bref(out), self.bref(out)]
+                ints = [rows, cols, E.dt_code(dt), E.dt_code(wv.dtype), 0, 0]
+                if blk != rows:
+                    ints += [blk, bstride]
                 self.step(
                     "rmsnorm_rows",
                     bufs,
-                    [rows, cols, E.dt_code(dt), E.dt_code(wv.dtype), 0, 0],
+                    ints,
                     [p["eps"]],
-                    note=f"{rows}x{cols}",
+                    note=f"{rows}x{cols}" + (f" in blocks of {blk} rows, stride {bstride}" if blk != rows else ""),
                 )
             self.vals[("o", root.id)] = out
         elif c.kind == "attention":
@@ -391,6 +409,23 @@ class Lowering:
             raise NotImplementedError("attention with mismatched head counts")
         # output stored (B, S, H, D): the traced transpose(0,2,1,3) after it is free
         out = self.tmp_view((B, S, H, D), BF16)
+        if p.get("pos") is not None:
+            # one query row against keys 0..pos of the cache: split over keys, then merged
+            posv = self.materialize(self.get(p["pos"]), dense=True)
+            skv = p["skv"]
+            splits = max(1, min(256, min(-(-2 * 148 // max(1, B * k_heads)), -(-skv // 64))))
+            ws = self.tmp_view((B * H * splits * (D + 2),), np.float32)
+            ints = [B, H, k_heads, skv, D, splits, E.dt_code(posv.dtype)]
+            ints += qs[:2] + ks[:3] + vs[:3] + [H * D, D]
+            self.step(
+                "attn_decode",
+                [self.bref(qv), self.bref(kv), self.bref(vv), self.bref(out), self.bref(posv), self.bref(ws)],
+                ints,
+                [p["scale"]],
+                note=f"decode B{B} H{H}/{k_heads} L{skv} D{D} x{splits}",
+            )
+            self.vals[("o", root.id)] = out.with_(shape=(B, H, S, D), strides=(S * H * D, D, H * D, 1))
+            return
         ints = [B, H, k_heads, S, p["skv"], D, int(p["causal"])]
         ints += qs[:3] + ks[:3] + vs[:3] + [S * H * D, D, H * D]
         self.step(
@@ -905,7 +940,12 @@ class Lowering:
         if np.dtype(upd.dtype) != np.dtype(op.result_dtype):
             # NumPy casts the assigned values to the array's dtype; the kernels copy bytes
             ue = E.op("convert", [self.expr_of(ue)], tuple(upd.shape), np.dtype(op.result_dtype))
-        uv = self.materialize(ue, dense=True)
+        upd_blocks = None  # (block elements, block stride) of an update view read in place
+        if isinstance(ue, V.View) and not ue.is_dense():
+            shp, (st,) = V.collapse(ue.shape, [ue.strides])
+            if len(shp) == 2 and st[1] == 1 and st[0] >= shp[1]:
+                upd_blocks = (int(shp[0]), int(shp[1]), int(st[0]))
+        uv = ue if upd_blocks else self.materialize(ue, dense=True)
         r = len(x.shape)
         es = np.dtype(op.result_dtype).itemsize
         ins = list(a["inserted_window_dims"])
@@ -928,12 +968,17 @@ class Lowering:
             pre = int(np.prod(x.shape[:ax])) if ax else 1
             post = int(np.prod(x.shape[ax + 1 :])) if ax + 1 < r else 1
             n_idx = int(np.prod(ind.shape)) if len(ind.shape) else 1
-            self.step(
-                "scatter_rows",
-                [self.bref(out), self.bref(iv), self.bref(uv)],
-                [E.dt_code(iv.dtype), pre, int(x.shape[ax]), post * es, n_idx],
-            )
+            ints = [E.dt_code(iv.dtype), pre, int(x.shape[ax]), post * es, n_idx]
+            if upd_blocks:
+                nb, blk, bst = upd_blocks
+                if nb == pre and blk == n_idx * post:
+                    ints.append(bst * es)  # (n_idx, post) dense per pre block: read in place
+                else:
+                    uv = self.materialize(uv, dense=True)
+            self.step("scatter_rows", [self.bref(out), self.bref(iv), self.bref(uv)], ints)
         else:
+            if upd_blocks:
+                uv = self.materialize(uv, dense=True)
             n = int(np.prod(upd.shape)) if len(upd.shape) else 1
             ints = [E.dt_code(iv.dtype), r, es, n] + [int(s) for s in x.shape] + list(V.dense_strides(x.shape))
             self.step("scatter_pts", [self.bref(out), self.bref(iv), self.bref(uv)], ints)

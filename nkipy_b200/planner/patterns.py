@@ -142,7 +142,10 @@ def _exclusive(gi: GraphIndex, ops, root) -> bool:
     return True
 
 
-def match_softmax(gi: GraphIndex, div_op) -> Optional[Claim]:
+def match_softmax(gi: GraphIndex, div_op, allow_bf16=False) -> Optional[Claim]:
+    """Row softmax in fp32; ``allow_bf16`` also takes the all-bf16 form (the
+    Qwen3 ``softmax_kernel``), for callers that evaluate it inside a fused
+    attention kernel in fp32."""
     if div_op.op_name != "divide" or len(div_op.result_shape) < 1:
         return None
     shape = tuple(div_op.result_shape)
@@ -169,7 +172,8 @@ def match_softmax(gi: GraphIndex, div_op) -> Optional[Claim]:
     x2 = last_axis_reduce(m_base, "maximum", ops)
     if x2 is None or tkey(x2) != tkey(x):
         return None
-    if np.dtype(div_op.result_dtype) != np.float32 or tuple(x.shape) != shape:
+    ok_dt = np.dtype(div_op.result_dtype) == np.float32 or (allow_bf16 and str(np.dtype(div_op.result_dtype)) == "bfloat16")
+    if not ok_dt or tuple(x.shape) != shape:
         return None
     if not _exclusive(gi, ops, div_op):
         return None
@@ -212,7 +216,8 @@ def match_rmsnorm(gi: GraphIndex, mul_op) -> Optional[Claim]:
         if psq is None or psq.op_name != "sqrt":
             continue
         ops.append(psq)
-        pa = GraphIndex.producer(psq.operands[0])
+        # ``(z + eps).astype(x.dtype)`` with x already fp32 traces as a copy
+        pa = GraphIndex.producer(strip(psq.operands[0], ops, allowed=("copy",)))
         if pa is None or pa.op_name != "add":
             continue
         ops.append(pa)
@@ -397,13 +402,14 @@ def match_attention(gi: GraphIndex, dot2) -> Optional[Claim]:
     div = GraphIndex.producer(pp.operands[0]) if pp.op_name == "convert" else pp
     if div is None or div.op_name != "divide":
         return None
-    sm = match_softmax(gi, div)
+    sm = match_softmax(gi, div, allow_bf16=True)
     if sm is None or sm.root is not pp:
         return None
     ops = [pp] + list(sm.interior)
     x = sm.params["x"]
     sq, skv = int(x.shape[2]), int(x.shape[3])
     causal = False
+    pos = None  # decode: the run-time row of a causal mask table
     px = GraphIndex.producer(x)
     scaled = x
     if px is not None and px.op_name == "add":
@@ -418,18 +424,25 @@ def match_attention(gi: GraphIndex, dot2) -> Optional[Claim]:
                     ops += tmp + [pc, px]
                     scaled = a
                     break
+            if sq == 1:
+                got = _mask_row_at(base, skv, tmp)
+                if got is not None:
+                    pos = got
+                    ops += tmp + [px]
+                    scaled = a
+                    break
         if scaled is x:
             return None
     scale = 1.0
-    raw = scaled
-    ps = GraphIndex.producer(scaled)
+    raw = _strip_float_converts(scaled, ops)
+    ps = GraphIndex.producer(raw)
     if ps is not None and ps.op_name in ("divide", "multiply"):
         tmp = []
         c = scalar_const(ps.operands[1], tmp)
         if c is not None and c != 0:
             scale = 1.0 / c if ps.op_name == "divide" else c
             ops += tmp + [ps]
-            raw = ps.operands[0]
+            raw = _strip_float_converts(ps.operands[0], ops)
     pr = GraphIndex.producer(raw)
     if pr is None or pr.op_name != "dot":
         return None
@@ -461,15 +474,66 @@ def match_attention(gi: GraphIndex, dot2) -> Optional[Claim]:
     for po in (qops, kops, vops):
         if po and _exclusive(gi, po + ops, dot2):
             path_ops += po
+    if pos is not None and d != 128:
+        return None
     params = dict(
         q=q_src, q_map=q_map, k=k_src, k_map=[k_map[0], k_map[1], k_map[3], k_map[2]], v=v_src, v_map=v_map,
         n_rep=k_rep, scale=scale, causal=causal, sq=sq, skv=skv, d=d, heads=int(q_t.shape[1]),
-        batch=int(q_t.shape[0]),
+        batch=int(q_t.shape[0]), pos=pos,
     )
     if not path_ops:
         # the operand paths are shared: read the dot operands as they are
         params.update(q=q_t, q_map=[0, 1, 2, 3], k=kt_t, k_map=[0, 1, 3, 2], v=v_t, v_map=[0, 1, 2, 3], n_rep=1)
     return Claim("attention", dot2, ops + path_ops, params)
+
+
+def _strip_float_converts(t, ops: list):
+    """Skip float -> float ``convert`` nodes (the traced scale is computed in
+    fp32 between a bf16 dot and a bf16 cast)."""
+    while True:
+        p = GraphIndex.producer(t)
+        if p is None or p.op_name != "convert" or not (_is_float(p.result_dtype) and _is_float(p.operands[0].dtype)):
+            return t
+        ops.append(p)
+        t = p.operands[0]
+
+
+def _mask_row_at(base, skv, ops: list):
+    """The index tensor ``pos`` when ``base`` is row ``pos`` of a constant causal
+    mask table (0 up to the diagonal, large negative above), gathered at run
+    time: the decode step's ``causal_mask[start_pos, :L]``
+    (``examples/models/qwen3/kernels/attention.py:128-140``)."""
+    pg = GraphIndex.producer(base)
+    if pg is None or pg.op_name != "gather":
+        return None
+    a = pg.attributes
+    if list(a.get("collapsed_slice_dims", [])) != [0] or list(a.get("start_index_map", [])) != [0]:
+        return None
+    tbl, idx = pg.operands
+    if len(tbl.shape) != 2 or int(np.prod(idx.shape)) != 1 or np.dtype(idx.dtype).kind not in "iu":
+        return None
+    if list(a.get("slice_sizes", [])) != [1, skv]:
+        return None
+    local = [pg]
+    src = tbl
+    psl = GraphIndex.producer(src)
+    if psl is not None and psl.op_name == "slice":
+        sa = psl.attributes
+        if list(sa["start_indices"]) != [0, 0] or set(sa["strides"]) != {1} or int(sa["limit_indices"][1]) != skv:
+            return None
+        local.append(psl)
+        src = psl.operands[0]
+    pc = GraphIndex.producer(src)
+    if pc is None or pc.op_name != "constant" or not isinstance(pc.attributes.get("value"), np.ndarray):
+        return None
+    table = np.asarray(pc.attributes["value"])
+    rows = int(tbl.shape[0])
+    if table.ndim != 2 or table.shape[0] < rows or table.shape[1] < skv:
+        return None
+    if _is_causal_mask(table[:rows, :skv], rows, skv) is not True or rows != skv:
+        return None
+    ops += local + [pc]
+    return idx
 
 
 def _const_value(t):

@@ -9,10 +9,40 @@ float32, with the tolerances of the benchmark definition (1e-5 relative for
 fp32 elementwise/reduction, 2e-2 for bf16 matmul paths, exact for indices).
 """
 
+import contextlib
+
 import ml_dtypes
 import numpy as np
 
 bfloat16 = np.dtype(ml_dtypes.bfloat16)
+
+
+@contextlib.contextmanager
+def fp32_accumulated_bf16_sums():
+    """Run a kernel body's direct call with ``np.sum`` over bf16 accumulated in
+    float32 (result rounded to bf16 once).
+
+    NumPy reduces an ml_dtypes bf16 array strictly in order with a bf16
+    rounding after every add, so a long sum stagnates once its ulp exceeds
+    twice the addend (1000 x 0.2 sums to 64).  The traced ``reduce`` leaves the
+    accumulation order open and the device kernels accumulate in fp32, so
+    long bf16 reductions (the decode softmax over a KV cache,
+    ``examples/models/qwen3/kernels/attention.py:141-143``) are compared against
+    the direct call with this one change.  Every other op of the body runs as
+    in the plain direct call."""
+    plain = np.sum
+
+    def sum32(a, axis=None, dtype=None, out=None, keepdims=False, **kw):
+        arr = np.asarray(a)
+        if arr.dtype == bfloat16 and dtype is None and out is None:
+            return plain(arr.astype(np.float32), axis=axis, keepdims=keepdims, **kw).astype(bfloat16)
+        return plain(a, axis=axis, dtype=dtype, out=out, keepdims=keepdims, **kw)
+
+    np.sum = sum32
+    try:
+        yield
+    finally:
+        np.sum = plain
 
 
 def softmax(x):

@@ -7,12 +7,15 @@ and ``cache_k``, and every step's output and the caches are compared with the
 NumPy direct call of the same kernel body.
 """
 
+import contextlib
+
 import ml_dtypes
 import numpy as np
 import pytest
 
 from nkipy_b200 import workloads as W
 from nkipy_b200.runtime import DeviceKernel, DeviceTensor
+from oracle import numpy_ref as O
 from tests.utils import BF16_RTOL, assert_close, on_device
 
 BF16 = np.dtype(ml_dtypes.bfloat16)
@@ -105,3 +108,40 @@ def test_successive_updates_in_place():
     got = on_device(k, a_dev, i, j, v, w)
     assert_close(got, want, 1e-5)
     np.testing.assert_array_equal(a_dev, a_cpu)
+
+
+@pytest.mark.parametrize("B,L,nq,nkv", [(2, 320, 16, 2), (3, 200, 8, 8)])
+def test_decode_attention_at_cache_edges(B, L, nq, nkv):
+    """The fused decode attention over random caches at the first position,
+    interior positions and the last row of the cache; several key chunks per
+    KV head and 1 to 8 query heads per KV head.  Up to 64 keys the plain direct
+    call is the reference; beyond, its bf16 softmax sum (accumulated in order
+    in bf16) stagnates, so the direct call with that sum accumulated in fp32
+    is (the rest of the body unchanged)."""
+    hd, D = 128, 512
+    kw = dict(n_heads=nq, head_dim=hd, n_kv_heads=nkv)
+    x, wqkv, qn, kn, wo = _inputs(B, L, nq, nkv, hd, D, 1, seed=5)
+    rng = np.random.default_rng(6)
+    ck0 = rng.standard_normal((B, L, nkv, hd), dtype=np.float32).astype(BF16)
+    cv0 = rng.standard_normal((B, L, nkv, hd), dtype=np.float32).astype(BF16)
+    dec = DeviceKernel.compile_and_load(W.cached_attention_kernel, x, wqkv, qn, kn, ck0, cv0,
+                                        np.array([0], np.int32), wo, name="cache_decode_edges", **kw)
+    w = {n: DeviceTensor.from_numpy(a) for n, a in
+         (("qkv_weight", wqkv), ("q_norm_weight", qn), ("k_norm_weight", kn), ("o_weight", wo))}
+    xd = DeviceTensor.from_numpy(x)
+    for pos in (0, 1, 63, 64, L // 2 + 7, L - 1):
+        ck, cv = ck0.copy(), cv0.copy()
+        with contextlib.nullcontext() if pos <= 64 else O.fp32_accumulated_bf16_sums():
+            want = W.cached_attention_kernel(x, wqkv, qn, kn, ck, cv, np.array([pos], np.int32), wo, **kw)
+        dk, dv = DeviceTensor.from_numpy(ck0), DeviceTensor.from_numpy(cv0)
+        out = DeviceTensor.empty((B, 1, D), BF16)
+        dec(inputs=dict(w, x=xd, start_pos=DeviceTensor.from_numpy(np.array([pos], np.int32)),
+                        **{"cache_k.must_alias_input": dk, "cache_v.must_alias_input": dv}),
+            outputs={"output0": out, "cache_k": dk, "cache_v": dv})
+        assert_close(out.numpy(), want, BF16_RTOL)
+        for got, exp in ((dk.numpy(), ck), (dv.numpy(), cv)):
+            # the new token's row is computed (bf16 rounding of a different
+            # accumulation order); every other row is untouched, bit for bit
+            assert_close(got[:, pos], exp[:, pos], BF16_RTOL)
+            keep = np.arange(L) != pos
+            np.testing.assert_array_equal(got[:, keep].view(np.uint16), exp[:, keep].view(np.uint16))

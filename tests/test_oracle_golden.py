@@ -146,3 +146,16 @@ def test_convolution_vectors():
                                V("conv2_y"), rtol=1e-6, atol=1e-6)
     np.testing.assert_allclose(CV.conv3d(V("conv3_x"), V("conv3_w"), None, stride=(1, 2, 1), padding=1), V("conv3_y"),
                                rtol=1e-6, atol=1e-6)
+
+
+def test_bf16_sum_accumulation_modes():
+    """NumPy sums ml_dtypes bf16 in order with bf16 rounding (stagnates);
+    the fp32-accumulated mode rounds once and leaves np.sum as it found it."""
+    a = np.full(1000, 0.2, O.bfloat16)
+    assert float(np.sum(a)) == 64.0
+    plain = np.sum
+    with O.fp32_accumulated_bf16_sums():
+        assert float(np.sum(a)) == 200.0
+        assert np.sum(a.reshape(10, 100), axis=-1, keepdims=True).shape == (10, 1)
+        assert np.sum(np.ones(5, np.float32)).dtype == np.float32
+    assert np.sum is plain

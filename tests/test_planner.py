@@ -163,6 +163,18 @@ def test_kv_cache_decode_updates_caches_in_place():
     assert [p.buffers[s.bufs[0][0]].kind for s in sc] == ["out", "out"]
     cache_ins = {i for i, b in enumerate(p.buffers) if b.kind == "in" and b.index in (4, 5)}
     assert not any(s.kernel == "ew" and s.bufs[1][0] in cache_ins for s in p.steps)
+    # the attention of the new token is one fused step reading the updated caches
+    kinds = [s.kernel for s in p.steps]
+    assert kinds.count("attn_decode") == 1
+    dec = p.steps[kinds.index("attn_decode")]
+    assert kinds.index("attn_decode") > max(i for i, k in enumerate(kinds) if k == "scatter_rows")
+    assert {p.buffers[dec.bufs[i][0]].kind for i in (1, 2)} == {"out"}
+    assert dec.ints[:7] == [2, 4, 2, 64, 128, dec.ints[5], 3] and dec.floats == [pytest.approx(128 ** -0.5)]
+    # per-head q/k RMSNorm rows and the new value row are read in place from the QKV projection
+    width = (4 + 2 * 2) * 128
+    assert [s.ints[6:] for s in p.steps if s.kernel == "rmsnorm_rows"] == [[4, width], [2, width]]
+    assert [len(s.ints) for s in sc] == [5, 6] and sc[1].ints[5] == width * 2
+    assert "ew" not in kinds[kinds.index("gemm_bf16"):kinds.index("rmsnorm_rows")]
 
 
 def test_readers_of_a_mutated_parameter_run_before_its_update():
