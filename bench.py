@@ -768,6 +768,8 @@ def measure_quick(wl, steps, warmup, local_rank, with_cpu):
         "dominant_achieved": achieved,
         "roofline_frac": frac,
         "bound": wl.bound,
+        "per_launch_ms": {f"{i}:{st['kernel']}": round(t, 4) for i, (st, t) in enumerate(zip(plan_steps, step_ms))}
+        if len(step_ms) <= 24 else None,
     }
     if with_cpu:
         cv, desc, _ = cpu_measure(wl, 1, 0, os.cpu_count() or 1)

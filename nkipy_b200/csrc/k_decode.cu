@@ -8,13 +8,15 @@
 // from device memory (clamped into the cache as a gather index is).
 //
 // Split over keys ("flash-decoding"): CTA (b, g, c) takes KV head g of batch b,
-// every query head of its group, and chunk c of the keys.  Four warps; lane l
-// of a warp scores key base + l for all heads of the group (the key row read
-// once, q from shared memory), then the warp folds its 32 scores into a running
-// max / sum per head and accumulates sum_s p_s v_s with lane l owning features
-// 4l..4l+3 (each value row read once per warp, coalesced).  The CTA writes its
-// partial (max, sum, unnormalised output) per head; a second kernel merges the
-// chunks of each (b, h).  fp32 throughout, bf16 output.
+// every query head of its group, and chunk c of the keys.  Four warps, each
+// taking tiles of 32 keys: the warp first issues the loads of the tile's 32
+// value rows (lane l owning features 4l..4l+3, coalesced, held in registers)
+// and of its key rows (lane l: key base + l, 16 bytes at a time, all in
+// flight), then scores every head of the group, folds the 32 scores into a
+// running max / sum per head and accumulates sum_s p_s v_s from the
+// registers.  The CTA writes its partial (max, sum, unnormalised output) per
+// head; a second kernel merges the chunks of each (b, h).  fp32 throughout,
+// bf16 output.
 #include "common.cuh"
 
 namespace nkb {
@@ -74,29 +76,36 @@ __global__ void __launch_bounds__(THREADS) attn_decode_kernel(const __grid_const
   for (int t0 = k0 + warp * KEY_TILE; t0 < k1; t0 += 4 * KEY_TILE) {
     const int s = t0 + lane;
     const bool live = s < k1;
+    const int nk = min(KEY_TILE, k1 - t0);
+    // the tile's value rows, loaded before they are needed (zeros past the chunk)
+    uint2 vv[KEY_TILE];
+#pragma unroll
+    for (int j = 0; j < KEY_TILE; ++j)
+      vv[j] = j < nk ? *reinterpret_cast<const uint2 *>(vbase + (int64_t)(t0 + j) * p.vs + 4 * lane) : make_uint2(0, 0);
+    // key row s, all 16-byte loads in flight
+    uint4 kr[D / 8];
+    const uint4 *krow = reinterpret_cast<const uint4 *>(kbase + (int64_t)(live ? s : t0) * p.ks);
+#pragma unroll
+    for (int j = 0; j < D / 8; ++j) kr[j] = krow[j];
     // scores of key s for every head of the group
     float sc[MAX_REP];
 #pragma unroll
     for (int r = 0; r < MAX_REP; ++r) sc[r] = 0.f;
-    if (live) {
-      const uint4 *krow = reinterpret_cast<const uint4 *>(kbase + (int64_t)s * p.ks);
-#pragma unroll 4
-      for (int j = 0; j < D / 8; ++j) {
-        const uint4 u = krow[j];
-        const __nv_bfloat162 *kk = reinterpret_cast<const __nv_bfloat162 *>(&u);
-        float kf[8];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(kk[e]);
-          kf[2 * e] = f.x;
-          kf[2 * e + 1] = f.y;
-        }
+    for (int j = 0; j < D / 8; ++j) {
+      const __nv_bfloat162 *kk = reinterpret_cast<const __nv_bfloat162 *>(&kr[j]);
+      float kf[8];
 #pragma unroll
-        for (int r = 0; r < MAX_REP; ++r) {
-          if (r < R) {
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(kk[e]);
+        kf[2 * e] = f.x;
+        kf[2 * e + 1] = f.y;
+      }
 #pragma unroll
-            for (int e = 0; e < 8; ++e) sc[r] = fmaf(s_q[r][8 * j + e], kf[e], sc[r]);
-          }
+      for (int r = 0; r < MAX_REP; ++r) {
+        if (r < R) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) sc[r] = fmaf(s_q[r][8 * j + e], kf[e], sc[r]);
         }
       }
     }
@@ -120,12 +129,11 @@ __global__ void __launch_bounds__(THREADS) attn_decode_kernel(const __grid_const
 #pragma unroll
       for (int j = 0; j < 4; ++j) o[r][j] *= corr;
     }
-    // sum_s p_s v_s: lane owns features 4*lane .. 4*lane+3
-    const int nk = min(KEY_TILE, k1 - t0);
-    for (int j = 0; j < nk; ++j) {
-      const uint2 vv = *reinterpret_cast<const uint2 *>(vbase + (int64_t)(t0 + j) * p.vs + 4 * lane);
-      const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vv.x));
-      const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vv.y));
+    // sum_s p_s v_s: lane owns features 4*lane .. 4*lane+3 (p = 0 past the chunk)
+#pragma unroll
+    for (int j = 0; j < KEY_TILE; ++j) {
+      const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vv[j].x));
+      const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vv[j].y));
 #pragma unroll
       for (int r = 0; r < MAX_REP; ++r) {
         if (r >= R) continue;
@@ -186,8 +194,8 @@ __global__ void __launch_bounds__(D) attn_decode_combine_kernel(const __grid_con
   p.out[(int64_t)b * p.ob + (int64_t)h * p.oh + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
 }
 
-// The planner picks the chunk count (enough CTAs for two per SM, chunks of at
-// least 64 keys) and sizes the workspace: B * H * splits * (D + 2) floats.
+// The planner picks the chunk count (chunks of ~128 keys, at least four CTAs
+// per SM in all) and sizes the workspace: B * H * splits * (D + 2) floats.
 // "attn_decode": ptrs q k v out pos ws; ints B H HKV S D splits pos_dtype
 //                qb qh kb kh ks vb vh vs ob oh; floats scale
 int check(const Step &s) {

@@ -71,6 +71,11 @@ struct Args {
   uint64_t ar_mc_flags;         // the slot through the multicast object
   const __nv_bfloat16 *ar_res;  // optional residual (dense, N columns): C = res + sum
   int ar_rank, ar_world;
+  // split-K (few output tiles, long K: the decode projections): work unit =
+  // (tile, split); split s takes k-blocks [s * kb / ksplit, (s + 1) * kb / ksplit)
+  // and stores its fp32 partial rows to ws[s][M][N]; a second kernel sums them
+  int ksplit;
+  float *ws;
 };
 
 constexpr int AR_WARPS = 4, AR_T = AR_WARPS * 32;  // all-reduce warps per CTA
@@ -111,6 +116,22 @@ __device__ __forceinline__ void tile_coords(int t, const Args &a, int &bm, int &
   const int within = r - g * group_span;
   bm = first_m + within % gsize;
   bn = within / gsize;
+}
+
+// Work unit t -> tile coordinates and its range of k-blocks.
+template <bool AR>
+__device__ __forceinline__ void unit_coords(int t, const Args &a, int k_blocks, int &bm, int &bn, int &bb, int &split,
+                                            int &kb0, int &kb1) {
+  split = 0;
+  if (!AR && a.ksplit > 1) {
+    const int per_split = a.tiles_m * a.tiles_n * (int)a.batch;
+    split = t / per_split;
+    t -= split * per_split;
+  }
+  tile_coords<AR>(t, a, bm, bn, bb);
+  const int ks = AR ? 1 : max(1, a.ksplit);
+  kb0 = (int)((int64_t)split * k_blocks / ks);
+  kb1 = (int)((int64_t)(split + 1) * k_blocks / ks);
 }
 
 // ---- fused all-reduce helpers ------------------------------------------------
@@ -286,7 +307,7 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int num_tiles = args.tiles_m * args.tiles_n * (int)args.batch;
+  const int num_tiles = args.tiles_m * args.tiles_n * (int)args.batch * (AR ? 1 : max(1, args.ksplit));
   const int k_blocks = (int)((args.K + BK - 1) / BK);
 
   if (threadIdx.x == 0) {
@@ -317,9 +338,9 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        int bm, bn, bb;
-        tile_coords<AR>(t, args, bm, bn, bb);
-        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+        int bm, bn, bb, split, kb0, kb1;
+        unit_coords<AR>(t, args, k_blocks, bm, bn, bb, split, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
@@ -362,7 +383,9 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
         if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+        int bm, bn, bb, split, kb0, kb1;
+        unit_coords<AR>(t, args, k_blocks, bm, bn, bb, split, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&full[s], ph, abort_flag)) {
@@ -380,7 +403,7 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
                                                 : smem_desc(a_addr + k * 32, 16, 1024);
             const uint64_t db = args.b_k_major ? smem_desc(b_addr + k * 32, 16, 1024)
                                                : smem_desc(b_addr + k * 2048, 64 * BK * 2, 1024);
-            umma_f16(d_tmem, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_f16(d_tmem, da, db, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[s]);  // stage s free once these MMAs have read it
         }
@@ -397,8 +420,8 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
     const int row_in_tile = quad * 32 + lane;
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
-      int bm, bn, bb;
-      tile_coords<AR>(t, args, bm, bn, bb);
+      int bm, bn, bb, split, kb0, kb1;
+      unit_coords<AR>(t, args, k_blocks, bm, bn, bb, split, kb0, kb1);
       const int acc = local & 1;
       const uint32_t acc_ph = (local >> 1) & 1;
       bool got = mbar_wait(&acc_full[acc], acc_ph, abort_flag);
@@ -523,6 +546,18 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
         const int64_t col = col0 + c * 32;
         if (!row_ok || col >= args.N) continue;
         const bool full_chunk = col + 32 <= args.N;
+        if (!AR && args.ksplit > 1) {
+          // this split's fp32 partial of the row (summed and rounded by splitk_reduce)
+          float *dst = args.ws + ((int64_t)split * args.M + row) * args.N + col;
+          if (full_chunk && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<uint4 *>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+          } else {
+            for (int j = 0; j < 32 && col + j < args.N; ++j) dst[j] = __uint_as_float(r[j]);
+          }
+          continue;
+        }
         if (args.c_f32) {
           float *dst = static_cast<float *>(args.C) + bb * args.sC + row * args.ldc + col;
           if (full_chunk && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
@@ -621,12 +656,55 @@ bool tc_eligible(const void *A, const void *B, int64_t lda, int64_t ldb, int64_t
   return true;
 }
 
+// C = bf16(sum over s of ws[s]) for the split-K partials ws[ksplit][M][N] (fp32).
+template <bool VEC>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restrict__ ws, __nv_bfloat16 *__restrict__ C,
+                                                            int64_t M, int64_t N, int64_t ldc, int ks) {
+  const int64_t per = VEC ? 4 : 1;
+  const int64_t n = M * N / per;
+  const int64_t plane = M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i * per, row = e / N, col = e - row * N;
+    if (VEC) {
+      float4 acc = *reinterpret_cast<const float4 *>(ws + e);
+      for (int s = 1; s < ks; ++s) {
+        const float4 v = *reinterpret_cast<const float4 *>(ws + s * plane + e);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      __nv_bfloat16 *dst = C + row * ldc + col;
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+      uint2 u;
+      u.x = *reinterpret_cast<const uint32_t *>(&lo);
+      u.y = *reinterpret_cast<const uint32_t *>(&hi);
+      *reinterpret_cast<uint2 *>(dst) = u;
+    } else {
+      float acc = ws[e];
+      for (int s = 1; s < ks; ++s) acc += ws[s * plane + e];
+      C[row * ldc + col] = __float2bfloat16_rn(acc);
+    }
+  }
+}
+
+int splitk_reduce(const float *ws, __nv_bfloat16 *C, int64_t M, int64_t N, int64_t ldc, int ks, cudaStream_t st,
+                  int device) {
+  const bool vec = N % 4 == 0 && ldc % 4 == 0 && (reinterpret_cast<uintptr_t>(C) & 7) == 0;
+  const int64_t work = M * N / (vec ? 4 : 1);
+  const unsigned grid = (unsigned)std::min<int64_t>((work + 255) / 256, (int64_t)num_sms(device) * 8);
+  if (vec) splitk_reduce_kernel<true><<<grid, 256, 0, st>>>(ws, C, M, N, ldc, ks);
+  else splitk_reduce_kernel<false><<<grid, 256, 0, st>>>(ws, C, M, N, ldc, ks);
+  return launch_status("splitk_reduce_kernel");
+}
+
 // C[b] = op(A[b]) @ op(B[b]).  a_mn_major: A stored K x M (lda = row stride of
 // that storage); b_k_major: B stored N x K.
 int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t N, int64_t K, int64_t lda,
             int64_t ldb, int64_t ldc, int64_t batch, int64_t sA, int64_t sB, int64_t sC, int a_mn_major, int b_k_major,
             cudaStream_t st, int device, int epi = 0, int64_t n_half = 0, const void *res = nullptr, int64_t ldr = 0,
-            const Args *rope = nullptr, const SymmAr *ar = nullptr, const void *ar_res = nullptr) {
+            const Args *rope = nullptr, const SymmAr *ar = nullptr, const void *ar_res = nullptr, int ksplit = 1,
+            float *ws = nullptr) {
   if (M == 0 || N == 0 || batch == 0) return NKB_OK;
   if (K == 0) return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: K == 0 takes the strided path");
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(NKB_ERR_UNSUPPORTED, "gemm: dims exceed int32");
@@ -662,6 +740,16 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   args.n_half = n_half;
   args.res = static_cast<const __nv_bfloat16 *>(res);
   args.ldr = ldr;
+  args.ksplit = 1;
+  args.ws = nullptr;
+  if (ksplit > 1) {
+    if (epi != 0 || c_f32 || batch != 1 || ar || !ws || (reinterpret_cast<uintptr_t>(ws) & 15) ||
+        ksplit > (K + BK - 1) / BK)
+      return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: split-K needs a plain bf16 product, one batch, a workspace and "
+                                       "at most one split per k-block");
+    args.ksplit = ksplit;
+    args.ws = ws;
+  }
   if (epi == 3) {
     if (!rope || c_f32 || batch != 1 || (rope->rope_hd != 64 && rope->rope_hd != 128) || rope->rope_seq <= 0)
       return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: rotary epilogue needs bf16 output, one batch, head_dim 64 or 128");
@@ -692,7 +780,7 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   }
   // one CTA per SM: every CTA of the fused kernel is resident at once, so its
   // all-reduce warps can wait for tiles of other CTAs
-  const int grid = (int)std::min<int64_t>(tiles, num_sms(device));
+  const int grid = (int)std::min<int64_t>(tiles * args.ksplit, num_sms(device));
   if (ar) {
     if (epi != 0 || c_f32 || batch != 1 || ldc != N || N % 8 || args.tiles_m > SYMM_AR_CHUNKS)
       return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: fused all-reduce needs a dense bf16 C, one batch, no epilogue");
@@ -706,7 +794,9 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   } else {
     gemm_bf16_tcgen05<false><<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, args);
   }
-  return launch_status("gemm_bf16_tcgen05");
+  if (int e = launch_status("gemm_bf16_tcgen05")) return e;
+  if (args.ksplit > 1) return splitk_reduce(ws, static_cast<__nv_bfloat16 *>(C), M, N, ldc, args.ksplit, st, device);
+  return NKB_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -782,14 +872,17 @@ int gemm_simt(const SimtArgs &p, cudaStream_t st) {
 //              [epi ldr]     (epi 2, fourth pointer R: C = A @ B + R, R row stride ldr)
 //              [epi hd seq q0 q1 k0 k1]  (epi 3, pointers COS SIN: rotary embedding of
 //                            the heads in columns [q0, q1) and [k0, k1))
+//              [epi ksplit]  (epi 4, pointer WS: split-K over ksplit k-ranges, fp32
+//                            partials in WS (ksplit * M * N floats), then summed)
 int tc_check(const Step &s) {
   const size_t n = s.ints.size();
   if (n != 13 && n != 15 && n != 20) return fail(NKB_ERR_PLAN, "gemm_bf16: bad parameters");
   const int epi = n > 13 ? (int)s.ints[13] : 0;
   if ((epi == 3) != (n == 20)) return fail(NKB_ERR_PLAN, "gemm_bf16: bad epilogue parameters");
-  const size_t ptrs = epi == 2 ? 4u : epi == 3 ? 5u : 3u;
+  const size_t ptrs = (epi == 2 || epi == 4) ? 4u : epi == 3 ? 5u : 3u;
   if (s.buf_ids.size() != ptrs) return fail(NKB_ERR_PLAN, "gemm_bf16: bad pointer count");
-  if (epi < 0 || epi > 3) return fail(NKB_ERR_PLAN, "gemm_bf16: unknown epilogue");
+  if (epi < 0 || epi > 4) return fail(NKB_ERR_PLAN, "gemm_bf16: unknown epilogue");
+  if (epi == 4 && s.ints[14] < 2) return fail(NKB_ERR_PLAN, "gemm_bf16: split-K needs two or more splits");
   return NKB_OK;
 }
 int tc_launch(const LaunchArgs &a) {
@@ -808,6 +901,10 @@ int tc_launch(const LaunchArgs &a) {
     rope.rope_r0[1] = q[18];
     rope.rope_r1[1] = q[19];
   }
+  if (epi == 4)
+    return gemm_tc(a.ptrs[0], a.ptrs[1], a.ptrs[2], (int)q[10], q[0], q[1], q[2], q[3], q[4], q[5], q[6], q[7], q[8],
+                   q[9], (int)q[11], (int)q[12], a.stream, a.device, 0, 0, nullptr, 0, nullptr, nullptr, nullptr,
+                   (int)q[14], static_cast<float *>(a.ptrs[3]));
   return gemm_tc(a.ptrs[0], a.ptrs[1], a.ptrs[2], (int)q[10], q[0], q[1], q[2], q[3], q[4], q[5], q[6], q[7], q[8],
                  q[9], (int)q[11], (int)q[12], a.stream, a.device, epi, n_half, epi == 2 ? a.ptrs[3] : nullptr, ldr,
                  epi == 3 ? &rope : nullptr);

@@ -417,6 +417,108 @@ int rmsnorm_any(const void *x, const void *r, const void *w, void *y, void *hs, 
 }
 
 // ---------------------------------------------------------------------------
+// RMSNorm of per-head rows followed by the half-split rotary embedding
+// ---------------------------------------------------------------------------
+// The q/k path of the Qwen3 attention (examples/models/qwen3/kernels/
+// attention.py:103-118, rmsnorm.py:4-21, rope.py:34-57): every (token, head)
+// row of head_dim = 2 * half bf16 values is normalised in fp32 and rounded to
+// bf16, then rotated with the cos / sin row of its position, each traced bf16
+// node rounded:  lo = r(r(x0 * cos) - r(x1 * sin)),  hi = r(r(x0 * sin) + r(x1 * cos)).
+// One warp per row, lane l owning columns 4l..4l+3, its partner half one
+// shuffle away.  Table row of row r: clamp(pos) (a run-time position, the
+// traced gather) plus, for per-token tables, the token index (r / H) % S.
+struct RopeRows {
+  const __nv_bfloat16 *cos, *sin;
+  int64_t tstride;    // elements between table rows
+  const void *pos;    // nullable: position 0
+  int pos_dt;
+  int64_t T, S, H;    // table rows (clamp bound), tokens, heads
+  int per_token;
+};
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+template <typename TW>
+__global__ void __launch_bounds__(256) rmsnorm_rope_kernel(const __nv_bfloat16 *__restrict__ x,
+                                                           const TW *__restrict__ w, __nv_bfloat16 *__restrict__ y,
+                                                           int64_t rows, int cols, float eps, int64_t xin,
+                                                           int64_t xos, const __grid_constant__ RopeRows rp) {
+  const int lane = threadIdx.x % 32;
+  const int half = cols / 2;
+  const int col = 4 * lane;
+  const bool has = col < cols;
+  int64_t p0 = 0;
+  if (rp.pos) {
+    const uint32_t raw = load_as_reg(rp.pos, 0, rp.pos_dt);
+    p0 = (rp.pos_dt == NKB_U32 || rp.pos_dt == NKB_U16 || rp.pos_dt == NKB_U8) ? (int64_t)raw : (int64_t)(int32_t)raw;
+    p0 = p0 < 0 ? 0 : (p0 >= rp.T ? rp.T - 1 : p0);
+  }
+  for (int64_t row = ((int64_t)blockIdx.x * 256 + threadIdx.x) / 32; row < rows; row += (int64_t)gridDim.x * 8) {
+    const int64_t ibase = (row / xin) * xos + (row % xin) * cols;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (has) load4(x + ibase + col, v);
+    float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float denom = sqrtf(__fdiv_rn(ss, (float)cols) + eps);
+    float o[4];
+    if (has) {
+      float wv[4];
+      load4(w + col, wv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = bf16_round(__fdiv_rn(v[j], denom) * wv[j]);
+    } else {
+      o[0] = o[1] = o[2] = o[3] = 0.f;
+    }
+    float other[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) other[j] = __shfl_xor_sync(0xffffffffu, o[j], half / 4);
+    if (has) {
+      const bool lo = col < half;
+      const int d = lo ? col : col - half;
+      const int64_t t = p0 + (rp.per_token ? (row / rp.H) % rp.S : 0);
+      float cs[4], sn[4];
+      load4(rp.cos + t * rp.tstride + d, cs);
+      load4(rp.sin + t * rp.tstride + d, sn);
+      float r[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float x0 = lo ? o[j] : other[j], x1 = lo ? other[j] : o[j];
+        r[j] = lo ? bf16_round(bf16_round(x0 * cs[j]) - bf16_round(x1 * sn[j]))
+                  : bf16_round(bf16_round(x0 * sn[j]) + bf16_round(x1 * cs[j]));
+      }
+      store4(y + row * cols + col, r);
+    }
+  }
+}
+
+int rmsnorm_rope_any(const void *x, const void *w, void *y, int wdt, int64_t rows, int64_t cols, float eps,
+                     int64_t xin, int64_t xos, const RopeRows &rp, cudaStream_t st, int dev) {
+  if (rows == 0) return NKB_OK;
+  if (cols != 64 && cols != 128) return fail(NKB_ERR_UNSUPPORTED, "rmsnorm_rope_rows: head_dim must be 64 or 128");
+  if (xin <= 0 || rows % xin || xos < xin * cols || xos % 4)
+    return fail(NKB_ERR_INVALID, "rmsnorm_rope_rows: bad input row blocks");
+  if (rp.T < 1 || rp.S < 1 || rp.H < 1 || rp.tstride < cols / 2 || rp.tstride % 4)
+    return fail(NKB_ERR_INVALID, "rmsnorm_rope_rows: bad table geometry");
+  // 4 bf16 (8 bytes) per lane; an fp32 weight is read 16 bytes at a time
+  if ((((uintptr_t)x | (uintptr_t)y | (uintptr_t)rp.cos | (uintptr_t)rp.sin) & 7) ||
+      ((uintptr_t)w & (wdt == NKB_F32 ? 15 : 7)))
+    return fail(NKB_ERR_UNSUPPORTED, "rmsnorm_rope_rows: operands not aligned for vector loads");
+  const unsigned grid = (unsigned)std::min<int64_t>((rows + 7) / 8, (int64_t)num_sms(dev) * 8);
+  const auto *xi = static_cast<const __nv_bfloat16 *>(x);
+  auto *yo = static_cast<__nv_bfloat16 *>(y);
+  if (wdt == NKB_BF16)
+    rmsnorm_rope_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(xi, static_cast<const __nv_bfloat16 *>(w), yo, rows,
+                                                            (int)cols, eps, xin, xos, rp);
+  else if (wdt == NKB_F32)
+    rmsnorm_rope_kernel<float><<<grid, 256, 0, st>>>(xi, static_cast<const float *>(w), yo, rows, (int)cols, eps, xin,
+                                                     xos, rp);
+  else
+    return fail(NKB_ERR_UNSUPPORTED, "rmsnorm_rope_rows: weight dtype");
+  return launch_status("rmsnorm_rope_kernel");
+}
+
+// ---------------------------------------------------------------------------
 // argmax / argmin over the last axis: first occurrence of the extreme value
 // (reference core/ops/reduce.py:227-311 lowers it to max -> compare -> iota
 // -> select -> min, i.e. the smallest index holding the maximum).
@@ -598,6 +700,30 @@ int rmsnorm_launch(const LaunchArgs &a) {
                      blocks ? q[6] : q[0], blocks ? q[7] : q[0] * q[1]);
 }
 
+// "rmsnorm_rope_rows": ptrs x w y cos sin pos (pos unused when has_pos = 0);
+// ints rows cols w_dtype in_block_rows in_block_stride table_stride has_pos
+//      pos_dtype table_rows S H per_token; floats eps.  x, y, cos, sin bf16.
+int rmsnorm_rope_check(const Step &s) {
+  if (s.buf_ids.size() != 6 || s.ints.size() != 12 || s.floats.size() != 1)
+    return fail(NKB_ERR_PLAN, "rmsnorm_rope_rows: bad parameters");
+  return NKB_OK;
+}
+int rmsnorm_rope_launch(const LaunchArgs &a) {
+  const auto &q = a.step->ints;
+  RopeRows rp;
+  rp.cos = static_cast<const __nv_bfloat16 *>(a.ptrs[3]);
+  rp.sin = static_cast<const __nv_bfloat16 *>(a.ptrs[4]);
+  rp.tstride = q[5];
+  rp.pos = q[6] ? a.ptrs[5] : nullptr;
+  rp.pos_dt = (int)q[7];
+  rp.T = q[8];
+  rp.S = q[9];
+  rp.H = q[10];
+  rp.per_token = (int)q[11];
+  return rmsnorm_rope_any(a.ptrs[0], a.ptrs[1], a.ptrs[2], (int)q[2], q[0], q[1], a.step->floats[0], q[3], q[4], rp,
+                          a.stream, a.device);
+}
+
 // "argmax_rows": ptrs x out; ints rows cols dtype is_max
 int argext_check(const Step &s) {
   if (s.buf_ids.size() != 2 || s.ints.size() != 4) return fail(NKB_ERR_PLAN, "argmax_rows: bad parameters");
@@ -654,6 +780,7 @@ int reduce_launch(const LaunchArgs &a) {
 
 NKB_REGISTER_KERNEL("softmax_rows", rows::softmax_launch, rows::softmax_check);
 NKB_REGISTER_KERNEL("rmsnorm_rows", rows::rmsnorm_launch, rows::rmsnorm_check);
+NKB_REGISTER_KERNEL("rmsnorm_rope_rows", rows::rmsnorm_rope_launch, rows::rmsnorm_rope_check);
 NKB_REGISTER_KERNEL("argmax_rows", rows::argext_launch, rows::argext_check);
 NKB_REGISTER_KERNEL("reduce", rows::reduce_launch, rows::reduce_check);
 

@@ -92,13 +92,178 @@ __global__ void __launch_bounds__(kThreads) topk_rows_kernel(const void *__restr
   }
 }
 
+// ---------------------------------------------------------------------------
+// k <= 32: one pass over the row.  A row is cut into `parts` ranges, one CTA
+// (256 threads) each; every thread keeps the KL largest keys it has seen in a
+// sorted register list (one compare against the list's last key rejects
+// almost every element), reading the row 16 bytes at a time.  The CTA then
+// merges its 256 lists (k rounds of warp max + pop per warp, then across the
+// eight warps); with several parts a second kernel merges the parts' lists.
+// ---------------------------------------------------------------------------
+constexpr int kPartThreads = 256;
+
+template <int KL>
+__device__ __forceinline__ void list_insert(uint64_t (&lst)[KL], uint64_t key) {
+  if (key > lst[KL - 1]) {
+#pragma unroll
+    for (int j = KL - 1; j > 0; --j) lst[j] = key > lst[j - 1] ? lst[j - 1] : (key > lst[j] ? key : lst[j]);
+    lst[0] = key > lst[0] ? key : lst[0];
+  }
+}
+
+// Top `k` keys over the lists of the warp's lanes (k <= KL); lane 0 ends with
+// them in out[0..k).  Lists are sorted descending; a lane pops its head when it wins.
+template <int KL>
+__device__ __forceinline__ void warp_merge(uint64_t (&lst)[KL], int k, uint64_t *out) {
+  const int lane = threadIdx.x & 31;
+  for (int r = 0; r < k; ++r) {
+    const uint64_t best = warp_max64(lst[0]);
+    if (lane == 0) out[r] = best;
+    if (lst[0] == best && best != 0) {  // keys are distinct: exactly one lane owns it
+#pragma unroll
+      for (int j = 0; j < KL - 1; ++j) lst[j] = lst[j + 1];
+      lst[KL - 1] = 0;
+    }
+  }
+}
+
+__device__ __forceinline__ uint64_t make_key(uint32_t img, int64_t c) {
+  return ((uint64_t)img << 32) | (uint32_t)~(uint32_t)c;
+}
+
+__device__ __forceinline__ void emit(const void *x, int64_t base, int64_t cols, int esize, uint64_t key, void *vals,
+                                     uint32_t *idx, int64_t o) {
+  uint32_t col = ~(uint32_t)(key & 0xffffffffu);
+  if (col >= cols) col = 0;  // only an empty-list sentinel (never reached when k <= cols) lies outside the row
+  idx[o] = col;
+  const uint8_t *src = static_cast<const uint8_t *>(x) + (base + col) * esize;
+  uint8_t *dst = static_cast<uint8_t *>(vals) + o * esize;
+  for (int b = 0; b < esize; ++b) dst[b] = src[b];
+}
+
+template <int KL>
+__global__ void __launch_bounds__(kPartThreads) topk_part_kernel(const void *__restrict__ x, int dt, int64_t rows,
+                                                                 int64_t cols, int parts, int64_t part_len, int k,
+                                                                 int esize, int vec, uint64_t *__restrict__ ws,
+                                                                 void *__restrict__ vals, uint32_t *__restrict__ idx) {
+  __shared__ uint64_t s_cand[kPartThreads / 32][KL];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t row = blockIdx.x / parts;
+  const int part = (int)(blockIdx.x % parts);
+  if (row >= rows) return;
+  const int64_t base = row * cols;
+  const int64_t c0 = (int64_t)part * part_len, c1 = min(cols, c0 + part_len);
+  uint64_t lst[KL];
+#pragma unroll
+  for (int j = 0; j < KL; ++j) lst[j] = 0;
+  if (vec == 2) {  // bf16 / f16 rows, 8 per 16-byte load (c0 and the row start 16-byte aligned)
+    const uint4 *p = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) + base + c0);
+    const int64_t n8 = (c1 - c0) / 8;
+    for (int64_t i = tid; i < n8; i += kPartThreads) {
+      const uint4 u = p[i];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t h = (w[e >> 1] >> ((e & 1) * 16)) & 0xffffu;
+        const uint32_t bits = dt == NKB_BF16 ? (h << 16) : __float_as_uint(__half2float(__ushort_as_half((uint16_t)h)));
+        list_insert<KL>(lst, make_key(order_bits(bits, dt), c0 + i * 8 + e));
+      }
+    }
+    for (int64_t c = c0 + n8 * 8 + tid; c < c1; c += kPartThreads)
+      list_insert<KL>(lst, make_key(order_bits(load_as_reg(x, base + c, dt), dt), c));
+  } else if (vec == 4) {  // fp32 / int32 / uint32 rows, 4 per load
+    const uint4 *p = reinterpret_cast<const uint4 *>(static_cast<const uint32_t *>(x) + base + c0);
+    const int64_t n4 = (c1 - c0) / 4;
+    for (int64_t i = tid; i < n4; i += kPartThreads) {
+      const uint4 u = p[i];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) list_insert<KL>(lst, make_key(order_bits(w[e], dt), c0 + i * 4 + e));
+    }
+    for (int64_t c = c0 + n4 * 4 + tid; c < c1; c += kPartThreads)
+      list_insert<KL>(lst, make_key(order_bits(load_as_reg(x, base + c, dt), dt), c));
+  } else {
+    for (int64_t c = c0 + tid; c < c1; c += kPartThreads)
+      list_insert<KL>(lst, make_key(order_bits(load_as_reg(x, base + c, dt), dt), c));
+  }
+  const int kk = parts > 1 ? KL : k;  // a part hands on its full list
+  warp_merge<KL>(lst, kk, s_cand[warp]);
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int j = 0; j < KL; ++j) lst[j] = (lane < kPartThreads / 32 && j < kk) ? s_cand[lane][j] : 0;
+    __shared__ uint64_t s_out[KL];
+    warp_merge<KL>(lst, kk, s_out);
+    __syncwarp();
+    if (parts > 1) {
+      if (lane < kk) ws[((int64_t)row * parts + part) * KL + lane] = s_out[lane];
+    } else if (lane < k) {
+      emit(x, base, cols, esize, s_out[lane], vals, idx, row * k + lane);
+    }
+  }
+}
+
+// one warp per row: the parts' lists (parts * KL keys) -> the row's top k
+template <int KL>
+__global__ void __launch_bounds__(256, 1) topk_merge_kernel(const void *__restrict__ x, int64_t rows, int64_t cols,
+                                                         int parts, int k, int esize,
+                                                         const uint64_t *__restrict__ ws, void *__restrict__ vals,
+                                                         uint32_t *__restrict__ idx) {
+  __shared__ uint64_t s_out[8][KL];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + warp;
+  if (row >= rows) return;  // whole warps leave together
+  uint64_t lst[KL];
+#pragma unroll
+  for (int j = 0; j < KL; ++j) lst[j] = 0;
+  const uint64_t *src = ws + row * parts * KL;
+  for (int i = lane; i < parts * KL; i += 32) list_insert<KL>(lst, src[i]);
+  warp_merge<KL>(lst, k, s_out[warp]);
+  __syncwarp();
+  if (lane < k) emit(x, row * cols, cols, esize, s_out[warp][lane], vals, idx, row * k + lane);
+}
+
+template <int KL>
+int topk_parts(const void *x, int dt, void *vals, uint32_t *idx, int64_t rows, int64_t cols, int k, int esize,
+               uint64_t *ws, int parts, cudaStream_t st, int device) {
+  int64_t part_len = (cols + parts - 1) / parts;
+  part_len = (part_len + 7) / 8 * 8;  // part starts stay 16-byte aligned
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
+  int vec = 0;
+  if (esize == 2 && (dt == NKB_BF16 || dt == NKB_F16) && (xa & 15) == 0 && (cols * 2) % 16 == 0) vec = 2;
+  if (esize == 4 && (dt == NKB_F32 || dt == NKB_I32 || dt == NKB_U32) && (xa & 15) == 0 && (cols * 4) % 16 == 0)
+    vec = 4;
+  topk_part_kernel<KL><<<(unsigned)(rows * parts), kPartThreads, 0, st>>>(x, dt, rows, cols, parts, part_len, k, esize,
+                                                                          vec, ws, vals, idx);
+  if (int e = launch_status("topk_part_kernel")) return e;
+  if (parts == 1) return NKB_OK;
+  topk_merge_kernel<KL><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, rows, cols, parts, k, esize, ws, vals, idx);
+  return launch_status("topk_merge_kernel");
+}
+
+// Parts per row for the one-pass path: enough CTAs for two per SM, at least
+// 4096 columns per part, at most 64 parts.
+int topk_parts_for(int64_t rows, int64_t cols, int sms) {
+  int64_t p = (2 * (int64_t)sms + rows - 1) / std::max<int64_t>(rows, 1);
+  p = std::min<int64_t>(p, std::max<int64_t>(1, cols / 4096));
+  return (int)std::max<int64_t>(1, std::min<int64_t>(p, 64));
+}
+
 int topk_any(const void *x, int dt, void *vals, uint32_t *idx, int64_t rows, int64_t cols, int64_t k,
-             cudaStream_t stream, int device) {
+             cudaStream_t stream, int device, uint64_t *ws = nullptr, int64_t ws_keys = 0) {
   const int es = dtype_size(dt);
   if (!es || dt == NKB_F8E4M3 || dt == NKB_F8E5M2) return fail(NKB_ERR_UNSUPPORTED, "topk: dtype");
   if (k < 1 || k > cols) return fail(NKB_ERR_INVALID, "topk: k must be in [1, cols]");
-  if (cols > 0xffffffffll) return fail(NKB_ERR_UNSUPPORTED, "topk: rows longer than 2^32");
+  if (cols >= 0xffffffffll) return fail(NKB_ERR_UNSUPPORTED, "topk: rows of 2^32 - 1 or more elements");
   if (rows == 0) return NKB_OK;
+  if (k <= 32 && rows <= INT32_MAX / 64) {
+    const int KL = k <= 8 ? 8 : k <= 16 ? 16 : 32;
+    int parts = topk_parts_for(rows, cols, num_sms(device));
+    if (parts > 1 && (!ws || ws_keys < rows * parts * KL)) parts = 1;  // no room for the parts' lists
+    if (KL == 8) return topk_parts<8>(x, dt, vals, idx, rows, cols, (int)k, es, ws, parts, stream, device);
+    if (KL == 16) return topk_parts<16>(x, dt, vals, idx, rows, cols, (int)k, es, ws, parts, stream, device);
+    return topk_parts<32>(x, dt, vals, idx, rows, cols, (int)k, es, ws, parts, stream, device);
+  }
   const bool staged = cols <= kSmemCols;
   const size_t smem = staged ? (size_t)cols * 4 : 0;
   if (smem > 48 * 1024)
@@ -109,16 +274,19 @@ int topk_any(const void *x, int dt, void *vals, uint32_t *idx, int64_t rows, int
   return launch_status("topk_rows_kernel");
 }
 
-// "topk_rows": ptrs x values indices; ints rows cols k dtype
+// "topk_rows": ptrs x values indices [ws]; ints rows cols k dtype [ws_keys]
+// (ws: room for the per-part key lists of the one-pass path, ws_keys uint64 keys)
 int check(const Step &s) {
-  if (s.buf_ids.size() != 3 || s.ints.size() != 4) return fail(NKB_ERR_PLAN, "topk_rows: bad parameters");
+  if (!((s.buf_ids.size() == 3 && s.ints.size() == 4) || (s.buf_ids.size() == 4 && s.ints.size() == 5)))
+    return fail(NKB_ERR_PLAN, "topk_rows: bad parameters");
   if (s.ints[2] < 1 || s.ints[2] > s.ints[1]) return fail(NKB_ERR_PLAN, "topk_rows: k out of range");
   return NKB_OK;
 }
 int launch(const LaunchArgs &a) {
   const auto &q = a.step->ints;
+  const bool has_ws = q.size() == 5;
   return topk_any(a.ptrs[0], (int)q[3], a.ptrs[1], static_cast<uint32_t *>(a.ptrs[2]), q[0], q[1], q[2], a.stream,
-                  a.device);
+                  a.device, has_ws ? static_cast<uint64_t *>(a.ptrs[3]) : nullptr, has_ws ? q[4] : 0);
 }
 
 }  // namespace topk

@@ -262,6 +262,7 @@ class Lowering:
             spec = IoSpec(r.name, tuple(r.shape), odt)
             outputs.append(spec)
             self.bind_output(i, r, spec)
+        self.split_k()
         lifetimes = self.lifetimes()
         scratch = pack_arena(self.buffers, lifetimes)
         symm = pack_symmetric(self.buffers)
@@ -285,6 +286,33 @@ class Lowering:
             self.step("copy_bytes", [self.bref(val), self.bref(out_view)], [spec.nbytes], note="result copy")
             return
         self.emit_ew(self.expr_of(val), out_view)
+
+    # B200: 148 SMs, tcgen05 GEMM tiles of 128 x 256 x 64
+    SMS, TILE_M, TILE_N, TILE_K = 148, 128, 256, 64
+
+    def split_k(self):
+        """Plain bf16 GEMMs with too few output tiles to occupy the SMs (the
+        decode projections: 8 rows against a weight matrix) split their K range
+        so about one work unit per SM streams its share of the weights; the
+        fp32 partials go to a workspace and are summed once.  Runs after every
+        fusion (an all-reduce merges only into a plain GEMM)."""
+        for s in self.steps:
+            if s.kernel != "gemm_bf16" or len(s.ints) != 13 or len(s.bufs) != 3:
+                continue
+            M, N, K = s.ints[:3]
+            if s.ints[6] != 1 or s.ints[10] != 0 or M <= 0 or N <= 0:
+                continue
+            tiles = -(-M // self.TILE_M) * -(-N // self.TILE_N)
+            k_blocks = -(-K // self.TILE_K)
+            if 2 * tiles > self.SMS or k_blocks < 4:
+                continue
+            ks = min(k_blocks // 2, self.SMS // tiles)
+            if ks < 2 or ks * M * N * 4 > (256 << 20):
+                continue
+            ws = self.new_buf("tmp", -1, ks * M * N * 4)
+            s.bufs.append((ws, 0))
+            s.ints += [4, ks]
+            s.note += f" split-k {ks}"
 
     def lifetimes(self):
         life = {}
@@ -315,6 +343,42 @@ class Lowering:
                 return val, rows, cols, shp[1] // cols, int(st[0])
         v, rows, cols = self.dense_rows(t)
         return v, rows, cols, rows, rows * cols
+
+    def lower_rmsnorm_rope(self, p, wv, out, shape):
+        """Per-head RMSNorm with the rotary embedding in its epilogue: one
+        ``rmsnorm_rope_rows`` launch reading the cos / sin rows itself (at the
+        run-time position for a gathered row, per token for a prefill table)."""
+        rp = p["rope"]
+        half = shape[3] // 2
+        tshape = (int(rp["rows"]), half)
+        tabs = []
+        for t in (rp["cos"], rp["sin"]):
+            v = self.get(t)
+            st = V.reshape_strides(v.shape, v.strides, tshape) if isinstance(v, V.View) else None
+            if st is None or st[1] != 1:
+                v = self.materialize(v, dense=True)
+                st = V.dense_strides(tshape)
+            tabs.append(v.with_(shape=tshape, strides=tuple(int(x) for x in st)))
+        cv, sv = tabs
+        if tshape[0] > 1 and cv.strides[0] != sv.strides[0]:
+            cv, sv = (self.materialize(v, dense=True) for v in tabs)
+        ts = int(cv.strides[0]) if tshape[0] > 1 else half
+        xv, rows, cols, blk, bstride = self.row_blocks(p["x"])
+        if rp["pos"] is not None:
+            posv = self.materialize(self.get(rp["pos"]), dense=True)
+            has_pos, pos_dt = 1, E.dt_code(posv.dtype)
+        else:
+            posv, has_pos, pos_dt = cv, 0, 0
+        B, S, H, _ = shape
+        ints = [rows, cols, E.dt_code(wv.dtype), blk, bstride, ts, has_pos, pos_dt, int(cv.shape[0]), S, H,
+                rp["per_token"]]
+        self.step(
+            "rmsnorm_rope_rows",
+            [self.bref(xv), self.bref(wv), self.bref(out), self.bref(cv), self.bref(sv), self.bref(posv)],
+            ints,
+            [p["eps"]],
+            note=f"{rows}x{cols} + rotary ({'position' if has_pos else 'per token' if rp['per_token'] else 'row 0'})",
+        )
 
     def lower_claim(self, c):
         root = c.root
@@ -351,6 +415,8 @@ class Lowering:
                 )
                 if hs is not None:
                     self.vals[tkey(p["sum_tensor"])] = hs
+            elif p.get("rope") is not None:
+                self.lower_rmsnorm_rope(p, wv, out, tuple(int(d) for d in root.result_shape))
             else:
                 xv, rows, cols, blk, bstride = self.row_blocks(p["x"])
                 bufs = [self.bref(xv), self.bref(xv), self.bref(wv), self.bref(out), self.bref(out)]
@@ -413,7 +479,10 @@ class Lowering:
             # one query row against keys 0..pos of the cache: split over keys, then merged
             posv = self.materialize(self.get(p["pos"]), dense=True)
             skv = p["skv"]
-            splits = max(1, min(256, min(-(-2 * 148 // max(1, B * k_heads)), -(-skv // 64))))
+            # chunks of ~128 keys (many CTAs: the last wave is a small share), at least
+            # four per SM in all, at most 256 chunks of 32 or more keys
+            bg = max(1, B * k_heads)
+            splits = max(1, min(256, -(-skv // 32), max(-(-skv // 128), -(-4 * 148 // bg))))
             ws = self.tmp_view((B * H * splits * (D + 2),), np.float32)
             ints = [B, H, k_heads, skv, D, splits, E.dt_code(posv.dtype)]
             ints += qs[:2] + ks[:3] + vs[:3] + [H * D, D]
@@ -426,7 +495,7 @@ class Lowering:
             )
             self.vals[("o", root.id)] = out.with_(shape=(B, H, S, D), strides=(S * H * D, D, H * D, 1))
             return
-        ints = [B, H, k_heads, S, p["skv"], D, int(p["causal"])]
+        ints = [B, H, k_heads, S, p.get("kv_len", p["skv"]), D, int(p["causal"])]
         ints += qs[:3] + ks[:3] + vs[:3] + [S * H * D, D, H * D]
         self.step(
             "flash_attn",
@@ -823,13 +892,15 @@ class Lowering:
         """``conv2d`` / ``conv3d`` (``core/ops/conv.py:230-312``) as one GEMM.
 
         The zero-padded input (one ``pad`` launch when the padding is not 0) is
-        read through a strided view of its kernel windows, ordered (batch,
-        output position, channel, kernel offset); one ``ew`` launch writes it
-        dense, so the correlation is cols (B*P x C*prod(k)) @ W^T (C*prod(k) x
-        OC): the weight, row-major (OC, C, *k), is a K-major right operand as
-        it lies.  The (B, P, OC) product is then moved to the (B, OC, *out)
-        result layout.  bf16 runs on ``gemm_bf16`` (fp32 accumulation), other
-        dtypes on ``gemm_simt``.
+        read through a strided view of its kernel windows, ordered (channel,
+        kernel offset, batch, output position); one ``ew`` launch writes it
+        dense, its innermost axis the output column (contiguous in the input
+        at stride 1, so the copy is coalesced on both sides).  The correlation
+        is then cols^T^T @ W^T: the window matrix is an M-major left operand
+        (C*prod(k) rows of B*P positions) and the weight, row-major
+        (OC, C, *k), a K-major right operand as it lies.  The (B, P, OC)
+        product is moved to the (B, OC, *out) result layout.  bf16 runs on
+        ``gemm_bf16`` (fp32 accumulation), other dtypes on ``gemm_simt``.
         """
         x, w = op.operands
         a = op.attributes
@@ -864,24 +935,24 @@ class Lowering:
             xv = pv
         xs = xv.strides
         win = xv.with_(
-            shape=(B,) + out_sp + (C,) + ks,
-            strides=(xs[0],) + tuple(xs[2 + i] * stride[i] for i in range(n)) + (xs[1],)
-            + tuple(xs[2 + i] * dil[i] for i in range(n)),
+            shape=(C,) + ks + (B,) + out_sp,
+            strides=(xs[1],) + tuple(xs[2 + i] * dil[i] for i in range(n)) + (xs[0],)
+            + tuple(xs[2 + i] * stride[i] for i in range(n)),
         )
         P, KK = int(np.prod(out_sp)), C * int(np.prod(ks))
-        cols = self.tmp_view((B * P, KK), x.dtype)
+        M, N, K = B * P, OC, KK
+        cols = self.tmp_view((KK, M), x.dtype)  # cols[kk, b * P + p]
         self.copy_view(win, cols.with_(shape=win.shape, strides=V.dense_strides(win.shape)))
         wv = self.materialize(self.get(w), dense=True)
-        M, N, K = B * P, OC, KK
         prod = self.tmp_view((B, P, OC), dt)
         eb = np.dtype(BF16).itemsize
         if (np.dtype(cols.dtype) == BF16 and np.dtype(wv.dtype) == BF16 and dt == BF16 and K % 8 == 0
-                and N % 8 == 0 and (wv.offset * eb) % 16 == 0):
+                and N % 8 == 0 and M % 8 == 0 and (wv.offset * eb) % 16 == 0):
             self.step("gemm_bf16", [self.bref(cols), self.bref(wv), self.bref(prod)],
-                      [M, N, K, K, K, N, 1, 0, 0, 0, 0, 0, 1], note=f"tc {M}x{N}x{K} convolution")
+                      [M, N, K, M, K, N, 1, 0, 0, 0, 0, 1, 1], note=f"tc {M}x{N}x{K} convolution")
         else:
             self.step("gemm_simt", [self.bref(cols), self.bref(wv), self.bref(prod)],
-                      [E.dt_code(cols.dtype), E.dt_code(wv.dtype), E.dt_code(dt), M, N, K, 1, K, 1, 1, K, N, 1, 0, 0, 0],
+                      [E.dt_code(cols.dtype), E.dt_code(wv.dtype), E.dt_code(dt), M, N, K, 1, 1, M, 1, K, N, 1, 0, 0, 0],
                       note=f"simt {M}x{N}x{K} convolution")
         # (B, P, OC) -> (B, OC, *out)
         moved = prod.with_(shape=(B, OC) + out_sp,
@@ -996,8 +1067,17 @@ class Lowering:
         shape = tuple(op.result_shape)
         vals = self.tmp_view(shape, x.dtype)
         idx = self.tmp_view(shape, np.uint32)
-        self.step("topk_rows", [self.bref(xv), self.bref(vals), self.bref(idx)],
-                  [rows, cols, k, E.dt_code(xv.dtype)], note=f"{rows}x{cols} k={k}")
+        bufs = [self.bref(xv), self.bref(vals), self.bref(idx)]
+        ints = [rows, cols, k, E.dt_code(xv.dtype)]
+        if k <= 32 and rows > 0:
+            # room for the one-pass kernel's per-part key lists: up to 64 parts of
+            # k rounded up to 8, 16 or 32 keys per row
+            kl = 8 if k <= 8 else 16 if k <= 16 else 32
+            keys = rows * min(64, max(1, cols // 4096)) * kl
+            ws = self.new_buf("tmp", -1, keys * 8)
+            bufs.append((ws, 0))
+            ints.append(keys)
+        self.step("topk_rows", bufs, ints, note=f"{rows}x{cols} k={k}")
         self.tuples[op.id] = (vals, idx)
 
     def op_get_tuple_element(self, op):

@@ -21,6 +21,7 @@ used only inside the composition, claims the nodes for one fused launch:
                    (``qwen3_embedding/kernels/attention.py:75-95``).
 """
 
+import hashlib
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional
 
@@ -277,6 +278,13 @@ def match_rmsnorm(gi: GraphIndex, mul_op) -> Optional[Claim]:
         if out_dtype != np.dtype(x.dtype):
             continue
         params = {"x": x, "w": w, "eps": eps, "out_dtype": out_dtype, "residual": None, "sum_needed": False}
+        if res is None and root is not mul_op:
+            rope = _rope_after_norm(gi, root, shape)
+            if rope is not None:
+                rops, params["rope"], cat = rope
+                ops.append(root)
+                ops += [o for o in rops if o is not cat]
+                root = cat
         if res is not None:
             params["residual"] = (res.operands[0], res.operands[1])
             inside = {id(o) for o in ops if o is not None} | {id(root), id(mul_op)}
@@ -287,6 +295,131 @@ def match_rmsnorm(gi: GraphIndex, mul_op) -> Optional[Claim]:
             params["sum_tensor"] = x
         return Claim("rmsnorm", root, [o for o in ops if o is not None and o is not root], params)
     return None
+
+
+def _carried_axes(t, ops: list):
+    """Follow reshape (unit axes only) and broadcast producers from ``t`` back to
+    the underlying value.  Returns ``(base, axes)``: ``axes[i]`` is the axis of
+    ``base`` that axis ``i`` of ``t`` runs along (None: broadcast or unit)."""
+    p = GraphIndex.producer(t)
+    shp = [int(d) for d in t.shape]
+    if p is None or p.op_name not in ("reshape", "broadcast"):
+        return t, [i if shp[i] != 1 else None for i in range(len(shp))]
+    base, axes = _carried_axes(p.operands[0], ops)
+    if base is None:
+        return None, None
+    ops.append(p)
+    src = [int(d) for d in p.operands[0].shape]
+    out = [None] * len(shp)
+    if p.op_name == "broadcast":
+        for i, d in enumerate(p.attributes["broadcast_dimensions"]):
+            out[d] = axes[i] if src[i] == shp[d] else None
+        return base, out
+    src_nu = [(axes[i], src[i]) for i in range(len(src)) if src[i] != 1]
+    dst_nu = [i for i in range(len(shp)) if shp[i] != 1]
+    if [n for _, n in src_nu] != [shp[i] for i in dst_nu]:
+        return None, None  # a reshape that merges or splits axes
+    for (a, _), i in zip(src_nu, dst_nu):
+        out[i] = a
+    return base, out
+
+
+def _table_row_gather(base):
+    """``(table, index)`` when ``base`` (1, n) is row ``index`` of a 2-D table,
+    gathered at run time (``tensor_apis.constant(cos)[start_pos]``)."""
+    pg = GraphIndex.producer(base)
+    if pg is None or pg.op_name != "gather" or len(base.shape) != 2 or int(base.shape[0]) != 1:
+        return None
+    a = pg.attributes
+    tbl, idx = pg.operands
+    if list(a.get("collapsed_slice_dims", [])) != [0] or list(a.get("start_index_map", [])) != [0]:
+        return None
+    if len(tbl.shape) != 2 or int(np.prod(idx.shape)) != 1 or np.dtype(idx.dtype).kind not in "iu":
+        return None
+    if list(a.get("slice_sizes", [])) != [1, int(tbl.shape[1])] or int(tbl.shape[1]) != int(base.shape[1]):
+        return None
+    return tbl, idx, pg
+
+
+def _rope_after_norm(gi: GraphIndex, heads_op, shape):
+    """The half-split rotation (rope.py:34-57) applied to the bf16 (B, S, H, hd)
+    output of a per-head RMSNorm, every node bf16, with cos / sin either a row
+    of a table gathered at a run-time position (decode) or an (S, hd/2) table
+    read per token (prefill).  Returns (ops, params, concatenate op) or None."""
+    if len(shape) != 4 or shape[3] not in (64, 128) or str(np.dtype(heads_op.result_dtype)) != "bfloat16":
+        return None
+    rot = _rotation_of(gi, heads_op)
+    if rot is None:
+        return None
+    cat, rops, cos_b, sin_b = rot
+    if any(str(np.dtype(o.result_dtype)) != "bfloat16" for o in rops):
+        return None
+    half = shape[3] // 2
+    src = {}
+    for m in (o for o in rops if o.op_name == "multiply"):
+        for t in m.operands:
+            if GraphIndex.producer(t) in rops:
+                continue  # the half slice
+            base, axes = _carried_axes(t, [])
+            if base is None or _table_key(base) not in (_table_key(cos_b), _table_key(sin_b)):
+                return None
+            src.setdefault(_table_key(base), set()).add(tuple(axes))
+    if len(src) != 2 or any(len(v) != 1 for v in src.values()):
+        return None
+    tables = {}
+    for name, b in (("cos", cos_b), ("sin", sin_b)):
+        bs = [int(d) for d in b.shape]
+        last = len(bs) - 1
+        if str(np.dtype(b.dtype)) != "bfloat16" or not bs or bs[last] != half:
+            return None
+        (axes,) = src[_table_key(b)]
+        nonunit = {i for i, d in enumerate(bs) if d != 1}
+        g = _table_row_gather(b)
+        if g is not None:
+            if list(axes) != [None, None, None, last]:
+                return None
+            tables[name] = {"table": g[0], "rows": int(g[0].shape[0]), "pos": g[1], "gather": g[2], "per_token": 0}
+        elif axes[3] == last and axes[0] is None and axes[2] is None and axes[1] is not None \
+                and bs[axes[1]] == shape[1] and nonunit <= {axes[1], last}:
+            # an (S, hd/2) table (possibly with unit axes) read per token
+            tables[name] = {"table": b, "rows": shape[1], "pos": None, "gather": None, "per_token": 1}
+        elif list(axes) == [None, None, None, last] and nonunit <= {last}:
+            tables[name] = {"table": b, "rows": 1, "pos": None, "gather": None, "per_token": 0}
+        else:
+            return None
+    c, sn = tables["cos"], tables["sin"]
+    if c["per_token"] != sn["per_token"] or (c["pos"] is None) != (sn["pos"] is None):
+        return None
+    if c["pos"] is not None and (tkey(c["pos"]) != tkey(sn["pos"]) or tuple(c["table"].shape) != tuple(sn["table"].shape)):
+        return None
+    params = {"cos": c["table"], "sin": sn["table"], "rows": c["rows"], "pos": c["pos"], "per_token": c["per_token"],
+              "gathers": [g for g in (c["gather"], sn["gather"]) if g is not None]}
+    return rops, params, cat
+
+
+def absorb_rope_gathers(gi: GraphIndex, claims, taken: set):
+    """A rotary-table row gathered at run time whose every use lies inside
+    fused RMSNorm + rotation claims (which read the table at the position
+    themselves): the gather and the reshape / broadcast views of its row are
+    taken out of the graph."""
+    for c in list(claims.values()):
+        rope = c.params.get("rope") if c.kind == "rmsnorm" else None
+        for g in (rope or {}).get("gathers", []):
+            if id(g) in taken or ("o", g.id) in gi.results:
+                continue
+            chain, frontier, ok = [g], [g], True
+            while frontier and ok:
+                op = frontier.pop()
+                for u in gi.consumers.get(("o", op.id), []):
+                    if id(u) in taken:
+                        continue
+                    if u.op_name in ("reshape", "broadcast") and ("o", u.id) not in gi.results:
+                        chain.append(u)
+                        frontier.append(u)
+                    else:
+                        ok = False
+            if ok:
+                taken |= {id(o) for o in chain}
 
 
 def match_argmax(gi: GraphIndex, cvt_op) -> Optional[Claim]:
@@ -371,19 +504,42 @@ def _trace_kv(t, ops: list):
     return cur, amap, n_rep
 
 
-def _is_causal_mask(arr, sq, skv) -> Optional[bool]:
+def _is_causal_mask(arr, sq, skv):
+    """True: causal with the queries at the end of the keys (query i sees keys
+    up to i + skv - sq); "prefix": query i sees keys 0..i only, so keys from
+    sq on are masked for every query (a cache prefill, ``mask[:S, :L]``);
+    False: all zero; None: anything else."""
     a = np.asarray(arr).astype(np.float32)
     a = a.reshape(a.shape[-2:]) if a.size == sq * skv else None
     if a is None or a.shape != (sq, skv):
         return None
-    shift = skv - sq
     rows = np.arange(sq)[:, None]
     cols = np.arange(skv)[None, :]
-    upper = cols > rows + shift
-    if np.all(a[~upper] == 0) and np.all(a[upper] <= -1000.0):
-        return True
+    for shift, kind in ((skv - sq, True), (0, "prefix")):
+        upper = cols > rows + shift
+        if np.all(a[~upper] == 0) and np.all(a[upper] <= -1000.0):
+            return kind
     if np.all(a == 0):
         return False
+    return None
+
+
+def _const_array(t, ops: list):
+    """The value of ``t`` when it is a constant or a slice of one."""
+    p = GraphIndex.producer(t)
+    if p is None:
+        return None
+    if p.op_name == "constant" and isinstance(p.attributes.get("value"), np.ndarray):
+        ops.append(p)
+        return np.asarray(p.attributes["value"])
+    if p.op_name == "slice":
+        v = _const_array(p.operands[0], ops)
+        if v is None:
+            return None
+        a = p.attributes
+        ops.append(p)
+        return v[tuple(slice(int(b), int(e), int(st)) for b, e, st in
+                       zip(a["start_indices"], a["limit_indices"], a["strides"]))]
     return None
 
 
@@ -409,6 +565,7 @@ def match_attention(gi: GraphIndex, dot2) -> Optional[Claim]:
     x = sm.params["x"]
     sq, skv = int(x.shape[2]), int(x.shape[3])
     causal = False
+    kv_len = skv  # keys read: a prefix-causal mask masks keys from sq on
     pos = None  # decode: the run-time row of a causal mask table
     px = GraphIndex.producer(x)
     scaled = x
@@ -416,12 +573,15 @@ def match_attention(gi: GraphIndex, dot2) -> Optional[Claim]:
         for a, m in (px.operands, px.operands[::-1]):
             tmp = []
             base = strip(m, tmp)
-            pc = GraphIndex.producer(base)
-            if pc is not None and pc.op_name == "constant" and isinstance(pc.attributes.get("value"), np.ndarray):
-                c = _is_causal_mask(pc.attributes["value"], sq, skv)
+            cops = []
+            val = _const_array(base, cops)
+            if val is not None:
+                c = _is_causal_mask(val, sq, skv)
                 if c is not None:
-                    causal = c
-                    ops += tmp + [pc, px]
+                    causal = bool(c)
+                    if c == "prefix":
+                        kv_len = sq
+                    ops += tmp + cops + [px]
                     scaled = a
                     break
             if sq == 1:
@@ -478,7 +638,7 @@ def match_attention(gi: GraphIndex, dot2) -> Optional[Claim]:
         return None
     params = dict(
         q=q_src, q_map=q_map, k=k_src, k_map=[k_map[0], k_map[1], k_map[3], k_map[2]], v=v_src, v_map=v_map,
-        n_rep=k_rep, scale=scale, causal=causal, sq=sq, skv=skv, d=d, heads=int(q_t.shape[1]),
+        n_rep=k_rep, scale=scale, causal=causal, sq=sq, skv=skv, kv_len=kv_len, d=d, heads=int(q_t.shape[1]),
         batch=int(q_t.shape[0]), pos=pos,
     )
     if not path_ops:
@@ -819,6 +979,16 @@ def _last_axis_slice(op, n_axes):
     return int(st[-1]), int(lim[-1])
 
 
+def _table_key(t):
+    """Identity of a rotary table operand: a traced constant (a NumPy table
+    becomes one constant node per use) by its value, anything else by tensor."""
+    pc = GraphIndex.producer(t)
+    if pc is not None and pc.op_name == "constant" and isinstance(pc.attributes.get("value"), np.ndarray):
+        v = np.ascontiguousarray(pc.attributes["value"])
+        return ("const", v.shape, str(v.dtype), hashlib.blake2b(v.tobytes(), digest_size=16).digest())
+    return tkey(t)
+
+
 def _rotation_of(gi: GraphIndex, heads_op):
     """heads_op's result (B, S, H, hd): the traced half-split rotation of
     rope.py:34-57, concatenate([x0 * cos - x1 * sin, x0 * sin + x1 * cos], -1)
@@ -849,7 +1019,7 @@ def _rotation_of(gi: GraphIndex, heads_op):
             other = b if tkey(a) == ("o", halves[i].id) else a
             base = _view_base(other, [])  # the table's reshape/broadcast views stay outside the claim
             ops.append(m)
-            prods[(i, tkey(base))] = (m, base)
+            prods[(i, _table_key(base))] = (m, base)
     # lo = x0*cos - x1*sin and hi = x0*sin + x1*cos: find the subtract and the add
     outs = {}
     for (i, bk), (m, base) in prods.items():
@@ -958,4 +1128,5 @@ def find_claims(graph) -> Dict[int, Claim]:
             taken |= ids
             claims[c.root.id] = c
             break
+    absorb_rope_gathers(gi, claims, taken)
     return claims, taken

@@ -39,8 +39,11 @@ def test_residual_rmsnorm(rows, cols):
     assert_close(got, O.residual_rmsnorm(x, r, w, 1e-6), FP32_RTOL)
 
 
-@pytest.mark.parametrize("m,k,n", [(256, 512, 256), (8192, 8192, 8192), (300, 200, 264), (128, 64, 256), (1000, 4096, 1000)])
+@pytest.mark.parametrize("m,k,n", [(256, 512, 256), (8192, 8192, 8192), (300, 200, 264), (128, 64, 256), (1000, 4096, 1000),
+                                   (8, 4096, 6144), (1, 4096, 4096), (5, 12288, 1000)])
 def test_matmul_bf16(m, k, n):
+    """Tiles of 128 x 256; products with few tiles (decode rows against a weight
+    matrix, ragged shapes) split their K range across the SMs."""
     rng = np.random.default_rng(5)
     a = (rng.standard_normal((m, k), dtype=np.float32) * 0.02).astype(BF16)
     b = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(BF16)
@@ -241,6 +244,9 @@ def test_chunked_linear_attention(shape):
         ((5, 7), 7, np.int32, False),
         ((1, 1), 1, np.float32, False),
         ((300, 130), 5, np.float16, True),
+        ((8, 32768), 16, BF16, False),  # 16-key lists, 8 parts per row
+        ((4, 65536), 32, np.float16, True),  # 32-key lists, 16 parts
+        ((6, 20000), 9, np.int32, False),  # ties in every part, 4 parts
     ],
 )
 def test_topk_exact(shape, k, dtype, asc):

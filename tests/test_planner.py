@@ -102,8 +102,10 @@ def test_topk_is_one_launch_with_two_results():
     p = plan_of(k, np.zeros((4, 100), np.float32))
     assert p.kernel_counts() == {"topk_rows": 1}
     assert [np.dtype(o.dtype) for o in p.outputs] == [np.dtype(np.float32), np.dtype(np.uint32)]
-    # both results are written straight into the output buffers
-    assert [p.buffers[b].kind for b, _ in p.steps[0].bufs[1:]] == ["out", "out"]
+    # both results are written straight into the output buffers; the fourth buffer
+    # holds the one-pass kernel's per-part key lists (1 part of 8 keys per row here)
+    assert [p.buffers[b].kind for b, _ in p.steps[0].bufs[1:]] == ["out", "out", "tmp"]
+    assert p.steps[0].ints == [4, 100, 5, E.dt_code(np.float32), 4 * 8]
 
 
 def _ag0(x):
@@ -170,11 +172,42 @@ def test_kv_cache_decode_updates_caches_in_place():
     assert kinds.index("attn_decode") > max(i for i, k in enumerate(kinds) if k == "scatter_rows")
     assert {p.buffers[dec.bufs[i][0]].kind for i in (1, 2)} == {"out"}
     assert dec.ints[:7] == [2, 4, 2, 64, 128, dec.ints[5], 3] and dec.floats == [pytest.approx(128 ** -0.5)]
-    # per-head q/k RMSNorm rows and the new value row are read in place from the QKV projection
+    # per-head q/k RMSNorm + rotary: one launch each, rows read in place from the QKV
+    # projection, the cos / sin rows read at the run-time position (no gather launch)
     width = (4 + 2 * 2) * 128
-    assert [s.ints[6:] for s in p.steps if s.kernel == "rmsnorm_rows"] == [[4, width], [2, width]]
+    rr = [s for s in p.steps if s.kernel == "rmsnorm_rope_rows"]
+    assert [s.ints[3:5] for s in rr] == [[4, width], [2, width]]
+    assert all(s.ints[6] == 1 and s.ints[8] == 64 and s.ints[11] == 0 for s in rr)
+    assert all(p.buffers[s.bufs[5][0]].kind == "in" and p.buffers[s.bufs[5][0]].index == 6 for s in rr)
+    # the 2-row projections have 2 and 1 output tiles: their K range is split across the SMs
+    gs = [s for s in p.steps if s.kernel == "gemm_bf16"]
+    assert [s.ints[13:] for s in gs] == [[4, 4], [4, 4]] and all(len(s.bufs) == 4 for s in gs)
+    assert [p.buffers[s.bufs[3][0]].nbytes for s in gs] == [4 * 2 * width * 4, 4 * 2 * 512 * 4]
+    # the new value row is scattered straight from the projection output
     assert [len(s.ints) for s in sc] == [5, 6] and sc[1].ints[5] == width * 2
-    assert "ew" not in kinds[kinds.index("gemm_bf16"):kinds.index("rmsnorm_rows")]
+    assert not {"ew", "take", "rmsnorm_rows"} & set(kinds)
+
+
+def test_cache_prefill_norm_and_rotary_fused_per_token():
+    B, L, nq, nkv, hd, D, S = 2, 128, 8, 2, 128, 1024, 32
+    kw = dict(n_heads=nq, head_dim=hd, n_kv_heads=nkv)
+    z = np.zeros((B, L, nkv, hd), BF16)
+    p = plan_of(W.cached_attention_kernel, np.zeros((B, S, D), BF16), np.zeros((D, (nq + 2 * nkv) * hd), BF16),
+                np.ones(hd, BF16), np.ones(hd, BF16), z, z, None, np.zeros((nq * hd, D), BF16), **kw)
+    rr = [s for s in p.steps if s.kernel == "rmsnorm_rope_rows"]
+    # rows, cols, w dtype, block rows, block stride, table stride, has_pos, pos dtype, table rows, S, H, per token
+    width = (nq + 2 * nkv) * hd
+    assert [s.ints for s in rr] == [[B * S * nq, hd, 1, nq, width, hd // 2, 0, 0, S, S, nq, 1],
+                                    [B * S * nkv, hd, 1, nkv, width, hd // 2, 0, 0, S, S, nkv, 1]]
+    # the NumPy cos / sin tables (one constant node per use) are read from one constant each
+    assert {p.buffers[s.bufs[i][0]].kind for s in rr for i in (3, 4)} == {"const"}
+    assert "take" not in p.kernel_counts()
+    # mask[:S, :L] is causal over the first S cache rows: one flash launch reading S keys
+    # of the updated caches
+    (fa,) = [s for s in p.steps if s.kernel == "flash_attn"]
+    assert fa.ints[:7] == [B, nq, nkv, S, S, hd, 1]
+    assert [p.buffers[fa.bufs[i][0]].kind for i in (1, 2)] == ["out", "out"]
+    assert fa.ints[10:13] == [L * nkv * hd, hd, nkv * hd]
 
 
 def test_readers_of_a_mutated_parameter_run_before_its_update():
