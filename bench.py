@@ -81,6 +81,8 @@ class Workload:
     # kernel inputs copied host -> device every e2e step (None: all of them);
     # the others are parameters uploaded once
     step_inputs = None
+    # outputs read back every e2e step (None: all of them)
+    step_outputs = None
 
     def kernel_and_args(self, rank, world):
         raise NotImplementedError
@@ -320,6 +322,8 @@ class Decode(Workload):
 
     name, metric, unit, bound, dtype, dominant = "decode", "decode tokens/s (KV-cache attention step)", "tokens/s", "hbm", "bf16", "*step*"
     B, L, H, NQ, NKV, HD = 8, 2048, 4096, 32, 8, 128
+    step_inputs = ("x", "start_pos")  # weights and caches stay resident between steps
+    step_outputs = ("output0",)  # the caches are updated in place on the device
 
     def _args(self, B, seed):
         from nkipy_b200 import workloads as W
@@ -576,7 +580,8 @@ def run_nkb(args, wl, rank, world, local_rank):
     in_names = [s["name"] for s in kernel.model_ref.io["inputs"]]
     arrays = [a for a in np_args if isinstance(a, np.ndarray)]
     ins = {n: DeviceTensor.from_numpy(a, name=n) for n, a in zip(in_names, arrays)}
-    outs = {t.name: t for t in kernel.allocate_output_tensors()}
+    # a mutated input (``<name>.must_alias_input``, the KV caches) is bound in place as its output
+    outs = {t.name: ins.get(f"{t.name}.must_alias_input", t) for t in kernel.allocate_output_tensors()}
     in_refs = {k: v.tensor_ref for k, v in ins.items()}
     out_refs = {k: v.tensor_ref for k, v in outs.items()}
     flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=f"cuda:{local_rank}")
@@ -616,7 +621,7 @@ def run_nkb(args, wl, rank, world, local_rank):
     pinned_in = [torch.empty(a.nbytes, dtype=torch.uint8, pin_memory=True).numpy() for a in step_arrays]
     for p, a in zip(pinned_in, step_arrays):
         p[:] = np.frombuffer(np.ascontiguousarray(a).tobytes(), dtype=np.uint8)
-    out_specs = kernel.model_ref.io["outputs"]
+    out_specs = [s for s in kernel.model_ref.io["outputs"] if wl.step_outputs is None or s["name"] in wl.step_outputs]
     pinned_out = [torch.empty(outs[s["name"]].tensor_ref.size, dtype=torch.uint8, pin_memory=True).numpy() for s in out_specs]
     barrier()
     t0 = time.perf_counter()

@@ -8,13 +8,14 @@
 // from device memory (clamped into the cache as a gather index is).
 //
 // Split over keys ("flash-decoding"): CTA (b, g, c) takes KV head g of batch b,
-// every query head of its group, and chunk c of the keys.  Four warps, each
-// taking tiles of 32 keys: the warp first issues the loads of the tile's 32
-// value rows (lane l owning features 4l..4l+3, coalesced, held in registers)
-// and of its key rows (lane l: key base + l, 16 bytes at a time, all in
-// flight), then scores every head of the group, folds the 32 scores into a
-// running max / sum per head and accumulates sum_s p_s v_s from the
-// registers.  The CTA writes its partial (max, sum, unnormalised output) per
+// every query head of its group (their count a compile-time constant), and
+// chunk c of the keys.  Four warps, each taking tiles of 32 keys: the warp
+// issues the loads of its key rows (lane l: key base + l, 16 bytes at a time,
+// all in flight) and of the first half of the tile's value rows (lane l
+// owning features 4l..4l+3, coalesced, held in registers), scores every head
+// of the group (q read from shared memory 16 bytes at a time), issues the
+// second half of the value rows, folds the 32 scores into a running max / sum
+// per head and accumulates sum_s p_s v_s from the registers.  The CTA writes its partial (max, sum, unnormalised output) per
 // head; a second kernel merges the chunks of each (b, h).  fp32 throughout,
 // bf16 output.
 #include "common.cuh"
@@ -43,14 +44,15 @@ __device__ __forceinline__ int64_t load_pos(const void *p, int dt) {
   return (dt == NKB_U32 || dt == NKB_U16 || dt == NKB_U8) ? (int64_t)raw : (int64_t)(int32_t)raw;
 }
 
-__global__ void __launch_bounds__(THREADS) attn_decode_kernel(const __grid_constant__ Params p) {
-  __shared__ float s_q[MAX_REP][D];
-  __shared__ float s_m[4][MAX_REP], s_l[4][MAX_REP];
-  __shared__ float s_o[4][MAX_REP][D];
+// R = query heads per KV head (compile-time: no work for absent heads).
+template <int R>
+__global__ void __launch_bounds__(THREADS, 2) attn_decode_kernel(const __grid_constant__ Params p) {
+  __shared__ __align__(16) float s_q[R][D];
+  __shared__ float s_m[4][R], s_l[4][R];
+  __shared__ float s_o[4][R][D];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int c = blockIdx.x % p.splits, bg = blockIdx.x / p.splits;
   const int b = bg / p.HKV, g = bg % p.HKV;
-  const int R = p.n_rep;
   int64_t pos = load_pos(p.pos, p.pos_dt);
   pos = pos < 0 ? 0 : (pos >= p.S ? p.S - 1 : pos);
   const int len = (int)pos + 1;  // keys 0..pos
@@ -63,9 +65,9 @@ __global__ void __launch_bounds__(THREADS) attn_decode_kernel(const __grid_const
   }
   __syncthreads();
 
-  float m[MAX_REP], l[MAX_REP], o[MAX_REP][4];
+  float m[R], l[R], o[R][4];
 #pragma unroll
-  for (int r = 0; r < MAX_REP; ++r) {
+  for (int r = 0; r < R; ++r) {
     m[r] = -INFINITY;
     l[r] = 0.f;
 #pragma unroll
@@ -73,24 +75,26 @@ __global__ void __launch_bounds__(THREADS) attn_decode_kernel(const __grid_const
   }
   const __nv_bfloat16 *kbase = p.k + (int64_t)b * p.kb + (int64_t)g * p.kh;
   const __nv_bfloat16 *vbase = p.v + (int64_t)b * p.vb + (int64_t)g * p.vh;
+  constexpr int HALF = KEY_TILE / 2;
+#pragma unroll 1
   for (int t0 = k0 + warp * KEY_TILE; t0 < k1; t0 += 4 * KEY_TILE) {
     const int s = t0 + lane;
     const bool live = s < k1;
     const int nk = min(KEY_TILE, k1 - t0);
-    // the tile's value rows, loaded before they are needed (zeros past the chunk)
-    uint2 vv[KEY_TILE];
-#pragma unroll
-    for (int j = 0; j < KEY_TILE; ++j)
-      vv[j] = j < nk ? *reinterpret_cast<const uint2 *>(vbase + (int64_t)(t0 + j) * p.vs + 4 * lane) : make_uint2(0, 0);
-    // key row s, all 16-byte loads in flight
+    // key row s (all 16-byte loads in flight) and the first half of the tile's
+    // value rows (lane l: features 4l..4l+3; zeros past the chunk)
     uint4 kr[D / 8];
     const uint4 *krow = reinterpret_cast<const uint4 *>(kbase + (int64_t)(live ? s : t0) * p.ks);
 #pragma unroll
     for (int j = 0; j < D / 8; ++j) kr[j] = krow[j];
-    // scores of key s for every head of the group
-    float sc[MAX_REP];
+    uint2 va[HALF];
 #pragma unroll
-    for (int r = 0; r < MAX_REP; ++r) sc[r] = 0.f;
+    for (int j = 0; j < HALF; ++j)
+      va[j] = j < nk ? *reinterpret_cast<const uint2 *>(vbase + (int64_t)(t0 + j) * p.vs + 4 * lane) : make_uint2(0, 0);
+    // scores of key s for every head of the group; q read 16 bytes at a time (broadcast)
+    float sc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) sc[r] = 0.f;
 #pragma unroll
     for (int j = 0; j < D / 8; ++j) {
       const __nv_bfloat162 *kk = reinterpret_cast<const __nv_bfloat162 *>(&kr[j]);
@@ -102,24 +106,35 @@ __global__ void __launch_bounds__(THREADS) attn_decode_kernel(const __grid_const
         kf[2 * e + 1] = f.y;
       }
 #pragma unroll
-      for (int r = 0; r < MAX_REP; ++r) {
-        if (r < R) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) sc[r] = fmaf(s_q[r][8 * j + e], kf[e], sc[r]);
-        }
+      for (int r = 0; r < R; ++r) {
+        const float4 qa = *reinterpret_cast<const float4 *>(&s_q[r][8 * j]);
+        const float4 qb = *reinterpret_cast<const float4 *>(&s_q[r][8 * j + 4]);
+        sc[r] = fmaf(qa.x, kf[0], sc[r]);
+        sc[r] = fmaf(qa.y, kf[1], sc[r]);
+        sc[r] = fmaf(qa.z, kf[2], sc[r]);
+        sc[r] = fmaf(qa.w, kf[3], sc[r]);
+        sc[r] = fmaf(qb.x, kf[4], sc[r]);
+        sc[r] = fmaf(qb.y, kf[5], sc[r]);
+        sc[r] = fmaf(qb.z, kf[6], sc[r]);
+        sc[r] = fmaf(qb.w, kf[7], sc[r]);
       }
     }
-    // online softmax per head over the warp's 32 keys
-    float pr[MAX_REP];
+    // second half of the value rows (the key registers are free now)
+    uint2 vb[HALF];
 #pragma unroll
-    for (int r = 0; r < MAX_REP; ++r) {
-      if (r >= R) continue;
-      float x = live ? sc[r] : -INFINITY;
+    for (int j = 0; j < HALF; ++j)
+      vb[j] = HALF + j < nk ? *reinterpret_cast<const uint2 *>(vbase + (int64_t)(t0 + HALF + j) * p.vs + 4 * lane)
+                            : make_uint2(0, 0);
+    // online softmax per head over the warp's 32 keys
+    float pr[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float x = live ? sc[r] : -INFINITY;
       float mx = x;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      const float mn = fmaxf(m[r], mx);
-      const float corr = __expf(m[r] - mn);  // 0 when m was -inf
+      const float mn = fmaxf(m[r], mx);      // finite: lane 0 of a tile is always live
+      const float corr = __expf(m[r] - mn);  // 0 while m is -inf
       pr[r] = live ? __expf(x - mn) : 0.f;
       float sum = pr[r];
 #pragma unroll
@@ -129,14 +144,14 @@ __global__ void __launch_bounds__(THREADS) attn_decode_kernel(const __grid_const
 #pragma unroll
       for (int j = 0; j < 4; ++j) o[r][j] *= corr;
     }
-    // sum_s p_s v_s: lane owns features 4*lane .. 4*lane+3 (p = 0 past the chunk)
+    // sum_s p_s v_s from the registers (p = 0 past the chunk)
 #pragma unroll
     for (int j = 0; j < KEY_TILE; ++j) {
-      const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vv[j].x));
-      const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vv[j].y));
+      const uint2 vv = j < HALF ? va[j] : vb[j - HALF];
+      const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vv.x));
+      const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vv.y));
 #pragma unroll
-      for (int r = 0; r < MAX_REP; ++r) {
-        if (r >= R) continue;
+      for (int r = 0; r < R; ++r) {
         const float pj = __shfl_sync(0xffffffffu, pr[r], j);
         o[r][0] = fmaf(pj, v01.x, o[r][0]);
         o[r][1] = fmaf(pj, v01.y, o[r][1]);
@@ -147,8 +162,7 @@ __global__ void __launch_bounds__(THREADS) attn_decode_kernel(const __grid_const
   }
   // merge the four warps' partials, then this chunk's partial per head -> workspace
 #pragma unroll
-  for (int r = 0; r < MAX_REP; ++r) {
-    if (r >= R) continue;
+  for (int r = 0; r < R; ++r) {
     if (lane == 0) {
       s_m[warp][r] = m[r];
       s_l[warp][r] = l[r];
@@ -203,8 +217,8 @@ int check(const Step &s) {
     return fail(NKB_ERR_PLAN, "attn_decode: bad parameters");
   const auto &q = s.ints;
   if (q[4] != D) return fail(NKB_ERR_UNSUPPORTED, "attn_decode: head_dim must be 128");
-  if (q[2] <= 0 || q[1] % q[2] || q[1] / q[2] > MAX_REP)
-    return fail(NKB_ERR_UNSUPPORTED, "attn_decode: at most 8 query heads per KV head");
+  if (q[2] <= 0 || q[1] % q[2] || q[1] / q[2] > MAX_REP || ((q[1] / q[2]) & (q[1] / q[2] - 1)))
+    return fail(NKB_ERR_UNSUPPORTED, "attn_decode: 1, 2, 4 or 8 query heads per KV head");
   if (q[5] < 1 || q[0] < 0 || q[3] < 1) return fail(NKB_ERR_PLAN, "attn_decode: sizes out of range");
   for (int i = 7; i < 17; ++i)
     if (q[i] < 0 || q[i] % 8) return fail(NKB_ERR_UNSUPPORTED, "attn_decode: strides must be multiples of 8");
@@ -242,7 +256,14 @@ int launch(const LaunchArgs &a) {
   p.chunk = (p.S + p.splits - 1) / p.splits;
   p.scale = a.step->floats[0];
   if (p.B == 0) return NKB_OK;
-  attn_decode_kernel<<<(unsigned)(p.B * p.HKV * p.splits), THREADS, 0, a.stream>>>(p);
+  const unsigned grid = (unsigned)(p.B * p.HKV * p.splits);
+  switch (p.n_rep) {
+    case 1: attn_decode_kernel<1><<<grid, THREADS, 0, a.stream>>>(p); break;
+    case 2: attn_decode_kernel<2><<<grid, THREADS, 0, a.stream>>>(p); break;
+    case 4: attn_decode_kernel<4><<<grid, THREADS, 0, a.stream>>>(p); break;
+    case 8: attn_decode_kernel<8><<<grid, THREADS, 0, a.stream>>>(p); break;
+    default: return fail(NKB_ERR_UNSUPPORTED, "attn_decode: 1, 2, 4 or 8 query heads per KV head");
+  }
   if (int s = launch_status("attn_decode_kernel")) return s;
   attn_decode_combine_kernel<<<(unsigned)(p.B * p.H), D, 0, a.stream>>>(p);
   return launch_status("attn_decode_combine_kernel");
