@@ -141,10 +141,43 @@ __device__ __forceinline__ void emit(const void *x, int64_t base, int64_t cols, 
   for (int b = 0; b < esize; ++b) dst[b] = src[b];
 }
 
+constexpr int RES_V = 16;  // 16-byte vectors per thread in the register-resident path
+
+// The kk-th largest (kk <= 32) of the block's per-thread values; every thread
+// of the block calls it and gets the same result.
+__device__ uint32_t block_kth_largest(uint32_t v, int kk) {
+  __shared__ uint32_t s_top[kPartThreads / 32][32];
+  __shared__ uint32_t s_res;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // each warp: its kk largest, popping one lane (the lowest among equals) per round
+  for (int r = 0; r < kk; ++r) {
+    const uint32_t m = __reduce_max_sync(0xffffffffu, v);
+    const int win = __ffs(__ballot_sync(0xffffffffu, v == m)) - 1;
+    if (lane == 0) s_top[warp][r] = m;
+    if (lane == win) v = 0;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // merge the warps' sorted lists: lane w < 8 walks list w
+    int ptr = 0;
+    uint32_t m = 0;
+    for (int r = 0; r < kk; ++r) {
+      const uint32_t head = (lane < kPartThreads / 32 && ptr < kk) ? s_top[lane][ptr] : 0u;
+      m = __reduce_max_sync(0xffffffffu, head);
+      const unsigned own = __ballot_sync(0xffffffffu, lane < kPartThreads / 32 && ptr < kk && head == m);
+      if (lane == __ffs(own) - 1) ++ptr;
+    }
+    if (lane == 0) s_res = m;
+  }
+  __syncthreads();
+  return s_res;
+}
+
 template <int KL>
 __global__ void __launch_bounds__(kPartThreads) topk_part_kernel(const void *__restrict__ x, int dt, int64_t rows,
                                                                  int64_t cols, int parts, int64_t part_len, int k,
-                                                                 int esize, int vec, uint64_t *__restrict__ ws,
+                                                                 int esize, int vec, int resident,
+                                                                 uint64_t *__restrict__ ws,
                                                                  void *__restrict__ vals, uint32_t *__restrict__ idx) {
   __shared__ uint64_t s_cand[kPartThreads / 32][KL];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -156,17 +189,115 @@ __global__ void __launch_bounds__(kPartThreads) topk_part_kernel(const void *__r
   uint64_t lst[KL];
 #pragma unroll
   for (int j = 0; j < KL; ++j) lst[j] = 0;
-  if (vec == 2) {  // bf16 / f16 rows, 8 per 16-byte load (c0 and the row start 16-byte aligned)
-    const uint4 *p = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) + base + c0);
-    const int64_t n8 = (c1 - c0) / 8;
-    for (int64_t i = tid; i < n8; i += kPartThreads) {
-      const uint4 u = p[i];
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  // A thread sees its columns in increasing order, so an element whose value
+  // image is below the image of its list's last key can never enter the list:
+  // a 32-bit compare rejects it.  The images of a 16-byte vector are computed
+  // branch-free and the warp votes once per vector, so the insert code is
+  // skipped by the whole warp unless some lane has a candidate (rare once the
+  // lists have filled).
+  constexpr int UNROLL = 4;  // 16-byte loads in flight per thread
+  const bool flt = dt == NKB_F32 || dt == NKB_BF16 || dt == NKB_F16;
+  const uint32_t sx = (dt == NKB_I32) ? 0x80000000u : 0u;  // signed int: flip the sign bit
+  auto image = [&](uint32_t bits) -> uint32_t {  // order_bits without a branch
+    return bits ^ (flt ? ((uint32_t)((int32_t)bits >> 31) | 0x80000000u) : sx);
+  };
+  // Loop bounds are taken from the warp's first index, so all 32 lanes run the
+  // same iterations (the vote needs every lane); a lane past the end holds no
+  // candidate.
+  const int64_t wtid = tid & ~31;
+  const int kk = parts > 1 ? KL : k;  // a part hands on its full list
+  if (resident) {
+    // The part fits in registers (at most RES_V 16-byte vectors per thread).
+    // Pass 1: each thread's largest value image; T = the kk-th largest of
+    // those maxima.  kk threads hold an element at or above T, so every one of
+    // the part's kk largest keys has an image >= T: pass 2 inserts only those
+    // elements (few), instead of testing every element against a list.
+    const int per = vec == 2 ? 8 : 4;
+    const int64_t nv = (c1 - c0) / per;
+    const uint4 *pv = reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(x) + (base + c0) * esize);
+    auto images = [&](const uint4 &v, uint32_t (&img)[8]) {
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const uint32_t h = (w[e >> 1] >> ((e & 1) * 16)) & 0xffffu;
-        const uint32_t bits = dt == NKB_BF16 ? (h << 16) : __float_as_uint(__half2float(__ushort_as_half((uint16_t)h)));
-        list_insert<KL>(lst, make_key(order_bits(bits, dt), c0 + i * 8 + e));
+        if (vec == 2) {
+          const uint32_t h = (w[e >> 1] >> ((e & 1) * 16)) & 0xffffu;
+          img[e] = image(dt == NKB_BF16 ? (h << 16) : __float_as_uint(__half2float(__ushort_as_half((uint16_t)h))));
+        } else {
+          img[e] = e < 4 ? image(w[e]) : 0u;
+        }
+      }
+    };
+    uint4 u[RES_V];
+#pragma unroll
+    for (int q = 0; q < RES_V; ++q) {
+      const int64_t i = tid + (int64_t)q * kPartThreads;
+      u[q] = i < nv ? pv[i] : make_uint4(0, 0, 0, 0);
+    }
+    uint32_t tmax = 0;
+#pragma unroll
+    for (int q = 0; q < RES_V; ++q) {
+      if (tid + (int64_t)q * kPartThreads < nv) {
+        uint32_t img[8];
+        images(u[q], img);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) tmax = max(tmax, e < per ? img[e] : 0u);
+      }
+    }
+    for (int64_t c = c0 + nv * per + tid; c < c1; c += kPartThreads)
+      tmax = max(tmax, order_bits(load_as_reg(x, base + c, dt), dt));
+    const uint32_t T = block_kth_largest(tmax, kk);
+    // every lane runs every q (the vote needs the whole warp); the insert code
+    // runs only when some lane of the warp holds a candidate
+#pragma unroll
+    for (int q = 0; q < RES_V; ++q) {
+      const int64_t i = tid + (int64_t)q * kPartThreads;
+      const bool valid = i < nv;
+      uint32_t img[8];
+      images(u[q], img);
+      bool cand = false;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) cand |= valid && e < per && img[e] >= T;
+      if (__any_sync(0xffffffffu, cand) && cand) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < per && img[e] >= T) list_insert<KL>(lst, make_key(img[e], c0 + i * per + e));
+      }
+    }
+    for (int64_t c = c0 + nv * per + tid; c < c1; c += kPartThreads) {
+      const uint32_t img = order_bits(load_as_reg(x, base + c, dt), dt);
+      if (img >= T) list_insert<KL>(lst, make_key(img, c));
+    }
+  } else if (vec == 2) {  // bf16 / f16 rows, 8 per 16-byte load (c0 and the row start 16-byte aligned)
+    const uint4 *p = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) + base + c0);
+    const int64_t n8 = (c1 - c0) / 8;
+    for (int64_t ib = wtid; ib < n8; ib += UNROLL * kPartThreads) {
+      uint4 u[UNROLL];
+#pragma unroll
+      for (int q = 0; q < UNROLL; ++q) {
+        const int64_t i = ib + lane + q * kPartThreads;
+        u[q] = i < n8 ? p[i] : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int q = 0; q < UNROLL; ++q) {
+        const int64_t i = ib + lane + q * kPartThreads;
+        const bool valid = i < n8;
+        const uint32_t w[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
+        uint32_t img[8];
+        bool cand = false;
+        const uint32_t thr = (uint32_t)(lst[KL - 1] >> 32);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const uint32_t h = (w[e >> 1] >> ((e & 1) * 16)) & 0xffffu;
+          const uint32_t bits =
+              dt == NKB_BF16 ? (h << 16) : __float_as_uint(__half2float(__ushort_as_half((uint16_t)h)));
+          img[e] = image(bits);
+          cand |= valid && img[e] >= thr;
+        }
+        if (__any_sync(0xffffffffu, cand) && valid) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (img[e] >= (uint32_t)(lst[KL - 1] >> 32)) list_insert<KL>(lst, make_key(img[e], c0 + i * 8 + e));
+        }
       }
     }
     for (int64_t c = c0 + n8 * 8 + tid; c < c1; c += kPartThreads)
@@ -174,11 +305,32 @@ __global__ void __launch_bounds__(kPartThreads) topk_part_kernel(const void *__r
   } else if (vec == 4) {  // fp32 / int32 / uint32 rows, 4 per load
     const uint4 *p = reinterpret_cast<const uint4 *>(static_cast<const uint32_t *>(x) + base + c0);
     const int64_t n4 = (c1 - c0) / 4;
-    for (int64_t i = tid; i < n4; i += kPartThreads) {
-      const uint4 u = p[i];
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    for (int64_t ib = wtid; ib < n4; ib += UNROLL * kPartThreads) {
+      uint4 u[UNROLL];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) list_insert<KL>(lst, make_key(order_bits(w[e], dt), c0 + i * 4 + e));
+      for (int q = 0; q < UNROLL; ++q) {
+        const int64_t i = ib + lane + q * kPartThreads;
+        u[q] = i < n4 ? p[i] : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int q = 0; q < UNROLL; ++q) {
+        const int64_t i = ib + lane + q * kPartThreads;
+        const bool valid = i < n4;
+        const uint32_t w[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
+        uint32_t img[4];
+        bool cand = false;
+        const uint32_t thr = (uint32_t)(lst[KL - 1] >> 32);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          img[e] = image(w[e]);
+          cand |= valid && img[e] >= thr;
+        }
+        if (__any_sync(0xffffffffu, cand) && valid) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (img[e] >= (uint32_t)(lst[KL - 1] >> 32)) list_insert<KL>(lst, make_key(img[e], c0 + i * 4 + e));
+        }
+      }
     }
     for (int64_t c = c0 + n4 * 4 + tid; c < c1; c += kPartThreads)
       list_insert<KL>(lst, make_key(order_bits(load_as_reg(x, base + c, dt), dt), c));
@@ -186,7 +338,6 @@ __global__ void __launch_bounds__(kPartThreads) topk_part_kernel(const void *__r
     for (int64_t c = c0 + tid; c < c1; c += kPartThreads)
       list_insert<KL>(lst, make_key(order_bits(load_as_reg(x, base + c, dt), dt), c));
   }
-  const int kk = parts > 1 ? KL : k;  // a part hands on its full list
   warp_merge<KL>(lst, kk, s_cand[warp]);
   __syncthreads();
   if (warp == 0) {
@@ -225,26 +376,40 @@ __global__ void __launch_bounds__(256, 1) topk_merge_kernel(const void *__restri
 
 template <int KL>
 int topk_parts(const void *x, int dt, void *vals, uint32_t *idx, int64_t rows, int64_t cols, int k, int esize,
-               uint64_t *ws, int parts, cudaStream_t st, int device) {
-  int64_t part_len = (cols + parts - 1) / parts;
-  part_len = (part_len + 7) / 8 * 8;  // part starts stay 16-byte aligned
+               uint64_t *ws, int64_t ws_keys, int parts, cudaStream_t st, int device) {
   const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
   int vec = 0;
   if (esize == 2 && (dt == NKB_BF16 || dt == NKB_F16) && (xa & 15) == 0 && (cols * 2) % 16 == 0) vec = 2;
   if (esize == 4 && (dt == NKB_F32 || dt == NKB_I32 || dt == NKB_U32) && (xa & 15) == 0 && (cols * 4) % 16 == 0)
     vec = 4;
+  // register-resident when a part fits in RES_V vectors per thread (more parts
+  // if the workspace has room for their lists)
+  int resident = 0;
+  if (vec) {
+    const int64_t cap = (int64_t)kPartThreads * RES_V * (vec == 2 ? 8 : 4);
+    const int64_t need = (cols + cap - 1) / cap;
+    if (need <= parts) {
+      resident = 1;
+    } else if (need <= 64 && ws && ws_keys >= rows * need * KL) {
+      parts = (int)need;
+      resident = 1;
+    }
+  }
+  int64_t part_len = (cols + parts - 1) / parts;
+  part_len = (part_len + 7) / 8 * 8;  // part starts stay 16-byte aligned
+  if (resident && part_len > (int64_t)kPartThreads * RES_V * (vec == 2 ? 8 : 4)) resident = 0;
   topk_part_kernel<KL><<<(unsigned)(rows * parts), kPartThreads, 0, st>>>(x, dt, rows, cols, parts, part_len, k, esize,
-                                                                          vec, ws, vals, idx);
+                                                                          vec, resident, ws, vals, idx);
   if (int e = launch_status("topk_part_kernel")) return e;
   if (parts == 1) return NKB_OK;
   topk_merge_kernel<KL><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, rows, cols, parts, k, esize, ws, vals, idx);
   return launch_status("topk_merge_kernel");
 }
 
-// Parts per row for the one-pass path: enough CTAs for two per SM, at least
+// Parts per row for the one-pass path: enough CTAs for four per SM, at least
 // 4096 columns per part, at most 64 parts.
 int topk_parts_for(int64_t rows, int64_t cols, int sms) {
-  int64_t p = (2 * (int64_t)sms + rows - 1) / std::max<int64_t>(rows, 1);
+  int64_t p = (4 * (int64_t)sms + rows - 1) / std::max<int64_t>(rows, 1);
   p = std::min<int64_t>(p, std::max<int64_t>(1, cols / 4096));
   return (int)std::max<int64_t>(1, std::min<int64_t>(p, 64));
 }
@@ -260,9 +425,9 @@ int topk_any(const void *x, int dt, void *vals, uint32_t *idx, int64_t rows, int
     const int KL = k <= 8 ? 8 : k <= 16 ? 16 : 32;
     int parts = topk_parts_for(rows, cols, num_sms(device));
     if (parts > 1 && (!ws || ws_keys < rows * parts * KL)) parts = 1;  // no room for the parts' lists
-    if (KL == 8) return topk_parts<8>(x, dt, vals, idx, rows, cols, (int)k, es, ws, parts, stream, device);
-    if (KL == 16) return topk_parts<16>(x, dt, vals, idx, rows, cols, (int)k, es, ws, parts, stream, device);
-    return topk_parts<32>(x, dt, vals, idx, rows, cols, (int)k, es, ws, parts, stream, device);
+    if (KL == 8) return topk_parts<8>(x, dt, vals, idx, rows, cols, (int)k, es, ws, ws_keys, parts, stream, device);
+    if (KL == 16) return topk_parts<16>(x, dt, vals, idx, rows, cols, (int)k, es, ws, ws_keys, parts, stream, device);
+    return topk_parts<32>(x, dt, vals, idx, rows, cols, (int)k, es, ws, ws_keys, parts, stream, device);
   }
   const bool staged = cols <= kSmemCols;
   const size_t smem = staged ? (size_t)cols * 4 : 0;
