@@ -652,7 +652,15 @@ def run_nkb(args, wl, rank, world, local_rank):
     peaks, peak_kind = load_peaks()
     dom = [i for i, s in enumerate(plan_steps) if s["kernel"] == wl.dominant]
     roof = None
-    if dom:
+    if wl.dominant == "*step*":
+        # no single dominant launch (the decode step): the whole step's algorithmic
+        # bytes over the device-timed step
+        peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+        achieved = wl.dominant_work() / (ms_per_step / 1e3) / 1e9
+        roof = {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": None, "peak_source": f"{peak_kind} (hbm_gbs)", "kernel": "whole step",
+                "launch_ms": ms_per_step, "work_per_launch": wl.dominant_work()}
+    elif dom:
         if wl.bound == "hbm":
             work = wl.dominant_work()
             dur = sum(step_ms[i] for i in dom) / len(dom)

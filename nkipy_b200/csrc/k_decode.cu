@@ -7,17 +7,15 @@
 // s > pos contribute nothing, so the kernel reads keys 0..pos only; pos comes
 // from device memory (clamped into the cache as a gather index is).
 //
-// Split over keys ("flash-decoding"): CTA (b, g, c) takes KV head g of batch b,
-// every query head of its group (their count a compile-time constant), and
-// chunk c of the keys.  Four warps, each taking tiles of 32 keys: the warp
-// issues the loads of its key rows (lane l: key base + l, 16 bytes at a time,
-// all in flight) and of the first half of the tile's value rows (lane l
-// owning features 4l..4l+3, coalesced, held in registers), scores every head
-// of the group (q read from shared memory 16 bytes at a time), issues the
-// second half of the value rows, folds the 32 scores into a running max / sum
-// per head and accumulates sum_s p_s v_s from the registers.  The CTA writes its partial (max, sum, unnormalised output) per
-// head; a second kernel merges the chunks of each (b, h).  fp32 throughout,
-// bf16 output.
+// Split over keys ("flash-decoding"): CTA (b, g, c) takes KV head g of batch b
+// and chunk c of the keys.  The R query heads of the group form the rows of
+// one m16 tensor-core tile (rows >= R zero), so scores and PV run on bf16
+// mma.sync m16n8k16 with fp32 accumulation: per 16-key tile S = Q K^T (16 mma)
+// and O += P V (16 mma), P converted to bf16 in registers.  Four warps per
+// CTA, each taking every fourth tile of the chunk through its own
+// double-buffered, XOR-swizzled shared-memory ring filled by cp.async.  The
+// CTA writes its partial (max, sum, unnormalised output) per head; a second
+// kernel merges the chunks of each (b, h).  fp32 softmax, bf16 output.
 #include "common.cuh"
 
 namespace nkb {
@@ -26,7 +24,6 @@ namespace decode {
 constexpr int D = 128;          // head dimension
 constexpr int MAX_REP = 8;      // query heads per KV head
 constexpr int THREADS = 128;    // four warps
-constexpr int KEY_TILE = 32;    // keys per warp step (one per lane)
 
 struct Params {
   const __nv_bfloat16 *q, *k, *v;
@@ -44,12 +41,60 @@ __device__ __forceinline__ int64_t load_pos(const void *p, int dt) {
   return (dt == NKB_U32 || dt == NKB_U16 || dt == NKB_U8) ? (int64_t)raw : (int64_t)(int32_t)raw;
 }
 
-// R = query heads per KV head (compile-time: no work for absent heads).
+// ---- mma.sync helpers (bf16 m16n8k16, fp32 accumulation) ---------------------
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+// byte offset of 16-byte chunk `chunk` of row `row` in a [rows][128] bf16 tile,
+// XOR-swizzled so the eight rows an ldmatrix reads fall in different banks
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return row * (D * 2) + ((chunk ^ (row & 7)) << 4);
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool pred) {
+  const int n = pred ? 16 : 0;  // zero-fill past the keys this warp may read
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;"); }
+__device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;"); }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float *c, const uint32_t *a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+constexpr int BN = 16;                      // keys per tile
+constexpr int TILE_BYTES = BN * D * 2;      // 4 KB per K or V tile
+constexpr int WARP_SMEM = 2 * 2 * TILE_BYTES;  // two stages of K and V per warp
+
+// CTA (b, g, c): the R query heads of KV head g form the rows of one m16 tile
+// (rows >= R are zero).  Each warp takes every fourth 16-key tile of chunk c,
+// double-buffered in its own swizzled shared-memory ring by cp.async, and
+// runs S = Q K^T (16 mma), an online softmax on the score fragments, and
+// O += P V (16 mma) with P converted to bf16 in registers.
 template <int R>
 __global__ void __launch_bounds__(THREADS, 2) attn_decode_kernel(const __grid_constant__ Params p) {
-  __shared__ __align__(16) float s_q[R][D];
-  __shared__ float s_m[4][R], s_l[4][R];
-  __shared__ float s_o[4][R][D];
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t *sQ = smem;                                   // 16 rows x 128, swizzled
+  uint8_t *sRing = smem + 16 * D * 2;                   // 4 warps x WARP_SMEM
+  float *s_o = reinterpret_cast<float *>(sRing + 4 * WARP_SMEM);  // [4][R][D]
+  float *s_m = s_o + 4 * R * D;                         // [4][R]
+  float *s_l = s_m + 4 * R;                             // [4][R]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int c = blockIdx.x % p.splits, bg = blockIdx.x / p.splits;
   const int b = bg / p.HKV, g = bg % p.HKV;
@@ -57,129 +102,159 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_kernel(const __grid_co
   pos = pos < 0 ? 0 : (pos >= p.S ? p.S - 1 : pos);
   const int len = (int)pos + 1;  // keys 0..pos
   const int k0 = c * p.chunk, k1 = min(k0 + p.chunk, len);
-
-  for (int i = threadIdx.x; i < R * D; i += THREADS) {
-    const int r = i / D, d = i % D;
-    const int h = g * R + r;
-    s_q[r][d] = __bfloat162float(p.q[(int64_t)b * p.qb + (int64_t)h * p.qh + d]) * p.scale;
-  }
-  __syncthreads();
-
-  float m[R], l[R], o[R][4];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    m[r] = -INFINITY;
-    l[r] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) o[r][j] = 0.f;
-  }
   const __nv_bfloat16 *kbase = p.k + (int64_t)b * p.kb + (int64_t)g * p.kh;
   const __nv_bfloat16 *vbase = p.v + (int64_t)b * p.vb + (int64_t)g * p.vh;
-  constexpr int HALF = KEY_TILE / 2;
+
+  // Q rows (zero past R): 16 rows x 16 chunks of 16 bytes
+  for (int i = threadIdx.x; i < 16 * (D / 8); i += THREADS) {
+    const int r = i / (D / 8), ch = i % (D / 8);
+    const bool ok = r < R;
+    const __nv_bfloat16 *src = p.q + (int64_t)b * p.qb + (int64_t)(g * R + (ok ? r : 0)) * p.qh + ch * 8;
+    cp_async16(smem_addr(sQ) + swz(r, ch), src, ok);
+  }
+  cp_commit();
+
+  // this warp's tiles: ts = k0 + (warp + 4 i) * BN, while ts < k1
+  const int n_tiles = k1 > k0 ? (k1 - k0 + BN - 1) / BN : 0;
+  const int my_tiles = n_tiles > warp ? (n_tiles - warp + 3) / 4 : 0;
+  uint8_t *ring = sRing + warp * WARP_SMEM;
+  auto load_tile = [&](int i, int stage) {
+    const int ts = k0 + (warp + 4 * i) * BN;
+    const uint32_t kd = smem_addr(ring + stage * 2 * TILE_BYTES), vd = kd + TILE_BYTES;
+#pragma unroll
+    for (int j = 0; j < BN * (D / 8) / 32; ++j) {  // 8 chunks of K and 8 of V per lane
+      const int idx = j * 32 + lane, r = idx / (D / 8), ch = idx % (D / 8);
+      const int key = ts + r;
+      const bool ok = key < k1;
+      const int64_t kr = ok ? key : k0;
+      cp_async16(kd + swz(r, ch), kbase + kr * p.ks + ch * 8, ok);
+      cp_async16(vd + swz(r, ch), vbase + kr * p.vs + ch * 8, ok);
+    }
+  };
+  if (my_tiles > 0) load_tile(0, 0);
+  cp_commit();
+
+  // Q fragments (A operand, rows = heads), kept in registers
+  asm volatile("cp.async.wait_group 1;");
+  __syncthreads();
+  uint32_t qf[D / 16][4];
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk)
+    ldsm_x4(smem_addr(sQ) + swz(lane % 16, kk * 2 + lane / 16), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+
 #pragma unroll 1
-  for (int t0 = k0 + warp * KEY_TILE; t0 < k1; t0 += 4 * KEY_TILE) {
-    const int s = t0 + lane;
-    const bool live = s < k1;
-    const int nk = min(KEY_TILE, k1 - t0);
-    // key row s (all 16-byte loads in flight) and the first half of the tile's
-    // value rows (lane l: features 4l..4l+3; zeros past the chunk)
-    uint4 kr[D / 8];
-    const uint4 *krow = reinterpret_cast<const uint4 *>(kbase + (int64_t)(live ? s : t0) * p.ks);
+  for (int i = 0; i < my_tiles; ++i) {
+    const int stage = i & 1;
+    __syncwarp();  // every lane is done reading the stage the next load overwrites
+    if (i + 1 < my_tiles) load_tile(i + 1, stage ^ 1);
+    cp_commit();
+    cp_wait1();
+    __syncwarp();  // this tile's copies, issued by every lane, are visible
+    const uint32_t kt = smem_addr(ring + stage * 2 * TILE_BYTES), vt = kt + TILE_BYTES;
+    const int ts = k0 + (warp + 4 * i) * BN;
+    // S = Q K^T: 16 rows (heads) x 16 keys
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-    for (int j = 0; j < D / 8; ++j) kr[j] = krow[j];
-    uint2 va[HALF];
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t b0, b1, b2, b3;
+      const int r = (lane % 8) + (lane / 16) * 8;
+      ldsm_x4(kt + swz(r, kk * 2 + (lane / 8) % 2), b0, b1, b2, b3);
+      mma16816(s[0], qf[kk], b0, b1);
+      mma16816(s[1], qf[kk], b2, b3);
+    }
+    // scale, mask keys past the chunk / the position, online softmax per row
+    float mx[2] = {m_r[0], m_r[1]};
 #pragma unroll
-    for (int j = 0; j < HALF; ++j)
-      va[j] = j < nk ? *reinterpret_cast<const uint2 *>(vbase + (int64_t)(t0 + j) * p.vs + 4 * lane) : make_uint2(0, 0);
-    // scores of key s for every head of the group; q read 16 bytes at a time (broadcast)
-    float sc[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) sc[r] = 0.f;
-#pragma unroll
-    for (int j = 0; j < D / 8; ++j) {
-      const __nv_bfloat162 *kk = reinterpret_cast<const __nv_bfloat162 *>(&kr[j]);
-      float kf[8];
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(kk[e]);
-        kf[2 * e] = f.x;
-        kf[2 * e + 1] = f.y;
+        const int key = ts + j * 8 + (lane % 4) * 2 + (e & 1);
+        const float v = key < k1 ? s[j][e] * p.scale : -INFINITY;
+        s[j][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
       }
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const float4 qa = *reinterpret_cast<const float4 *>(&s_q[r][8 * j]);
-        const float4 qb = *reinterpret_cast<const float4 *>(&s_q[r][8 * j + 4]);
-        sc[r] = fmaf(qa.x, kf[0], sc[r]);
-        sc[r] = fmaf(qa.y, kf[1], sc[r]);
-        sc[r] = fmaf(qa.z, kf[2], sc[r]);
-        sc[r] = fmaf(qa.w, kf[3], sc[r]);
-        sc[r] = fmaf(qb.x, kf[4], sc[r]);
-        sc[r] = fmaf(qb.y, kf[5], sc[r]);
-        sc[r] = fmaf(qb.z, kf[6], sc[r]);
-        sc[r] = fmaf(qb.w, kf[7], sc[r]);
-      }
+    for (int r2 = 0; r2 < 2; ++r2) {
+      mx[r2] = fmaxf(mx[r2], __shfl_xor_sync(0xffffffffu, mx[r2], 1));
+      mx[r2] = fmaxf(mx[r2], __shfl_xor_sync(0xffffffffu, mx[r2], 2));
     }
-    // second half of the value rows (the key registers are free now)
-    uint2 vb[HALF];
+    float alpha[2], rs[2] = {0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < HALF; ++j)
-      vb[j] = HALF + j < nk ? *reinterpret_cast<const uint2 *>(vbase + (int64_t)(t0 + HALF + j) * p.vs + 4 * lane)
-                            : make_uint2(0, 0);
-    // online softmax per head over the warp's 32 keys
-    float pr[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const float x = live ? sc[r] : -INFINITY;
-      float mx = x;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      const float mn = fmaxf(m[r], mx);      // finite: lane 0 of a tile is always live
-      const float corr = __expf(m[r] - mn);  // 0 while m is -inf
-      pr[r] = live ? __expf(x - mn) : 0.f;
-      float sum = pr[r];
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-      l[r] = l[r] * corr + sum;
-      m[r] = mn;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) o[r][j] *= corr;
+    for (int r2 = 0; r2 < 2; ++r2) {
+      alpha[r2] = __expf(m_r[r2] - mx[r2]);  // 0 while m was -inf (the first key of a tile is in range)
+      m_r[r2] = mx[r2];
     }
-    // sum_s p_s v_s from the registers (p = 0 past the chunk)
 #pragma unroll
-    for (int j = 0; j < KEY_TILE; ++j) {
-      const uint2 vv = j < HALF ? va[j] : vb[j - HALF];
-      const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vv.x));
-      const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&vv.y));
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const float pj = __shfl_sync(0xffffffffu, pr[r], j);
-        o[r][0] = fmaf(pj, v01.x, o[r][0]);
-        o[r][1] = fmaf(pj, v01.y, o[r][1]);
-        o[r][2] = fmaf(pj, v23.x, o[r][2]);
-        o[r][3] = fmaf(pj, v23.y, o[r][3]);
+      for (int e = 0; e < 4; ++e) {
+        const float pv = __expf(s[j][e] - m_r[e >> 1]);
+        s[j][e] = pv;
+        rs[e >> 1] += pv;
       }
+    uint32_t pf[4];
+    pf[0] = pack2(s[0][0], s[0][1]);
+    pf[1] = pack2(s[0][2], s[0][3]);
+    pf[2] = pack2(s[1][0], s[1][1]);
+    pf[3] = pack2(s[1][2], s[1][3]);
+#pragma unroll
+    for (int r2 = 0; r2 < 2; ++r2) l_r[r2] = l_r[r2] * alpha[r2] + rs[r2];
+#pragma unroll
+    for (int j = 0; j < D / 8; ++j) {
+      o[j][0] *= alpha[0];
+      o[j][1] *= alpha[0];
+      o[j][2] *= alpha[1];
+      o[j][3] *= alpha[1];
+    }
+    // O += P V: V tile read transposed by ldmatrix
+#pragma unroll
+    for (int j = 0; j < D / 8; j += 2) {
+      uint32_t b0, b1, b2, b3;
+      const int r = (lane % 8) + ((lane / 8) % 2) * 8;
+      ldsm_x4_t(vt + swz(r, j + lane / 16), b0, b1, b2, b3);
+      mma16816(o[j], pf, b0, b1);
+      mma16816(o[j + 1], pf, b2, b3);
     }
   }
-  // merge the four warps' partials, then this chunk's partial per head -> workspace
+  // row sums across the quad; rows (heads) < R go to the merge buffers
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    if (lane == 0) {
-      s_m[warp][r] = m[r];
-      s_l[warp][r] = l[r];
+  for (int r2 = 0; r2 < 2; ++r2) {
+    l_r[r2] += __shfl_xor_sync(0xffffffffu, l_r[r2], 1);
+    l_r[r2] += __shfl_xor_sync(0xffffffffu, l_r[r2], 2);
+  }
+#pragma unroll
+  for (int r2 = 0; r2 < 2; ++r2) {
+    const int row = lane / 4 + r2 * 8;
+    if (row < R) {
+      if (lane % 4 == 0) {
+        s_m[warp * R + row] = m_r[r2];
+        s_l[warp * R + row] = l_r[r2];
+      }
+#pragma unroll
+      for (int j = 0; j < D / 8; ++j) {
+        const int col = j * 8 + (lane % 4) * 2;
+        s_o[(warp * R + row) * D + col] = o[j][2 * r2];
+        s_o[(warp * R + row) * D + col + 1] = o[j][2 * r2 + 1];
+      }
     }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) s_o[warp][r][4 * lane + j] = o[r][j];
   }
   __syncthreads();
+  // this chunk's partial per head (max, sum, unnormalised output) -> workspace
   for (int i = threadIdx.x; i < R * D; i += THREADS) {
     const int r = i / D, d = i % D;
     float M = -INFINITY;
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w][r]);
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w * R + r]);
     float L = 0.f, O = 0.f;
     for (int w = 0; w < 4; ++w) {
-      const float f = s_m[w][r] == -INFINITY ? 0.f : __expf(s_m[w][r] - M);
-      L += s_l[w][r] * f;
-      O += s_o[w][r][d] * f;
+      const float mw = s_m[w * R + r];
+      const float f = mw == -INFINITY ? 0.f : __expf(mw - M);
+      L += s_l[w * R + r] * f;
+      O += s_o[(w * R + r) * D + d] * f;
     }
     const int h = g * R + r;
     float *dst = p.ws + (((int64_t)b * p.H + h) * p.splits + c) * (D + 2);
@@ -189,6 +264,11 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_kernel(const __grid_co
     }
     dst[2 + d] = O;
   }
+}
+
+template <int R>
+constexpr int smem_bytes() {
+  return 16 * D * 2 + 4 * WARP_SMEM + (4 * R * D + 8 * R) * 4;
 }
 
 // out[b, h, :] = merge of the chunks' partials
@@ -208,8 +288,8 @@ __global__ void __launch_bounds__(D) attn_decode_combine_kernel(const __grid_con
   p.out[(int64_t)b * p.ob + (int64_t)h * p.oh + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
 }
 
-// The planner picks the chunk count (chunks of ~128 keys, at least four CTAs
-// per SM in all) and sizes the workspace: B * H * splits * (D + 2) floats.
+// The planner picks the chunk count (chunks of ~512 keys, at least one CTA per
+// SM in all) and sizes the workspace: B * H * splits * (D + 2) floats.
 // "attn_decode": ptrs q k v out pos ws; ints B H HKV S D splits pos_dtype
 //                qb qh kb kh ks vb vh vs ob oh; floats scale
 int check(const Step &s) {
@@ -257,13 +337,24 @@ int launch(const LaunchArgs &a) {
   p.scale = a.step->floats[0];
   if (p.B == 0) return NKB_OK;
   const unsigned grid = (unsigned)(p.B * p.HKV * p.splits);
+  static bool attr_set[64][4] = {};
+  auto go = [&](auto kern, int smem, int slot) -> int {
+    if (a.device >= 0 && a.device < 64 && !attr_set[a.device][slot]) {
+      NKB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      attr_set[a.device][slot] = true;
+    }
+    kern<<<grid, THREADS, smem, a.stream>>>(p);
+    return NKB_OK;
+  };
+  int st = NKB_OK;
   switch (p.n_rep) {
-    case 1: attn_decode_kernel<1><<<grid, THREADS, 0, a.stream>>>(p); break;
-    case 2: attn_decode_kernel<2><<<grid, THREADS, 0, a.stream>>>(p); break;
-    case 4: attn_decode_kernel<4><<<grid, THREADS, 0, a.stream>>>(p); break;
-    case 8: attn_decode_kernel<8><<<grid, THREADS, 0, a.stream>>>(p); break;
+    case 1: st = go(attn_decode_kernel<1>, smem_bytes<1>(), 0); break;
+    case 2: st = go(attn_decode_kernel<2>, smem_bytes<2>(), 1); break;
+    case 4: st = go(attn_decode_kernel<4>, smem_bytes<4>(), 2); break;
+    case 8: st = go(attn_decode_kernel<8>, smem_bytes<8>(), 3); break;
     default: return fail(NKB_ERR_UNSUPPORTED, "attn_decode: 1, 2, 4 or 8 query heads per KV head");
   }
+  if (st) return st;
   if (int s = launch_status("attn_decode_kernel")) return s;
   attn_decode_combine_kernel<<<(unsigned)(p.B * p.H), D, 0, a.stream>>>(p);
   return launch_status("attn_decode_combine_kernel");

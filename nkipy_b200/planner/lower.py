@@ -479,10 +479,10 @@ class Lowering:
             # one query row against keys 0..pos of the cache: split over keys, then merged
             posv = self.materialize(self.get(p["pos"]), dense=True)
             skv = p["skv"]
-            # chunks of ~128 keys (many CTAs: the last wave is a small share), at least
-            # four per SM in all, at most 256 chunks of 32 or more keys
+            # chunks of ~512 keys (eight 16-key tiles per warp, double-buffered), at
+            # least one CTA per SM in all, at most 256 chunks of 16 or more keys
             bg = max(1, B * k_heads)
-            splits = max(1, min(256, -(-skv // 32), max(-(-skv // 128), -(-4 * 148 // bg))))
+            splits = max(1, min(256, -(-skv // 16), max(-(-skv // 512), -(-148 // bg))))
             ws = self.tmp_view((B * H * splits * (D + 2),), np.float32)
             ints = [B, H, k_heads, skv, D, splits, E.dt_code(posv.dtype)]
             ints += qs[:2] + ks[:3] + vs[:3] + [H * D, D]
