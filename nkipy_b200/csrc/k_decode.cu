@@ -17,6 +17,7 @@
 // CTA writes its partial (max, sum, unnormalised output) per head; a second
 // kernel merges the chunks of each (b, h).  fp32 softmax, bf16 output.
 #include "common.cuh"
+#include "mma_sync.cuh"
 
 namespace nkb {
 namespace decode {
@@ -41,42 +42,9 @@ __device__ __forceinline__ int64_t load_pos(const void *p, int dt) {
   return (dt == NKB_U32 || dt == NKB_U16 || dt == NKB_U8) ? (int64_t)raw : (int64_t)(int32_t)raw;
 }
 
-// ---- mma.sync helpers (bf16 m16n8k16, fp32 accumulation) ---------------------
-__device__ __forceinline__ uint32_t smem_addr(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-// byte offset of 16-byte chunk `chunk` of row `row` in a [rows][128] bf16 tile,
-// XOR-swizzled so the eight rows an ldmatrix reads fall in different banks
-__device__ __forceinline__ uint32_t swz(int row, int chunk) {
-  return row * (D * 2) + ((chunk ^ (row & 7)) << 4);
-}
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool pred) {
-  const int n = pred ? 16 : 0;  // zero-fill past the keys this warp may read
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n));
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;"); }
-__device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;"); }
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void mma16816(float *c, const uint32_t *a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t *>(&h);
-}
+using namespace mma;
+// byte offset of 16-byte chunk `chunk` of row `row` in a swizzled [rows][128] bf16 tile
+__device__ __forceinline__ uint32_t swz(int row, int chunk) { return mma::swz(row, chunk, D * 2); }
 
 constexpr int BN = 16;                      // keys per tile
 constexpr int TILE_BYTES = BN * D * 2;      // 4 KB per K or V tile
@@ -135,7 +103,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_kernel(const __grid_co
   cp_commit();
 
   // Q fragments (A operand, rows = heads), kept in registers
-  asm volatile("cp.async.wait_group 1;");
+  cp_wait<1>();
   __syncthreads();
   uint32_t qf[D / 16][4];
 #pragma unroll
@@ -153,7 +121,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_kernel(const __grid_co
     __syncwarp();  // every lane is done reading the stage the next load overwrites
     if (i + 1 < my_tiles) load_tile(i + 1, stage ^ 1);
     cp_commit();
-    cp_wait1();
+    cp_wait<1>();
     __syncwarp();  // this tile's copies, issued by every lane, are visible
     const uint32_t kt = smem_addr(ring + stage * 2 * TILE_BYTES), vt = kt + TILE_BYTES;
     const int ts = k0 + (warp + 4 * i) * BN;

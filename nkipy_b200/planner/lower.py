@@ -302,6 +302,8 @@ class Lowering:
             M, N, K = s.ints[:3]
             if s.ints[6] != 1 or s.ints[10] != 0 or M <= 0 or N <= 0:
                 continue
+            if self._skinny(s):
+                continue
             tiles = -(-M // self.TILE_M) * -(-N // self.TILE_N)
             k_blocks = -(-K // self.TILE_K)
             if 2 * tiles > self.SMS or k_blocks < 4:
@@ -313,6 +315,27 @@ class Lowering:
             s.bufs.append((ws, 0))
             s.ints += [4, ks]
             s.note += f" split-k {ks}"
+
+    def _skinny(self, s) -> bool:
+        """At most 16 rows of A (K contiguous) against B (N contiguous): the
+        ``gemm_skinny`` kernel (mma.sync with the rows as one m16 tile, B
+        streamed once), its K range split for two CTAs per SM."""
+        M, N, K, lda, ldb, ldc = s.ints[:6]
+        a_mn, b_k = s.ints[11], s.ints[12]
+        if M > 16 or a_mn or b_k or K % 8 or N % 8 or lda % 8 or ldb % 8 or ldc % 2:
+            return False
+        if s.bufs[0][1] % 16 or s.bufs[1][1] % 16 or s.bufs[2][1] % 4:
+            return False
+        col_blocks = -(-N // 256)
+        splits = -(-2 * self.SMS // col_blocks)
+        kc = min(1024, max(64, -(-(-(-K // splits)) // 64) * 64))
+        ks = -(-K // kc)
+        ws = self.new_buf("tmp", -1, ks * M * N * 4 if ks > 1 else 16)
+        s.kernel = "gemm_skinny"
+        s.bufs = s.bufs[:3] + [(ws, 0)]
+        s.ints = [M, N, K, lda, ldb, ldc, kc]
+        s.note = f"{M}x{N}x{K} k-ranges {ks}"
+        return True
 
     def lifetimes(self):
         life = {}

@@ -40,10 +40,11 @@ def test_residual_rmsnorm(rows, cols):
 
 
 @pytest.mark.parametrize("m,k,n", [(256, 512, 256), (8192, 8192, 8192), (300, 200, 264), (128, 64, 256), (1000, 4096, 1000),
-                                   (8, 4096, 6144), (1, 4096, 4096), (5, 12288, 1000)])
+                                   (8, 4096, 6144), (1, 4096, 4096), (5, 12288, 1000), (16, 200, 264), (3, 64, 8)])
 def test_matmul_bf16(m, k, n):
-    """Tiles of 128 x 256; products with few tiles (decode rows against a weight
-    matrix, ragged shapes) split their K range across the SMs."""
+    """Tiles of 128 x 256 on tcgen05; products with few tiles split their K range
+    across the SMs; at most 16 rows (decode rows against a weight matrix, ragged
+    K ranges and column blocks) run on the skinny mma.sync kernel."""
     rng = np.random.default_rng(5)
     a = (rng.standard_normal((m, k), dtype=np.float32) * 0.02).astype(BF16)
     b = (rng.standard_normal((k, n), dtype=np.float32) * 0.02).astype(BF16)

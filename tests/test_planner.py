@@ -179,10 +179,12 @@ def test_kv_cache_decode_updates_caches_in_place():
     assert [s.ints[3:5] for s in rr] == [[4, width], [2, width]]
     assert all(s.ints[6] == 1 and s.ints[8] == 64 and s.ints[11] == 0 for s in rr)
     assert all(p.buffers[s.bufs[5][0]].kind == "in" and p.buffers[s.bufs[5][0]].index == 6 for s in rr)
-    # the 2-row projections have 2 and 1 output tiles: their K range is split across the SMs
-    gs = [s for s in p.steps if s.kernel == "gemm_bf16"]
-    assert [s.ints[13:] for s in gs] == [[4, 4], [4, 4]] and all(len(s.bufs) == 4 for s in gs)
-    assert [p.buffers[s.bufs[3][0]].nbytes for s in gs] == [4 * 2 * width * 4, 4 * 2 * 512 * 4]
+    # the 2-row projections run on the skinny GEMM (rows as one m16 tile), K split into
+    # 64-row ranges: 8 of them, each CTA's fp32 partial rows in the workspace
+    gs = [s for s in p.steps if s.kernel == "gemm_skinny"]
+    assert [s.ints for s in gs] == [[2, width, 512, 512, width, width, 64], [2, 512, 512, 512, 512, 512, 64]]
+    assert [p.buffers[s.bufs[3][0]].nbytes for s in gs] == [8 * 2 * width * 4, 8 * 2 * 512 * 4]
+    assert "gemm_bf16" not in kinds
     # the new value row is scattered straight from the projection output
     assert [len(s.ints) for s in sc] == [5, 6] and sc[1].ints[5] == width * 2
     assert not {"ew", "take", "rmsnorm_rows"} & set(kinds)
