@@ -914,11 +914,11 @@ class Lowering:
     def op_convolution(self, op):
         """``conv2d`` / ``conv3d`` (``core/ops/conv.py:230-312``) as one GEMM.
 
-        The zero-padded input (one ``pad`` launch when the padding is not 0) is
-        read through a strided view of its kernel windows, ordered (channel,
-        kernel offset, batch, output position); one ``ew`` launch writes it
-        dense, its innermost axis the output column (contiguous in the input
-        at stride 1, so the copy is coalesced on both sides).  The correlation
+        One ``im2col`` launch writes the window matrix, ordered (channel, kernel
+        offset) x (batch, output position), from the dense input with zeros
+        where a window reaches into the padding (its writes contiguous along the
+        innermost output axis; other element sizes take a ``pad`` launch and a
+        strided ``ew`` copy of the same matrix).  The correlation
         is then cols^T^T @ W^T: the window matrix is an M-major left operand
         (C*prod(k) rows of B*P positions) and the weight, row-major
         (OC, C, *k), a K-major right operand as it lies.  The (B, P, OC)
@@ -949,23 +949,29 @@ class Lowering:
         out_sp = tuple(int(s) for s in op.result_shape[2:])
         dt = np.dtype(op.result_dtype)
         xv = self.materialize(self.get(x), dense=True)
-        if any(lo or hi for lo, hi in pads):
-            pshape = (B, C) + tuple(int(x.shape[2 + i]) + pads[i][0] + pads[i][1] for i in range(n))
-            pv = self.tmp_view(pshape, x.dtype)
-            ints = [n + 2, np.dtype(x.dtype).itemsize, pv.size, 0] + [int(s) for s in x.shape] + list(pshape)
-            ints += [0, 0] + [lo for lo, _ in pads]
-            self.step("pad", [self.bref(xv), self.bref(pv)], ints, note="convolution padding")
-            xv = pv
-        xs = xv.strides
-        win = xv.with_(
-            shape=(C,) + ks + (B,) + out_sp,
-            strides=(xs[1],) + tuple(xs[2 + i] * dil[i] for i in range(n)) + (xs[0],)
-            + tuple(xs[2 + i] * stride[i] for i in range(n)),
-        )
         P, KK = int(np.prod(out_sp)), C * int(np.prod(ks))
         M, N, K = B * P, OC, KK
-        cols = self.tmp_view((KK, M), x.dtype)  # cols[kk, b * P + p]
-        self.copy_view(win, cols.with_(shape=win.shape, strides=V.dense_strides(win.shape)))
+        cols = self.tmp_view((KK, M), x.dtype)  # cols[kk, b * P + p], zero where a window reaches the padding
+        es = np.dtype(x.dtype).itemsize
+        if es in (2, 4):
+            ints = [n, es, B, C] + [int(d) for d in x.shape[2:]] + list(ks) + list(out_sp) + stride
+            ints += [lo for lo, _ in pads] + dil
+            self.step("im2col", [self.bref(xv), self.bref(cols)], ints, note="convolution windows")
+        else:
+            if any(lo or hi for lo, hi in pads):
+                pshape = (B, C) + tuple(int(x.shape[2 + i]) + pads[i][0] + pads[i][1] for i in range(n))
+                pv = self.tmp_view(pshape, x.dtype)
+                ints = [n + 2, es, pv.size, 0] + [int(s_) for s_ in x.shape] + list(pshape)
+                ints += [0, 0] + [lo for lo, _ in pads]
+                self.step("pad", [self.bref(xv), self.bref(pv)], ints, note="convolution padding")
+                xv = pv
+            xs = xv.strides
+            win = xv.with_(
+                shape=(C,) + ks + (B,) + out_sp,
+                strides=(xs[1],) + tuple(xs[2 + i] * dil[i] for i in range(n)) + (xs[0],)
+                + tuple(xs[2 + i] * stride[i] for i in range(n)),
+            )
+            self.copy_view(win, cols.with_(shape=win.shape, strides=V.dense_strides(win.shape)))
         wv = self.materialize(self.get(w), dense=True)
         prod = self.tmp_view((B, P, OC), dt)
         eb = np.dtype(BF16).itemsize

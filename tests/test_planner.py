@@ -329,8 +329,12 @@ def test_convolution_plans():
         return cc_ops.conv3d(x, w, stride=(1, 2, 1), padding=1, dilation=(2, 1, 1))
 
     p = plan_of(c2, np.zeros((2, 16, 12, 12), BF16), np.zeros((32, 16, 3, 3), BF16), np.zeros(32, BF16))
-    # pad, im2col copy, tensor-core GEMM, layout move fused with the bias add
-    assert [s.kernel for s in p.steps] == ["pad", "ew", "gemm_bf16", "ew"]
+    # window matrix (padding as zeros), tensor-core GEMM, layout move fused with the bias add
+    assert [s.kernel for s in p.steps] == ["im2col", "gemm_bf16", "ew"]
+    assert p.steps[0].ints == [2, 2, 2, 16, 12, 12, 3, 3, 12, 12, 1, 1, 1, 1, 1, 1]
     p = plan_of(c3, np.zeros((1, 2, 6, 7, 8), np.float32), np.zeros((3, 2, 2, 3, 2), np.float32))
     kinds = p.kernel_counts()
-    assert kinds["gemm_simt"] == 1 and kinds["pad"] == 1
+    assert kinds["gemm_simt"] == 1 and kinds["im2col"] == 1 and "pad" not in kinds
+    (im,) = [s for s in p.steps if s.kernel == "im2col"]
+    # 3-D: input 6x7x8, kernel 2x3x2, output 6x4x9, stride (1, 2, 1), low padding 1, dilation (2, 1, 1)
+    assert im.ints == [3, 4, 1, 2, 6, 7, 8, 2, 3, 2, 6, 4, 9, 1, 2, 1, 1, 1, 1, 2, 1, 1]
