@@ -338,3 +338,23 @@ def test_convolution_plans():
     (im,) = [s for s in p.steps if s.kernel == "im2col"]
     # 3-D: input 6x7x8, kernel 2x3x2, output 6x4x9, stride (1, 2, 1), low padding 1, dilation (2, 1, 1)
     assert im.ints == [3, 4, 1, 2, 6, 7, 8, 2, 3, 2, 6, 4, 9, 1, 2, 1, 1, 1, 1, 2, 1, 1]
+
+
+def test_skinny_gemm_selection():
+    """At most 16 rows with K-contiguous A and N-contiguous B take the skinny
+    mma.sync GEMM; more rows or a transposed operand keep the tcgen05 kernel."""
+    def mm(a, b):
+        return a @ b
+
+    def mm_bt(a, b):
+        return a @ b.T
+
+    z = lambda *s: np.zeros(s, BF16)  # noqa: E731
+    p = plan_of(mm, z(16, 4096), z(4096, 1024))
+    (s,) = p.steps
+    M, N, K, lda, ldb, ldc, kc = s.ints
+    assert s.kernel == "gemm_skinny" and (M, N, K, lda, ldb, ldc) == (16, 1024, 4096, 4096, 1024, 1024)
+    # 4 column blocks of 256: K split for two CTAs per SM (74 ranges wanted, 64-row multiples)
+    assert kc == 64 and p.buffers[s.bufs[3][0]].nbytes == (4096 // 64) * 16 * 1024 * 4
+    assert plan_of(mm, z(17, 4096), z(4096, 1024)).steps[0].kernel == "gemm_bf16"
+    assert plan_of(mm_bt, z(8, 4096), z(1024, 4096)).steps[0].kernel == "gemm_bf16"
