@@ -50,6 +50,7 @@ struct Args {
   void *C;
   int64_t M, N, K, ldc, sC, batch;
   int c_f32, a_mn_major, b_k_major;
+  int a_bcast, b_bcast;  // batch stride 0: every batch reads operand batch 0
   int tiles_m, tiles_n;
   // epi == 1 (SwiGLU): B holds [gate | up] halves of width n_half; a CTA
   // computes 128 gate + the matching 128 up columns and writes
@@ -351,22 +352,22 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
           uint8_t *a_dst = sA + s * A_STAGE_BYTES;
           uint8_t *b_dst = sB + s * B_STAGE_BYTES;
           if (!args.a_mn_major) {
-            tma_load_3d(a_dst, &map_a, &full[s], kb * BK, bm * BM, bb);
+            tma_load_3d(a_dst, &map_a, &full[s], kb * BK, bm * BM, args.a_bcast ? 0 : bb);
           } else {
             for (int j = 0; j < BM / 64; ++j)
-              tma_load_3d(a_dst + j * (64 * BK * 2), &map_a, &full[s], bm * BM + j * 64, kb * BK, bb);
+              tma_load_3d(a_dst + j * (64 * BK * 2), &map_a, &full[s], bm * BM + j * 64, kb * BK, args.a_bcast ? 0 : bb);
           }
           if (args.b_k_major) {
-            tma_load_3d(b_dst, &map_b, &full[s], kb * BK, bn * BN, bb);
+            tma_load_3d(b_dst, &map_b, &full[s], kb * BK, bn * BN, args.b_bcast ? 0 : bb);
           } else if (args.epi == 1) {
             const int n0 = bn * (BN / 2);
             for (int j = 0; j < BN / 64; ++j) {
               const int col = (j < 2) ? n0 + j * 64 : (int)args.n_half + n0 + (j - 2) * 64;
-              tma_load_3d(b_dst + j * (64 * BK * 2), &map_b, &full[s], col, kb * BK, bb);
+              tma_load_3d(b_dst + j * (64 * BK * 2), &map_b, &full[s], col, kb * BK, args.b_bcast ? 0 : bb);
             }
           } else {
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_3d(b_dst + j * (64 * BK * 2), &map_b, &full[s], bn * BN + j * 64, kb * BK, bb);
+              tma_load_3d(b_dst + j * (64 * BK * 2), &map_b, &full[s], bn * BN + j * 64, kb * BK, args.b_bcast ? 0 : bb);
           }
         }
       }
@@ -710,8 +711,6 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(NKB_ERR_UNSUPPORTED, "gemm: dims exceed int32");
   // broadcast operands (batch stride 0) reuse batch index 0 via a size-1 batch dim
   const uint64_t ba = sA ? batch : 1, bb = sB ? batch : 1;
-  if ((sA == 0 && batch > 1) || (sB == 0 && batch > 1))
-    return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: broadcast batch operands take the strided path");
   CUtensorMap ma, mb;
   int s;
   if (!a_mn_major) s = make_map(&ma, A, K, M, ba, lda, sA, BK, BM);
@@ -736,6 +735,8 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   args.c_f32 = c_f32;
   args.a_mn_major = a_mn_major;
   args.b_k_major = b_k_major;
+  args.a_bcast = sA == 0 && batch > 1;  // one operand matrix shared by every batch (its map has one)
+  args.b_bcast = sB == 0 && batch > 1;
   args.epi = epi;
   args.n_half = n_half;
   args.res = static_cast<const __nv_bfloat16 *>(res);

@@ -921,8 +921,11 @@ class Lowering:
         strided ``ew`` copy of the same matrix).  The correlation
         is then cols^T^T @ W^T: the window matrix is an M-major left operand
         (C*prod(k) rows of B*P positions) and the weight, row-major
-        (OC, C, *k), a K-major right operand as it lies.  The (B, P, OC)
-        product is moved to the (B, OC, *out) result layout.  bf16 runs on
+        (OC, C, *k), a K-major right operand as it lies; with a multiple of 8
+        output positions per image (bf16) it is instead one batched product
+        per image, out[b] = W @ cols[:, b], the weight shared by the images
+        and the result written in the (B, OC, *out) layout directly.  Otherwise
+        the (B, P, OC) product is moved to the (B, OC, *out) result layout.  bf16 runs on
         ``gemm_bf16`` (fp32 accumulation), other dtypes on ``gemm_simt``.
         """
         x, w = op.operands
@@ -973,8 +976,17 @@ class Lowering:
             )
             self.copy_view(win, cols.with_(shape=win.shape, strides=V.dense_strides(win.shape)))
         wv = self.materialize(self.get(w), dense=True)
-        prod = self.tmp_view((B, P, OC), dt)
         eb = np.dtype(BF16).itemsize
+        bf = np.dtype(cols.dtype) == BF16 and np.dtype(wv.dtype) == BF16 and dt == BF16
+        if bf and K % 8 == 0 and P % 8 == 0 and M % 8 == 0 and (wv.offset * eb) % 16 == 0:
+            # per image: out[b] (OC x P) = W (OC x K, shared by every image) @ cols[:, b] (K x P),
+            # written straight in the (B, OC, *out) result layout
+            out = self.tmp_view((B, OC) + out_sp, dt)
+            self.step("gemm_bf16", [self.bref(wv), self.bref(cols), self.bref(out)],
+                      [OC, P, K, K, M, P, B, 0, P, OC * P, 0, 0, 0], note=f"tc {B}x{OC}x{P}x{K} convolution")
+            self.put(op, out)
+            return
+        prod = self.tmp_view((B, P, OC), dt)
         if (np.dtype(cols.dtype) == BF16 and np.dtype(wv.dtype) == BF16 and dt == BF16 and K % 8 == 0
                 and N % 8 == 0 and M % 8 == 0 and (wv.offset * eb) % 16 == 0):
             self.step("gemm_bf16", [self.bref(cols), self.bref(wv), self.bref(prod)],
