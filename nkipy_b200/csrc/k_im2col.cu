@@ -5,6 +5,8 @@
 // strided copy: one read of the input (through L2) and one coalesced write of
 // the matrix (contiguous along the innermost output axis).  Element size 2 or
 // 4 bytes.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace nkb {
@@ -82,51 +84,54 @@ __global__ void __launch_bounds__(RX * RY) im2col_kernel(const __grid_constant__
 // output row decomposed once, the 8 inputs gathered from L1 / L2), so every
 // store is 16 bytes and a warp writes 512 contiguous bytes.
 constexpr int VT = 256;  // threads (groups of 8) per block
+// I: the index type (32-bit when every index of the launch fits, fewer instructions)
+template <typename I>
 __global__ void __launch_bounds__(VT) im2col8_kernel(const __grid_constant__ Params p) {
   const uint16_t *x = static_cast<const uint16_t *>(p.x);
   uint16_t *cols = static_cast<uint16_t *>(p.cols);
   const int n = p.n;
-  const int64_t O = p.out[n - 1], G = O / 8;
-  const int64_t g = (int64_t)blockIdx.x * VT + threadIdx.x;  // group over (row, o / 8)
-  if (g >= p.M / 8) return;
-  const int64_t row = g / G, o0 = (g - row * G) * 8;
-  int64_t ibase[MAXN] = {0, 0, 0}, q = row;  // window origin per outer input axis
+  const I O = (I)p.out[n - 1], G = O / 8, M = (I)p.M;
+  const I g = (I)blockIdx.x * VT + (I)threadIdx.x;  // group over (row, o / 8)
+  if (g >= M / 8) return;
+  const I row = g / G, o0 = (g - row * G) * 8;
+  I ibase[MAXN] = {0, 0, 0}, q = row;  // window origin per outer input axis
   for (int d = n - 2; d >= 0; --d) {
-    const int64_t o = q % p.out[d];
-    q /= p.out[d];
-    ibase[d] = o * p.stride[d] - p.pad[d];
+    const I od = (I)p.out[d];
+    const I o = q % od;
+    q /= od;
+    ibase[d] = o * (I)p.stride[d] - (I)p.pad[d];
   }
-  const int64_t b = q;
-  const int64_t kk0 = (int64_t)blockIdx.y * KKB;
-  int64_t kof[MAXN] = {0, 0, 0}, r = kk0;
+  const I b = q;
+  const I kk0 = (I)blockIdx.y * KKB;
+  I kof[MAXN] = {0, 0, 0}, r = kk0;
   for (int d = n - 1; d >= 0; --d) {
-    kof[d] = r % p.ks[d];
-    r /= p.ks[d];
+    kof[d] = r % (I)p.ks[d];
+    r /= (I)p.ks[d];
   }
-  int64_t c = r;
-  const int64_t kk1 = min(p.KK, kk0 + KKB);
-  const int64_t s = p.stride[n - 1], W = p.in[n - 1];
-  for (int64_t kk = kk0; kk < kk1; ++kk) {
-    int64_t base = (b * p.C + c) * p.in_plane, plane = 1;
+  I c = r;
+  const I kk1 = min((I)p.KK, kk0 + KKB);
+  const I s = (I)p.stride[n - 1], W = (I)p.in[n - 1], C = (I)p.C, plane_all = (I)p.in_plane;
+  for (I kk = kk0; kk < kk1; ++kk) {
+    I base = (b * C + c) * plane_all, plane = 1;
     bool ok = true;
     for (int d = n - 2; d >= 0; --d) {
-      plane *= p.in[d + 1];
-      const int64_t i = ibase[d] + kof[d] * p.dil[d];
-      ok = ok && i >= 0 && i < p.in[d];
+      plane *= (I)p.in[d + 1];
+      const I i = ibase[d] + kof[d] * (I)p.dil[d];
+      ok = ok && i >= 0 && i < (I)p.in[d];
       base += i * plane;
     }
-    const int64_t i0 = o0 * s + kof[n - 1] * p.dil[n - 1] - p.pad[n - 1];
+    const I i0 = o0 * s + kof[n - 1] * (I)p.dil[n - 1] - (I)p.pad[n - 1];
     uint32_t w[4];
 #pragma unroll
     for (int e = 0; e < 8; e += 2) {
-      const int64_t ia = i0 + e * s, ib = ia + s;
+      const I ia = i0 + e * s, ib = ia + s;
       const uint32_t va = (ok && ia >= 0 && ia < W) ? x[base + ia] : 0u;
       const uint32_t vb = (ok && ib >= 0 && ib < W) ? x[base + ib] : 0u;
       w[e / 2] = va | (vb << 16);
     }
-    *reinterpret_cast<uint4 *>(cols + kk * p.M + row * O + o0) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4 *>(cols + (int64_t)kk * M + (int64_t)row * O + o0) = make_uint4(w[0], w[1], w[2], w[3]);
     for (int d = n - 1; d >= 0; --d) {
-      if (++kof[d] < p.ks[d]) break;
+      if (++kof[d] < (I)p.ks[d]) break;
       kof[d] = 0;
       if (d == 0) ++c;
     }
@@ -175,7 +180,14 @@ int launch(const LaunchArgs &a) {
   if (p.esize == 2 && p.out[p.n - 1] % 8 == 0 && (reinterpret_cast<uintptr_t>(p.cols) & 15) == 0 &&
       gy <= 65535 && (p.M / 8 + VT - 1) / VT <= INT32_MAX) {
     dim3 grid((unsigned)((p.M / 8 + VT - 1) / VT), (unsigned)gy);
-    im2col8_kernel<<<grid, VT, 0, a.stream>>>(p);
+    // 32-bit indices when the input, the matrix row length and every window coordinate fit
+    int64_t lim = std::max<int64_t>(p.B * p.C * p.in_plane, p.M + VT * 8);
+    for (int d = 0; d < p.n; ++d)
+      lim = std::max<int64_t>(lim, (p.out[d] + 8) * p.stride[d] + p.ks[d] * p.dil[d] + p.pad[d] + p.in[d]);
+    if (lim < INT32_MAX / 2)
+      im2col8_kernel<int32_t><<<grid, VT, 0, a.stream>>>(p);
+    else
+      im2col8_kernel<int64_t><<<grid, VT, 0, a.stream>>>(p);
     return launch_status("im2col8_kernel");
   }
   if (gy > 65535 || (rows + RY - 1) / RY > INT32_MAX) return fail(NKB_ERR_UNSUPPORTED, "im2col: too large");
