@@ -10,7 +10,13 @@ line.  Workloads (``--workload``):
   rmsnorm  fp32 (16384, 4096) residual add + RMSNorm         HBM GB/s
   gemm     bf16 8192^3 matmul, fp32 accumulate               TFLOP/s
   bmm      bf16 32 x 2048^3 batched matmul                   TFLOP/s
+  linattn  bf16 (8, 16, 4096, 128) chunked linear attention  HBM GB/s
   layer    Llama decoder layer, batch 4 x 2048, TP = N       tokens/s
+  decode   Qwen3 attention decode step, KV cache resident    tokens/s
+  topk     top-8 of (128, 151936) bf16 logits                HBM GB/s
+  conv     conv2d bf16 3x3, (16, 128, 56, 56)                TFLOP/s
+  ewchain  fp32 (16384, 4096) silu(gate) * up                HBM GB/s
+  transpose fp32 (8192, 8192) materialised transpose         HBM GB/s
 
 Timing: W untimed warm-up steps, then K steps each preceded by an L2 flush
 (256 MiB written, then read back, outside the timed events: the lines it
@@ -26,15 +32,23 @@ weights as device tensors, examples/models/qwen3/qwen3.py:280-336); there
 only the activations ``x`` move per step.
 ``--impl reference`` times the CPU path of the same kernel (the NumPy
 direct call restated in ``oracle/``) on a bounded sample, on rank 0 only.
+
+Parity: after the timed regions, rank 0 reads the outputs back and compares a
+bounded sample with the oracle (the checker, never the thing measured), at
+every GPU count: for the decoder layer the first 256 tokens of sequence 0,
+which by causality depend only on that sequence's first 256 input tokens.
+The line's ``parity`` object (and each suite entry's) says whether it held.
 """
 
 import argparse
 import concurrent.futures
 import json
 import os
+import shutil
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -67,6 +81,31 @@ def load_peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
+def compare(got, want, rtol, sample, exact=False):
+    """Parity of a device result against the oracle on a bounded sample, with
+    the tests' criteria: bit-exact for integer/index work; fp32 elementwise
+    ``|d| <= rtol |want| + 1e-7 max(1, max|want|)``; bf16 paths normwise
+    ``|d| <= rtol max|want|``."""
+    if exact:
+        got, want = np.asarray(got), np.asarray(want)
+        if got.dtype == want.dtype:  # bit patterns (floats: the sign of zero and NaNs included)
+            ok = got.shape == want.shape and bool(np.array_equal(np.ascontiguousarray(got).view(np.uint8),
+                                                                 np.ascontiguousarray(want).view(np.uint8)))
+        else:
+            ok = got.shape == want.shape and bool(np.array_equal(got, want))
+        return {"ok": ok, "max_rel_err": 0.0 if ok else None, "tol": "exact", "sample": sample}
+    g, w = np.asarray(got).astype(np.float32), np.asarray(want).astype(np.float32)
+    peak = max(1e-30, float(np.max(np.abs(w)))) if w.size else 1.0
+    d = np.abs(g - w)
+    err = float(np.max(d)) / peak if d.size else 0.0
+    if rtol <= 1e-5:
+        ok = bool(np.all(d <= rtol * np.abs(w) + 1e-7 * max(1.0, peak)))
+    else:
+        ok = bool(err <= rtol)
+    ok = ok and bool(np.all(np.isfinite(g)))
+    return {"ok": ok, "max_rel_err": err, "tol": rtol, "sample": sample}
+
+
 # ---------------------------------------------------------------------------
 # workloads
 # ---------------------------------------------------------------------------
@@ -94,12 +133,26 @@ class Workload:
         """Algorithmic bytes (hbm) or flops (tensor) of one dominant launch."""
         raise NotImplementedError
 
+    def cpu_prepare(self):
+        """Inputs of the bounded CPU sample, built once outside the timed steps."""
+        return ()
+
+    def cpu_inputs(self):
+        if getattr(self, "_cpu_in", None) is None:
+            self._cpu_in = self.cpu_prepare()
+        return self._cpu_in
+
     def cpu_step(self, threads):
-        """One bounded CPU sample: returns (units processed, description)."""
+        """One bounded CPU sample on ``cpu_inputs()``: returns (units processed, description)."""
         raise NotImplementedError
 
     def config(self, world):
         return {}
+
+    def parity(self, outs, args):
+        """Compare the device outputs (output name -> ndarray) with the oracle on
+        a bounded sample of the inputs ``args``; returns the ``compare`` record."""
+        return None
 
 
 class Softmax(Workload):
@@ -121,14 +174,23 @@ class Softmax(Workload):
     def cpu_step(self, threads):
         from oracle import numpy_ref as O
 
-        rows = 1024
-        x = np.random.default_rng(7).standard_normal((rows, self.COLS), dtype=np.float32)
+        (x,) = self.cpu_inputs()
+        rows = x.shape[0]
         _parallel_rows(O.softmax, [x], threads)
         return 2 * rows * self.COLS * 4 / 1e9, f"{rows} of {self.ROWS} rows per step"
+
+    def cpu_prepare(self):
+        return (np.random.default_rng(7).standard_normal((1024, self.COLS), dtype=np.float32),)
 
     def config(self, world):
         return {"workload": "softmax fp32 (4096, 4096) last axis", "shape": [self.ROWS, self.COLS],
                 "l2": "flushed between steps (256 MiB written, then read back)"}
+
+    def parity(self, outs, args):
+        from oracle import numpy_ref as O
+
+        x = args[0][:256]
+        return compare(outs["output0"][:256], O.softmax(x), 1e-5, "rows 0..255")
 
 
 class RmsNorm(Workload):
@@ -153,17 +215,26 @@ class RmsNorm(Workload):
     def cpu_step(self, threads):
         from oracle import numpy_ref as O
 
-        rows = 2048
-        rng = np.random.default_rng(8)
-        x = rng.standard_normal((rows, self.COLS), dtype=np.float32)
-        r = rng.standard_normal((rows, self.COLS), dtype=np.float32)
-        w = rng.uniform(0.5, 1.5, self.COLS).astype(np.float32)
+        x, r, w = self.cpu_inputs()
+        rows = x.shape[0]
         _parallel_rows(lambda a, b: O.residual_rmsnorm(a, b, w, 1e-6), [x, r], threads)
         return (3 * rows * self.COLS * 4 + self.COLS * 4) / 1e9, f"{rows} of {self.ROWS} rows per step"
+
+    def cpu_prepare(self):
+        rng = np.random.default_rng(8)
+        x = rng.standard_normal((2048, self.COLS), dtype=np.float32)
+        r = rng.standard_normal((2048, self.COLS), dtype=np.float32)
+        return x, r, rng.uniform(0.5, 1.5, self.COLS).astype(np.float32)
 
     def config(self, world):
         return {"workload": "residual add + RMSNorm fp32 (16384, 4096), eps 1e-6", "shape": [self.ROWS, self.COLS],
                 "l2": "inputs (805 MB) exceed L2; also flushed between steps"}
+
+    def parity(self, outs, args):
+        from oracle import numpy_ref as O
+
+        x, r, w = args
+        return compare(outs["output0"][:256], O.residual_rmsnorm(x[:256], r[:256], w, 1e-6), 1e-5, "rows 0..255")
 
 
 class Gemm(Workload):
@@ -187,16 +258,25 @@ class Gemm(Workload):
     def cpu_step(self, threads):
         from oracle import numpy_ref as O
 
-        m = 1024
-        rng = np.random.default_rng(9)
-        a = (rng.standard_normal((m, self.N), dtype=np.float32) * 0.02).astype(BF16)
-        b = (rng.standard_normal((self.N, self.N), dtype=np.float32) * 0.02).astype(BF16)
+        a, b = self.cpu_inputs()
+        m = a.shape[0]
         O.matmul(a, b)
         return 2 * m * self.N * self.N / 1e12, f"{m} of {self.N} rows of A per step (fp32 BLAS, {threads} threads)"
+
+    def cpu_prepare(self):
+        rng = np.random.default_rng(9)
+        a = (rng.standard_normal((1024, self.N), dtype=np.float32) * 0.02).astype(BF16)
+        return a, (rng.standard_normal((self.N, self.N), dtype=np.float32) * 0.02).astype(BF16)
 
     def config(self, world):
         return {"workload": "matmul bf16 (8192,8192)@(8192,8192), fp32 acc, bf16 out", "M": self.N, "N": self.N,
                 "K": self.N, "l2": "operands+result 384 MB exceed L2; also flushed between steps"}
+
+    def parity(self, outs, args):
+        from oracle import numpy_ref as O
+
+        a, b = args
+        return compare(outs["output0"][:128], O.matmul(a[:128], b), 2e-2, "rows 0..127")
 
 
 class Bmm(Gemm):
@@ -220,15 +300,24 @@ class Bmm(Gemm):
     def cpu_step(self, threads):
         from oracle import numpy_ref as O
 
-        rng = np.random.default_rng(10)
-        a = (rng.standard_normal((2, self.S, self.S), dtype=np.float32) * 0.02).astype(BF16)
-        b = (rng.standard_normal((2, self.S, self.S), dtype=np.float32) * 0.02).astype(BF16)
+        a, b = self.cpu_inputs()
         O.matmul(a, b)
         return 2 * 2 * self.S**3 / 1e12, f"2 of {self.B} batches per step"
+
+    def cpu_prepare(self):
+        rng = np.random.default_rng(10)
+        a = (rng.standard_normal((2, self.S, self.S), dtype=np.float32) * 0.02).astype(BF16)
+        return a, (rng.standard_normal((2, self.S, self.S), dtype=np.float32) * 0.02).astype(BF16)
 
     def config(self, world):
         return {"workload": "batched matmul bf16 bmk,bkn->bmn b=32 m=n=k=2048", "batch": self.B, "M": self.S,
                 "l2": "operands 805 MB exceed L2; also flushed between steps"}
+
+    def parity(self, outs, args):
+        from oracle import numpy_ref as O
+
+        a, b = args
+        return compare(outs["output0"][31], O.matmul(a[31], b[31]), 2e-2, "batch 31")
 
 
 class LinAttn(Workload):
@@ -248,17 +337,29 @@ class LinAttn(Workload):
         return 4 * int(np.prod(self.SHAPE)) * 2
 
     def cpu_step(self, threads):
-        from nkipy_b200 import workloads as W
         from oracle import numpy_ref as O
 
-        q, k, v = W.make_inputs("linattn", seed=7, scale=1 / 8)
-        q, k, v = q[:, :2], k[:, :2], v[:, :2]
+        q, k, v = self.cpu_inputs()
         O.linear_attention_recurrent(q, k, v)
         return 4 * q.size * 2 / 1e9, "1 x 2 of 8 x 16 (batch, head) pairs per step"
+
+    def cpu_prepare(self):
+        from nkipy_b200 import workloads as W
+
+        q, k, v = W.make_inputs("linattn", seed=7, scale=1 / 8)
+        return tuple(np.ascontiguousarray(t[:, :2]) for t in (q, k, v))
 
     def config(self, world):
         return {"workload": "chunked causal linear attention bf16 (8,16,4096,128), elu+1, chunk 64, fp32 state",
                 "shape": list(self.SHAPE), "l2": "inputs 403 MB exceed L2; also flushed between steps"}
+
+    def parity(self, outs, args):
+        from oracle import numpy_ref as O
+
+        q, k, v = args
+        sl = (slice(7, 8), slice(15, 16))
+        return compare(outs["output0"][sl], O.linear_attention_recurrent(q[sl], k[sl], v[sl]), 2e-2,
+                       "(batch, head) (7, 15)")
 
 
 class Layer(Workload):
@@ -271,13 +372,24 @@ class Layer(Workload):
 
         self.shape = W.LayerShape()
 
+    PREFIX = 256  # tokens of sequence 0 in the CPU sample and the parity check
+
+    def _full(self):
+        from nkipy_b200 import workloads as W
+
+        if getattr(self, "_weights", None) is None:
+            s = self.shape
+            self._weights = W.layer_weights(s, seed=0)
+            self._x = np.random.default_rng(500).standard_normal((s.batch, s.seq, s.hidden),
+                                                                 dtype=np.float32).astype(BF16)
+        return self._weights, self._x
+
     def kernel_and_args(self, rank, world):
         from nkipy_b200 import workloads as W
 
         s = self.shape
-        full = W.layer_weights(s, seed=0)
+        full, x = self._full()
         shard = W.shard_layer_weights(full, s, rank, world)
-        x = np.random.default_rng(500).standard_normal((s.batch, s.seq, s.hidden), dtype=np.float32).astype(BF16)
         args, kwargs = W.layer_args(x, shard, s, world)
         return W.llama_decoder_layer_kernel, args, kwargs
 
@@ -296,15 +408,27 @@ class Layer(Workload):
     def dominant_work(self):
         return None  # computed from the per-launch table
 
-    def cpu_step(self, threads):
-        from nkipy_b200 import workloads as W
+    def _oracle_prefix(self):
+        """The oracle's layer on the first PREFIX tokens of sequence 0 of the bench input."""
         from oracle import numpy_ref as O
 
-        s = W.LayerShape(batch=1, seq=256)
-        full = W.layer_weights(s, seed=0)
-        x = np.random.default_rng(501).standard_normal((1, 256, s.hidden), dtype=np.float32).astype(BF16)
-        O.llama_layer(x, full, s.n_heads, s.n_kv_heads, s.head_dim, s.eps, s.theta)
-        return 256, "1 x 256 tokens of the layer per step"
+        full, x = self._full()
+        s = self.shape
+        return O.llama_layer(x[:1, : self.PREFIX], full, s.n_heads, s.n_kv_heads, s.head_dim, s.eps, s.theta)
+
+    def cpu_prepare(self):
+        return self._full()
+
+    def cpu_step(self, threads):
+        self.cpu_inputs()
+        self._oracle_prefix()
+        return self.PREFIX, f"1 x {self.PREFIX} tokens of the layer per step (sequence 0, tokens 0..{self.PREFIX - 1})"
+
+    def parity(self, outs, args):
+        # output tokens 0..PREFIX-1 of sequence 0 depend only on its input tokens 0..PREFIX-1 (causal attention)
+        y = outs["output0"]
+        return compare(y[:1, : self.PREFIX], self._oracle_prefix(), 2e-2,
+                       f"sequence 0, tokens 0..{self.PREFIX - 1} (causal prefix) of the full-shape run")
 
     def config(self, world):
         s = self.shape
@@ -351,10 +475,26 @@ class Decode(Workload):
         w = self.H * (self.NQ + 2 * self.NKV) * self.HD * 2 + self.NQ * self.HD * self.H * 2
         return w + 2 * self.B * self.L * self.NKV * self.HD * 2
 
+    def cpu_prepare(self):
+        return self._args(1, 11)
+
     def cpu_step(self, threads):
-        fn, args, kw = self._args(1, 11)
+        fn, args, kw = self.cpu_inputs()
+        # the caches are mutated in place by the direct call: work on copies
+        args = tuple(a.copy() if isinstance(a, np.ndarray) else a for a in args)
         fn(*args, **kw)
         return 1, f"1 of {self.B} sequences per step (NumPy direct call)"
+
+    def parity(self, outs, args):
+        from oracle import numpy_ref as O
+
+        fn, _, kw = self._args(self.B, 700)
+        # sequence 0 alone, on copies of its original inputs (the device caches
+        # were updated in place at the same position by every timed step)
+        x, wqkv, qn, kn, ck, cv, pos, wo = self._args(self.B, 700)[1]
+        with O.fp32_accumulated_bf16_sums():  # long bf16 softmax sums, accumulated in fp32 as on the device
+            want = fn(x[:1].copy(), wqkv, qn, kn, ck[:1].copy(), cv[:1].copy(), pos, wo, **kw)
+        return compare(outs["output0"][:1], want, 2e-2, "sequence 0 of 8")
 
     def config(self, world):
         return {"workload": "Qwen3 attention decode step bf16, KV cache 2048 resident and updated in place, "
@@ -388,10 +528,20 @@ class TopK(Workload):
     def cpu_step(self, threads):
         from oracle import numpy_ref as O
 
-        rows = 16
-        x = np.random.default_rng(12).standard_normal((rows, self.COLS), dtype=np.float32).astype(BF16)
+        (x,) = self.cpu_inputs()
         O.topk(x, self.K)
-        return rows * self.COLS * 2 / 1e9, f"{rows} of {self.ROWS} rows per step"
+        return x.shape[0] * self.COLS * 2 / 1e9, f"{x.shape[0]} of {self.ROWS} rows per step"
+
+    def cpu_prepare(self):
+        return (np.random.default_rng(12).standard_normal((16, self.COLS), dtype=np.float32).astype(BF16),)
+
+    def parity(self, outs, args):
+        from oracle import numpy_ref as O
+
+        vals, idx = O.topk(args[0][:16], self.K)
+        a = compare(outs["output1"][:16], idx, 0, "rows 0..15", exact=True)
+        b = compare(outs["output0"][:16], vals, 0, "rows 0..15", exact=True)
+        return {**a, "ok": a["ok"] and b["ok"]}
 
     def config(self, world):
         return {"workload": "top-8 bf16 (128, 151936) last axis", "shape": [self.ROWS, self.COLS], "k": self.K,
@@ -426,20 +576,114 @@ class Conv(Workload):
     def cpu_step(self, threads):
         from oracle import numpy_ref as O
 
-        rng = np.random.default_rng(13)
-        x = rng.standard_normal((1, self.C, self.HW, self.HW), dtype=np.float32).astype(BF16)
-        w = (rng.standard_normal((self.OC, self.C, 3, 3), dtype=np.float32) * 0.05).astype(BF16)
+        x, w = self.cpu_inputs()
         O.conv_nd(x, w, padding=1)
         return 2 * self.OC * self.C * 9 * self.HW * self.HW / 1e12, f"1 of {self.B} images per step"
+
+    def cpu_prepare(self):
+        rng = np.random.default_rng(13)
+        x = rng.standard_normal((1, self.C, self.HW, self.HW), dtype=np.float32).astype(BF16)
+        return x, (rng.standard_normal((self.OC, self.C, 3, 3), dtype=np.float32) * 0.05).astype(BF16)
+
+    def parity(self, outs, args):
+        from oracle import numpy_ref as O
+
+        x, w = args
+        return compare(outs["output0"][15:16], O.conv_nd(x[15:16], w, padding=1), 2e-2, "image 15 of 16")
 
     def config(self, world):
         return {"workload": "conv2d bf16 x(16,128,56,56) w(128,128,3,3) padding 1",
                 "l2": "flushed between steps"}
 
 
-WORKLOADS = {w.name: w for w in (Softmax, RmsNorm, Gemm, Bmm, LinAttn, Layer, Decode, TopK, Conv)}
+class EwChain(Workload):
+    """silu(gate) * up over fp32 (16384, 4096): one fused elementwise chain
+    (the SwiGLU activation, examples/models/qwen3_embedding/kernels/ffn.py)."""
+
+    name, metric, unit, bound, dtype, dominant = "ewchain", "HBM GB/s (fused elementwise chain)", "GB/s", "hbm", "f32", "ew"
+    ROWS, COLS = 16384, 4096
+
+    def kernel_and_args(self, rank, world):
+        from nkipy_b200 import workloads as W
+
+        rng = np.random.default_rng(1000 + rank)
+        g = rng.standard_normal((self.ROWS, self.COLS), dtype=np.float32)
+        u = rng.standard_normal((self.ROWS, self.COLS), dtype=np.float32)
+        return W.silu_mul_kernel, (g, u), {}
+
+    def units_per_step(self, world):
+        return 3 * self.ROWS * self.COLS * 4 / 1e9
+
+    def dominant_work(self):
+        return 3 * self.ROWS * self.COLS * 4
+
+    def cpu_prepare(self):
+        rng = np.random.default_rng(14)
+        return tuple(rng.standard_normal((2048, self.COLS), dtype=np.float32) for _ in range(2))
+
+    def cpu_step(self, threads):
+        from nkipy_b200 import workloads as W
+
+        g, u = self.cpu_inputs()
+        _parallel_rows(W.silu_mul_kernel, [g, u], threads)
+        return 3 * g.size * 4 / 1e9, f"{g.shape[0]} of {self.ROWS} rows per step (NumPy direct call)"
+
+    def parity(self, outs, args):
+        from nkipy_b200 import workloads as W
+
+        g, u = args
+        return compare(outs["output0"][:256], W.silu_mul_kernel(g[:256], u[:256]), 1e-5, "rows 0..255")
+
+    def config(self, world):
+        return {"workload": "silu(gate) * up fp32 (16384, 4096)", "shape": [self.ROWS, self.COLS],
+                "l2": "inputs 537 MB exceed L2; also flushed between steps"}
+
+
+class Transpose(Workload):
+    """np.transpose of fp32 (8192, 8192), materialised (core/ops/transform.py:55-79)."""
+
+    name, metric, unit, bound, dtype, dominant = "transpose", "HBM GB/s (materialised transpose)", "GB/s", "hbm", "f32", "transpose_tiles"
+    N = 8192
+
+    def kernel_and_args(self, rank, world):
+        from nkipy_b200 import workloads as W
+
+        x = np.random.default_rng(1100 + rank).standard_normal((self.N, self.N), dtype=np.float32)
+        return W.transpose_kernel, (x,), {}
+
+    def units_per_step(self, world):
+        return 2 * self.N * self.N * 4 / 1e9
+
+    def dominant_work(self):
+        return 2 * self.N * self.N * 4
+
+    def cpu_prepare(self):
+        return (np.random.default_rng(15).standard_normal((2048, self.N), dtype=np.float32),)
+
+    def cpu_step(self, threads):
+        (x,) = self.cpu_inputs()
+        # column blocks of the transposed result, one per thread
+        out = np.empty((x.shape[1], x.shape[0]), np.float32)
+        bounds = np.linspace(0, x.shape[1], threads + 1).astype(int)
+
+        def part(i):
+            out[bounds[i]:bounds[i + 1]] = x[:, bounds[i]:bounds[i + 1]].T
+
+        with concurrent.futures.ThreadPoolExecutor(max_workers=threads) as ex:
+            list(ex.map(part, range(threads)))
+        return 2 * x.size * 4 / 1e9, f"{x.shape[0]} of {self.N} rows per step"
+
+    def parity(self, outs, args):
+        return compare(outs["output0"], np.ascontiguousarray(args[0].T), 0, "whole output", exact=True)
+
+    def config(self, world):
+        return {"workload": "transpose fp32 (8192, 8192) materialised", "shape": [self.N, self.N],
+                "l2": "input 268 MB exceeds L2; also flushed between steps"}
+
+
+WORKLOADS = {w.name: w for w in (Softmax, RmsNorm, Gemm, Bmm, LinAttn, Layer, Decode, TopK, Conv, EwChain, Transpose)}
 DEFAULT_WORKLOAD = "layer"
-SUITE = ("softmax", "rmsnorm", "gemm", "bmm", "linattn", "decode", "topk", "conv")
+SUITE = ("softmax", "rmsnorm", "gemm", "bmm", "linattn", "decode", "topk", "conv", "ewchain", "transpose")
 
 
 def _parallel_rows(fn, arrays, threads):
@@ -461,11 +705,13 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+        # samples go to a private temporary file (NKB_CLOCKS_CSV keeps them at a chosen path)
+        self.keep = os.environ.get("NKB_CLOCKS_CSV")
+        self.path = self.keep or os.path.join(tempfile.mkdtemp(prefix="nkb_clocks_"), f"gpu{gpu_index}.csv")
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            os.makedirs(os.path.dirname(os.path.abspath(self.path)), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
@@ -497,6 +743,8 @@ class ClockSampler:
                 for n, v in zip(names, p[5:9]):
                     if v.lower() == "active":
                         reasons.add(n)
+        if not self.keep:
+            shutil.rmtree(os.path.dirname(self.path), ignore_errors=True)
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
@@ -561,6 +809,40 @@ def profile_traffic(wl):
     return None
 
 
+def _outputs_numpy(kernel, outs):
+    """Every plan output read back to the host (name -> ndarray)."""
+    return {s["name"]: outs[s["name"]].numpy() for s in kernel.model_ref.io["outputs"]}
+
+
+def _roofline(wl, plan_steps, step_ms, ms_per_step, peaks, peak_kind):
+    """Roofline record of the dominant kernel: algorithmic work per launch over its
+    mean CUDA-event launch time (``nkb_time_steps``), against the measured peak.
+    Every kernel here is timed on its own (a 0.06 s timed region of ms-long
+    steps), so GEMMs are set against the burst bf16 figure."""
+    dom = [i for i, st in enumerate(plan_steps) if st["kernel"] == wl.dominant]
+    if wl.dominant == "*step*":
+        # no single dominant launch (the decode step): the whole step's algorithmic
+        # bytes over the device-timed step
+        peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+        achieved = wl.dominant_work() / (ms_per_step / 1e3) / 1e9
+        return {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": None, "peak_source": f"{peak_kind} (hbm_gbs)", "kernel": "whole step",
+                "launch_ms": ms_per_step, "work_per_launch": wl.dominant_work()}
+    if not dom:
+        return None
+    dur = sum(step_ms[i] for i in dom) / len(dom)
+    if wl.bound == "hbm":
+        work = wl.dominant_work()
+        achieved, key, unit = work / (dur / 1e3) / 1e9, "hbm_gbs", "GB/s"
+    else:
+        work = sum(plan_steps[i]["flops"] for i in dom) / len(dom)
+        achieved, key, unit = work / (dur / 1e3) / 1e12, "bf16_tflops", "TFLOP/s"
+    peak = float(peaks.get(key, PEAKS_FALLBACK[key]))
+    return {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+            "traffic": None, "peak_source": f"{peak_kind} ({key})", "kernel": wl.dominant, "launch_ms": dur,
+            "work_per_launch": work}
+
+
 def run_nkb(args, wl, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -591,6 +873,12 @@ def run_nkb(args, wl, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize()
 
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local_rank}")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     # clocks are sampled from the start of warm-up to the end of the e2e region
     sampler = ClockSampler(local_rank)
     sampler.start()
@@ -605,39 +893,58 @@ def run_nkb(args, wl, rank, world, local_rank):
         barrier()
         total_ms += spike.time_execute(kernel.model_ref, in_refs, out_refs, warmup=0, iters=1, use_graph=True)[0]
     barrier()
-    t = torch.tensor([total_ms], dtype=torch.float64, device=f"cuda:{local_rank}")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
+    total_ms = max_over_ranks(total_ms)
     ms_per_step = total_ms / args.steps
 
     # per-launch times for the roofline of the dominant kernel
     step_ms = spike.time_steps(kernel.model_ref, in_refs, out_refs, iters=max(3, min(args.steps, 10)))
     plan_steps = _plan_steps(kernel.plan_path)
 
-    # end to end through the public API, pinned host memory
+    # End to end through the public API, pinned host memory.  Per step the job
+    # uploads every step input once and reads every step output once.  For the
+    # tensor-parallel layer (N > 1) the token rows are split across the ranks:
+    # rank r uploads its 1/N of x's rows, an in-place all-gather over NVLink
+    # gives every rank the whole x, and after the execute rank r reads back its
+    # 1/N of y's rows; whole-job bytes crossing the host boundary are the same
+    # as at N = 1.
     step_names = [n for n in in_names if wl.step_inputs is None or n in wl.step_inputs]
     step_arrays = [a for n, a in zip(in_names, arrays) if n in step_names]
-    pinned_in = [torch.empty(a.nbytes, dtype=torch.uint8, pin_memory=True).numpy() for a in step_arrays]
-    for p, a in zip(pinned_in, step_arrays):
-        p[:] = np.frombuffer(np.ascontiguousarray(a).tobytes(), dtype=np.uint8)
     out_specs = [s for s in kernel.model_ref.io["outputs"] if wl.step_outputs is None or s["name"] in wl.step_outputs]
-    pinned_out = [torch.empty(outs[s["name"]].tensor_ref.size, dtype=torch.uint8, pin_memory=True).numpy() for s in out_specs]
+    split = cc and kernel.model_ref.comm is not None and all(
+        a.nbytes % world == 0 for a in step_arrays) and all(
+        outs[s["name"]].tensor_ref.size % world == 0 for s in out_specs)
+    parts = world if split else 1
+    part = rank if split else 0
+    pinned_in = []
+    for a in step_arrays:
+        n = a.nbytes // parts
+        p = torch.empty(n, dtype=torch.uint8, pin_memory=True).numpy()
+        p[:] = np.ascontiguousarray(a).reshape(-1).view(np.uint8)[part * n : (part + 1) * n]
+        pinned_in.append(p)
+    pinned_out = [torch.empty(outs[s["name"]].tensor_ref.size // parts, dtype=torch.uint8, pin_memory=True).numpy()
+                  for s in out_specs]
     barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         for n, p in zip(step_names, pinned_in):
-            spike.tensor_write_from_pybuffer(ins[n].tensor_ref, p)
+            spike.tensor_write_from_pybuffer(ins[n].tensor_ref, p, offset=part * p.nbytes)
+            if split:
+                spike.all_gather_in_place(kernel.model_ref, ins[n].tensor_ref, p.nbytes)
         spike.execute(kernel.model_ref, in_refs, out_refs, use_graph=True)
         for s, p in zip(out_specs, pinned_out):
-            spike.tensor_read_to_pybuffer(outs[s["name"]].tensor_ref, p)
+            spike.tensor_read_to_pybuffer(outs[s["name"]].tensor_ref, p, offset=part * p.nbytes)
     barrier()
-    e2e_s = time.perf_counter() - t0
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
     clocks = sampler.stop()
-    te = torch.tensor([e2e_s], dtype=torch.float64, device=f"cuda:{local_rank}")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_s = float(te.item())
+
+    # parity of the full-shape run against the oracle (rank 0 checks, the others wait)
+    parity = None
+    if rank == 0 and not args.no_parity:
+        try:
+            parity = wl.parity(_outputs_numpy(kernel, outs), arrays)
+        except Exception as e:  # report, never hide, a failing check
+            parity = {"ok": False, "error": f"{type(e).__name__}: {e}"}
+    barrier()
 
     units = wl.units_per_step(world)
     if wl.scaling == "weak":
@@ -650,38 +957,9 @@ def run_nkb(args, wl, rank, world, local_rank):
     if rank != 0:
         return
     peaks, peak_kind = load_peaks()
-    dom = [i for i, s in enumerate(plan_steps) if s["kernel"] == wl.dominant]
-    roof = None
-    if wl.dominant == "*step*":
-        # no single dominant launch (the decode step): the whole step's algorithmic
-        # bytes over the device-timed step
-        peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
-        achieved = wl.dominant_work() / (ms_per_step / 1e3) / 1e9
-        roof = {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": None, "peak_source": f"{peak_kind} (hbm_gbs)", "kernel": "whole step",
-                "launch_ms": ms_per_step, "work_per_launch": wl.dominant_work()}
-    elif dom:
-        if wl.bound == "hbm":
-            work = wl.dominant_work()
-            dur = sum(step_ms[i] for i in dom) / len(dom)
-            achieved = work / (dur / 1e3) / 1e9
-            peak = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
-            unit = "GB/s"
-        else:
-            flops = [s["flops"] for s in plan_steps]
-            dur = sum(step_ms[i] for i in dom)
-            work = sum(flops[i] for i in dom)
-            achieved = work / (dur / 1e3) / 1e12
-            key = "bf16_tflops" if wl.name != "layer" else "bf16_tflops_sustained"
-            peak = float(peaks.get(key, PEAKS_FALLBACK[key]))
-            unit = "TFLOP/s"
-            work = work / len(dom)
-            dur = dur / len(dom)
-        # the committed ncu summaries are single-GPU captures
-        traffic = profile_traffic(wl) if world == 1 else None
-        roof = {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
-                "traffic": traffic, "peak_source": f"{peak_kind} ({key if wl.bound != 'hbm' else 'hbm_gbs'})",
-                "kernel": wl.dominant, "launch_ms": dur, "work_per_launch": work}
+    roof = _roofline(wl, plan_steps, step_ms, ms_per_step, peaks, peak_kind)
+    if roof is not None and world == 1:
+        roof["traffic"] = profile_traffic(wl)  # the committed ncu summaries are single-GPU captures
 
     cpu = None
     if world == 1 and not args.no_cpu:
@@ -692,6 +970,12 @@ def run_nkb(args, wl, rank, world, local_rank):
     in_bytes = int(sum(a.nbytes for a in step_arrays))
     resident = [n for n in in_names if n not in step_names]
     out_bytes = int(sum(outs[s["name"]].tensor_ref.size for s in out_specs))
+    e2e = {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes}
+    if split:
+        e2e["split"] = (f"whole-job bytes; rank r uploads 1/{world} of the step inputs' rows, all-gathers them "
+                        f"in place over NVLink, and reads back 1/{world} of the output rows")
+    if resident:
+        e2e["resident_bytes"] = int(sum(a.nbytes for n, a in zip(in_names, arrays) if n in resident))
     line = {
         "metric": wl.metric,
         "value": value,
@@ -708,15 +992,12 @@ def run_nkb(args, wl, rank, world, local_rank):
         "config": wl.config(world),
         "roofline": roof,
         "cpu_baseline": cpu,
-        "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes,
-                **({"resident_parameters": resident,
-                    "resident_bytes": int(sum(a.nbytes for n, a in zip(in_names, arrays) if n in resident))}
-                   if resident else {})},
+        "e2e": e2e,
         "gpu_launches": kernel.model_ref.num_launches * args.steps,
-        "launches_per_step": kernel.model_ref.num_launches,
         "clocks": clocks,
-        "per_launch_ms": {f"{i}:{s['kernel']}": round(ms, 4) for i, (s, ms) in enumerate(zip(plan_steps, step_ms))}
-        if len(step_ms) <= 64 else None,
+        "launches_per_step": kernel.model_ref.num_launches,
+        "per_launch_ms": {f"{i}:{st['kernel']}": round(ms, 4) for i, (st, ms) in enumerate(zip(plan_steps, step_ms))}
+        if len(step_ms) <= 24 else None,
     }
     if world == 1 and not args.no_suite:
         suite = {}
@@ -724,15 +1005,18 @@ def run_nkb(args, wl, rank, world, local_rank):
             if name == wl.name:
                 continue
             try:
-                suite[name] = measure_quick(WORKLOADS[name](), 5, 2, local_rank, not args.no_cpu)
+                suite[name] = measure_quick(WORKLOADS[name](), 5, 3, local_rank, not args.no_cpu, not args.no_parity)
             except Exception as e:  # report, never hide, a failing configuration
                 suite[name] = {"error": f"{type(e).__name__}: {e}"}
         line["suite"] = suite
+    # last, so that it stays in view at the end of a long line
+    line["parity"] = parity
     print(json.dumps(line), flush=True)
 
 
-def measure_quick(wl, steps, warmup, local_rank, with_cpu):
-    """Single-GPU measurement of one workload for the suite object (same method, fewer steps)."""
+def measure_quick(wl, steps, warmup, local_rank, with_cpu, with_parity):
+    """Single-GPU measurement of one workload for the suite object (same method,
+    fewer steps); a compact record: value, roofline fraction, CPU baseline, parity."""
     import torch
 
     from nkipy_b200.runtime import DeviceKernel, DeviceTensor
@@ -743,9 +1027,11 @@ def measure_quick(wl, steps, warmup, local_rank, with_cpu):
     kernel = DeviceKernel.compile_and_load(fn, *np_args, name=f"suite_{wl.name}", is_spmd=False, **kwargs)
     names = [t["name"] for t in kernel.model_ref.io["inputs"]]
     arrays = [a for a in np_args if isinstance(a, np.ndarray)]
-    ins = {n: DeviceTensor.from_numpy(a, name=n).tensor_ref for n, a in zip(names, arrays)}
+    dins = {n: DeviceTensor.from_numpy(a, name=n) for n, a in zip(names, arrays)}
+    ins = {n: t.tensor_ref for n, t in dins.items()}
     # a mutated input (``<name>.must_alias_input``) is bound in place as its output
-    outs = {t.name: ins.get(f"{t.name}.must_alias_input", t.tensor_ref) for t in kernel.allocate_output_tensors()}
+    douts = {t.name: dins.get(f"{t.name}.must_alias_input", t) for t in kernel.allocate_output_tensors()}
+    outs = {n: t.tensor_ref for n, t in douts.items()}
     flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=f"cuda:{local_rank}")
     for _ in range(warmup):
         spike.execute(kernel.model_ref, ins, outs, use_graph=True)
@@ -756,38 +1042,28 @@ def measure_quick(wl, steps, warmup, local_rank, with_cpu):
         total += spike.time_execute(kernel.model_ref, ins, outs, warmup=0, iters=1, use_graph=True)[0]
     ms = total / steps
     step_ms = spike.time_steps(kernel.model_ref, ins, outs, iters=3)
-    plan_steps = _plan_steps(kernel.plan_path)
-    peaks, _ = load_peaks()
-    dom = [i for i, st in enumerate(plan_steps) if st["kernel"] == wl.dominant]
-    frac = achieved = None
-    if wl.dominant == "*step*":  # whole-step roofline (no single dominant launch)
-        achieved = wl.dominant_work() / (ms / 1e3) / 1e9
-        frac = achieved / float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
-    elif dom:
-        dur = sum(step_ms[i] for i in dom)
-        if wl.bound == "hbm":
-            achieved = wl.dominant_work() * len(dom) / (dur / 1e3) / 1e9
-            frac = achieved / float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
-        else:
-            achieved = sum(plan_steps[i]["flops"] for i in dom) / (dur / 1e3) / 1e12
-            frac = achieved / float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+    peaks, peak_kind = load_peaks()
+    roof = _roofline(wl, _plan_steps(kernel.plan_path), step_ms, ms, peaks, peak_kind)
     out = {
-        "metric": wl.metric,
-        "value": wl.units_per_step(1) / (ms / 1e3),
+        "value": round(wl.units_per_step(1) / (ms / 1e3), 4),
         "unit": wl.unit,
-        "ms_per_step": ms,
-        "launches_per_step": kernel.model_ref.num_launches,
-        "dominant_kernel": wl.dominant,
-        "dominant_achieved": achieved,
-        "roofline_frac": frac,
-        "bound": wl.bound,
-        "per_launch_ms": {f"{i}:{st['kernel']}": round(t, 4) for i, (st, t) in enumerate(zip(plan_steps, step_ms))}
-        if len(step_ms) <= 24 else None,
+        "ms": round(ms, 4),
+        "launches": kernel.model_ref.num_launches,
+        "frac": round(roof["frac"], 3) if roof else None,
     }
     if with_cpu:
-        cv, desc, _ = cpu_measure(wl, 1, 0, os.cpu_count() or 1)
-        out["cpu_baseline"] = {"value": cv, "unit": wl.unit, "cores": os.cpu_count() or 1, "kind": "port", "sample": desc}
-    del kernel, ins, outs
+        cv, _, _ = cpu_measure(wl, 1, 0, os.cpu_count() or 1)
+        out["cpu"] = float(f"{cv:.4g}")
+    if with_parity:
+        try:
+            par = wl.parity(_outputs_numpy(kernel, douts), arrays)
+            out["parity"] = bool(par["ok"])
+            if par.get("max_rel_err") is not None and par["tol"] != "exact":
+                out["err"] = float(f"{par['max_rel_err']:.3g}")
+        except Exception as e:  # report, never hide, a failing check
+            out["parity"] = False
+            out["err"] = f"{type(e).__name__}: {e}"[:120]
+    del kernel, ins, outs, dins, douts
     return out
 
 
@@ -826,6 +1102,7 @@ def main():
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-suite", action="store_true", help="at N=1, skip measuring the other configurations")
+    ap.add_argument("--no-parity", action="store_true", help="skip the parity check against the oracle")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))

@@ -350,6 +350,23 @@ class Spike:
         if flag.value:
             raise NkbError(7, "a kernel's bounded wait expired; results are invalid")
 
+    def all_gather_in_place(self, model: NkbModel, tensor: NkbTensor, bytes_per_rank: int, offset: int = 0):
+        """All-gather over the model's communicator, in place in ``tensor``:
+        rank r contributes the ``bytes_per_rank`` bytes at ``offset + r *
+        bytes_per_rank`` and every rank ends with all ``world`` blocks (the
+        reference's ``all_gather`` collective, ``core/ops/collectives.py:34-53``,
+        issued outside a plan).  Ordered with the runtime's other work on its
+        stream; bounds-checked against the tensor."""
+        self._live(tensor)
+        if model.comm is None or model.world_size <= 1:
+            return
+        n, world = int(bytes_per_rank), model.world_size
+        if offset < 0 or n < 0 or offset + n * world > tensor.size:
+            raise SpikeError(f"all-gather of {world} x {n} bytes at offset {offset} exceeds tensor of {tensor.size} bytes")
+        base = tensor.va + int(offset)
+        _nkb.call("nkb_comm_all_gather", model.comm, ctypes.c_void_p(base + model.rank_id * n), ctypes.c_void_p(base),
+                  n, 6, None)  # 6: NKB_U8
+
     def time_execute(self, model: NkbModel, inputs, outputs, warmup: int, iters: int, use_graph: bool = True):
         I, ni, O, no = self._io_lists(model, inputs, outputs)
         ms = (ctypes.c_float * iters)()

@@ -177,6 +177,22 @@ def llama_decoder_layer_kernel(
 
 
 # ---------------------------------------------------------------------------
+# elementwise chain and layout move (the memory-bound kernel families of the
+# path on their own)
+# ---------------------------------------------------------------------------
+def silu_mul_kernel(gate, up):
+    """The SwiGLU activation of ``examples/models/qwen3_embedding/kernels/
+    ffn.py:11-46`` on its own: one fused elementwise chain (negate, exp, add,
+    reciprocal, two multiplies) over two inputs."""
+    return silu(gate) * up
+
+
+def transpose_kernel(x):
+    """A materialised 2-D transpose (``core/ops/transform.py:55-79``)."""
+    return np.transpose(x)
+
+
+# ---------------------------------------------------------------------------
 # 6. Qwen3 attention with a KV cache (prefill and one-token decode)
 # ---------------------------------------------------------------------------
 def qk_rmsnorm(x, weight, eps):

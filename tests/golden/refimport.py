@@ -12,10 +12,12 @@ import os
 import sys
 import types
 
-REF_ROOT = os.environ.get("NKIPY_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("NKIPY_REFERENCE_ROOT", "")
 
 
 def import_reference():
+    if not REF_ROOT:
+        raise RuntimeError("set NKIPY_REFERENCE_ROOT to a checkout of shaojiex-aws/nkipy to regenerate the fixtures")
     src = os.path.join(REF_ROOT, "nkipy", "src")
     if not os.path.isdir(src):
         raise RuntimeError(f"reference tree not found under {REF_ROOT}")
