@@ -332,6 +332,14 @@ __device__ __forceinline__ void store_run(void *p, int64_t off, int64_t st, int 
   for (int k = 0; k < VEC; ++k) store_from_reg(p, off + k * st, dt, v[k]);
 }
 
+// Instruction flags of the row-run kernel, set at launch from the program:
+// an operand equal to the previous instruction's destination is read from
+// the accumulator (that result, still in registers); a result is written to
+// the shared-memory register file only when a later instruction reads it
+// from there or it is the output.
+constexpr uint8_t F_A_ACC = 1, F_B_ACC = 2, F_C_ACC = 4, F_KEEP = 8;
+constexpr int kPre = 4;  // inputs whose run is loaded up front, all loads in flight together
+
 template <typename IDX, int VEC>
 __global__ void __launch_bounds__(256) ew_rows_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint32_t sreg[];
@@ -341,6 +349,7 @@ __global__ void __launch_bounds__(256) ew_rows_kernel(const __grid_constant__ Pa
   const IDX inner = (IDX)p.shape[last];
   const IDX runs_per_row = inner / VEC;
   const IDX runs = (IDX)(p.n / VEC);
+  const int n_pre = p.n_in < kPre ? p.n_in : kPre;
   for (IDX c = (IDX)blockIdx.x * blockDim.x + threadIdx.x; c < runs; c += (IDX)gridDim.x * blockDim.x) {
     const IDX row = c / runs_per_row;
     const IDX col = (c - row * runs_per_row) * VEC;
@@ -356,11 +365,26 @@ __global__ void __launch_bounds__(256) ew_rows_kernel(const __grid_constant__ Pa
       oo += (int64_t)id * p.out_strides[d];
       for (int k = 0; k < p.n_in; ++k) base[k] += (int64_t)id * p.in_strides[k][d];
     }
+    // the run of each of the first kPre inputs, loaded before any arithmetic
+    uint32_t pre[kPre][VEC];
+#pragma unroll
+    for (int k = 0; k < kPre; ++k)
+      if (k < n_pre) load_run<VEC>(p.in[k], base[k], p.in_strides[k][last], p.in_dtype[k], pre[k]);
+    uint32_t acc[VEC];
     for (int pc = 0; pc < p.n_instr; ++pc) {
       const Instr I = p.prog[pc];
       uint32_t d[VEC];
       if (I.op == LD) {
-        load_run<VEC>(p.in[I.a], base[I.a], p.in_strides[I.a][last], p.in_dtype[I.a], d);
+        if (I.a < n_pre) {
+#pragma unroll
+          for (int k = 0; k < kPre; ++k)
+            if (I.a == k) {
+#pragma unroll
+              for (int v = 0; v < VEC; ++v) d[v] = pre[k][v];
+            }
+        } else {
+          load_run<VEC>(p.in[I.a], base[I.a], p.in_strides[I.a][last], p.in_dtype[I.a], d);
+        }
       } else if (I.op == IOTA) {
         int64_t id = 0;
         if (I.a == last) {
@@ -378,22 +402,78 @@ __global__ void __launch_bounds__(256) ew_rows_kernel(const __grid_constant__ Pa
         for (int v = 0; v < VEC; ++v) d[v] = (uint32_t)(int32_t)(id + (I.a == last ? v : 0));
       } else {
         uint32_t A[VEC], B[VEC], C[VEC];
+        if (I.pad & F_A_ACC) {
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) {
-          A[v] = R[(I.a * VEC + v) * T];
-          B[v] = I.bimm ? I.imm : R[(I.b * VEC + v) * T];
-          C[v] = R[(I.c * VEC + v) * T];
+          for (int v = 0; v < VEC; ++v) A[v] = acc[v];
+        } else {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) A[v] = R[(I.a * VEC + v) * T];
+        }
+        if (I.bimm) {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) B[v] = I.imm;
+        } else if (I.pad & F_B_ACC) {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) B[v] = acc[v];
+        } else {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) B[v] = R[(I.b * VEC + v) * T];
+        }
+        if (I.op != SEL) {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) C[v] = 0u;
+        } else if (I.pad & F_C_ACC) {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) C[v] = acc[v];
+        } else {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) C[v] = R[(I.c * VEC + v) * T];
         }
         compute<VEC>(I, A, B, C, d);
       }
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) R[(I.dst * VEC + v) * T] = d[v];
+      for (int v = 0; v < VEC; ++v) acc[v] = d[v];
+      if (I.pad & F_KEEP) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) R[(I.dst * VEC + v) * T] = d[v];
+      }
     }
     uint32_t o[VEC];
+    if (p.prog[p.n_instr - 1].dst == p.out_reg) {
 #pragma unroll
-    for (int v = 0; v < VEC; ++v) o[v] = R[(p.out_reg * VEC + v) * T];
+      for (int v = 0; v < VEC; ++v) o[v] = acc[v];
+    } else {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) o[v] = R[(p.out_reg * VEC + v) * T];
+    }
     store_run<VEC>(p.out, oo, p.out_strides[last], p.out_dtype, o);
   }
+}
+
+// Sets the accumulator and keep flags of the row-run kernel (see F_A_ACC).
+void set_row_flags(Params &p) {
+  // the instruction whose result a register holds at each point, for KEEP
+  int def[kRegs];
+  for (int g = 0; g < kRegs; ++g) def[g] = -1;
+  auto reads = [&](int j, int reg, uint8_t acc_flag) {
+    Instr &J = p.prog[j];
+    if (j > 0 && p.prog[j - 1].dst == reg) {
+      J.pad |= acc_flag;
+    } else if (def[reg] >= 0) {
+      p.prog[def[reg]].pad |= F_KEEP;
+    }
+  };
+  for (int j = 0; j < p.n_instr; ++j) {
+    Instr &J = p.prog[j];
+    J.pad = 0;
+    if (J.op != LD && J.op != IOTA && J.op != CF && J.op != CI) {
+      reads(j, J.a, F_A_ACC);
+      if (!J.bimm) reads(j, J.b, F_B_ACC);
+      if (J.op == SEL) reads(j, J.c, F_C_ACC);
+    }
+    def[J.dst] = j;
+  }
+  if (p.prog[p.n_instr - 1].dst != p.out_reg && def[p.out_reg] >= 0) p.prog[def[p.out_reg]].pad |= F_KEEP;
 }
 
 // Step layout ("ew"):
@@ -480,6 +560,7 @@ int launch(const LaunchArgs &a) {
         if (I.op == SEL) nregs = max(nregs, (int)I.c + 1);
       }
     }
+    set_row_flags(p);
     const bool v8 = p.shape[p.rank - 1] % 8 == 0;
     const int vec = v8 ? 8 : 4;
     const size_t smem = (size_t)nregs * vec * threads * 4;

@@ -187,17 +187,19 @@ int gemm_read_and_clear_error(int *flag);
 int linattn_read_and_clear_error(int *flag);
 int nvls_read_and_clear_error(int *flag);
 int fa_read_and_clear_error(int *flag);
+int transpose_read_and_clear_error(int *flag);
 }
 
 extern "C" int nkb_device_error(int *flag) {
   if (int s = ensure_init()) return s;
   if (!flag) return fail(NKB_ERR_INVALID, "flag is NULL");
-  int g = 0, l = 0, n = 0, f = 0;
+  int g = 0, l = 0, n = 0, f = 0, t = 0;
   if (int s = nkb::gemm_read_and_clear_error(&g)) return s;
   if (int s = nkb::linattn_read_and_clear_error(&l)) return s;
   if (int s = nkb::nvls_read_and_clear_error(&n)) return s;
   if (int s = nkb::fa_read_and_clear_error(&f)) return s;
-  *flag = g | l | n | f;
+  if (int s = nkb::transpose_read_and_clear_error(&t)) return s;
+  *flag = g | l | n | f | t;
   return NKB_OK;
 }
 

@@ -199,7 +199,39 @@ class Lowering:
                           strides=tuple(dst.strides[k] for k in keep)),
             )
 
+    def try_transpose(self, src: V.View, dst: V.View) -> bool:
+        """dst = src as one ``transpose_tiles`` launch (TMA-staged tile
+        transpose) when the copy moves the innermost axis: after merging the
+        axes contiguous in both views, the source's unit-stride axis C is not
+        the destination's unit-stride axis R, at most three other axes remain,
+        nothing is broadcast, and every stride and base offset is a multiple of
+        16 bytes (the TMA rules).  Element sizes 2 and 4."""
+        esize = np.dtype(src.dtype).itemsize
+        if esize not in (2, 4) or np.dtype(src.dtype) != np.dtype(dst.dtype) or src.shape != dst.shape:
+            return False
+        if (src.offset * esize) % 16 or (dst.offset * esize) % 16 or src.size < 1024:
+            return False
+        shape, (ds, ss) = V.collapse(src.shape, [dst.strides, src.strides])
+        if len(shape) < 2 or len(shape) > 5 or 0 in ss or 0 in ds:
+            return False
+        r_ax = len(shape) - 1
+        if ds[r_ax] != 1 or ss[r_ax] == 1 or 1 not in ss:
+            return False
+        c_ax = ss.index(1)
+        batch = [i for i in range(len(shape)) if i not in (c_ax, r_ax)]
+        strides = [ss[r_ax], ds[c_ax]] + [s for i in batch for s in (ss[i], ds[i])]
+        if any((s * esize) % 16 for s in strides):
+            return False
+        ints = [esize, int(shape[c_ax]), int(shape[r_ax]), int(ss[r_ax]), int(ds[c_ax]), len(batch)]
+        for i in batch:
+            ints += [int(shape[i]), int(ss[i]), int(ds[i])]
+        self.step("transpose_tiles", [self.bref(src), self.bref(dst)], ints,
+                  note=f"{tuple(src.shape)} {np.dtype(src.dtype).name} axes C={c_ax} R={r_ax}")
+        return True
+
     def emit_ew(self, expr: E.Expr, out: V.View, depth=0):
+        if expr.kind == "leaf" and self.try_transpose(expr.view, out):
+            return
         try:
             c = E.compile_ew(expr, out)
         except E.TooBig:

@@ -101,6 +101,30 @@ def test_elementwise_chain_broadcast():
     assert_close(on_device(k, x, y, z), k(x, y, z), 1e-5)
 
 
+@pytest.mark.parametrize("dtype,shape", [(np.float32, (64, 256)), (np.float32, (3, 5, 96)), (BF16, (40, 512)),
+                                         (np.float32, (7, 13))])
+def test_elementwise_chain_register_reuse(dtype, shape):
+    """Six inputs (four loaded up front, two at their load instruction),
+    values read again several instructions later, a select on a
+    recomputed value, a result that is not the last instruction's; row-run
+    kernel (8- and 4-element runs) and the generic kernel (13 columns)."""
+
+    def k(a, b, c, d, e, f):
+        t = a * b + c
+        u = np.where(t > d, t, e * t)
+        return u - f * a + np.exp(-u) * b, t
+
+    rng = np.random.default_rng(24)
+    args = [rng.standard_normal(shape, dtype=np.float32).astype(dtype) for _ in range(6)]
+    got = on_device(k, *args)
+    want = k(*args)
+    for g, w in zip(got, want):
+        if dtype == BF16:
+            assert_close(g, w, BF16_RTOL)
+        else:
+            assert_close(g, w, FP32_RTOL)
+
+
 def test_argmax_exact():
     def k(x):
         return np.argmax(x, axis=-1)
@@ -369,3 +393,42 @@ def test_convolution(n, x_shape, w_shape, kw, dtype, bias):
         # each output is a dot product over the window: bounded by its terms' magnitudes
         mag = O.conv_nd(np.abs(x), np.abs(w), np.abs(b) if bias else None, **kw)
         assert_close(got, want, FP32_RTOL, atol=FP32_RTOL * mag)
+
+
+# Layout moves whose innermost axis changes run on the TMA tile-transpose
+# kernel (2- and 4-byte elements, 16-byte aligned strides); the others on the
+# elementwise copy.  Bit-exact either way.
+@pytest.mark.parametrize(
+    "shape,perm,dtype",
+    [
+        ((8192, 8192), (1, 0), np.float32),
+        ((8192, 8192), (1, 0), BF16),
+        ((1000, 776), (1, 0), np.float32),  # ragged edges in both axes
+        ((776, 1000), (1, 0), BF16),
+        ((64, 128, 256), (2, 0, 1), np.float32),  # two axes merge into R
+        ((8, 16, 24, 40), (3, 2, 1, 0), np.float32),  # two batch axes, R shorter than a tile
+        ((4, 128, 2000), (0, 2, 1), np.int32),
+        ((2, 3, 4, 32, 64), (2, 1, 0, 4, 3), np.float16),  # three batch axes
+        ((3, 100, 36), (0, 2, 1), BF16),  # 72-byte rows: elementwise copy
+        ((300, 1000), (1, 0), np.int8),  # 1-byte elements: elementwise copy
+    ],
+)
+def test_transpose_layout_move_exact(shape, perm, dtype):
+    from nkipy_b200.runtime import DeviceKernel, DeviceTensor
+
+    rng = np.random.default_rng(23)
+    if np.dtype(dtype).kind in "iu":
+        x = rng.integers(-100, 100, shape).astype(dtype)
+    else:
+        x = rng.standard_normal(shape, dtype=np.float32).astype(dtype)
+
+    def kern(a):
+        return np.transpose(a, perm)
+
+    k = DeviceKernel.compile_and_load(kern, x, name="transpose_test", is_spmd=False)
+    aligned = np.dtype(dtype).itemsize in (2, 4) and shape != (3, 100, 36)
+    assert k.model_ref.io["kernels"] == ({"transpose_tiles": 1} if aligned else {"ew": 1}), k.model_ref.io["kernels"]
+    got = next(iter(k(inputs={"a": DeviceTensor.from_numpy(x, name="a")}).values())).numpy()
+    want = np.ascontiguousarray(np.transpose(x, perm))
+    assert got.shape == want.shape
+    np.testing.assert_array_equal(got.view(np.uint8), want.view(np.uint8))
