@@ -207,10 +207,14 @@ NKB_API int nkb_comm_all_to_all(nkb_comm comm, const void *send, void *recv, siz
  * rejected with NKB_ERR_INVALID.  The function itself calls no cudaMalloc,
  * cudaFree or allocating library routine; its first call on a device looks up
  * the array's device address (cudaGetSymbolAddress), so make that first call
- * before any stream capture.  All calls share the one array: calls that
+ * before any stream capture (the lookup is repeated, once, on a device whose
+ * CUDA context was reset since).  All calls share the one array: calls that
  * overlap on the GPU (different streams, or several host threads) race and
  * must be serialised by the caller.  Each call writes every workspace entry
- * it reads, so the array needs no clearing between calls. */
+ * it reads, so the array needs no clearing between calls.  The return status
+ * covers argument checks and the launch only: the kernel's waits are
+ * bounded, and one that expires is reported afterwards by nkb_device_error()
+ * (read it after synchronising the stream; the output is then invalid). */
 #define NKB_LINATTN_SCRATCH_BYTES (64u << 20)
 NKB_API int nkb_linear_attention_noalloc(const void *q, const void *k, const void *v, void *out, int64_t B, int64_t H,
                                          int64_t T, int64_t D, void *stream);

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -123,6 +124,32 @@ inline int launch_status(const char *what) {
 }
 
 int num_sms(int device);
+
+// Id of the calling thread's current CUDA context (0 when there is none).
+// A context created after a cudaDeviceReset gets a new id, and the kernels'
+// module is loaded into it afresh.
+unsigned long long context_id();
+
+// One-time set-up per (device, CUDA context), e.g. a kernel's
+// cudaFuncSetAttribute: thread-safe, and repeated after the device's context
+// was reset, since the attribute belonged to the module of the old context.
+class ContextOnce {
+ public:
+  template <class F>
+  int run(int device, F &&set) {
+    const unsigned long long id = context_id();
+    if (device < 0 || device >= 64 || id == 0) return set();
+    std::lock_guard<std::mutex> lk(mu_);
+    if (done_[device] == id) return NKB_OK;
+    if (int s = set()) return s;
+    done_[device] = id;
+    return NKB_OK;
+  }
+
+ private:
+  std::mutex mu_;
+  unsigned long long done_[64] = {};
+};
 
 // NCCL all-reduce entry (implemented in the runtime, which owns the dlopen).
 int comm_all_reduce(void *comm, const void *src, void *dst, size_t count, int dtype, cudaStream_t stream);

@@ -264,11 +264,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1) flash_fwd_kernel(const __grid_c
 template <int D>
 int launch_d(const Params &p, cudaStream_t st) {
   const int smem = (BM + 4 * BN) * D * 2;
-  static bool attr = false;
-  if (!attr) {
-    NKB_CUDA_TRY(cudaFuncSetAttribute(flash_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
+  static ContextOnce attr;
+  int dev = 0;
+  NKB_CUDA_TRY(cudaGetDevice(&dev));
+  if (int s = attr.run(dev, [&]() -> int {
+        NKB_CUDA_TRY(cudaFuncSetAttribute(flash_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        return NKB_OK;
+      }))
+    return s;
   dim3 grid((p.Sq + BM - 1) / BM, p.B * p.H);
   flash_fwd_kernel<D><<<grid, WARPS * 32, smem, st>>>(p);
   return launch_status("flash_fwd_kernel");

@@ -305,12 +305,13 @@ int launch(const LaunchArgs &a) {
   p.scale = a.step->floats[0];
   if (p.B == 0) return NKB_OK;
   const unsigned grid = (unsigned)(p.B * p.HKV * p.splits);
-  static bool attr_set[64][4] = {};
+  static ContextOnce attr_set[4];
   auto go = [&](auto kern, int smem, int slot) -> int {
-    if (a.device >= 0 && a.device < 64 && !attr_set[a.device][slot]) {
-      NKB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      attr_set[a.device][slot] = true;
-    }
+    if (int s = attr_set[slot].run(a.device, [&]() -> int {
+          NKB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+          return NKB_OK;
+        }))
+      return s;
     kern<<<grid, THREADS, smem, a.stream>>>(p);
     return NKB_OK;
   };

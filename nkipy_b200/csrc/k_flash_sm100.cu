@@ -364,11 +364,12 @@ int fa_tc_launch(const void *q, const void *k, const void *v, void *o, int B, in
                  int causal, float scale, const int64_t *qst, const int64_t *kst, const int64_t *vst,
                  const int64_t *ost, cudaStream_t st, int device) {
   using namespace fa;
-  static bool attr[64] = {false};
-  if (device >= 0 && device < 64 && !attr[device]) {
-    NKB_CUDA_TRY(cudaFuncSetAttribute(fa_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-    attr[device] = true;
-  }
+  static ContextOnce attr;
+  if (int s = attr.run(device, []() -> int {
+        NKB_CUDA_TRY(cudaFuncSetAttribute(fa_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        return NKB_OK;
+      }))
+    return s;
   CUtensorMap mq, mk, mv, mo;
   if (int s = make_map(&mq, Operand{q, qst[0], qst[1], qst[2]}, B, H, Sq)) return s;
   if (int s = make_map(&mk, Operand{k, kst[0], kst[1], kst[2]}, B, Hkv, Skv)) return s;

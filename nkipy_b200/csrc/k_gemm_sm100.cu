@@ -772,13 +772,15 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   args.tiles_n = (int)((N + (epi == 1 ? BN / 2 : BN) - 1) / (epi == 1 ? BN / 2 : BN));
   const int64_t tiles = (int64_t)args.tiles_m * args.tiles_n * batch;
   if (tiles > INT32_MAX) return fail(NKB_ERR_UNSUPPORTED, "gemm: too many tiles");
-  static bool attr_set[64] = {false};
-  if (device >= 0 && device < 64 && !attr_set[device]) {
-    NKB_CUDA_TRY(
-        cudaFuncSetAttribute(gemm_bf16_tcgen05<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    NKB_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tcgen05<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr_set[device] = true;
-  }
+  static ContextOnce attr_set;
+  if (int s = attr_set.run(device, []() -> int {
+        NKB_CUDA_TRY(
+            cudaFuncSetAttribute(gemm_bf16_tcgen05<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        NKB_CUDA_TRY(
+            cudaFuncSetAttribute(gemm_bf16_tcgen05<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        return NKB_OK;
+      }))
+    return s;
   // one CTA per SM: every CTA of the fused kernel is resident at once, so its
   // all-reduce warps can wait for tiles of other CTAs
   const int grid = (int)std::min<int64_t>(tiles * args.ksplit, num_sms(device));

@@ -7,6 +7,8 @@
 // 4 bytes.
 #include <algorithm>
 
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace nkb {
@@ -184,7 +186,9 @@ int launch(const LaunchArgs &a) {
     int64_t lim = std::max<int64_t>(p.B * p.C * p.in_plane, p.M + VT * 8);
     for (int d = 0; d < p.n; ++d)
       lim = std::max<int64_t>(lim, (p.out[d] + 8) * p.stride[d] + p.ks[d] * p.dil[d] + p.pad[d] + p.in[d]);
-    if (lim < INT32_MAX / 2)
+    // NKB_IM2COL_INDEX64 (any value) takes the 64-bit instantiation at any size:
+    // the switch the tests use to run it on small inputs
+    if (lim < INT32_MAX / 2 && !getenv("NKB_IM2COL_INDEX64"))
       im2col8_kernel<int32_t><<<grid, VT, 0, a.stream>>>(p);
     else
       im2col8_kernel<int64_t><<<grid, VT, 0, a.stream>>>(p);

@@ -486,11 +486,12 @@ size_t workspace_bytes(int BH, int G) { return (size_t)BH * G * (D * D + D) * si
 
 static int run(const Operand &q, const Operand &k, const Operand &v, const Operand &o, float *ws, int B, int H, int T,
                int G, cudaStream_t st, int device) {
-  static bool attr[64] = {false};
-  if (device >= 0 && device < 64 && !attr[device]) {
-    NKB_CUDA_TRY(cudaFuncSetAttribute(linattn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-    attr[device] = true;
-  }
+  static ContextOnce attr;
+  if (int s = attr.run(device, []() -> int {
+        NKB_CUDA_TRY(cudaFuncSetAttribute(linattn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        return NKB_OK;
+      }))
+    return s;
   if (q.ss <= 0 || k.ss <= 0 || v.ss <= 0 || o.ss <= 0)
     return fail(NKB_ERR_UNSUPPORTED, "linattn: token strides must be positive");
   CUtensorMap mq, mk, mv, mo;
@@ -571,20 +572,25 @@ namespace linattn {
 static __device__ __align__(256) unsigned char g_scratch[NKB_LINATTN_SCRATCH_BYTES];
 
 static void *g_scratch_addr[64];
+static unsigned long long g_scratch_ctx[64];
 static std::mutex g_scratch_mu;
 
 // Device address of the fixed workspace on the current device.  In host code
 // `g_scratch` only names a host-side stand-in, so the address is looked up
-// once per device with that device current.
+// once per device with that device current -- and looked up again when the
+// device's CUDA context changed (after a cudaDeviceReset the module, and the
+// array with it, is loaded afresh at another address).
 static int scratch_address(int device, void **out) {
   if (device < 0 || device >= 64) return fail(NKB_ERR_INVALID, "device index out of range");
+  const unsigned long long ctx = context_id();
   std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (!g_scratch_addr[device]) {
+  if (!g_scratch_addr[device] || ctx == 0 || g_scratch_ctx[device] != ctx) {
     void *ptr = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&ptr, g_scratch);
     if (e != cudaSuccess || !ptr)
       return fail(NKB_ERR_CUDA, std::string("cudaGetSymbolAddress(linear-attention scratch): ") + cudaGetErrorString(e));
     g_scratch_addr[device] = ptr;
+    g_scratch_ctx[device] = ctx;
   }
   *out = g_scratch_addr[device];
   return NKB_OK;
@@ -600,7 +606,9 @@ extern "C" int nkb_linear_attention_noalloc(const void *q, const void *k, const 
   if (!q || !k || !v || !out) return fail(NKB_ERR_INVALID, "linear attention: NULL pointer");
   if (D != linattn::D) return fail(NKB_ERR_UNSUPPORTED, "linear attention: head_dim must be 128");
   if (B < 0 || H < 0 || T < 0 || T % 64) return fail(NKB_ERR_UNSUPPORTED, "linear attention: length must be a multiple of 64");
-  if (B * H > (1 << 24) || T > (1 << 30)) return fail(NKB_ERR_INVALID, "linear attention: sizes too large");
+  // each factor bounded before the product is formed (caller-supplied sizes)
+  if (B > (1 << 24) || H > (1 << 24) || B * H > (1 << 24) || T > (1 << 30))
+    return fail(NKB_ERR_INVALID, "linear attention: sizes too large");
   const uintptr_t al = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
                        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out);
   if (al & 15) return fail(NKB_ERR_UNSUPPORTED, "linear attention: pointers must be 16-byte aligned");

@@ -150,12 +150,13 @@ int launch(const LaunchArgs &a) {
       (reinterpret_cast<uintptr_t>(p.C) & 3) || (p.ks > 1 && (reinterpret_cast<uintptr_t>(p.ws) & 7)))
     return fail(NKB_ERR_UNSUPPORTED, "gemm_skinny: operands not aligned for 16-byte copies");
   const int smem = 16 * p.kc * 2 + STAGES * STAGE_BYTES;
-  static bool attr_set[64] = {};
-  if (a.device >= 0 && a.device < 64 && !attr_set[a.device]) {
-    NKB_CUDA_TRY(cudaFuncSetAttribute(skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      16 * MAX_KC * 2 + STAGES * STAGE_BYTES));
-    attr_set[a.device] = true;
-  }
+  static ContextOnce attr_set;
+  if (int s = attr_set.run(a.device, []() -> int {
+        NKB_CUDA_TRY(cudaFuncSetAttribute(skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          16 * MAX_KC * 2 + STAGES * STAGE_BYTES));
+        return NKB_OK;
+      }))
+    return s;
   dim3 grid((unsigned)((p.N + NT - 1) / NT), (unsigned)p.ks);
   skinny_kernel<<<grid, THREADS, smem, a.stream>>>(p);
   if (int e = launch_status("skinny_kernel")) return e;

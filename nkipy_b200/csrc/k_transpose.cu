@@ -277,13 +277,13 @@ int make_map(CUtensorMap *m, const void *base, int E, int rank, const uint64_t *
 template <int E, int RANK>
 int run(const CUtensorMap &mi, const CUtensorMap &mo, const Params &p, int device, cudaStream_t stream) {
   constexpr int SMEM = (STAGES + OUTBUF) * TILES * Geo<E>::TILE_BYTES + 1024;
-  static std::once_flag once[64];
-  static cudaError_t attr_err[64];
-  const int d = device >= 0 && device < 64 ? device : 0;
-  std::call_once(once[d], [&] {
-    attr_err[d] = cudaFuncSetAttribute(transpose_tiles_kernel<E, RANK>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-  });
-  if (attr_err[d] != cudaSuccess) return fail(NKB_ERR_CUDA, std::string("transpose_tiles: ") + cudaGetErrorString(attr_err[d]));
+  static ContextOnce attr;
+  if (int s = attr.run(device, []() -> int {
+        NKB_CUDA_TRY(
+            cudaFuncSetAttribute(transpose_tiles_kernel<E, RANK>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        return NKB_OK;
+      }))
+    return s;
   const int per_sm = (227 * 1024) / SMEM;
   const int64_t grid = std::min<int64_t>(p.n_groups, (int64_t)num_sms(device) * std::max(1, per_sm));
   transpose_tiles_kernel<E, RANK><<<(unsigned)grid, THREADS, SMEM, stream>>>(mi, mo, p);

@@ -8,6 +8,7 @@
 // captured CUDA graph).  NCCL is loaded with dlopen so the library has no
 // link-time dependency on a particular NCCL build.
 
+#include <cuda.h>
 #include <dlfcn.h>
 
 #include <cmath>
@@ -52,6 +53,32 @@ const KernelEntry *find_kernel(const std::string &name) {
   for (const auto &e : registry())
     if (name == e.name) return &e;
   return nullptr;
+}
+
+// Driver entry points resolved through the runtime (libnkb links no driver
+// symbol directly, so it loads on machines without a driver).
+unsigned long long context_id() {
+  using GetCurrent = CUresult (*)(CUcontext *);
+  using GetId = CUresult (*)(CUcontext, unsigned long long *);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
 }
 
 int num_sms(int device) {

@@ -110,7 +110,7 @@ def test_successive_updates_in_place():
     np.testing.assert_array_equal(a_dev, a_cpu)
 
 
-@pytest.mark.parametrize("B,L,nq,nkv", [(2, 320, 16, 2), (3, 200, 8, 8)])
+@pytest.mark.parametrize("B,L,nq,nkv", [(2, 320, 16, 2), (3, 200, 8, 8), (2, 320, 8, 4), (1, 200, 16, 4)])
 def test_decode_attention_at_cache_edges(B, L, nq, nkv):
     """The fused decode attention over random caches at the first position,
     interior positions and the last row of the cache; several key chunks per

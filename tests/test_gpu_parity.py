@@ -372,6 +372,10 @@ def test_greedy_sampling_single_device():
         (2, (3, 3, 17, 13), (5, 3, 4, 2), dict(stride=(2, 1), padding=(1, 3)), np.float32, True),
         (2, (1, 2, 9, 9), (3, 2, 3, 3), dict(stride=1, padding=2, dilation=2), np.float32, False),
         (3, (1, 2, 6, 7, 8), (4, 2, 2, 3, 2), dict(stride=(1, 2, 1), padding=1), np.float32, True),
+        # bf16 with the last output axis a multiple of 8: the 16-byte window kernel
+        (2, (2, 8, 32, 32), (16, 8, 3, 3), dict(stride=2, padding=1), BF16, True),  # stride 2
+        (2, (1, 4, 24, 24), (8, 4, 3, 3), dict(stride=1, padding=2, dilation=2), BF16, False),  # dilation 2
+        (3, (1, 2, 6, 7, 16), (4, 2, 2, 3, 3), dict(stride=(1, 2, 1), padding=1), BF16, True),  # 3-D
     ],
 )
 def test_convolution(n, x_shape, w_shape, kw, dtype, bias):
@@ -432,3 +436,16 @@ def test_transpose_layout_move_exact(shape, perm, dtype):
     want = np.ascontiguousarray(np.transpose(x, perm))
     assert got.shape == want.shape
     np.testing.assert_array_equal(got.view(np.uint8), want.view(np.uint8))
+
+
+def test_convolution_bf16_window_kernel_64bit_indices(monkeypatch):
+    """The 16-byte window kernel's 64-bit index instantiation (taken for very
+    large inputs) on a small case, through its switch NKB_IM2COL_INDEX64."""
+    from nkipy_b200.core import ops as OPS
+
+    monkeypatch.setenv("NKB_IM2COL_INDEX64", "1")
+    rng = np.random.default_rng(25)
+    x = rng.standard_normal((2, 8, 32, 32), dtype=np.float32).astype(BF16)
+    w = (rng.standard_normal((16, 8, 3, 3), dtype=np.float32) * 0.1).astype(BF16)
+    got = on_device(lambda x, w: OPS.conv2d(x, w, stride=2, padding=1), x, w)
+    assert_close(got, O.conv_nd(x, w, None, stride=2, padding=1), BF16_RTOL)

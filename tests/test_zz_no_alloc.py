@@ -1,4 +1,5 @@
-"""The allocation-free linear-attention entry point agrees with the planned path.
+"""The allocation-free linear-attention entry point agrees with the planned path
+(and with the CPU oracle).
 
 ``nkb_linear_attention_noalloc`` exists for callers that cannot allocate device
 memory when they run the kernel (a host whose caching allocator owns the whole
@@ -7,7 +8,8 @@ synchronise the device): the caller passes only inputs and the output, and
 the kernel's workspace is a fixed device array inside libnkb.  This test calls
 it through the C ABI twice in a row on the same buffers and compares each
 result with the existing entry point (the planned kernel run by nkb_execute)
-within the bf16 tolerance of the other GPU tests.
+within the bf16 tolerance of the other GPU tests; the last result is also
+compared with the oracle on one (batch, head) pair.
 """
 
 import ctypes
@@ -53,6 +55,14 @@ def test_noalloc_linear_attention_matches_planned_path():
         got = np.empty_like(q)
         spike.tensor_read_to_pybuffer(out, got)
         assert_close(got, want, BF16_RTOL)
+        flag = ctypes.c_int()
+        _nkb.call("nkb_device_error", ctypes.byref(flag))
+        assert flag.value == 0  # no bounded wait of the kernel expired
+    # and against the CPU oracle (the recurrent form) on one (batch, head) pair
+    from oracle import numpy_ref as O
+
+    sl = (slice(1, 2), slice(3, 4))
+    assert_close(got[sl], O.linear_attention_recurrent(q[sl], k[sl], v[sl]), BF16_RTOL)
 
 
 def test_noalloc_rejects_oversized_workspace():
