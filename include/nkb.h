@@ -114,6 +114,20 @@ NKB_API int nkb_time_steps(nkb_plan plan, const nkb_buf *ins, int n_in, const nk
  * instead of hanging; the CUDA context stays usable). */
 NKB_API int nkb_device_error(int *flag);
 
+/* Budget of every wait on a counter that another rank (or another CTA)
+ * advances -- the fused GEMM + all-reduce's row-block arrivals, the in-switch
+ * all-reduce's barrier -- in microseconds at the GPU's maximum SM clock
+ * (default 1,000,000).  Read by each launch.  No counterpart in the reference,
+ * whose collectives run inside NRT with its own timeouts. */
+NKB_API int nkb_set_wait_limit_us(uint64_t us);
+NKB_API int nkb_get_wait_limit_us(uint64_t *us);
+/* Diagnostics of the bounded wait: one thread polls the device counter
+ * `counter` until it reaches `target` or the wait limit passes; an expired
+ * wait is reported by nkb_device_error() like a kernel's, and the CUDA
+ * context stays usable.  Lets a test drive the expiry path on one GPU with a
+ * counter that nothing advances.  No counterpart in the reference. */
+NKB_API int nkb_wait_probe(const uint32_t *counter, uint32_t target, void *stream);
+
 /* ---- collectives (NrtModel load with nrt_load_collectives(rank, world),
  *      model.cpp:38-52).  NCCL is resolved at run time (dlopen).  The unique
  *      id is NKB_COMM_ID_BYTES bytes, produced on rank 0 and broadcast by the

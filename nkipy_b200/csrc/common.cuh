@@ -125,6 +125,31 @@ inline int launch_status(const char *what) {
 
 int num_sms(int device);
 
+// Budget, in SM clock cycles, of the waits on counters that other ranks or
+// other CTAs advance (the fused GEMM + all-reduce, the in-switch all-reduce
+// barrier): set with nkb_set_wait_limit_us, 1 s by default.  Kernels receive
+// it in their launch arguments.
+long long wait_limit_cycles();
+
+// Polls a counter (sys-scope acquire) until it reaches `target` (wrapping
+// compare); false when `limit` cycles passed or *abort became nonzero first.
+// `sleep_ns` > 0 lets the thread sleep between polls.
+__device__ __forceinline__ bool wait_counter_geq(const uint32_t *p, uint32_t target, long long limit,
+                                                 volatile int *abort, unsigned sleep_ns) {
+  auto value = [p]() {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+  };
+  if ((int)(value() - target) >= 0) return true;
+  const long long t0 = clock64();
+  while ((int)(value() - target) < 0) {
+    if ((abort && *abort) || clock64() - t0 > limit) return false;
+    if (sleep_ns) __nanosleep(sleep_ns);
+  }
+  return true;
+}
+
 // Id of the calling thread's current CUDA context (0 when there is none).
 // A context created after a cudaDeviceReset gets a new id, and the kernels'
 // module is loaded into it afresh.

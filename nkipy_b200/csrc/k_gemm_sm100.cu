@@ -72,6 +72,7 @@ struct Args {
   uint64_t ar_mc_flags;         // the slot through the multicast object
   const __nv_bfloat16 *ar_res;  // optional residual (dense, N columns): C = res + sum
   int ar_rank, ar_world;
+  long long ar_wait;            // budget of each wait on the counts (SM clock cycles)
   // split-K (few output tiles, long K: the decode projections): work unit =
   // (tile, split); split s takes k-blocks [s * kb / ksplit, (s + 1) * kb / ksplit)
   // and stores its fp32 partial rows to ws[s][M][N]; a second kernel sums them
@@ -136,7 +137,6 @@ __device__ __forceinline__ void unit_coords(int t, const Args &a, int k_blocks, 
 }
 
 // ---- fused all-reduce helpers ------------------------------------------------
-constexpr long long AR_WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
   uint32_t v;
@@ -204,14 +204,7 @@ __device__ void ar_comm(const Args &a, int ct, volatile int *abort_flag) {
     // is what keeps eight reductions in flight per thread)
     int ce = c;
     if (lane == 0) {
-      const long long t0 = clock64();
-      while (!ready(c)) {
-        if (*abort_flag || clock64() - t0 > AR_WAIT_CYCLES) {
-          ok = false;
-          break;
-        }
-        __nanosleep(256);
-      }
+      ok = wait_counter_geq(a.ar_flags + c, need, a.ar_wait, abort_flag, 256);
       if (ok)
         for (ce = c + 1; ce < a.tiles_m && ce < c + AR_RUN && ready(ce);) ++ce;
     }
@@ -280,14 +273,7 @@ __device__ void ar_comm(const Args &a, int ct, volatile int *abort_flag) {
       asm volatile("fence.acq_rel.sys;" ::: "memory");
       mc_red_add_release(mc_done, 1);
       const uint32_t target = d0 - d0 % (uint32_t)a.ar_world + (uint32_t)a.ar_world;
-      const long long t0 = clock64();
-      while ((int)(ld_acquire_sys(done) - target) < 0) {
-        if (clock64() - t0 > AR_WAIT_CYCLES) {
-          atomicExch(&g_device_error, 1);
-          break;
-        }
-        __nanosleep(256);
-      }
+      if (!wait_counter_geq(done, target, a.ar_wait, nullptr, 256)) atomicExch(&g_device_error, 1);
     }
   }
 }
@@ -793,6 +779,7 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
     args.ar_res = static_cast<const __nv_bfloat16 *>(ar_res);
     args.ar_rank = ar->rank;
     args.ar_world = ar->world;
+    args.ar_wait = wait_limit_cycles();
     gemm_bf16_tcgen05<true><<<grid, AR_THREADS, SMEM_BYTES, st>>>(ma, mb, args);
   } else {
     gemm_bf16_tcgen05<false><<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, args);

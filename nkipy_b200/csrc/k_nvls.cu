@@ -27,7 +27,6 @@ namespace nkb {
 namespace nvls {
 
 constexpr int MAX_CTAS = 256, MAX_WORLD = 16, THREADS = 512;
-constexpr long long WAIT_CYCLES = 2000000000LL;  // ~1 s at 1.9 GHz
 
 __device__ int g_error = 0;
 
@@ -41,6 +40,7 @@ struct Args {
   uint32_t *epochs;         // [MAX_CTAS] per-CTA launch counters (device memory)
   size_t slice;             // bytes per slice (multiple of 16)
   int rank, world, f32;
+  long long wait;           // budget of each barrier wait (SM clock cycles)
 };
 
 __device__ __forceinline__ uint32_t ld_acquire(const uint32_t *p) {
@@ -81,14 +81,9 @@ __device__ bool barrier(const Args &a, int phase, uint32_t epoch) {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
     const size_t slot = ((size_t)phase * MAX_CTAS + blockIdx.x) * MAX_WORLD;
     st_release(a.peer_flags[t] + slot + a.rank, epoch);
-    const uint32_t *mine = a.flags + slot + t;
-    const long long t0 = clock64();
-    while ((int)(ld_acquire(mine) - epoch) < 0) {
-      if (clock64() - t0 > WAIT_CYCLES) {
-        atomicExch(&g_error, 1);
-        ok = 0;
-        break;
-      }
+    if (!wait_counter_geq(a.flags + slot + t, epoch, a.wait, nullptr, 0)) {
+      atomicExch(&g_error, 1);
+      ok = 0;
     }
   }
   __syncthreads();
@@ -188,6 +183,7 @@ int nvls_all_reduce(void *buf, void *mc_buf, const void *res, void *dst, size_t 
   a.slice = count * dtype_size(dtype) / world;
   a.rank = rank;
   a.world = world;
+  a.wait = wait_limit_cycles();
   a.f32 = dtype == NKB_F32;
   if (res && ((reinterpret_cast<uintptr_t>(res) | reinterpret_cast<uintptr_t>(dst)) & 15))
     return fail(NKB_ERR_UNSUPPORTED, "all-reduce + add: residual and destination must be 16-byte aligned");

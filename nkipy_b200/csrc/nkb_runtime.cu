@@ -215,6 +215,8 @@ int linattn_read_and_clear_error(int *flag);
 int nvls_read_and_clear_error(int *flag);
 int fa_read_and_clear_error(int *flag);
 int transpose_read_and_clear_error(int *flag);
+int waits_read_and_clear_error(int *flag);
+int wait_probe_launch(const uint32_t *counter, uint32_t target, cudaStream_t stream);
 }
 
 extern "C" int nkb_device_error(int *flag) {
@@ -226,8 +228,15 @@ extern "C" int nkb_device_error(int *flag) {
   if (int s = nkb::nvls_read_and_clear_error(&n)) return s;
   if (int s = nkb::fa_read_and_clear_error(&f)) return s;
   if (int s = nkb::transpose_read_and_clear_error(&t)) return s;
-  *flag = g | l | n | f | t;
+  int w = 0;
+  if (int s = nkb::waits_read_and_clear_error(&w)) return s;
+  *flag = g | l | n | f | t | w;
   return NKB_OK;
+}
+
+extern "C" int nkb_wait_probe(const uint32_t *counter, uint32_t target, void *stream) {
+  if (int s = ensure_init()) return s;
+  return nkb::wait_probe_launch(counter, target, stream ? static_cast<cudaStream_t>(stream) : g_rt.stream);
 }
 
 extern "C" int nkb_synchronize(void) {

@@ -82,6 +82,9 @@ def _declare(lib):
         "nkb_synchronize": [],
         "nkb_time_steps": [c_plan, pp, i32, pp, i32, i32, ctypes.POINTER(ctypes.c_float)],
         "nkb_device_error": [ctypes.POINTER(i32)],
+        "nkb_set_wait_limit_us": [ctypes.c_uint64],
+        "nkb_get_wait_limit_us": [ctypes.POINTER(ctypes.c_uint64)],
+        "nkb_wait_probe": [vp, ctypes.c_uint32, vp],
         "nkb_comm_unique_id": [vp],
         "nkb_comm_init": [vp, i32, i32, i32, pp],
         "nkb_comm_free": [c_comm],

@@ -68,3 +68,18 @@ def test_null_arguments_rejected():
     lib = _nkb.lib()
     assert lib.nkb_device_count(None) == 1
     assert lib.nkb_plan_num_io(None, None, None) == 1
+
+
+def test_wait_limit_setting():
+    lib = _nkb.lib()
+    old = ctypes.c_uint64()
+    assert lib.nkb_get_wait_limit_us(ctypes.byref(old)) == 0 and old.value > 0
+    try:
+        assert lib.nkb_set_wait_limit_us(5000) == 0
+        v = ctypes.c_uint64()
+        lib.nkb_get_wait_limit_us(ctypes.byref(v))
+        assert v.value == 5000
+        assert lib.nkb_set_wait_limit_us(0) == 1 and b"positive" in lib.nkb_last_error()
+        assert lib.nkb_get_wait_limit_us(None) == 1
+    finally:
+        lib.nkb_set_wait_limit_us(old.value)
