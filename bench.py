@@ -408,13 +408,14 @@ class Layer(Workload):
     def dominant_work(self):
         return None  # computed from the per-launch table
 
-    def _oracle_prefix(self):
-        """The oracle's layer on the first PREFIX tokens of sequence 0 of the bench input."""
+    def _oracle_prefix(self, seq=0):
+        """The oracle's layer on the first PREFIX tokens of sequence ``seq`` of the bench input."""
         from oracle import numpy_ref as O
 
         full, x = self._full()
         s = self.shape
-        return O.llama_layer(x[:1, : self.PREFIX], full, s.n_heads, s.n_kv_heads, s.head_dim, s.eps, s.theta)
+        return O.llama_layer(x[seq : seq + 1, : self.PREFIX], full, s.n_heads, s.n_kv_heads, s.head_dim, s.eps,
+                             s.theta)
 
     def cpu_prepare(self):
         return self._full()
@@ -425,10 +426,43 @@ class Layer(Workload):
         return self.PREFIX, f"1 x {self.PREFIX} tokens of the layer per step (sequence 0, tokens 0..{self.PREFIX - 1})"
 
     def parity(self, outs, args):
-        # output tokens 0..PREFIX-1 of sequence 0 depend only on its input tokens 0..PREFIX-1 (causal attention)
+        # output tokens 0..PREFIX-1 of a sequence depend only on its input tokens 0..PREFIX-1 (causal
+        # attention); the first and the last sequence (under TP with the e2e row split, the last one's
+        # input reached rank 0 through the all-gather)
         y = outs["output0"]
-        return compare(y[:1, : self.PREFIX], self._oracle_prefix(), 2e-2,
-                       f"sequence 0, tokens 0..{self.PREFIX - 1} (causal prefix) of the full-shape run")
+        last = self.shape.batch - 1
+        a = compare(y[:1, : self.PREFIX], self._oracle_prefix(0), 2e-2, "")
+        b = compare(y[last : last + 1, : self.PREFIX], self._oracle_prefix(last), 2e-2, "")
+        return {"ok": a["ok"] and b["ok"], "max_rel_err": max(a["max_rel_err"], b["max_rel_err"]), "tol": 2e-2,
+                "sample": f"sequences 0 and {last}, tokens 0..{self.PREFIX - 1} (causal prefixes) of the full-shape run"}
+
+    def sampling_parity(self, rank, world):
+        """Vocabulary-parallel greedy sampling (examples/models/qwen3/kernels/sampling.py:113-147) at this
+        world size: top-1 per rank, all-gather of the ranks' maxima and ids, top-1 over the ranks.  Every
+        rank runs it (collectives inside); rank 0 checks the ids."""
+        from nkipy_b200 import workloads as W
+        from nkipy_b200.runtime import DeviceKernel, DeviceTensor
+
+        B, S, H, V = 4, 8, 4096, 32000
+        rng = np.random.default_rng(17)
+        h = rng.standard_normal((B, S, H), dtype=np.float32).astype(BF16)
+        nw = rng.uniform(0.5, 1.5, H).astype(BF16)
+        lm = (rng.standard_normal((H, V), dtype=np.float32) * 0.05).astype(BF16)
+        shard = np.ascontiguousarray(lm[:, rank * (V // world) : (rank + 1) * (V // world)])
+        k = DeviceKernel.compile_and_load(W.greedy_sampling_kernel, h, nw, shard, name="bench_sampling",
+                                          is_spmd=False, cc_enabled=True, rank_id=rank, world_size=world,
+                                          max_batch_size=B, tp_world=world)
+        names = [t["name"] for t in k.model_ref.io["inputs"]]
+        outs = k(inputs={n: DeviceTensor.from_numpy(a, name=n) for n, a in zip(names, (h, nw, shard))})
+        ids = next(iter(outs.values())).numpy().reshape(-1).astype(np.int64)
+        if rank != 0:
+            return None
+        logits = W.qk_rmsnorm(h, nw, 1e-6)[:, -1, :].astype(np.float32) @ lm.astype(np.float32)
+        best = logits.max(axis=1)
+        picked = logits[np.arange(B), np.clip(ids, 0, V - 1)]
+        # the chosen token holds the largest logit up to the bf16 rounding of the device's logits
+        ok = bool(np.all((ids >= 0) & (ids < V)) and np.all(picked >= best - (2.0**-7 * np.abs(best) + 1e-6)))
+        return {"ok": ok, "ids": ids.tolist(), "sample": f"greedy sampling, vocabulary {V} split over {world} ranks"}
 
     def config(self, world):
         s = self.shape
@@ -945,6 +979,13 @@ def run_nkb(args, wl, rank, world, local_rank):
         except Exception as e:  # report, never hide, a failing check
             parity = {"ok": False, "error": f"{type(e).__name__}: {e}"}
     barrier()
+    if cc and not args.no_parity:
+        # the vocabulary-parallel sampling step with its all-gathers, on every rank
+        samp = wl.sampling_parity(rank, world)
+        if rank == 0:
+            parity = dict(parity or {}, sampling=samp)
+            parity["ok"] = bool(parity.get("ok")) and bool(samp and samp.get("ok"))
+        barrier()
 
     units = wl.units_per_step(world)
     if wl.scaling == "weak":
