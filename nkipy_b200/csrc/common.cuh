@@ -40,7 +40,7 @@ inline int dtype_size(int dt) {
     default: return 0;
   }
 }
-inline bool dtype_is_float(int dt) {
+__host__ __device__ inline bool dtype_is_float(int dt) {
   return dt == NKB_F32 || dt == NKB_BF16 || dt == NKB_F16 || dt == NKB_F8E4M3 || dt == NKB_F8E5M2;
 }
 
@@ -58,6 +58,18 @@ __device__ __forceinline__ uint32_t load_as_reg(const void *p, int64_t i, int dt
     case NKB_U8: return static_cast<const uint8_t *>(p)[i];
     case NKB_BOOL: return static_cast<const uint8_t *>(p)[i] ? 1u : 0u;
     default: return 0u;
+  }
+}
+
+// One element of storage type `dt` at p[i] as an fp32 value (integers and
+// bools converted by value: a product of mixed integer and float operands
+// computes in fp32, as the traced dot's result type says).
+__device__ __forceinline__ float load_as_float(const void *p, int64_t i, int dt) {
+  const uint32_t r = load_as_reg(p, i, dt);
+  switch (dt) {
+    case NKB_I32: case NKB_I16: case NKB_I8: return (float)(int32_t)r;
+    case NKB_U32: case NKB_U16: case NKB_U8: case NKB_BOOL: return (float)r;
+    default: return __uint_as_float(r);
   }
 }
 

@@ -815,12 +815,12 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const __grid_constant__ 
       const int mm = i / TK, kk = i % TK;
       const int64_t gm = m0 + mm, gk = k0 + kk;
       As[kk][mm] = (gm < p.M && gk < p.K)
-                       ? __uint_as_float(load_as_reg(p.A, bz * p.sA + gm * p.a_rs + gk * p.a_cs, p.adt))
+                       ? load_as_float(p.A, bz * p.sA + gm * p.a_rs + gk * p.a_cs, p.adt)
                        : 0.f;
       const int nn = i % T, kb = i / T;
       const int64_t gn = n0 + nn, gk2 = k0 + kb;
       Bs[kb][nn] = (gn < p.N && gk2 < p.K)
-                       ? __uint_as_float(load_as_reg(p.B, bz * p.sB + gk2 * p.b_rs + gn * p.b_cs, p.bdt))
+                       ? load_as_float(p.B, bz * p.sB + gk2 * p.b_rs + gn * p.b_cs, p.bdt)
                        : 0.f;
     }
     __syncthreads();
@@ -843,7 +843,9 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const __grid_constant__ 
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int64_t gm = m0 + ty * 4 + i, gn = n0 + tx * 4 + j;
-      if (gm < p.M && gn < p.N) store_from_reg(p.C, bz * p.sC + gm * p.c_rs + gn * p.c_cs, p.cdt, __float_as_uint(acc[i][j]));
+      if (gm < p.M && gn < p.N)
+        store_from_reg(p.C, bz * p.sC + gm * p.c_rs + gn * p.c_cs, p.cdt,
+                       dtype_is_float(p.cdt) ? __float_as_uint(acc[i][j]) : (uint32_t)__float2int_rn(acc[i][j]));
     }
 }
 

@@ -77,3 +77,13 @@ def test_concatenate_exact(axis):
     a = rng.standard_normal((4, 5), dtype=np.float32)
     b = rng.standard_normal((4, 7) if axis == 1 else (3, 5), dtype=np.float32)
     _exact(on_device(lambda x, y: np.concatenate([x, y], axis=axis), a, b), np.concatenate([a, b], axis=axis))
+
+
+def test_integer_matmul_values():
+    """An integer product (int32 @ int32 -> int32) on the CUDA-core GEMM,
+    accumulated in fp32: exact while every partial sum fits 24 bits."""
+    rng = np.random.default_rng(37)
+    a = rng.integers(-20, 20, (33, 70)).astype(np.int32)
+    b = rng.integers(-20, 20, (70, 45)).astype(np.int32)
+    got = on_device(lambda x, y: x @ y, a, b)
+    np.testing.assert_array_equal(np.asarray(got).astype(np.int64), a.astype(np.int64) @ b.astype(np.int64))
