@@ -62,9 +62,6 @@ struct Params {
   int64_t in_off[kMaxIn];
   int64_t in_strides[kMaxIn][kMaxRank];
   Instr prog[kMaxInstr];
-  // row-run kernel: inputs k < kSlots with bit k set are prefetched one run
-  // ahead into shared memory by cp.async; registers of the shared-memory file
-  int pf_mask, n_slots, nregs;
 };
 
 __device__ __forceinline__ float rnd_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
@@ -97,7 +94,9 @@ __device__ __forceinline__ void compute(const Instr I, const uint32_t (&A)[VEC],
       case FREM: LANES SETF(fmodf(FA, FB)); break;
       case FNEG: LANES SETF(-FA); break;
       case FABS: LANES SETF(fabsf(FA)); break;
-      case FEXP: LANES SETF(expf(FA)); break;
+      // exp as ex2.approx of the scaled argument: relative error about |x| * 6e-8 + 2e-7
+      // (below the 1e-5 bar of fp32 elementwise work for every non-overflowing x)
+      case FEXP: LANES SETF(__expf(FA)); break;
       case FLOG: LANES SETF(logf(FA)); break;
       case FSQRT: LANES SETF(sqrtf(FA)); break;
       case FRSQRT: LANES SETF(1.0f / sqrtf(FA)); break;
@@ -109,7 +108,7 @@ __device__ __forceinline__ void compute(const Instr I, const uint32_t (&A)[VEC],
       case FSIGN: LANES SETF(fsignf(FA)); break;
       case RBF: LANES SETF(rnd_bf16(FA)); break;
       case RF16: LANES SETF(rnd_f16(FA)); break;
-      case FRCP: LANES SETF(1.0f / FA); break;
+      case FRCP: LANES SETF(__frcp_rn(FA)); break;  // correctly rounded, as 1.0f / x
       case FEQ: LANES SETI(FA == FB); break;
       case FNE: LANES SETI(FA != FB); break;
       case FLT: LANES SETI(FA < FB); break;
@@ -341,139 +340,38 @@ __device__ __forceinline__ void store_run(void *p, int64_t off, int64_t st, int 
 // the shared-memory register file only when a later instruction reads it
 // from there or it is the output.
 constexpr uint8_t F_A_ACC = 1, F_B_ACC = 2, F_C_ACC = 4, F_KEEP = 8;
-
-// Prefetched inputs.  Each thread copies the runs of its next row-run ahead
-// of time with cp.async (no registers held while the copy is in flight), two
-// stages, and reads back only what it copied itself, so a per-thread
-// cp.async.wait_group is the only synchronisation.  A stage holds, per
-// prefetched input, the run as 16-byte (or 8-byte) chunks laid out
-// [chunk][thread] so that a warp's reads of one chunk are contiguous.
-constexpr int kSlots = 4;  // inputs 0..3 can be prefetched
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async8(uint32_t dst, const void *src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
-// bytes of one prefetched run: VEC fp32 or VEC bf16 elements
-template <int VEC>
-__device__ __forceinline__ int run_bytes(int dt) { return dt == NKB_F32 ? VEC * 4 : VEC * 2; }
-
-// Word offset of chunk j (16 bytes = 4 words) of input slot k in stage st, thread t.
-template <int VEC>
-__device__ __forceinline__ int stage_word(int st, int k, int j, int t, int T, int n_slots) {
-  constexpr int CH = VEC / 4;  // 16-byte chunks of an fp32 run (bf16 runs use half of them)
-  return ((st * n_slots + k) * CH + j) * T * 4 + t * 4;
-}
-
-template <int VEC>
-__device__ __forceinline__ void prefetch_run(uint32_t stage_base, const Params &p, int k, int64_t off, int st, int t,
-                                             int T) {
-  const int dt = p.in_dtype[k];
-  if (dt == NKB_F32) {
-    const float *src = static_cast<const float *>(p.in[k]) + off;
-#pragma unroll
-    for (int j = 0; j < VEC / 4; ++j) cp_async16(stage_base + 4u * stage_word<VEC>(st, k, j, t, T, p.n_slots), src + 4 * j);
-  } else {  // bf16: VEC elements are VEC * 2 bytes
-    const __nv_bfloat16 *src = static_cast<const __nv_bfloat16 *>(p.in[k]) + off;
-    if (VEC == 8)
-      cp_async16(stage_base + 4u * stage_word<VEC>(st, k, 0, t, T, p.n_slots), src);
-    else
-      cp_async8(stage_base + 4u * stage_word<VEC>(st, k, 0, t, T, p.n_slots), src);
-  }
-}
-
-template <int VEC>
-__device__ __forceinline__ void read_prefetched(const uint32_t *S, const Params &p, int k, int st, int t, int T,
-                                                uint32_t (&d)[VEC]) {
-  if (p.in_dtype[k] == NKB_F32) {
-#pragma unroll
-    for (int j = 0; j < VEC / 4; ++j) {
-      const uint4 v = *reinterpret_cast<const uint4 *>(S + stage_word<VEC>(st, k, j, t, T, p.n_slots));
-      d[4 * j] = v.x, d[4 * j + 1] = v.y, d[4 * j + 2] = v.z, d[4 * j + 3] = v.w;
-    }
-  } else if (VEC == 8) {
-    const uint4 v = *reinterpret_cast<const uint4 *>(S + stage_word<VEC>(st, k, 0, t, T, p.n_slots));
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) d[2 * i] = w[i] << 16, d[2 * i + 1] = w[i] & 0xffff0000u;
-  } else {
-    const uint2 v = *reinterpret_cast<const uint2 *>(S + stage_word<VEC>(st, k, 0, t, T, p.n_slots));
-    d[0] = v.x << 16, d[1] = v.x & 0xffff0000u;
-    if (VEC > 2) d[2] = v.y << 16, d[3] = v.y & 0xffff0000u;
-  }
-}
-
-// Element offsets of run c of every input and of the output.
-template <typename IDX, int VEC>
-__device__ __forceinline__ void run_offsets(const Params &p, IDX c, IDX runs_per_row, int64_t *base, int64_t &oo,
-                                            IDX &row, IDX &col) {
-  const int last = p.rank - 1;
-  row = c / runs_per_row;
-  col = (c - row * runs_per_row) * VEC;
-  oo = p.out_off + (int64_t)col * p.out_strides[last];
-  for (int k = 0; k < p.n_in; ++k) base[k] = p.in_off[k] + (int64_t)col * p.in_strides[k][last];
-  IDX rem = row;
-  for (int d = last - 1; d >= 0; --d) {
-    const IDX s = (IDX)p.shape[d];
-    const IDX q = rem / s;
-    const IDX id = rem - q * s;
-    rem = q;
-    oo += (int64_t)id * p.out_strides[d];
-    for (int k = 0; k < p.n_in; ++k) base[k] += (int64_t)id * p.in_strides[k][d];
-  }
-}
-
+constexpr int kPre = 4;  // inputs whose run is loaded up front, all loads in flight together
 
 template <typename IDX, int VEC>
 __global__ void __launch_bounds__(256) ew_rows_kernel(const __grid_constant__ Params p) {
-  extern __shared__ __align__(16) uint32_t sreg[];
-  const int T = blockDim.x, t = threadIdx.x;
-  uint32_t *R = sreg + t;                          // register (g, lane v) at R[(g * VEC + v) * T]
-  const uint32_t *S = sreg + p.nregs * VEC * T;    // prefetch stages
-  const uint32_t stage_base = static_cast<uint32_t>(__cvta_generic_to_shared(S));
+  extern __shared__ uint32_t sreg[];
+  const int T = blockDim.x;
+  uint32_t *R = sreg + threadIdx.x;  // register (g, lane v) at R[(g * VEC + v) * T]
   const int last = p.rank - 1;
-  const IDX runs_per_row = (IDX)p.shape[last] / VEC;
+  const IDX inner = (IDX)p.shape[last];
+  const IDX runs_per_row = inner / VEC;
   const IDX runs = (IDX)(p.n / VEC);
-  const IDX step = (IDX)gridDim.x * blockDim.x;
-  int64_t base[kMaxIn], nbase[kMaxIn];
-  int64_t oo = 0, noo = 0;
-  IDX row = 0, col = 0, nrow = 0, ncol = 0;
-  IDX c = (IDX)blockIdx.x * blockDim.x + t;
-  if (c < runs) {
-    run_offsets<IDX, VEC>(p, c, runs_per_row, nbase, noo, nrow, ncol);
-#pragma unroll
-    for (int k = 0; k < kSlots; ++k)
-      if (p.pf_mask >> k & 1) prefetch_run<VEC>(stage_base, p, k, nbase[k], 0, t, T);
-  }
-  cp_async_commit();
-  for (int it = 0; c < runs; c += step, ++it) {
-    const int st = it & 1;
-    for (int k = 0; k < p.n_in; ++k) base[k] = nbase[k];
-    oo = noo, row = nrow, col = ncol;
-    // the next run's prefetch goes out before this run's arithmetic
-    if (c + step < runs) {
-      run_offsets<IDX, VEC>(p, c + step, runs_per_row, nbase, noo, nrow, ncol);
-#pragma unroll
-      for (int k = 0; k < kSlots; ++k)
-        if (p.pf_mask >> k & 1) prefetch_run<VEC>(stage_base, p, k, nbase[k], st ^ 1, t, T);
+  for (IDX c = (IDX)blockIdx.x * blockDim.x + threadIdx.x; c < runs; c += (IDX)gridDim.x * blockDim.x) {
+    const IDX row = c / runs_per_row;
+    const IDX col = (c - row * runs_per_row) * VEC;
+    int64_t oo = p.out_off + (int64_t)col * p.out_strides[last];
+    int64_t base[kMaxIn];
+    for (int k = 0; k < p.n_in; ++k) base[k] = p.in_off[k] + (int64_t)col * p.in_strides[k][last];
+    IDX rem = row;
+    for (int d = last - 1; d >= 0; --d) {
+      const IDX s = (IDX)p.shape[d];
+      const IDX q = rem / s;
+      const IDX id = rem - q * s;
+      rem = q;
+      oo += (int64_t)id * p.out_strides[d];
+      for (int k = 0; k < p.n_in; ++k) base[k] += (int64_t)id * p.in_strides[k][d];
     }
-    cp_async_commit();
-    cp_async_wait1();  // this run's copies have landed
     uint32_t acc[VEC];
     for (int pc = 0; pc < p.n_instr; ++pc) {
       const Instr I = p.prog[pc];
       uint32_t d[VEC];
       if (I.op == LD) {
-        if (I.a < kSlots && (p.pf_mask >> I.a & 1))
-          read_prefetched<VEC>(S, p, I.a, st, t, T, d);
-        else
-          load_run<VEC>(p.in[I.a], base[I.a], p.in_strides[I.a][last], p.in_dtype[I.a], d);
+        load_run<VEC>(p.in[I.a], base[I.a], p.in_strides[I.a][last], p.in_dtype[I.a], d);
       } else if (I.op == IOTA) {
         int64_t id = 0;
         if (I.a == last) {
@@ -537,7 +435,6 @@ __global__ void __launch_bounds__(256) ew_rows_kernel(const __grid_constant__ Pa
     }
     store_run<VEC>(p.out, oo, p.out_strides[last], p.out_dtype, o);
   }
-  cp_async_wait0();
 }
 
 // Sets the accumulator and keep flags of the row-run kernel (see F_A_ACC).
@@ -653,24 +550,7 @@ int launch(const LaunchArgs &a) {
     set_row_flags(p);
     const bool v8 = p.shape[p.rank - 1] % 8 == 0;
     const int vec = v8 ? 8 : 4;
-    // inputs 0..kSlots-1 read as whole runs (unit inner stride, fp32 or bf16, every
-    // run 16-byte aligned for fp32 and 8-runs of bf16, 8-byte for 4-runs of bf16)
-    // are prefetched by cp.async
-    p.pf_mask = 0;
-    p.n_slots = 0;
-    p.nregs = nregs;
-    for (int k = 0; k < p.n_in && k < kSlots; ++k) {
-      const int dt = p.in_dtype[k];
-      if ((dt != NKB_F32 && dt != NKB_BF16) || p.in_strides[k][p.rank - 1] != 1) continue;
-      const int64_t align = dt == NKB_F32 ? 4 : (v8 ? 8 : 4);  // in elements
-      bool ok = p.in_off[k] % align == 0 && (reinterpret_cast<uintptr_t>(p.in[k]) & 15) == 0;
-      for (int d = 0; d + 1 < p.rank; ++d) ok = ok && p.in_strides[k][d] % align == 0;
-      if (ok) {
-        p.pf_mask |= 1 << k;
-        p.n_slots = k + 1;
-      }
-    }
-    const size_t smem = ((size_t)nregs * vec + (size_t)2 * p.n_slots * vec) * threads * 4;
+    const size_t smem = (size_t)nregs * vec * threads * 4;
     int64_t blocks2 = (p.n / vec + threads - 1) / threads;
     if (blocks2 > cap) blocks2 = cap;
     if (blocks2 < 1) blocks2 = 1;

@@ -21,11 +21,14 @@
 // down-cast at trace time) and 1-byte moves keep the elementwise copy, so the
 // kernel is built for 2- and 4-byte elements.
 //
-// A persistent grid walks groups of 4 tiles (consecutive tiles along R, so
-// each output row receives 512 contiguous bytes), with 4 load stages in
-// flight and two output buffers; one thread issues every copy.  All waits
-// are bounded; on expiry the CTA raises the device error flag, lets copies
-// still in flight land, and returns.  No cluster multicast anywhere.
+// A persistent grid of 256-thread CTAs, each four independent teams of 64
+// threads; team k of CTA b takes tiles 4b + k, 4b + k + 4 * grid, ...
+// (consecutive tiles along R, so the four teams of a CTA fill 512 contiguous
+// bytes of each output row), with 4 load stages in flight and two output
+// buffers of its own, its first thread issuing its copies, and only its own
+// named barrier between them.  All waits are bounded; on expiry the team
+// raises the device error flag, lets copies still in flight land, and
+// returns.  No cluster multicast anywhere.
 #include "sm100.cuh"
 
 namespace nkb {
@@ -37,10 +40,9 @@ constexpr int THREADS = 256, TILES = 4, STAGES = 4, OUTBUF = 2;
 __device__ int g_error = 0;
 
 struct Params {
-  int64_t n_groups;
+  int64_t n_tiles;
   int n_c, n_r;  // tiles along C (the input's contiguous axis) and R (the output's)
   int bdim[3];   // batch extents (1 when absent)
-  int n_tiles_last;  // tiles in the final group (1..4)
 };
 
 template <int E>
@@ -133,90 +135,97 @@ __device__ __forceinline__ void block_transpose(const uint4 *v, uint4 *w) {
   }
 }
 
+// bar.sync over `threads` threads on barrier `id`, returning the AND of `pred`
+__device__ __forceinline__ bool team_and(int id, int threads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(threads)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void team_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Four independent teams of 64 threads per CTA, each a pipeline of its own:
+// STAGES input tiles and OUTBUF output tiles, its leader (first thread)
+// issuing its copies; a team synchronises on its own named barrier only.
 template <int E, int RANK>
 __global__ void __launch_bounds__(THREADS) transpose_tiles_kernel(const __grid_constant__ CUtensorMap min,
                                                                   const __grid_constant__ CUtensorMap mout,
                                                                   const __grid_constant__ Params p) {
   using G = Geo<E>;
-  constexpr int GROUP_BYTES = TILES * G::TILE_BYTES;
+  constexpr int TEAM = THREADS / TILES;  // 64 threads: one 16-byte block of the tile each
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *in_buf = smem;                              // [STAGES][TILES][TILE_BYTES]
-  uint8_t *out_buf = smem + STAGES * GROUP_BYTES;      // [OUTBUF][TILES][TILE_BYTES]
-  __shared__ __align__(8) uint64_t full[STAGES];
-  __shared__ int abort_flag;
+  __shared__ __align__(8) uint64_t full[TILES][STAGES];
+  __shared__ int abort_flag[TILES];
 
-  const int tid = threadIdx.x;
-  const int64_t first = blockIdx.x, step = gridDim.x;
-  if (tid == 0) {
-    prefetch_map(&min);
-    prefetch_map(&mout);
-    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
-    abort_flag = 0;
+  const int tid = threadIdx.x, team = tid / TEAM, unit = tid % TEAM;
+  const bool leader = unit == 0;
+  uint8_t *in_buf = smem + team * (STAGES + OUTBUF) * G::TILE_BYTES;  // [STAGES][TILE_BYTES]
+  uint8_t *out_buf = in_buf + STAGES * G::TILE_BYTES;                 // [OUTBUF][TILE_BYTES]
+  const int64_t first = (int64_t)blockIdx.x * TILES + team, step = (int64_t)gridDim.x * TILES;
+  if (leader) {
+    if (team == 0) {
+      prefetch_map(&min);
+      prefetch_map(&mout);
+    }
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[team][s], 1);
+    abort_flag[team] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  auto tiles_in = [&](int64_t g) { return g == p.n_groups - 1 ? p.n_tiles_last : TILES; };
-  auto issue_load = [&](int64_t g, int s) {
-    const int n = tiles_in(g);
-    mbar_expect_tx(&full[s], (uint32_t)(n * G::TILE_BYTES));
-    for (int i = 0; i < n; ++i) {
-      int ic[5], oc[5];
-      tile_coords(p, g * TILES + i, G::T, ic, oc);
-      tma_load<RANK>(in_buf + (s * TILES + i) * G::TILE_BYTES, &min, &full[s], ic);
-    }
+  auto issue_load = [&](int64_t t, int s) {
+    int ic[5], oc[5];
+    tile_coords(p, t, G::T, ic, oc);
+    mbar_expect_tx(&full[team][s], (uint32_t)G::TILE_BYTES);
+    tma_load<RANK>(in_buf + s * G::TILE_BYTES, &min, &full[team][s], ic);
   };
-  if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      const int64_t g = first + s * step;
-      if (g < p.n_groups) issue_load(g, s);
-    }
-  }
+  if (leader)
+    for (int s = 0; s < STAGES; ++s)
+      if (first + s * step < p.n_tiles) issue_load(first + s * step, s);
 
-  // this thread's V x V block of its tile
-  const int tile = tid >> 6, unit = tid & 63;
+  // this thread's V x V block of the tile
   const int rb = unit & 7, c = (unit & 7) ^ (unit >> 3);
   int it = 0;
-  for (int64_t g = first; g < p.n_groups; g += step, ++it) {
+  for (int64_t t = first; t < p.n_tiles; t += step, ++it) {
     const int s = it % STAGES, ob = it % OUTBUF;
-    const int n = tiles_in(g);
-    bool ok = mbar_wait(&full[s], (it / STAGES) & 1, &abort_flag, &g_error);
-    if (tid == 0) bulk_wait_read<OUTBUF - 1>();  // the store that last read out_buf[ob] is done with it
-    // one decision for the whole CTA, so that every thread meets the same barriers
-    if (!__syncthreads_and(ok)) break;
-    if (tile < n) {
-      const uint8_t *src = in_buf + (s * TILES + tile) * G::TILE_BYTES;
-      uint8_t *dst = out_buf + (ob * TILES + tile) * G::TILE_BYTES;
-      uint4 v[G::V], w[G::V];
+    bool ok = mbar_wait(&full[team][s], (it / STAGES) & 1, &abort_flag[team], &g_error);
+    if (leader) bulk_wait_read<OUTBUF - 1>();  // the store that last read out_buf[ob] is done with it
+    // one decision for the whole team, so that its threads meet the same barriers
+    if (!team_and(1 + team, TEAM, ok)) break;
+    const uint8_t *src = in_buf + s * G::TILE_BYTES;
+    uint8_t *dst = out_buf + ob * G::TILE_BYTES;
+    uint4 v[G::V], w[G::V];
 #pragma unroll
-      for (int q = 0; q < G::V; ++q) {
-        const int row = G::V * rb + q;
-        v[q] = *reinterpret_cast<const uint4 *>(src + row * 128 + ((c ^ (row & 7)) << 4));
-      }
-      block_transpose<E>(v, w);
-#pragma unroll
-      for (int e = 0; e < G::V; ++e) {
-        const int row = G::V * c + e;
-        *reinterpret_cast<uint4 *>(dst + row * 128 + ((rb ^ (row & 7)) << 4)) = w[e];
-      }
-      fence_proxy_async_smem();
+    for (int q = 0; q < G::V; ++q) {
+      const int row = G::V * rb + q;
+      v[q] = *reinterpret_cast<const uint4 *>(src + row * 128 + ((c ^ (row & 7)) << 4));
     }
-    __syncthreads();
-    if (tid == 0) {
-      for (int i = 0; i < n; ++i) {
-        int ic[5], oc[5];
-        tile_coords(p, g * TILES + i, G::T, ic, oc);
-        tma_store<RANK>(&mout, out_buf + (ob * TILES + i) * G::TILE_BYTES, oc);
-      }
+    block_transpose<E>(v, w);
+#pragma unroll
+    for (int e = 0; e < G::V; ++e) {
+      const int row = G::V * c + e;
+      *reinterpret_cast<uint4 *>(dst + row * 128 + ((rb ^ (row & 7)) << 4)) = w[e];
+    }
+    fence_proxy_async_smem();
+    team_sync(1 + team, TEAM);
+    if (leader) {
+      int ic[5], oc[5];
+      tile_coords(p, t, G::T, ic, oc);
+      tma_store<RANK>(&mout, dst, oc);
       bulk_commit();
-      const int64_t next = g + STAGES * step;  // every thread has read stage s: refill it
-      if (next < p.n_groups) issue_load(next, s);
+      const int64_t next = t + STAGES * step;  // every thread of the team has read stage s: refill it
+      if (next < p.n_tiles) issue_load(next, s);
     }
   }
-  if (tid == 0) {
+  if (leader) {
     bulk_wait<0>();
-    if (abort_flag) {
+    if (abort_flag[team]) {
       // bounded drain of loads that may still be landing in shared memory
       const long long t0 = clock64();
       while (clock64() - t0 < 2000000) {
@@ -276,7 +285,7 @@ int make_map(CUtensorMap *m, const void *base, int E, int rank, const uint64_t *
 
 template <int E, int RANK>
 int run(const CUtensorMap &mi, const CUtensorMap &mo, const Params &p, int device, cudaStream_t stream) {
-  constexpr int SMEM = (STAGES + OUTBUF) * TILES * Geo<E>::TILE_BYTES + 1024;
+  constexpr int SMEM = (STAGES + OUTBUF) * TILES * Geo<E>::TILE_BYTES + 1024;  // four teams
   static ContextOnce attr;
   if (int s = attr.run(device, []() -> int {
         NKB_CUDA_TRY(
@@ -285,7 +294,8 @@ int run(const CUtensorMap &mi, const CUtensorMap &mo, const Params &p, int devic
       }))
     return s;
   const int per_sm = (227 * 1024) / SMEM;
-  const int64_t grid = std::min<int64_t>(p.n_groups, (int64_t)num_sms(device) * std::max(1, per_sm));
+  const int64_t grid =
+      std::min<int64_t>((p.n_tiles + TILES - 1) / TILES, (int64_t)num_sms(device) * std::max(1, per_sm));
   transpose_tiles_kernel<E, RANK><<<(unsigned)grid, THREADS, SMEM, stream>>>(mi, mo, p);
   return launch_status("transpose_tiles_kernel");
 }
@@ -321,8 +331,7 @@ int launch(const LaunchArgs &a) {
   p.n_r = (int)((R + T - 1) / T);
   const int64_t n_tiles = (int64_t)p.n_c * p.n_r * nbatch;
   if (!n_tiles) return NKB_OK;
-  p.n_groups = (n_tiles + TILES - 1) / TILES;
-  p.n_tiles_last = (int)(n_tiles - (p.n_groups - 1) * TILES);
+  p.n_tiles = n_tiles;
   CUtensorMap mi, mo;
   if (int s = make_map(&mi, a.ptrs[0], E, rank, din, sin)) return s;
   if (int s = make_map(&mo, a.ptrs[1], E, rank, dout, sout)) return s;

@@ -412,6 +412,16 @@ def compile_ew(expr: Expr, out: V.View) -> CompiledEw:
             prog.emit("IOR", r, a, a)  # register move
             done(args[0])
             return r
+        if (name == "divide" and len(args) == 2 and k == "F" and args[0].kind == "const"
+                and kind(args[1].dtype) == "F" and np.float32(args[0].value) == np.float32(1.0)):
+            # 1 / x: the correctly rounded reciprocal, the same value as the division
+            a = value(args[1])
+            r = prog.alloc()
+            prog.emit("FRCP", r, a)
+            _round_float(prog, r, e.dtype)
+            for x in e.args:
+                done(x)
+            return r
         imm_b = None
         if name in ELEMENTWISE_BINARY and len(args) == 2:
             if args[1].kind != "const" and args[0].kind == "const" and name in ("add", "multiply", "maximum", "minimum", "and", "or", "xor"):
