@@ -32,6 +32,8 @@
 // on expiry the CTA raises a device error flag, stops issuing work, waits
 // (bounded) for its in-flight copies, frees its TMEM and exits.
 
+#include <cstdlib>
+
 #include "sm100.cuh"
 
 namespace nkb {
@@ -52,6 +54,7 @@ struct Args {
   int c_f32, a_mn_major, b_k_major;
   int a_bcast, b_bcast;  // batch stride 0: every batch reads operand batch 0
   int tiles_m, tiles_n;
+  int tiles_m2;  // 256-row tiles (CTA pairs)
   // epi == 1 (SwiGLU): B holds [gate | up] halves of width n_half; a CTA
   // computes 128 gate + the matching 128 up columns and writes
   // silu(gate) * up (N = n_half output columns).
@@ -98,7 +101,9 @@ __host__ __device__ constexpr uint32_t make_idesc(int a_mn_major, int b_mn_major
   return idesc_bf16(BM, BN, a_mn_major, b_mn_major);
 }
 
-template <bool AR>
+// Tile t -> (row tile, column tile, batch); row tiles are 128 rows, or 256
+// for a CTA pair (PAIR).
+template <bool AR, bool PAIR>
 __device__ __forceinline__ void tile_coords(int t, const Args &a, int &bm, int &bn, int &bb) {
   if (AR) {  // row block by row block, so blocks complete (and are reduced) in order
     bb = 0;
@@ -106,22 +111,23 @@ __device__ __forceinline__ void tile_coords(int t, const Args &a, int &bm, int &
     bn = t - bm * a.tiles_n;
     return;
   }
-  const int per_batch = a.tiles_m * a.tiles_n;
+  const int tm = PAIR ? a.tiles_m2 : a.tiles_m;
+  const int per_batch = tm * a.tiles_n;
   bb = t / per_batch;
   int r = t - bb * per_batch;
-  // group 16 M-tiles together so a wave of CTAs shares B column panels in L2
-  constexpr int GROUP = 16;
+  // group 2048 rows of tiles together so a wave of CTAs shares B column panels in L2
+  constexpr int GROUP = PAIR ? 8 : 16;
   const int group_span = GROUP * a.tiles_n;
   const int g = r / group_span;
   const int first_m = g * GROUP;
-  const int gsize = min(a.tiles_m - first_m, GROUP);
+  const int gsize = min(tm - first_m, GROUP);
   const int within = r - g * group_span;
   bm = first_m + within % gsize;
   bn = within / gsize;
 }
 
 // Work unit t -> tile coordinates and its range of k-blocks.
-template <bool AR>
+template <bool AR, bool PAIR>
 __device__ __forceinline__ void unit_coords(int t, const Args &a, int k_blocks, int &bm, int &bn, int &bb, int &split,
                                             int &kb0, int &kb1) {
   split = 0;
@@ -130,7 +136,7 @@ __device__ __forceinline__ void unit_coords(int t, const Args &a, int k_blocks, 
     split = t / per_split;
     t -= split * per_split;
   }
-  tile_coords<AR>(t, a, bm, bn, bb);
+  tile_coords<AR, PAIR>(t, a, bm, bn, bb);
   const int ks = AR ? 1 : max(1, a.ksplit);
   kb0 = (int)((int64_t)split * k_blocks / ks);
   kb1 = (int)((int64_t)(split + 1) * k_blocks / ks);
@@ -278,33 +284,49 @@ __device__ void ar_comm(const Args &a, int ct, volatile int *abort_flag) {
   }
 }
 
-template <bool AR>
+// PAIR: a cluster of two CTAs computes 256 x 256 tiles with
+// tcgen05.mma.cta_group::2 (M = 256): each CTA loads its own 128 rows of A
+// and its own 128 columns of B (plain TMA loads, no multicast) and keeps its
+// 128 rows of the accumulator in its own TMEM.  Both CTAs' loads complete on
+// the leader's (rank 0) stage barriers; the leader's single MMA thread issues
+// the products and signals stage release and accumulator completion to both
+// CTAs (tcgen05.commit multicast); both epilogues report a drained
+// accumulator to the leader.  Per SM this moves 32 KB through shared memory
+// per 64-deep k-block instead of 48 KB for the same flops.
+template <bool AR, bool PAIR>
 __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Args args) {
+  constexpr int NST = PAIR ? 6 : STAGES;                             // stages of the load ring
+  constexpr int B_BYTES = PAIR ? (BN / 2) * BK * 2 : B_STAGE_BYTES;  // this CTA's B per stage
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *sA = smem;
-  uint8_t *sB = smem + STAGES * A_STAGE_BYTES;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + STAGES * B_STAGE_BYTES);
-  uint64_t *full = bars;                  // [STAGES]
-  uint64_t *empty = bars + STAGES;        // [STAGES]
-  uint64_t *acc_full = bars + 2 * STAGES;   // [2]
-  uint64_t *acc_empty = bars + 2 * STAGES + 2;  // [2]
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+  uint8_t *sB = smem + NST * A_STAGE_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + NST * B_BYTES);
+  uint64_t *full = bars;                  // [NST]
+  uint64_t *empty = bars + NST;           // [NST]
+  uint64_t *acc_full = bars + 2 * NST;      // [2]
+  uint64_t *acc_empty = bars + 2 * NST + 2;  // [2]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * NST + 4);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int num_tiles = args.tiles_m * args.tiles_n * (int)args.batch * (AR ? 1 : max(1, args.ksplit));
+  const uint32_t rank = PAIR ? cluster_rank() : 0;  // 0: the leader of the pair
+  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // first tile of this CTA (pair)
+  const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int num_tiles =
+      (PAIR ? args.tiles_m2 : args.tiles_m) * args.tiles_n * (int)args.batch * (AR ? 1 : max(1, args.ksplit));
   const int k_blocks = (int)((args.K + BK - 1) / BK);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
+      // drained by the 128 epilogue threads, or by the 4 + 4 epilogue warps of a pair
+      mbar_init(&acc_empty[i], PAIR ? 8 : 128);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -312,21 +334,61 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
     prefetch_map(&map_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
+    if (PAIR)
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    else
+      tmem_alloc(tmem_slot, TMEM_COLS);
   }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync();  // the leader's barriers exist before the peer signals them
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the leader's stage and accumulator-drained barriers, as seen from this CTA
+  const uint32_t full_leader = PAIR ? map_to_rank(smem_u32(full), 0) : 0;
+  const uint32_t acc_empty_leader = PAIR ? map_to_rank(smem_u32(acc_empty), 0) : 0;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = unit0; t < num_tiles && ok; t += units) {
         int bm, bn, bb, split, kb0, kb1;
-        unit_coords<AR>(t, args, k_blocks, bm, bn, bb, split, kb0, kb1);
+        unit_coords<AR, PAIR>(t, args, k_blocks, bm, bn, bb, split, kb0, kb1);
+        if (PAIR) {
+          const int row0 = (bm * 2 + (int)rank) * BM;
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            const int s = it % NST;
+            const uint32_t ph = (it / NST) & 1;
+            if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            // the leader expects both CTAs' bytes; the peer's may land first
+            if (rank == 0) mbar_expect_tx(&full[s], 2 * (A_STAGE_BYTES + B_BYTES));
+            const uint32_t fb = full_leader + 8u * s;
+            uint8_t *a_dst = sA + s * A_STAGE_BYTES;
+            uint8_t *b_dst = sB + s * B_BYTES;
+            if (!args.a_mn_major) {
+              tma_load_3d_pair(a_dst, &map_a, fb, kb * BK, row0, args.a_bcast ? 0 : bb);
+            } else {
+              for (int j = 0; j < BM / 64; ++j)
+                tma_load_3d_pair(a_dst + j * (64 * BK * 2), &map_a, fb, row0 + j * 64, kb * BK, args.a_bcast ? 0 : bb);
+            }
+            if (args.b_k_major) {
+              tma_load_3d_pair(b_dst, &map_b, fb, kb * BK, bn * BN + (int)rank * (BN / 2), args.b_bcast ? 0 : bb);
+            } else {
+              // SwiGLU: the leader holds the 128 gate columns, the peer the matching 128 up columns
+              const int c0 = args.epi == 1 ? (int)rank * (int)args.n_half + bn * (BN / 2) : bn * BN + (int)rank * (BN / 2);
+              for (int j = 0; j < BN / 128; ++j)
+                tma_load_3d_pair(b_dst + j * (64 * BK * 2), &map_b, fb, c0 + j * 64, kb * BK, args.b_bcast ? 0 : bb);
+            }
+          }
+          continue;
+        }
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -360,7 +422,43 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    if (PAIR && lane == 0 && rank == 0) {
+      // the leader issues the pair's products: M = 256 (128 rows in each CTA), N = 256
+      const uint32_t idesc = idesc_bf16(2 * BM, BN, args.a_mn_major, args.b_k_major ? 0 : 1);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int t = unit0; t < num_tiles && ok; t += units, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_ph = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        int bm, bn, bb, split, kb0, kb1;
+        unit_coords<AR, PAIR>(t, args, k_blocks, bm, bn, bb, split, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % NST;
+          const uint32_t ph = (it / NST) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * A_STAGE_BYTES);
+          const uint32_t b_addr = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t da = args.a_mn_major ? smem_desc(a_addr + k * 2048, 64 * BK * 2, 1024)
+                                                : smem_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t db = args.b_k_major ? smem_desc(b_addr + k * 32, 16, 1024)
+                                               : smem_desc(b_addr + k * 2048, 64 * BK * 2, 1024);
+            umma_f16_pair(d_tmem, da, db, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[s]);  // stage s free in both CTAs once these MMAs have read it
+        }
+        if (!ok) break;
+        umma_commit_pair(&acc_full[acc]);  // both CTAs' accumulator rows ready
+      }
+    } else if (!PAIR && lane == 0) {
       const uint32_t idesc = make_idesc(args.a_mn_major, args.b_k_major ? 0 : 1);
       int it = 0, local = 0;
       bool ok = true;
@@ -371,7 +469,7 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         int bm, bn, bb, split, kb0, kb1;
-        unit_coords<AR>(t, args, k_blocks, bm, bn, bb, split, kb0, kb1);
+        unit_coords<AR, PAIR>(t, args, k_blocks, bm, bn, bb, split, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -405,17 +503,28 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
     // ---------------- epilogue (warps 2..5) ----------------
     const int quad = warp % 4;  // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
+    // the accumulator has been read: every thread (one CTA), or each warp once (pair, at the leader)
+    auto drained = [&](int acc) {
+      tc_fence_before();
+      if (PAIR) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc_empty_leader + 8u * acc);
+      } else {
+        mbar_arrive(&acc_empty[acc]);
+      }
+    };
     int local = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    for (int t = unit0; t < num_tiles; t += units, ++local) {
       int bm, bn, bb, split, kb0, kb1;
-      unit_coords<AR>(t, args, k_blocks, bm, bn, bb, split, kb0, kb1);
+      unit_coords<AR, PAIR>(t, args, k_blocks, bm, bn, bb, split, kb0, kb1);
       const int acc = local & 1;
       const uint32_t acc_ph = (local >> 1) & 1;
       bool got = mbar_wait(&acc_full[acc], acc_ph, abort_flag);
       if (AR) got = named_bar_and(1, 128, got);  // the four warps leave together
       if (!got) break;
       tc_fence_after();
-      const int64_t row = (int64_t)bm * BM + row_in_tile;
+      const int bm_own = PAIR ? bm * 2 + (int)rank : bm;  // this CTA's 128-row block
+      const int64_t row = (int64_t)bm_own * BM + row_in_tile;
       const bool row_ok = row < args.M;
       if (args.epi == 1) {
         const int64_t col0 = (int64_t)bn * (BN / 2);
@@ -454,8 +563,7 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
               dst[j] = reinterpret_cast<__nv_bfloat16 *>(packed)[j];
           }
         }
-        tc_fence_before();
-        mbar_arrive(&acc_empty[acc]);
+        drained(acc);
         continue;
       }
       const int64_t col0 = (int64_t)bn * BN;
@@ -523,8 +631,7 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
             }
           }
         }
-        tc_fence_before();
-        mbar_arrive(&acc_empty[acc]);
+        drained(acc);
         continue;
       }
       for (int c = 0; c < BN / 32; ++c) {
@@ -593,13 +700,12 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
+      drained(acc);
       if (AR) {
         named_bar(1, 128);  // the tile is stored by all four warps
         if (warp == 2 && lane == 0) {
           asm volatile("fence.acq_rel.sys;" ::: "memory");
-          mc_red_add_release(args.ar_mc_flags + 4ull * bm, 1);
+          mc_red_add_release(args.ar_mc_flags + 4ull * bm_own, 1);
         }
       }
     }
@@ -607,18 +713,27 @@ __global__ void __launch_bounds__(AR ? AR_THREADS : THREADS, 1)
 
   // teardown: every role has left its loop (normally or after an abort)
   tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync();  // neither CTA of the pair still signals the other's barriers
+  else
+    __syncthreads();
   if (*abort_flag && warp == 0 && lane == 0) {
     // bounded drain of copies that may still be landing in shared memory
     const long long t0 = clock64();
     while (clock64() - t0 < 2000000) {
     }
   }
-  __syncthreads();
+  if (PAIR)
+    cluster_sync();
+  else
+    __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -707,7 +822,11 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   if (epi == 1 && (b_k_major || c_f32 || n_half % 64 || N != n_half))
     return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: SwiGLU epilogue needs N-major B, bf16 output and n_half % 64 == 0");
   const int64_t bcols = epi == 1 ? 2 * n_half : N;
-  if (b_k_major) s = make_map(&mb, B, K, bcols, bb, ldb, sB, BK, BN);
+  // CTA pairs (256 x 256 tiles) for products with more than one row tile and no
+  // split or fused all-reduce; NKB_GEMM_PAIR=0 keeps single CTAs (comparisons)
+  const char *pe = getenv("NKB_GEMM_PAIR");
+  const bool pair = ksplit <= 1 && !ar && M > BM && !(pe && pe[0] == '0');
+  if (b_k_major) s = make_map(&mb, B, K, bcols, bb, ldb, sB, BK, pair ? BN / 2 : BN);
   else s = make_map(&mb, B, bcols, K, bb, ldb, sB, 64, BK);
   if (s) return s;
   Args args;
@@ -755,15 +874,18 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
     args.rope_seq = rope->rope_seq;
   }
   args.tiles_m = (int)((M + BM - 1) / BM);
+  args.tiles_m2 = (int)((M + 2 * BM - 1) / (2 * BM));
   args.tiles_n = (int)((N + (epi == 1 ? BN / 2 : BN) - 1) / (epi == 1 ? BN / 2 : BN));
   const int64_t tiles = (int64_t)args.tiles_m * args.tiles_n * batch;
   if (tiles > INT32_MAX) return fail(NKB_ERR_UNSUPPORTED, "gemm: too many tiles");
   static ContextOnce attr_set;
   if (int s = attr_set.run(device, []() -> int {
-        NKB_CUDA_TRY(
-            cudaFuncSetAttribute(gemm_bf16_tcgen05<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-        NKB_CUDA_TRY(
-            cudaFuncSetAttribute(gemm_bf16_tcgen05<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        NKB_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tcgen05<false, false>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        NKB_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tcgen05<true, false>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        NKB_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tcgen05<false, true>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         return NKB_OK;
       }))
     return s;
@@ -780,9 +902,37 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
     args.ar_rank = ar->rank;
     args.ar_world = ar->world;
     args.ar_wait = wait_limit_cycles();
-    gemm_bf16_tcgen05<true><<<grid, AR_THREADS, SMEM_BYTES, st>>>(ma, mb, args);
+    gemm_bf16_tcgen05<true, false><<<grid, AR_THREADS, SMEM_BYTES, st>>>(ma, mb, args);
+  } else if (pair) {
+    // one cluster of two CTAs per pair of SMs, persistent over the 256 x 256 tiles
+    const int64_t ptiles = (int64_t)args.tiles_m2 * args.tiles_n * batch;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // as many pairs as can be resident at once (clusters stay inside a GPC)
+    static ContextOnce occ;
+    static int max_clusters[64];
+    const int dslot = device >= 0 && device < 64 ? device : 0;
+    if (int s = occ.run(device, [&]() -> int {
+          cfg.gridDim = dim3((unsigned)num_sms(device));
+          int n = 0;
+          NKB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, gemm_bf16_tcgen05<false, true>, &cfg));
+          max_clusters[dslot] = std::max(1, n);
+          return NKB_OK;
+        }))
+      return s;
+    cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(ptiles, max_clusters[dslot])));
+    NKB_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_bf16_tcgen05<false, true>, ma, mb, args));
   } else {
-    gemm_bf16_tcgen05<false><<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, args);
+    gemm_bf16_tcgen05<false, false><<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, args);
   }
   if (int e = launch_status("gemm_bf16_tcgen05")) return e;
   if (args.ksplit > 1) return splitk_reduce(ws, static_cast<__nv_bfloat16 *>(C), M, N, ldc, args.ksplit, st, device);
