@@ -843,6 +843,16 @@ def profile_traffic(wl):
     return None
 
 
+def _tensor_numpy(spike, t, spec):
+    """A device buffer read back as the plan io spec's array."""
+    import ml_dtypes as md
+
+    dt = np.dtype(md.bfloat16) if spec["dtype"] == "bfloat16" else np.dtype(spec["dtype"])
+    raw = np.frombuffer(spike.tensor_read(t), dtype=np.uint8)
+    n = int(np.prod(spec["shape"], dtype=np.int64)) * dt.itemsize
+    return raw[:n].view(dt).reshape(spec["shape"])
+
+
 def _outputs_numpy(kernel, outs):
     """Every plan output read back to the host (name -> ndarray)."""
     return {s["name"]: outs[s["name"]].numpy() for s in kernel.model_ref.io["outputs"]}
@@ -957,16 +967,16 @@ def run_nkb(args, wl, rank, world, local_rank):
         pinned_in.append(p)
     pinned_out = [torch.empty(outs[s["name"]].tensor_ref.size // parts, dtype=torch.uint8, pin_memory=True).numpy()
                   for s in out_specs]
+    # the public pipelined API: each step's upload and read-back overlap the
+    # neighbouring steps' compute (two device buffer sets, three streams)
+    resident = {n: ins[n] for n in in_names if n not in step_names}
+    host_in = dict(zip(step_names, pinned_in))
+    host_out = {sp["name"]: p for sp, p in zip(out_specs, pinned_out)}
+    bind = {name: t for name, t in outs.items() if f"{name}.must_alias_input" in ins}
+    kernel.run_steps(resident, host_in, host_out, 2, split=split, bind=bind)  # buffers, graphs
     barrier()
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        for n, p in zip(step_names, pinned_in):
-            spike.tensor_write_from_pybuffer(ins[n].tensor_ref, p, offset=part * p.nbytes)
-            if split:
-                spike.all_gather_in_place(kernel.model_ref, ins[n].tensor_ref, p.nbytes)
-        spike.execute(kernel.model_ref, in_refs, out_refs, use_graph=True)
-        for s, p in zip(out_specs, pinned_out):
-            spike.tensor_read_to_pybuffer(outs[s["name"]].tensor_ref, p, offset=part * p.nbytes)
+    e2e_outs = kernel.run_steps(resident, host_in, host_out, args.steps, split=split, bind=bind)
     barrier()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     clocks = sampler.stop()
@@ -975,7 +985,10 @@ def run_nkb(args, wl, rank, world, local_rank):
     parity = None
     if rank == 0 and not args.no_parity:
         try:
-            parity = wl.parity(_outputs_numpy(kernel, outs), arrays)
+            # the last end-to-end step's outputs (under the TP row split its input was
+            # completed by the all-gather)
+            got = {sp["name"]: _tensor_numpy(spike, e2e_outs[sp["name"]], sp) for sp in kernel.model_ref.io["outputs"]}
+            parity = wl.parity(got, arrays)
         except Exception as e:  # report, never hide, a failing check
             parity = {"ok": False, "error": f"{type(e).__name__}: {e}"}
     barrier()

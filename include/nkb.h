@@ -73,6 +73,21 @@ NKB_API int nkb_buf_info(nkb_buf buf, size_t *bytes, int *device, void **device_
 NKB_API int nkb_h2d(nkb_buf dst, const void *src, size_t bytes, size_t offset);
 NKB_API int nkb_d2h(nkb_buf src, void *dst, size_t bytes, size_t offset);
 NKB_API int nkb_memset(nkb_buf dst, int value, size_t bytes, size_t offset);
+/* Streams, events and asynchronous (bounds-checked) copies, for callers that
+ * overlap the copies of one step with the compute of another.  The
+ * reference's tensor_write / tensor_read are synchronous and have no such
+ * calls; these add the pipelined form.  Streams are non-blocking streams of
+ * the runtime's device; NULL stream = the runtime's own stream.  Host memory
+ * must be page-locked (pinned) for the copies to run asynchronously. */
+NKB_API int nkb_stream_create(void **stream);
+NKB_API int nkb_stream_destroy(void *stream);
+NKB_API int nkb_stream_synchronize(void *stream);
+NKB_API int nkb_event_create(void **event);
+NKB_API int nkb_event_destroy(void *event);
+NKB_API int nkb_event_record(void *event, void *stream);
+NKB_API int nkb_stream_wait_event(void *stream, void *event);
+NKB_API int nkb_h2d_async(nkb_buf dst, const void *src, size_t bytes, size_t offset, void *stream);
+NKB_API int nkb_d2h_async(nkb_buf src, void *dst, size_t bytes, size_t offset, void *stream);
 /* device-to-device copy between buffers (synchronous, bounds-checked) */
 NKB_API int nkb_copy(nkb_buf dst, size_t dst_offset, nkb_buf src, size_t src_offset, size_t bytes);
 

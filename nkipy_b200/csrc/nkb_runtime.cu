@@ -344,6 +344,86 @@ extern "C" int nkb_d2h(nkb_buf src, void *dst, size_t bytes, size_t offset) {
   return NKB_OK;
 }
 
+// ---- streams, events and asynchronous copies (pipelined callers) ----------
+extern "C" int nkb_stream_create(void **stream) {
+  if (int s = ensure_init()) return s;
+  if (!stream) return fail(NKB_ERR_INVALID, "stream is NULL");
+  cudaStream_t st = nullptr;
+  NKB_CUDA_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  *stream = st;
+  return NKB_OK;
+}
+
+extern "C" int nkb_stream_destroy(void *stream) {
+  if (int s = ensure_init()) return s;
+  if (!stream) return fail(NKB_ERR_INVALID, "stream is NULL");
+  NKB_CUDA_TRY(cudaStreamDestroy(static_cast<cudaStream_t>(stream)));
+  return NKB_OK;
+}
+
+extern "C" int nkb_stream_synchronize(void *stream) {
+  if (int s = ensure_init()) return s;
+  NKB_CUDA_TRY(cudaStreamSynchronize(stream ? static_cast<cudaStream_t>(stream) : g_rt.stream));
+  return NKB_OK;
+}
+
+extern "C" int nkb_event_create(void **event) {
+  if (int s = ensure_init()) return s;
+  if (!event) return fail(NKB_ERR_INVALID, "event is NULL");
+  cudaEvent_t e = nullptr;
+  NKB_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  *event = e;
+  return NKB_OK;
+}
+
+extern "C" int nkb_event_destroy(void *event) {
+  if (int s = ensure_init()) return s;
+  if (!event) return fail(NKB_ERR_INVALID, "event is NULL");
+  NKB_CUDA_TRY(cudaEventDestroy(static_cast<cudaEvent_t>(event)));
+  return NKB_OK;
+}
+
+extern "C" int nkb_event_record(void *event, void *stream) {
+  if (int s = ensure_init()) return s;
+  if (!event) return fail(NKB_ERR_INVALID, "event is NULL");
+  NKB_CUDA_TRY(cudaEventRecord(static_cast<cudaEvent_t>(event), stream ? static_cast<cudaStream_t>(stream) : g_rt.stream));
+  return NKB_OK;
+}
+
+extern "C" int nkb_stream_wait_event(void *stream, void *event) {
+  if (int s = ensure_init()) return s;
+  if (!event) return fail(NKB_ERR_INVALID, "event is NULL");
+  NKB_CUDA_TRY(cudaStreamWaitEvent(stream ? static_cast<cudaStream_t>(stream) : g_rt.stream,
+                                   static_cast<cudaEvent_t>(event), 0));
+  return NKB_OK;
+}
+
+extern "C" int nkb_h2d_async(nkb_buf dst, const void *src, size_t bytes, size_t offset, void *stream) {
+  if (int s = ensure_init()) return s;
+  if (!buf_ok(dst)) return fail(NKB_ERR_STATE, "write to an invalid or freed buffer");
+  if (offset > dst->bytes || bytes > dst->bytes - offset)
+    return fail(NKB_ERR_INVALID, "write of " + std::to_string(bytes) + " bytes at offset " + std::to_string(offset) +
+                                     " exceeds buffer of " + std::to_string(dst->bytes) + " bytes");
+  if (!bytes) return NKB_OK;
+  if (!src) return fail(NKB_ERR_INVALID, "source is NULL");
+  NKB_CUDA_TRY(cudaMemcpyAsync(static_cast<char *>(dst->ptr) + offset, src, bytes, cudaMemcpyHostToDevice,
+                               stream ? static_cast<cudaStream_t>(stream) : g_rt.stream));
+  return NKB_OK;
+}
+
+extern "C" int nkb_d2h_async(nkb_buf src, void *dst, size_t bytes, size_t offset, void *stream) {
+  if (int s = ensure_init()) return s;
+  if (!buf_ok(src)) return fail(NKB_ERR_STATE, "read from an invalid or freed buffer");
+  if (offset > src->bytes || bytes > src->bytes - offset)
+    return fail(NKB_ERR_INVALID, "read of " + std::to_string(bytes) + " bytes at offset " + std::to_string(offset) +
+                                     " exceeds buffer of " + std::to_string(src->bytes) + " bytes");
+  if (!bytes) return NKB_OK;
+  if (!dst) return fail(NKB_ERR_INVALID, "destination is NULL");
+  NKB_CUDA_TRY(cudaMemcpyAsync(dst, static_cast<char *>(src->ptr) + offset, bytes, cudaMemcpyDeviceToHost,
+                               stream ? static_cast<cudaStream_t>(stream) : g_rt.stream));
+  return NKB_OK;
+}
+
 extern "C" int nkb_memset(nkb_buf dst, int value, size_t bytes, size_t offset) {
   if (int s = ensure_init()) return s;
   if (!buf_ok(dst)) return fail(NKB_ERR_STATE, "memset of an invalid or freed buffer");
@@ -701,12 +781,20 @@ struct nkb_plan_s {
   std::vector<nkb::Step> steps;
   std::vector<const nkb::KernelEntry *> entries;
   nkb_comm comm = nullptr;
-  // graph replay cache
-  cudaGraphExec_t graph_exec = nullptr;
-  cudaStream_t graph_stream = nullptr;
-  std::vector<void *> graph_key;
+  // graph replay cache: one instantiated graph per (io pointers, stream), a
+  // few of them (alternating io buffer sets, as a pipelined caller binds)
+  struct GraphEntry {
+    std::vector<void *> key;
+    cudaStream_t stream = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    uint64_t used = 0;
+  };
+  static constexpr size_t kGraphCache = 4;
+  std::vector<GraphEntry> graphs;
+  uint64_t graph_clock = 0;
   ~nkb_plan_s() {
-    if (graph_exec) cudaGraphExecDestroy(graph_exec);
+    for (auto &g : graphs)
+      if (g.exec) cudaGraphExecDestroy(g.exec);
     for (void *p : const_ptrs)
       if (p) cudaFree(p);
     if (arena) cudaFree(arena);
@@ -981,10 +1069,22 @@ int launch_steps(nkb_plan plan, const std::vector<void *> &base, cudaStream_t st
 
 int execute_on(nkb_plan plan, const std::vector<void *> &base, cudaStream_t stream, bool use_graph) {
   if (!use_graph) return launch_steps(plan, base, stream);
-  if (!plan->graph_exec || plan->graph_key != base || plan->graph_stream != stream) {
-    if (plan->graph_exec) {
-      cudaGraphExecDestroy(plan->graph_exec);
-      plan->graph_exec = nullptr;
+  nkb_plan_s::GraphEntry *hit = nullptr;
+  for (auto &g : plan->graphs)
+    if (g.exec && g.stream == stream && g.key == base) hit = &g;
+  if (!hit) {
+    // a free slot, else the least recently used one
+    if (plan->graphs.size() < nkb_plan_s::kGraphCache) {
+      plan->graphs.emplace_back();
+      hit = &plan->graphs.back();
+    } else {
+      hit = &plan->graphs[0];
+      for (auto &g : plan->graphs)
+        if (g.used < hit->used) hit = &g;
+    }
+    if (hit->exec) {
+      cudaGraphExecDestroy(hit->exec);
+      hit->exec = nullptr;
     }
     cudaGraph_t g = nullptr;
     NKB_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
@@ -995,13 +1095,17 @@ int execute_on(nkb_plan plan, const std::vector<void *> &base, cudaStream_t stre
       return s;
     }
     if (e != cudaSuccess) return fail(NKB_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
-    e = cudaGraphInstantiate(&plan->graph_exec, g, 0);
+    e = cudaGraphInstantiate(&hit->exec, g, 0);
     cudaGraphDestroy(g);
-    if (e != cudaSuccess) return fail(NKB_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
-    plan->graph_key = base;
-    plan->graph_stream = stream;
+    if (e != cudaSuccess) {
+      hit->exec = nullptr;
+      return fail(NKB_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    }
+    hit->key = base;
+    hit->stream = stream;
   }
-  NKB_CUDA_TRY(cudaGraphLaunch(plan->graph_exec, stream));
+  hit->used = ++plan->graph_clock;
+  NKB_CUDA_TRY(cudaGraphLaunch(hit->exec, stream));
   return NKB_OK;
 }
 

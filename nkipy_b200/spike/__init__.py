@@ -206,6 +206,24 @@ class SpikeModel:
         if auto:
             return outputs
 
+    def run_steps(self, resident: Dict[str, SpikeTensor], host_inputs, host_outputs, steps: int, split: bool = False,
+                  bind: Dict[str, SpikeTensor] = None, use_graph: bool = True):
+        """Run ``steps`` executes with each step's copies overlapping other steps'
+        compute (``nkipy_b200.spike.pipeline.run_pipelined``): ``resident`` device
+        inputs stay, ``host_inputs`` (name -> page-locked array, or a sequence of
+        them, one per step) are uploaded every step, ``host_outputs`` (name ->
+        page-locked array) receive every step's result; ``bind`` fixes outputs to
+        tensors (a mutated input's in-place output); ``split`` uploads and reads
+        back this rank's rows only, the inputs completed by an all-gather.
+        Device buffers, streams and events are kept on the model for the next call."""
+        from nkipy_b200.spike.pipeline import run_pipelined
+
+        self._validate_io(resident, bind or {})
+        state = self.__dict__.setdefault("_pipeline_state", {})
+        return run_pipelined(get_spike_singleton(), self.model_ref, {k: v.tensor_ref for k, v in resident.items()},
+                             host_inputs, host_outputs, steps, split=split,
+                             bind={k: v.tensor_ref for k, v in (bind or {}).items()}, use_graph=use_graph, state=state)
+
     def benchmark(self, inputs, outputs=None, warmup_iter=5, benchmark_iter=5, mode: str = "device"):
         """'device': CUDA-event time per execute; 'host': wall clock per synchronous execute."""
         if mode not in ("device", "host"):

@@ -82,6 +82,15 @@ def _declare(lib):
         "nkb_synchronize": [],
         "nkb_time_steps": [c_plan, pp, i32, pp, i32, i32, ctypes.POINTER(ctypes.c_float)],
         "nkb_device_error": [ctypes.POINTER(i32)],
+        "nkb_stream_create": [pp],
+        "nkb_stream_destroy": [vp],
+        "nkb_stream_synchronize": [vp],
+        "nkb_event_create": [pp],
+        "nkb_event_destroy": [vp],
+        "nkb_event_record": [vp, vp],
+        "nkb_stream_wait_event": [vp, vp],
+        "nkb_h2d_async": [c_buf, vp, sz, sz, vp],
+        "nkb_d2h_async": [c_buf, vp, sz, sz, vp],
         "nkb_set_wait_limit_us": [ctypes.c_uint64],
         "nkb_get_wait_limit_us": [ctypes.POINTER(ctypes.c_uint64)],
         "nkb_wait_probe": [vp, ctypes.c_uint32, vp],
