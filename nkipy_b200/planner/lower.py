@@ -1094,6 +1094,11 @@ class Lowering:
         es = np.dtype(op.result_dtype).itemsize
         ins = list(a["inserted_window_dims"])
         xs, us = tuple(int(d) for d in x.shape), tuple(int(d) for d in upd.shape)
+        if (len(ins) == 1 and len(us) == r - 1 and int(np.prod(ind.shape)) == 1
+                and list(a["update_window_dims"]) == [d for d in range(r) if d != ins[0]]):
+            # one index and an update without the indexed axis (``x[i] = row`` with a
+            # one-element index array): the window form with that axis of size 1
+            us = us[: ins[0]] + (1,) + us[ins[0]:]
         window = (
             len(ins) == 1
             and list(a["update_window_dims"]) == [d for d in range(r) if d != ins[0]]
