@@ -56,6 +56,7 @@ __device__ __forceinline__ void store4(__nv_bfloat16 *p, const float *v) {
 }
 __device__ __forceinline__ float load1(const float *p) { return *p; }
 __device__ __forceinline__ float load1(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
+__device__ __forceinline__ float load1(const __half *p) { return __half2float(*p); }
 __device__ __forceinline__ void store1(float *p, float v) { *p = v; }
 __device__ __forceinline__ void store1(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
 
@@ -579,6 +580,9 @@ int argext_any(const void *x, int dt, int32_t *out, int64_t rows, int64_t cols, 
   } else if (dt == NKB_BF16) {
     if (is_max) argext_kernel<__nv_bfloat16, true><<<g, 256, 0, st>>>((const __nv_bfloat16 *)x, out, rows, cols);
     else argext_kernel<__nv_bfloat16, false><<<g, 256, 0, st>>>((const __nv_bfloat16 *)x, out, rows, cols);
+  } else if (dt == NKB_F16) {
+    if (is_max) argext_kernel<__half, true><<<g, 256, 0, st>>>((const __half *)x, out, rows, cols);
+    else argext_kernel<__half, false><<<g, 256, 0, st>>>((const __half *)x, out, rows, cols);
   } else {
     return fail(NKB_ERR_UNSUPPORTED, "argmax_rows: dtype not supported");
   }

@@ -25,6 +25,7 @@ import hashlib
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional
 
+import ml_dtypes
 import numpy as np
 
 NOISE = ("reshape", "broadcast")
@@ -460,6 +461,8 @@ def match_argmax(gi: GraphIndex, cvt_op) -> Optional[Claim]:
         return None
     if not _exclusive(gi, ops, cvt_op):
         return None
+    if np.dtype(x.dtype) not in (np.dtype(np.float32), np.dtype(np.float16), np.dtype(ml_dtypes.bfloat16)):
+        return None  # the row kernel reads floats; other dtypes keep the generic lowering
     return Claim("argmax", cvt_op, [o for o in ops if o is not None], {"x": x, "is_max": comp == "maximum"})
 
 

@@ -46,3 +46,12 @@ kernel_specs = [
         TensorInputSpec(dtype_spec=_I32, shape_spec=ShapeSpec([1], (1,)), default_value=np.array([5], np.int32)),
     ], description="row written in place at a run-time position"),
 ]
+
+
+def argmax_int(x):
+    return np.argmax(x, axis=-1)
+
+
+kernel_specs.append(KernelSpec(argmax_int, [
+    TensorInputSpec(dtype_spec=CommonTypes.INTS, shape_spec=ShapeSpec([(1, 40), (1, 300)], (17, 300)))],
+    description="argmax of integers (first occurrence)"))
