@@ -823,9 +823,9 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
     return fail(NKB_ERR_UNSUPPORTED, "gemm_tc: SwiGLU epilogue needs N-major B, bf16 output and n_half % 64 == 0");
   const int64_t bcols = epi == 1 ? 2 * n_half : N;
   // CTA pairs (256 x 256 tiles) for products with more than one row tile and no
-  // split or fused all-reduce; NKB_GEMM_PAIR=0 keeps single CTAs (comparisons)
+  // split; NKB_GEMM_PAIR=0 keeps single CTAs (comparisons)
   const char *pe = getenv("NKB_GEMM_PAIR");
-  const bool pair = ksplit <= 1 && !ar && M > BM && !(pe && pe[0] == '0');
+  const bool pair = ksplit <= 1 && M > BM && !(pe && pe[0] == '0');
   if (b_k_major) s = make_map(&mb, B, K, bcols, bb, ldb, sB, BK, pair ? BN / 2 : BN);
   else s = make_map(&mb, B, bcols, K, bb, ldb, sB, 64, BK);
   if (s) return s;
@@ -886,6 +886,8 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         NKB_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tcgen05<false, true>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        NKB_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tcgen05<true, true>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         return NKB_OK;
       }))
     return s;
@@ -902,12 +904,13 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
     args.ar_rank = ar->rank;
     args.ar_world = ar->world;
     args.ar_wait = wait_limit_cycles();
-    gemm_bf16_tcgen05<true, false><<<grid, AR_THREADS, SMEM_BYTES, st>>>(ma, mb, args);
-  } else if (pair) {
+    if (!pair) gemm_bf16_tcgen05<true, false><<<grid, AR_THREADS, SMEM_BYTES, st>>>(ma, mb, args);
+  }
+  if (pair) {
     // one cluster of two CTAs per pair of SMs, persistent over the 256 x 256 tiles
     const int64_t ptiles = (int64_t)args.tiles_m2 * args.tiles_n * batch;
     cudaLaunchConfig_t cfg = {};
-    cfg.blockDim = dim3(THREADS);
+    cfg.blockDim = dim3(ar ? AR_THREADS : THREADS);
     cfg.dynamicSmemBytes = SMEM_BYTES;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -917,21 +920,32 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    // as many pairs as can be resident at once (clusters stay inside a GPC)
+    // as many pairs as can be resident at once (clusters stay inside a GPC); the
+    // fused all-reduce relies on every CTA being resident
     static ContextOnce occ;
-    static int max_clusters[64];
+    static int max_clusters[64][2];
     const int dslot = device >= 0 && device < 64 ? device : 0;
     if (int s = occ.run(device, [&]() -> int {
-          cfg.gridDim = dim3((unsigned)num_sms(device));
-          int n = 0;
-          NKB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, gemm_bf16_tcgen05<false, true>, &cfg));
-          max_clusters[dslot] = std::max(1, n);
+          for (int v = 0; v < 2; ++v) {
+            cudaLaunchConfig_t c = cfg;
+            c.blockDim = dim3(v ? AR_THREADS : THREADS);
+            c.gridDim = dim3((unsigned)num_sms(device));
+            int n = 0;
+            if (v)
+              NKB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, gemm_bf16_tcgen05<true, true>, &c));
+            else
+              NKB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, gemm_bf16_tcgen05<false, true>, &c));
+            max_clusters[dslot][v] = std::max(1, n);
+          }
           return NKB_OK;
         }))
       return s;
-    cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(ptiles, max_clusters[dslot])));
-    NKB_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_bf16_tcgen05<false, true>, ma, mb, args));
-  } else {
+    cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(ptiles, max_clusters[dslot][ar ? 1 : 0])));
+    if (ar)
+      NKB_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_bf16_tcgen05<true, true>, ma, mb, args));
+    else
+      NKB_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_bf16_tcgen05<false, true>, ma, mb, args));
+  } else if (!ar) {
     gemm_bf16_tcgen05<false, false><<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, args);
   }
   if (int e = launch_status("gemm_bf16_tcgen05")) return e;
