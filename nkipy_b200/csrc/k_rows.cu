@@ -358,6 +358,82 @@ __global__ void __launch_bounds__(256) rmsnorm_stream_kernel(const T *__restrict
   }
 }
 
+// bf16 rows of up to 8192 columns (the decoder layer's norms): 256 threads, 8
+// consecutive columns per thread per chunk (16-byte loads and stores), the row
+// sum rounded to bf16 as the trace does, and the normalisation as a multiply
+// by the reciprocal of sqrt(mean + eps) (within one fp32 ulp of the division,
+// the result then rounded to bf16).
+__device__ __forceinline__ void load8(const __nv_bfloat16 *p, float *v) {
+  const uint4 t = *reinterpret_cast<const uint4 *>(p);
+  const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
+    v[2 * i] = f.x, v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void load8(const float *p, float *v) {
+  const float4 a = *reinterpret_cast<const float4 *>(p), b = *reinterpret_cast<const float4 *>(p + 4);
+  v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+__device__ __forceinline__ void store8(__nv_bfloat16 *p, const float *v) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t *>(&h);
+  }
+  *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <int CHUNKS, typename TW, bool RES, bool SUM_OUT>
+__global__ void __launch_bounds__(256) rmsnorm_bf16_kernel(const __nv_bfloat16 *__restrict__ x,
+                                                           const __nv_bfloat16 *__restrict__ r,
+                                                           const TW *__restrict__ w, __nv_bfloat16 *__restrict__ y,
+                                                           __nv_bfloat16 *__restrict__ hsum, int64_t rows, int cols,
+                                                           float eps, int64_t xin, int64_t xos) {
+  __shared__ float smem[32];
+  const int t = threadIdx.x;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int64_t base = row * cols;
+    const int64_t ibase = (row / xin) * xos + (row % xin) * cols;
+    float v[CHUNKS][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+      const int col = (c * 256 + t) * 8;
+      if (col < cols) {
+        load8(x + ibase + col, v[c]);
+        if (RES) {
+          float rv[8];
+          load8(r + ibase + col, rv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[c][j] = __bfloat162float(__float2bfloat16_rn(v[c][j] + rv[j]));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[c][j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[c][j] * v[c][j];
+    }
+    ss = row_reduce_sum<256>(ss, smem);
+    const float inv = 1.0f / sqrtf(__fdiv_rn(ss, (float)cols) + eps);
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+      const int col = (c * 256 + t) * 8;
+      if (col < cols) {
+        if (SUM_OUT) store8(hsum + base + col, v[c]);
+        float wv[8], o[8];
+        load8(w + col, wv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = v[c][j] * inv * wv[j];
+        store8(y + base + col, o);
+      }
+    }
+  }
+}
+
 template <typename T, typename TW, bool RES, bool SUM_OUT>
 int rmsnorm_dispatch3(const void *x, const void *r, const void *w, void *y, void *hs, int64_t rows, int64_t cols,
                       float eps, int64_t xin, int64_t xos, cudaStream_t st, int device) {
@@ -371,6 +447,19 @@ int rmsnorm_dispatch3(const void *x, const void *r, const void *w, void *y, void
                        (!SUM_OUT || (uintptr_t)hs % 16 == 0);
   const int64_t cap = (int64_t)num_sms(device) * 32;
   auto grid = [&](int rpb) { return (unsigned)std::min<int64_t>((rows + rpb - 1) / rpb, cap); };
+  if constexpr (sizeof(T) == 2) {
+    const bool a16 = aligned && cols % 8 == 0 && xos % 8 == 0 && cols > 1024 && cols <= 8192;
+    if (a16) {
+      const unsigned g = (unsigned)std::min<int64_t>(rows, (int64_t)num_sms(device) * 8);
+      if (cols <= 2048)
+        rmsnorm_bf16_kernel<1, TW, RES, SUM_OUT><<<g, 256, 0, st>>>(xi, ri, wi, yo, ho, rows, (int)cols, eps, xin, xos);
+      else if (cols <= 4096)
+        rmsnorm_bf16_kernel<2, TW, RES, SUM_OUT><<<g, 256, 0, st>>>(xi, ri, wi, yo, ho, rows, (int)cols, eps, xin, xos);
+      else
+        rmsnorm_bf16_kernel<4, TW, RES, SUM_OUT><<<g, 256, 0, st>>>(xi, ri, wi, yo, ho, rows, (int)cols, eps, xin, xos);
+      return launch_status("rmsnorm_rows");
+    }
+  }
 #define RMS_LAUNCH(TH, CH, RPB) \
   rmsnorm_reg_kernel<TH, CH, T, TW, RES, SUM_OUT><<<grid(RPB), 256, 0, st>>>(xi, ri, wi, yo, ho, rows, (int)cols, eps, \
                                                                        xin, xos)

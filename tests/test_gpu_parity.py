@@ -39,6 +39,26 @@ def test_residual_rmsnorm(rows, cols):
     assert_close(got, O.residual_rmsnorm(x, r, w, 1e-6), FP32_RTOL)
 
 
+@pytest.mark.parametrize("rows,cols,res", [(16, 4096, True), (5, 2048, False), (3, 8192, True), (7, 1536, True),
+                                           (8192, 4096, True)])
+def test_residual_rmsnorm_bf16(rows, cols, res):
+    """bf16 rows (the decoder layer's norms) on the 16-byte-vector kernel; the
+    direct call rounds the residual sum and the result to bf16, so the device
+    result may differ by one bf16 unit in the last place."""
+    rng = np.random.default_rng(26)
+    x = rng.standard_normal((rows, cols), dtype=np.float32).astype(BF16)
+    r = rng.standard_normal((rows, cols), dtype=np.float32).astype(BF16)
+    w = rng.uniform(0.5, 1.5, cols).astype(BF16)
+    if res:
+        got = on_device(W.residual_rmsnorm_kernel, x, r, w)
+        want = W.residual_rmsnorm_kernel(x, r, w)
+    else:
+        got = on_device(lambda a, g: W.rmsnorm(a, g, 1e-6), x, w)
+        want = W.rmsnorm(x, w, 1e-6)
+    assert got.dtype == BF16
+    assert_close(got, want, 2**-7, atol=2**-7)
+
+
 @pytest.mark.parametrize("m,k,n", [(256, 512, 256), (8192, 8192, 8192), (300, 200, 264), (128, 64, 256), (1000, 4096, 1000),
                                    (8, 4096, 6144), (1, 4096, 4096), (5, 12288, 1000), (16, 200, 264), (3, 64, 8)])
 def test_matmul_bf16(m, k, n):
@@ -104,8 +124,8 @@ def test_elementwise_chain_broadcast():
 @pytest.mark.parametrize("dtype,shape", [(np.float32, (64, 256)), (np.float32, (3, 5, 96)), (BF16, (40, 512)),
                                          (np.float32, (7, 13))])
 def test_elementwise_chain_register_reuse(dtype, shape):
-    """Six inputs (four loaded up front, two at their load instruction),
-    values read again several instructions later, a select on a
+    """Six inputs, values read again several instructions later (from the
+    shared-memory register file, not the accumulator), a select on a
     recomputed value, a result that is not the last instruction's; row-run
     kernel (8- and 4-element runs) and the generic kernel (13 columns)."""
 
