@@ -124,6 +124,14 @@ NKB_API int nkb_synchronize(void);
 NKB_API int nkb_time_steps(nkb_plan plan, const nkb_buf *ins, int n_in, const nkb_buf *outs, int n_out, int iters,
                            float *step_ms);
 
+/* One execute with CUDA events between its launches (no graph): writes each
+ * launch's start (relative to the first) and duration in milliseconds into
+ * start_ms / dur_ms[0..n_launches-1].  Every launch of the runtime is also an
+ * NVTX range named after its kernel.  Replaces the per-execute profile of the
+ * reference (Spike::execute with save_trace / ntff_name, spike/src/model.cpp:97-103). */
+NKB_API int nkb_trace_execute(nkb_plan plan, const nkb_buf *ins, int n_in, const nkb_buf *outs, int n_out,
+                              float *start_ms, float *dur_ms);
+
 /* Reads and clears the device error flag that a kernel raises when one of
  * its bounded waits expires (the kernel then frees its resources and exits
  * instead of hanging; the CUDA context stays usable). */

@@ -10,6 +10,7 @@
 
 #include <cuda.h>
 #include <dlfcn.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <cmath>
 #include <cstdio>
@@ -1058,7 +1059,10 @@ int launch_steps(nkb_plan plan, const std::vector<void *> &base, cudaStream_t st
     for (size_t j = 0; j < st.buf_ids.size(); ++j)
       ptrs[j] = static_cast<char *>(base[st.buf_ids[j]]) + st.buf_offsets[j];
     nkb::LaunchArgs a{&st, ptrs.data(), stream, plan->comm ? (void *)plan->comm : nullptr, plan->device};
+    // one NVTX range per launch, named after the kernel (seen by a profiler when one is attached)
+    nvtxRangePushA(st.kernel.c_str());
     int s = plan->entries[i]->launch(a);
+    nvtxRangePop();
     if (s) {
       std::string m = nkb_last_error();
       return fail(s, "step " + std::to_string(i) + " (" + st.kernel + "): " + m);
@@ -1167,6 +1171,39 @@ void flush_l2(void *scratch, size_t bytes, cudaStream_t st) {
                                                                static_cast<uint4 *>(scratch) + bytes / 16 - 1);
 }
 }  // namespace
+
+extern "C" int nkb_trace_execute(nkb_plan plan, const nkb_buf *ins, int n_in, const nkb_buf *outs, int n_out,
+                                 float *start_ms, float *dur_ms) {
+  if (int s = ensure_init()) return s;
+  if (!plan || !start_ms || !dur_ms) return fail(NKB_ERR_INVALID, "bad trace arguments");
+  std::vector<void *> base;
+  if (int s = resolve_io(plan, ins, n_in, outs, n_out, base)) return s;
+  const size_t n = plan->steps.size();
+  std::vector<cudaEvent_t> ev(n + 1);
+  for (auto &e : ev) NKB_CUDA_TRY(cudaEventCreate(&e));
+  std::vector<void *> ptrs;
+  int status = NKB_OK;
+  cudaEventRecord(ev[0], g_rt.stream);
+  for (size_t i = 0; i < n && !status; ++i) {
+    const nkb::Step &st = plan->steps[i];
+    ptrs.resize(st.buf_ids.size());
+    for (size_t j = 0; j < st.buf_ids.size(); ++j)
+      ptrs[j] = static_cast<char *>(base[st.buf_ids[j]]) + st.buf_offsets[j];
+    nkb::LaunchArgs a{&st, ptrs.data(), g_rt.stream, plan->comm ? (void *)plan->comm : nullptr, plan->device};
+    nvtxRangePushA(st.kernel.c_str());
+    status = plan->entries[i]->launch(a);
+    nvtxRangePop();
+    cudaEventRecord(ev[i + 1], g_rt.stream);
+  }
+  cudaError_t e = cudaStreamSynchronize(g_rt.stream);
+  if (!status && e != cudaSuccess) status = fail(NKB_ERR_CUDA, std::string("traced execute: ") + cudaGetErrorString(e));
+  for (size_t i = 0; i < n && !status; ++i) {
+    cudaEventElapsedTime(&start_ms[i], ev[0], ev[i]);
+    cudaEventElapsedTime(&dur_ms[i], ev[i], ev[i + 1]);
+  }
+  for (auto &x : ev) cudaEventDestroy(x);
+  return status;
+}
 
 extern "C" int nkb_time_steps(nkb_plan plan, const nkb_buf *ins, int n_in, const nkb_buf *outs, int n_out, int iters,
                               float *step_ms) {

@@ -82,6 +82,7 @@ def _declare(lib):
         "nkb_synchronize": [],
         "nkb_time_steps": [c_plan, pp, i32, pp, i32, i32, ctypes.POINTER(ctypes.c_float)],
         "nkb_device_error": [ctypes.POINTER(i32)],
+        "nkb_trace_execute": [c_plan, pp, i32, pp, i32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float)],
         "nkb_stream_create": [pp],
         "nkb_stream_destroy": [vp],
         "nkb_stream_synchronize": [vp],

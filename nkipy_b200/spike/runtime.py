@@ -88,6 +88,7 @@ class NkbModel:
         self.world_size = world_size
         self.comm = comm
         self.symmetric = False  # all-reduces run inside NVSwitch (bound symmetric region)
+        self.last_trace = None  # path of the last execute's trace (save_trace=True)
         n = ctypes.c_int()
         _nkb.call("nkb_plan_num_launches", handle, ctypes.byref(n))
         self.num_launches = n.value
@@ -343,7 +344,16 @@ class Spike:
     def execute(self, model: NkbModel, inputs: Dict[str, NkbTensor], outputs: Dict[str, NkbTensor],
                 ntff_name: Optional[str] = None, save_trace: bool = False, use_graph: bool = False):
         I, ni, O, no = self._io_lists(model, inputs, outputs)
-        _nkb.call("nkb_execute", model.handle, I, ni, O, no, None, int(use_graph))
+        if save_trace:
+            # the reference writes a device profile of this execute (an NTFF file named
+            # ntff_name); here: a Chrome-trace JSON of the execute's launches
+            n = max(1, model.num_launches)
+            start, dur = (ctypes.c_float * n)(), (ctypes.c_float * n)()
+            _nkb.call("nkb_trace_execute", model.handle, I, ni, O, no, start, dur)
+            model.last_trace = write_trace(model, [float(x) for x in start[: model.num_launches]],
+                                           [float(x) for x in dur[: model.num_launches]], ntff_name)
+        else:
+            _nkb.call("nkb_execute", model.handle, I, ni, O, no, None, int(use_graph))
         _nkb.call("nkb_synchronize")
         flag = ctypes.c_int()
         _nkb.call("nkb_device_error", ctypes.byref(flag))
@@ -388,6 +398,26 @@ class Spike:
                 size = int(np.prod(spec["shape"], dtype=np.int64)) * (2 if dt is None else dt.itemsize)
                 dst[spec["name"]] = TensorMetadata(size=size, dtype=spec["dtype"], shape=list(spec["shape"]))
         return info
+
+
+def write_trace(model, start_ms, dur_ms, path=None) -> str:
+    """Chrome-trace JSON (chrome://tracing, Perfetto) of one execute: an event per
+    launch, named after its kernel, on the device's timeline.  ``path`` defaults
+    to ``<plan>.trace.json``; a name without a directory goes next to the plan."""
+    kernels = []
+    with open(model.path) as f:
+        for line in f:
+            if line.startswith("step "):
+                kernels.append(line.split()[1])
+    events = [{"name": k, "cat": "kernel", "ph": "X", "ts": s * 1e3, "dur": d * 1e3, "pid": model.core_id,
+               "tid": 0, "args": {"launch": i}} for i, (k, s, d) in enumerate(zip(kernels, start_ms, dur_ms))]
+    if not path:
+        path = model.path + ".trace.json"
+    elif not os.path.dirname(path):
+        path = os.path.join(os.path.dirname(model.path), path)
+    with open(path, "w") as f:
+        json.dump({"traceEvents": events, "displayTimeUnit": "ms"}, f)
+    return path
 
 
 # -- plan files ---------------------------------------------------------------------

@@ -141,3 +141,22 @@ def test_malformed_plans_rejected_at_load(text, word):
     st = lib.nkb_plan_load(raw, len(raw), get_spike_singleton().device, ctypes.byref(h))
     assert st == PLAN, (st, lib.nkb_last_error())
     assert word in lib.nkb_last_error()
+
+
+def test_save_trace_writes_a_launch_timeline(tmp_path):
+    """save_trace=True (the reference's per-execute profile) writes a Chrome
+    trace of the execute's launches, one event per kernel, next to the plan
+    or at ntff_name."""
+    import json
+
+    from nkipy_b200.runtime import DeviceKernel, DeviceTensor
+
+    x = np.random.default_rng(42).standard_normal((64, 4096), dtype=np.float32)
+    k = DeviceKernel.compile_and_load(W.softmax_kernel, x, name="trace_softmax", is_spmd=False)
+    name = k.model_ref.io["inputs"][0]["name"]
+    path = str(tmp_path / "softmax.trace.json")
+    outs = k(inputs={name: DeviceTensor.from_numpy(x, name=name)}, save_trace=True, ntff_name=path)
+    with open(path) as f:
+        ev = json.load(f)["traceEvents"]
+    assert [e["name"] for e in ev] == ["softmax_rows"] and ev[0]["dur"] > 0
+    assert_close(next(iter(outs.values())).numpy(), O.softmax(x), FP32_RTOL, atol=1e-7)
