@@ -184,6 +184,41 @@ __device__ __forceinline__ void compute(const Instr I, const uint32_t (&A)[VEC],
   }
 }
 
+// Opcodes applied to the accumulator in place (operand a = the previous result).
+__device__ __forceinline__ bool inplace_op(uint8_t op) {
+  return op == FADD || op == FSUB || op == FMUL || op == FDIV || op == FNEG || op == FEXP || op == FRCP ||
+         op == FMAX || op == FMIN;
+}
+
+template <int VEC>
+__device__ __forceinline__ void compute_inplace(const Instr I, uint32_t (&x)[VEC], const uint32_t (&B)[VEC]) {
+#define LANES _Pragma("unroll") for (int v = 0; v < VEC; ++v)
+#define FX __uint_as_float(x[v])
+#define FB __uint_as_float(B[v])
+#define SETF(e) x[v] = __float_as_uint(e)
+  switch (I.op) {
+    case FADD: LANES SETF(FX + FB); break;
+    case FSUB: LANES SETF(FX - FB); break;
+    case FMUL: LANES SETF(FX * FB); break;
+    case FDIV: LANES SETF(FX / FB); break;
+    case FNEG: LANES SETF(-FX); break;
+    case FEXP: LANES SETF(__expf(FX)); break;
+    case FRCP: LANES SETF(__frcp_rn(FX)); break;
+    case FMAX: LANES SETF((FX != FX || FB != FB) ? __int_as_float(0x7fc00000) : fmaxf(FX, FB)); break;
+    case FMIN: LANES SETF((FX != FX || FB != FB) ? __int_as_float(0x7fc00000) : fminf(FX, FB)); break;
+    default: break;
+  }
+  if (I.rnd == 1) {
+    LANES x[v] = __float_as_uint(rnd_bf16(__uint_as_float(x[v])));
+  } else if (I.rnd == 2) {
+    LANES x[v] = __float_as_uint(rnd_f16(__uint_as_float(x[v])));
+  }
+#undef LANES
+#undef FX
+#undef FB
+#undef SETF
+}
+
 __device__ __forceinline__ void exec_one(const Instr I, const int64_t (*idx)[kVec], uint32_t (*r)[kVec]) {
   uint32_t A[kVec], B[kVec], C[kVec], d[kVec];
 #pragma unroll
@@ -387,6 +422,24 @@ __global__ void __launch_bounds__(256) ew_rows_kernel(const __grid_constant__ Pa
         }
 #pragma unroll
         for (int v = 0; v < VEC; ++v) d[v] = (uint32_t)(int32_t)(id + (I.a == last ? v : 0));
+      } else if ((I.pad & F_A_ACC) && inplace_op(I.op)) {
+        uint32_t B[VEC];
+        if (I.bimm) {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) B[v] = I.imm;
+        } else if (I.pad & F_B_ACC) {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) B[v] = acc[v];
+        } else {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) B[v] = R[(I.b * VEC + v) * T];
+        }
+        compute_inplace<VEC>(I, acc, B);
+        if (I.pad & F_KEEP) {
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) R[(I.dst * VEC + v) * T] = acc[v];
+        }
+        continue;
       } else {
         uint32_t A[VEC], B[VEC], C[VEC];
         if (I.pad & F_A_ACC) {
