@@ -50,7 +50,7 @@ class _Resources:
         return e
 
     def __del__(self):
-        if _nkb._lib is None:
+        if getattr(_nkb, "_lib", None) is None:
             return
         try:
             for e in self.up + self.done + self.down:

@@ -65,7 +65,7 @@ class NkbTensor:
         return ptr.value or 0
 
     def __del__(self):
-        if not self._freed and self.handle and _nkb._lib is not None:
+        if not self._freed and self.handle and getattr(_nkb, "_lib", None) is not None:
             try:
                 _nkb.lib().nkb_free(self.handle)
             except Exception:
@@ -97,7 +97,7 @@ class NkbModel:
         self.scratch_bytes = s.value
 
     def __del__(self):
-        if self.handle and _nkb._lib is not None:
+        if self.handle and getattr(_nkb, "_lib", None) is not None:
             try:
                 _nkb.lib().nkb_plan_free(self.handle)
             except Exception:
