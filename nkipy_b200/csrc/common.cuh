@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include <mutex>
+#include <utility>
 #include <string>
 #include <vector>
 
@@ -103,6 +104,10 @@ struct LaunchArgs {
   cudaStream_t stream;
   void *comm;         // bound NCCL communicator (collective steps only)
   int device;
+  // the launch may overlap the previous kernel on the stream (programmatic
+  // dependent launch): false for the first step of an execute, which must
+  // follow whatever ran on the stream before it in full
+  bool pdl = false;
 };
 
 using LaunchFn = int (*)(const LaunchArgs &);
@@ -136,6 +141,34 @@ inline int launch_status(const char *what) {
 }
 
 int num_sms(int device);
+
+// Programmatic dependent launch.  A kernel started by launch_pdl may begin
+// while the kernel before it on the stream is still draining (inside a CUDA
+// graph the edge between the two becomes a programmatic one), so its launch
+// and set-up overlap that kernel's tail.  Such a kernel calls pdl_wait()
+// before its first global read or write (it returns once every earlier
+// kernel on the stream has finished and its writes are visible), then
+// pdl_trigger() so that the next kernel can be launched in turn.  Both are
+// no-ops for a kernel started without the attribute, which launch_pdl gives
+// only when `pdl` is true and NKB_PDL is not 0.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+bool pdl_enabled();
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Budget, in SM clock cycles, of the waits on counters that other ranks or
 // other CTAs advance (the fused GEMM + all-reduce, the in-switch all-reduce

@@ -66,6 +66,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_kernel(const __grid_co
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int c = blockIdx.x % p.splits, bg = blockIdx.x / p.splits;
   const int b = bg / p.HKV, g = bg % p.HKV;
+  pdl_wait();
+  pdl_trigger();
   int64_t pos = load_pos(p.pos, p.pos_dt);
   pos = pos < 0 ? 0 : (pos >= p.S ? p.S - 1 : pos);
   const int len = (int)pos + 1;  // keys 0..pos
@@ -243,6 +245,8 @@ constexpr int smem_bytes() {
 __global__ void __launch_bounds__(D) attn_decode_combine_kernel(const __grid_constant__ Params p) {
   const int bh = blockIdx.x, d = threadIdx.x;
   const int b = bh / p.H, h = bh % p.H;
+  pdl_wait();
+  pdl_trigger();
   const float *src = p.ws + (int64_t)bh * p.splits * (D + 2);
   float M = -INFINITY;
   for (int c = 0; c < p.splits; ++c) M = fmaxf(M, src[c * (D + 2)]);
@@ -312,7 +316,7 @@ int launch(const LaunchArgs &a) {
           return NKB_OK;
         }))
       return s;
-    kern<<<grid, THREADS, smem, a.stream>>>(p);
+    NKB_CUDA_TRY(launch_pdl(a.pdl, kern, grid, THREADS, smem, a.stream, p));
     return NKB_OK;
   };
   int st = NKB_OK;
@@ -325,7 +329,7 @@ int launch(const LaunchArgs &a) {
   }
   if (st) return st;
   if (int s = launch_status("attn_decode_kernel")) return s;
-  attn_decode_combine_kernel<<<(unsigned)(p.B * p.H), D, 0, a.stream>>>(p);
+  launch_pdl(true, attn_decode_combine_kernel, (unsigned)(p.B * p.H), D, 0, a.stream, p);
   return launch_status("attn_decode_combine_kernel");
 }
 

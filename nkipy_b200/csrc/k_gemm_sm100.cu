@@ -81,6 +81,9 @@ struct Args {
   // and stores its fp32 partial rows to ws[s][M][N]; a second kernel sums them
   int ksplit;
   float *ws;
+  // raster: row tiles per group (a wave of CTAs walks the columns of one
+  // group, sharing its A panels and each B column panel in L2)
+  int group;
 };
 
 constexpr int AR_WARPS = 4, AR_T = AR_WARPS * 32;  // all-reduce warps per CTA
@@ -115,12 +118,11 @@ __device__ __forceinline__ void tile_coords(int t, const Args &a, int &bm, int &
   const int per_batch = tm * a.tiles_n;
   bb = t / per_batch;
   int r = t - bb * per_batch;
-  // group 2048 rows of tiles together so a wave of CTAs shares B column panels in L2
-  constexpr int GROUP = PAIR ? 8 : 16;
-  const int group_span = GROUP * a.tiles_n;
+  const int group = a.group;
+  const int group_span = group * a.tiles_n;
   const int g = r / group_span;
-  const int first_m = g * GROUP;
-  const int gsize = min(tm - first_m, GROUP);
+  const int first_m = g * group;
+  const int gsize = min(tm - first_m, group);
   const int within = r - g * group_span;
   bm = first_m + within % gsize;
   bn = within / gsize;
@@ -762,6 +764,8 @@ bool tc_eligible(const void *A, const void *B, int64_t lda, int64_t ldb, int64_t
 template <bool VEC>
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restrict__ ws, __nv_bfloat16 *__restrict__ C,
                                                             int64_t M, int64_t N, int64_t ldc, int ks) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t per = VEC ? 4 : 1;
   const int64_t n = M * N / per;
   const int64_t plane = M * N;
@@ -795,8 +799,8 @@ int splitk_reduce(const float *ws, __nv_bfloat16 *C, int64_t M, int64_t N, int64
   const bool vec = N % 4 == 0 && ldc % 4 == 0 && (reinterpret_cast<uintptr_t>(C) & 7) == 0;
   const int64_t work = M * N / (vec ? 4 : 1);
   const unsigned grid = (unsigned)std::min<int64_t>((work + 255) / 256, (int64_t)num_sms(device) * 8);
-  if (vec) splitk_reduce_kernel<true><<<grid, 256, 0, st>>>(ws, C, M, N, ldc, ks);
-  else splitk_reduce_kernel<false><<<grid, 256, 0, st>>>(ws, C, M, N, ldc, ks);
+  if (vec) launch_pdl(true, splitk_reduce_kernel<true>, grid, 256, 0, st, ws, C, M, N, ldc, ks);
+  else launch_pdl(true, splitk_reduce_kernel<false>, grid, 256, 0, st, ws, C, M, N, ldc, ks);
   return launch_status("splitk_reduce_kernel");
 }
 
@@ -878,6 +882,12 @@ int gemm_tc(const void *A, const void *B, void *C, int c_f32, int64_t M, int64_t
   args.tiles_n = (int)((N + (epi == 1 ? BN / 2 : BN) - 1) / (epi == 1 ? BN / 2 : BN));
   const int64_t tiles = (int64_t)args.tiles_m * args.tiles_n * batch;
   if (tiles > INT32_MAX) return fail(NKB_ERR_UNSUPPORTED, "gemm: too many tiles");
+  // raster group: 2048 rows of tiles (NKB_GEMM_GROUP overrides, in row tiles)
+  {
+    const char *ge = getenv("NKB_GEMM_GROUP");
+    const int g = ge ? atoi(ge) : 0;
+    args.group = g > 0 ? g : (pair ? 8 : 16);
+  }
   static ContextOnce attr_set;
   if (int s = attr_set.run(device, []() -> int {
         NKB_CUDA_TRY(cudaFuncSetAttribute(gemm_bf16_tcgen05<false, false>,

@@ -101,6 +101,8 @@ __global__ void pad_kernel(const __grid_constant__ PadParams p) {
 __global__ void scatter_rows_kernel(uint8_t *__restrict__ out, const void *__restrict__ ind, int ind_dt,
                                     const uint8_t *__restrict__ upd, int64_t pre, int64_t axis_len, int64_t post_bytes,
                                     int64_t n_idx, int64_t upd_pre_bytes) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t r = blockIdx.x; r < pre * n_idx; r += gridDim.x) {
     const int64_t p = r / n_idx, j = r - p * n_idx;
     const int64_t dst_row = load_index(ind, j, ind_dt);
@@ -215,8 +217,8 @@ int srows_launch(const LaunchArgs &a) {
   const auto &q = a.step->ints;
   if (q[1] * q[4] == 0 || q[3] == 0) return NKB_OK;
   const int64_t upd_pre = q.size() == 6 ? q[5] : q[4] * q[3];
-  scatter_rows_kernel<<<grid_for(q[1] * q[4], a.device, 32), 128, 0, a.stream>>>(
-      (uint8_t *)a.ptrs[0], a.ptrs[1], (int)q[0], (const uint8_t *)a.ptrs[2], q[1], q[2], q[3], q[4], upd_pre);
+  launch_pdl(a.pdl, scatter_rows_kernel, grid_for(q[1] * q[4], a.device, 32), 128, 0, a.stream, (uint8_t *)a.ptrs[0],
+             a.ptrs[1], (int)q[0], (const uint8_t *)a.ptrs[2], q[1], q[2], q[3], q[4], upd_pre);
   return launch_status("scatter_rows_kernel");
 }
 

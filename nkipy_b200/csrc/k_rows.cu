@@ -533,6 +533,8 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_kernel(const __nv_bfloat16 *
                                                            const TW *__restrict__ w, __nv_bfloat16 *__restrict__ y,
                                                            int64_t rows, int cols, float eps, int64_t xin,
                                                            int64_t xos, const __grid_constant__ RopeRows rp) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x % 32;
   const int half = cols / 2;
   const int col = 4 * lane;
@@ -583,7 +585,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_kernel(const __nv_bfloat16 *
 }
 
 int rmsnorm_rope_any(const void *x, const void *w, void *y, int wdt, int64_t rows, int64_t cols, float eps,
-                     int64_t xin, int64_t xos, const RopeRows &rp, cudaStream_t st, int dev) {
+                     int64_t xin, int64_t xos, const RopeRows &rp, cudaStream_t st, int dev, bool pdl) {
   if (rows == 0) return NKB_OK;
   if (cols != 64 && cols != 128) return fail(NKB_ERR_UNSUPPORTED, "rmsnorm_rope_rows: head_dim must be 64 or 128");
   if (xin <= 0 || rows % xin || xos < xin * cols || xos % 4)
@@ -598,11 +600,11 @@ int rmsnorm_rope_any(const void *x, const void *w, void *y, int wdt, int64_t row
   const auto *xi = static_cast<const __nv_bfloat16 *>(x);
   auto *yo = static_cast<__nv_bfloat16 *>(y);
   if (wdt == NKB_BF16)
-    rmsnorm_rope_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(xi, static_cast<const __nv_bfloat16 *>(w), yo, rows,
-                                                            (int)cols, eps, xin, xos, rp);
+    launch_pdl(pdl, rmsnorm_rope_kernel<__nv_bfloat16>, grid, 256, 0, st, xi, static_cast<const __nv_bfloat16 *>(w), yo,
+               rows, (int)cols, eps, xin, xos, rp);
   else if (wdt == NKB_F32)
-    rmsnorm_rope_kernel<float><<<grid, 256, 0, st>>>(xi, static_cast<const float *>(w), yo, rows, (int)cols, eps, xin,
-                                                     xos, rp);
+    launch_pdl(pdl, rmsnorm_rope_kernel<float>, grid, 256, 0, st, xi, static_cast<const float *>(w), yo, rows, (int)cols,
+               eps, xin, xos, rp);
   else
     return fail(NKB_ERR_UNSUPPORTED, "rmsnorm_rope_rows: weight dtype");
   return launch_status("rmsnorm_rope_kernel");
@@ -814,7 +816,7 @@ int rmsnorm_rope_launch(const LaunchArgs &a) {
   rp.H = q[10];
   rp.per_token = (int)q[11];
   return rmsnorm_rope_any(a.ptrs[0], a.ptrs[1], a.ptrs[2], (int)q[2], q[0], q[1], a.step->floats[0], q[3], q[4], rp,
-                          a.stream, a.device);
+                          a.stream, a.device, a.pdl);
 }
 
 // "argmax_rows": ptrs x out; ints rows cols dtype is_max

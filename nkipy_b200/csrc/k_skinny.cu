@@ -32,6 +32,7 @@ struct Params {
   float *ws;  // [ks][M][N] fp32 partials when ks > 1
   int64_t M, N, K, lda, ldb, ldc;
   int kc, ks;
+  int b_pre;  // B is never written by an earlier step: its first stages load before pdl_wait
 };
 
 __global__ void __launch_bounds__(THREADS, 2) skinny_kernel(const __grid_constant__ Params p) {
@@ -44,16 +45,6 @@ __global__ void __launch_bounds__(THREADS, 2) skinny_kernel(const __grid_constan
   const int64_t kbeg = (int64_t)s * p.kc, kend = min(p.K, kbeg + p.kc);
   const int nstage = (int)((kend - kbeg + KT - 1) / KT);
 
-  // A slice: rows 0..15 (zero past M), k in [kbeg, kbeg + kc) (zero past K)
-  const int cpr = p.kc / 8;  // 16-byte chunks per row of the slice
-  for (int i = tid; i < 16 * cpr; i += THREADS) {
-    const int r = i / cpr, c = i % cpr;
-    const int64_t k = kbeg + c * 8;
-    const bool ok = r < p.M && k < p.K;
-    const __nv_bfloat16 *src = p.A + (ok ? (int64_t)r * p.lda + k : 0);
-    cp_async16(smem_addr(sA) + (c / 8) * (16 * 128) + swz(r, c % 8, 128), src, ok);
-  }
-  cp_commit();
   auto load_stage = [&](int st, int buf) {
     const int64_t k0 = kbeg + (int64_t)st * KT;
     const uint32_t dst = smem_addr(sB + buf * STAGE_BYTES);
@@ -66,9 +57,29 @@ __global__ void __launch_bounds__(THREADS, 2) skinny_kernel(const __grid_constan
       cp_async16(dst + swz(r, c, NT * 2), src, ok);
     }
   };
+  // B stages that no earlier step writes (weights) start loading before the
+  // wait on the previous kernel; everything else waits for it
+  if (p.b_pre)
+    for (int st = 0; st < STAGES - 1; ++st)
+      if (st < nstage) load_stage(st, st);
+  pdl_wait();
+  pdl_trigger();
+  // A slice: rows 0..15 (zero past M), k in [kbeg, kbeg + kc) (zero past K)
+  const int cpr = p.kc / 8;  // 16-byte chunks per row of the slice
+  for (int i = tid; i < 16 * cpr; i += THREADS) {
+    const int r = i / cpr, c = i % cpr;
+    const int64_t k = kbeg + c * 8;
+    const bool ok = r < p.M && k < p.K;
+    const __nv_bfloat16 *src = p.A + (ok ? (int64_t)r * p.lda + k : 0);
+    cp_async16(smem_addr(sA) + (c / 8) * (16 * 128) + swz(r, c % 8, 128), src, ok);
+  }
+  // cp.async groups: 0 = A and stage 0 (with b_pre: the first STAGES - 1
+  // stages), then one per remaining prologue stage (empty with b_pre)
+  if (!p.b_pre && nstage > 0) load_stage(0, 0);
+  cp_commit();
 #pragma unroll
-  for (int st = 0; st < STAGES - 1; ++st) {
-    if (st < nstage) load_stage(st, st);
+  for (int st = 1; st < STAGES - 1; ++st) {
+    if (!p.b_pre && st < nstage) load_stage(st, st);
     cp_commit();
   }
 
@@ -116,11 +127,14 @@ __global__ void __launch_bounds__(THREADS, 2) skinny_kernel(const __grid_constan
   }
 }
 
-// "gemm_skinny": ptrs A B C WS; ints M N K lda ldb ldc kc.  A (M x K, K contiguous),
+// "gemm_skinny": ptrs A B C WS; ints M N K lda ldb ldc kc [b_pre].  A (M x K, K contiguous),
 // B (K x N, N contiguous), C (M x N) bf16; M <= 16; the planner sizes WS for
-// ceil(K / kc) * M * N floats (unused with one k-range).
+// ceil(K / kc) * M * N floats (unused with one k-range).  b_pre = 1 when no
+// step of the plan writes B (a weight), so B may be read before the previous
+// kernel has finished.
 int check(const Step &st) {
-  if (st.buf_ids.size() != 4 || st.ints.size() != 7) return fail(NKB_ERR_PLAN, "gemm_skinny: bad parameters");
+  if (st.buf_ids.size() != 4 || (st.ints.size() != 7 && st.ints.size() != 8))
+    return fail(NKB_ERR_PLAN, "gemm_skinny: bad parameters");
   const auto &q = st.ints;
   if (q[0] < 0 || q[0] > 16) return fail(NKB_ERR_UNSUPPORTED, "gemm_skinny: at most 16 rows");
   if (q[2] % 8 || q[1] % 8 || q[3] % 8 || q[4] % 8 || q[5] % 2)
@@ -143,6 +157,7 @@ int launch(const LaunchArgs &a) {
   p.ldb = q[4];
   p.ldc = q[5];
   p.kc = (int)q[6];
+  p.b_pre = q.size() > 7 ? (int)q[7] : 0;
   if (p.M == 0 || p.N == 0) return NKB_OK;
   if (p.K == 0) return fail(NKB_ERR_UNSUPPORTED, "gemm_skinny: K == 0");
   p.ks = (int)((p.K + p.kc - 1) / p.kc);
@@ -158,7 +173,7 @@ int launch(const LaunchArgs &a) {
       }))
     return s;
   dim3 grid((unsigned)((p.N + NT - 1) / NT), (unsigned)p.ks);
-  skinny_kernel<<<grid, THREADS, smem, a.stream>>>(p);
+  launch_pdl(a.pdl, skinny_kernel, grid, THREADS, smem, a.stream, p);
   if (int e = launch_status("skinny_kernel")) return e;
   if (p.ks > 1) return gemm::splitk_reduce(p.ws, p.C, p.M, p.N, p.ldc, p.ks, a.stream, a.device);
   return NKB_OK;

@@ -93,6 +93,14 @@ int num_sms(int device) {
   return cached[device];
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *e = getenv("NKB_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 }  // namespace nkb
 
 using nkb::fail;
@@ -1059,6 +1067,7 @@ int launch_steps(nkb_plan plan, const std::vector<void *> &base, cudaStream_t st
     for (size_t j = 0; j < st.buf_ids.size(); ++j)
       ptrs[j] = static_cast<char *>(base[st.buf_ids[j]]) + st.buf_offsets[j];
     nkb::LaunchArgs a{&st, ptrs.data(), stream, plan->comm ? (void *)plan->comm : nullptr, plan->device};
+    a.pdl = i > 0;  // the first step follows earlier work on the stream in full
     // one NVTX range per launch, named after the kernel (seen by a profiler when one is attached)
     nvtxRangePushA(st.kernel.c_str());
     int s = plan->entries[i]->launch(a);

@@ -363,9 +363,13 @@ class Lowering:
         kc = min(1024, max(64, -(-(-(-K // splits)) // 64) * 64))
         ks = -(-K // kc)
         ws = self.new_buf("tmp", -1, ks * M * N * 4 if ks > 1 else 16)
+        # B that no step writes (a constant, or an input not updated in place)
+        # may be read while the previous kernel drains
+        bb = self.buffers[s.bufs[1][0]]
+        b_pre = int(bb.kind == "const" or (bb.kind == "in" and bb.index not in self.mutated_params))
         s.kernel = "gemm_skinny"
         s.bufs = s.bufs[:3] + [(ws, 0)]
-        s.ints = [M, N, K, lda, ldb, ldc, kc]
+        s.ints = [M, N, K, lda, ldb, ldc, kc, b_pre]
         s.note = f"{M}x{N}x{K} k-ranges {ks}"
         return True
 

@@ -180,9 +180,10 @@ def test_kv_cache_decode_updates_caches_in_place():
     assert all(s.ints[6] == 1 and s.ints[8] == 64 and s.ints[11] == 0 for s in rr)
     assert all(p.buffers[s.bufs[5][0]].kind == "in" and p.buffers[s.bufs[5][0]].index == 6 for s in rr)
     # the 2-row projections run on the skinny GEMM (rows as one m16 tile), K split into
-    # 64-row ranges: 8 of them, each CTA's fp32 partial rows in the workspace
+    # 64-row ranges: 8 of them, each CTA's fp32 partial rows in the workspace; the
+    # weights (inputs no step writes) may be read while the previous kernel drains
     gs = [s for s in p.steps if s.kernel == "gemm_skinny"]
-    assert [s.ints for s in gs] == [[2, width, 512, 512, width, width, 64], [2, 512, 512, 512, 512, 512, 64]]
+    assert [s.ints for s in gs] == [[2, width, 512, 512, width, width, 64, 1], [2, 512, 512, 512, 512, 512, 64, 1]]
     assert [p.buffers[s.bufs[3][0]].nbytes for s in gs] == [8 * 2 * width * 4, 8 * 2 * 512 * 4]
     assert "gemm_bf16" not in kinds
     # the new value row is scattered straight from the projection output
@@ -352,8 +353,12 @@ def test_skinny_gemm_selection():
     z = lambda *s: np.zeros(s, BF16)  # noqa: E731
     p = plan_of(mm, z(16, 4096), z(4096, 1024))
     (s,) = p.steps
-    M, N, K, lda, ldb, ldc, kc = s.ints
+    M, N, K, lda, ldb, ldc, kc, b_pre = s.ints
     assert s.kernel == "gemm_skinny" and (M, N, K, lda, ldb, ldc) == (16, 1024, 4096, 4096, 1024, 1024)
+    assert b_pre == 1  # B is a plan input that no step writes
+    # B computed by an earlier step: read only after that step has finished
+    (sk,) = [t for t in plan_of(lambda a, b: a @ (b + b), z(16, 4096), z(4096, 1024)).steps if t.kernel == "gemm_skinny"]
+    assert sk.ints[7] == 0
     # 4 column blocks of 256: K split for two CTAs per SM (74 ranges wanted, 64-row multiples)
     assert kc == 64 and p.buffers[s.bufs[3][0]].nbytes == (4096 // 64) * 16 * 1024 * 4
     assert plan_of(mm, z(17, 4096), z(4096, 1024)).steps[0].kernel == "gemm_bf16"
