@@ -98,12 +98,34 @@ __global__ void pad_kernel(const __grid_constant__ PadParams p) {
 // (pre, n_idx, post), dense within each of the `pre` blocks, blocks
 // `upd_pre_bytes` apart.  Duplicate indices: the last writer wins in an
 // unspecified order, as for XLA with unique_indices = false.
-__global__ void scatter_rows_kernel(uint8_t *__restrict__ out, const void *__restrict__ ind, int ind_dt,
-                                    const uint8_t *__restrict__ upd, int64_t pre, int64_t axis_len, int64_t post_bytes,
-                                    int64_t n_idx, int64_t upd_pre_bytes) {
+// One launch may carry two scatters (the decode step's K and V cache rows):
+// blocks [0, seg[0].blocks) take the first, the rest the second.
+struct ScatterSeg {
+  uint8_t *out;
+  const void *ind;
+  const uint8_t *upd;
+  int64_t pre, axis_len, post_bytes, n_idx, upd_pre_bytes;
+  int ind_dt;
+  unsigned blocks;
+};
+struct ScatterLaunch {
+  ScatterSeg seg[2];
+  int nseg;
+};
+
+__global__ void scatter_rows_kernel(const __grid_constant__ ScatterLaunch L) {
   pdl_wait();
   pdl_trigger();
-  for (int64_t r = blockIdx.x; r < pre * n_idx; r += gridDim.x) {
+  const int si = (L.nseg > 1 && blockIdx.x >= L.seg[0].blocks) ? 1 : 0;
+  const ScatterSeg &S = L.seg[si];
+  uint8_t *__restrict__ out = S.out;
+  const void *__restrict__ ind = S.ind;
+  const uint8_t *__restrict__ upd = S.upd;
+  const int ind_dt = S.ind_dt;
+  const int64_t pre = S.pre, axis_len = S.axis_len, post_bytes = S.post_bytes, n_idx = S.n_idx,
+                upd_pre_bytes = S.upd_pre_bytes;
+  const int64_t bx = (int64_t)blockIdx.x - (si ? L.seg[0].blocks : 0);
+  for (int64_t r = bx; r < pre * n_idx; r += S.blocks) {
     const int64_t p = r / n_idx, j = r - p * n_idx;
     const int64_t dst_row = load_index(ind, j, ind_dt);
     if (dst_row < 0 || dst_row >= axis_len) continue;  // out-of-range updates are skipped
@@ -205,20 +227,39 @@ int pad_launch(const LaunchArgs &a) {
 }
 
 // "scatter_rows": ptrs out idx upd; ints ind_dtype pre axis_len post_bytes n_idx
-// [upd_pre_bytes] (absent: the updates are dense)
+// [upd_pre_bytes] (absent: the updates are dense).  Two scatters merged by the
+// planner: 6 ptrs, 12 ints (both with upd_pre_bytes).
 int srows_check(const Step &s) {
-  if (s.buf_ids.size() != 3 || (s.ints.size() != 5 && s.ints.size() != 6))
+  const bool two = s.buf_ids.size() == 6 && s.ints.size() == 12;
+  if (!two && (s.buf_ids.size() != 3 || (s.ints.size() != 5 && s.ints.size() != 6)))
     return fail(NKB_ERR_PLAN, "scatter_rows: bad parameters");
-  if (s.ints.size() == 6 && s.ints[5] < s.ints[4] * s.ints[3])
-    return fail(NKB_ERR_PLAN, "scatter_rows: update blocks overlap");
+  for (size_t o = 0; o < s.ints.size(); o += 6)
+    if (s.ints.size() >= o + 6 && s.ints[o + 5] < s.ints[o + 4] * s.ints[o + 3])
+      return fail(NKB_ERR_PLAN, "scatter_rows: update blocks overlap");
   return NKB_OK;
 }
 int srows_launch(const LaunchArgs &a) {
-  const auto &q = a.step->ints;
-  if (q[1] * q[4] == 0 || q[3] == 0) return NKB_OK;
-  const int64_t upd_pre = q.size() == 6 ? q[5] : q[4] * q[3];
-  launch_pdl(a.pdl, scatter_rows_kernel, grid_for(q[1] * q[4], a.device, 32), 128, 0, a.stream, (uint8_t *)a.ptrs[0],
-             a.ptrs[1], (int)q[0], (const uint8_t *)a.ptrs[2], q[1], q[2], q[3], q[4], upd_pre);
+  const auto &all = a.step->ints;
+  ScatterLaunch L;
+  L.nseg = all.size() == 12 ? 2 : 1;
+  unsigned grid = 0;
+  for (int i = 0; i < L.nseg; ++i) {
+    const int64_t *q = all.data() + 6 * i;
+    ScatterSeg &S = L.seg[i];
+    S.out = static_cast<uint8_t *>(a.ptrs[3 * i]);
+    S.ind = a.ptrs[3 * i + 1];
+    S.upd = static_cast<const uint8_t *>(a.ptrs[3 * i + 2]);
+    S.ind_dt = (int)q[0];
+    S.pre = q[1];
+    S.axis_len = q[2];
+    S.post_bytes = q[3];
+    S.n_idx = q[4];
+    S.upd_pre_bytes = (L.nseg == 2 || all.size() == 6) ? q[5] : q[4] * q[3];
+    S.blocks = (S.pre * S.n_idx == 0 || S.post_bytes == 0) ? 0u : grid_for(S.pre * S.n_idx, a.device, 32);
+    grid += S.blocks;
+  }
+  if (grid == 0) return NKB_OK;
+  launch_pdl(a.pdl, scatter_rows_kernel, grid, 128, 0, a.stream, L);
   return launch_status("scatter_rows_kernel");
 }
 

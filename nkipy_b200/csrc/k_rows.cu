@@ -528,13 +528,36 @@ struct RopeRows {
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// One launch may carry two row sets (the q and the k heads of a decode step):
+// blocks [0, seg[0].blocks) take the first, the rest the second.
+struct RopeSeg {
+  const __nv_bfloat16 *x;
+  const void *w;
+  __nv_bfloat16 *y;
+  int64_t rows, xin, xos;
+  RopeRows rp;
+  unsigned blocks;
+};
+struct RopeLaunch {
+  RopeSeg seg[2];
+  int nseg, cols;
+  float eps;
+};
+
 template <typename TW>
-__global__ void __launch_bounds__(256) rmsnorm_rope_kernel(const __nv_bfloat16 *__restrict__ x,
-                                                           const TW *__restrict__ w, __nv_bfloat16 *__restrict__ y,
-                                                           int64_t rows, int cols, float eps, int64_t xin,
-                                                           int64_t xos, const __grid_constant__ RopeRows rp) {
+__global__ void __launch_bounds__(256) rmsnorm_rope_kernel(const __grid_constant__ RopeLaunch L) {
   pdl_wait();
   pdl_trigger();
+  const int si = (L.nseg > 1 && blockIdx.x >= L.seg[0].blocks) ? 1 : 0;
+  const RopeSeg &S = L.seg[si];
+  const __nv_bfloat16 *__restrict__ x = S.x;
+  const TW *__restrict__ w = static_cast<const TW *>(S.w);
+  __nv_bfloat16 *__restrict__ y = S.y;
+  const int64_t rows = S.rows, xin = S.xin, xos = S.xos;
+  const int cols = L.cols;
+  const float eps = L.eps;
+  const RopeRows &rp = S.rp;
+  const int64_t bx = (int64_t)blockIdx.x - (si ? L.seg[0].blocks : 0);
   const int lane = threadIdx.x % 32;
   const int half = cols / 2;
   const int col = 4 * lane;
@@ -545,7 +568,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_kernel(const __nv_bfloat16 *
     p0 = (rp.pos_dt == NKB_U32 || rp.pos_dt == NKB_U16 || rp.pos_dt == NKB_U8) ? (int64_t)raw : (int64_t)(int32_t)raw;
     p0 = p0 < 0 ? 0 : (p0 >= rp.T ? rp.T - 1 : p0);
   }
-  for (int64_t row = ((int64_t)blockIdx.x * 256 + threadIdx.x) / 32; row < rows; row += (int64_t)gridDim.x * 8) {
+  for (int64_t row = (bx * 256 + threadIdx.x) / 32; row < rows; row += (int64_t)S.blocks * 8) {
     const int64_t ibase = (row / xin) * xos + (row % xin) * cols;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
     if (has) load4(x + ibase + col, v);
@@ -584,9 +607,10 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_kernel(const __nv_bfloat16 *
   }
 }
 
-int rmsnorm_rope_any(const void *x, const void *w, void *y, int wdt, int64_t rows, int64_t cols, float eps,
-                     int64_t xin, int64_t xos, const RopeRows &rp, cudaStream_t st, int dev, bool pdl) {
-  if (rows == 0) return NKB_OK;
+// Validates one row set and fills its launch record (blocks: 8 rows each, at
+// most 8 CTAs per SM).
+static int rope_seg(const void *x, const void *w, void *y, int wdt, int64_t rows, int64_t cols, int64_t xin,
+                    int64_t xos, const RopeRows &rp, int dev, RopeSeg *out) {
   if (cols != 64 && cols != 128) return fail(NKB_ERR_UNSUPPORTED, "rmsnorm_rope_rows: head_dim must be 64 or 128");
   if (xin <= 0 || rows % xin || xos < xin * cols || xos % 4)
     return fail(NKB_ERR_INVALID, "rmsnorm_rope_rows: bad input row blocks");
@@ -596,17 +620,26 @@ int rmsnorm_rope_any(const void *x, const void *w, void *y, int wdt, int64_t row
   if ((((uintptr_t)x | (uintptr_t)y | (uintptr_t)rp.cos | (uintptr_t)rp.sin) & 7) ||
       ((uintptr_t)w & (wdt == NKB_F32 ? 15 : 7)))
     return fail(NKB_ERR_UNSUPPORTED, "rmsnorm_rope_rows: operands not aligned for vector loads");
-  const unsigned grid = (unsigned)std::min<int64_t>((rows + 7) / 8, (int64_t)num_sms(dev) * 8);
-  const auto *xi = static_cast<const __nv_bfloat16 *>(x);
-  auto *yo = static_cast<__nv_bfloat16 *>(y);
+  if (wdt != NKB_BF16 && wdt != NKB_F32) return fail(NKB_ERR_UNSUPPORTED, "rmsnorm_rope_rows: weight dtype");
+  out->x = static_cast<const __nv_bfloat16 *>(x);
+  out->w = w;
+  out->y = static_cast<__nv_bfloat16 *>(y);
+  out->rows = rows;
+  out->xin = xin;
+  out->xos = xos;
+  out->rp = rp;
+  out->blocks = (unsigned)std::min<int64_t>((rows + 7) / 8, (int64_t)num_sms(dev) * 8);
+  return NKB_OK;
+}
+
+static int rope_launch(RopeLaunch &L, int wdt, cudaStream_t st, bool pdl) {
+  unsigned grid = 0;
+  for (int i = 0; i < L.nseg; ++i) grid += L.seg[i].blocks;
+  if (grid == 0) return NKB_OK;
   if (wdt == NKB_BF16)
-    launch_pdl(pdl, rmsnorm_rope_kernel<__nv_bfloat16>, grid, 256, 0, st, xi, static_cast<const __nv_bfloat16 *>(w), yo,
-               rows, (int)cols, eps, xin, xos, rp);
-  else if (wdt == NKB_F32)
-    launch_pdl(pdl, rmsnorm_rope_kernel<float>, grid, 256, 0, st, xi, static_cast<const float *>(w), yo, rows, (int)cols,
-               eps, xin, xos, rp);
+    launch_pdl(pdl, rmsnorm_rope_kernel<__nv_bfloat16>, grid, 256, 0, st, L);
   else
-    return fail(NKB_ERR_UNSUPPORTED, "rmsnorm_rope_rows: weight dtype");
+    launch_pdl(pdl, rmsnorm_rope_kernel<float>, grid, 256, 0, st, L);
   return launch_status("rmsnorm_rope_kernel");
 }
 
@@ -798,25 +831,38 @@ int rmsnorm_launch(const LaunchArgs &a) {
 // "rmsnorm_rope_rows": ptrs x w y cos sin pos (pos unused when has_pos = 0);
 // ints rows cols w_dtype in_block_rows in_block_stride table_stride has_pos
 //      pos_dtype table_rows S H per_token; floats eps.  x, y, cos, sin bf16.
+// Two row sets (6 more ptrs, 12 more ints, the same cols, weight dtype and
+// eps) run in one launch: the planner merges adjacent independent steps.
 int rmsnorm_rope_check(const Step &s) {
-  if (s.buf_ids.size() != 6 || s.ints.size() != 12 || s.floats.size() != 1)
+  const size_t n = s.ints.size() / 12;
+  if ((n != 1 && n != 2) || s.ints.size() != 12 * n || s.buf_ids.size() != 6 * n || s.floats.size() != 1)
     return fail(NKB_ERR_PLAN, "rmsnorm_rope_rows: bad parameters");
+  if (n == 2 && (s.ints[1] != s.ints[13] || s.ints[2] != s.ints[14]))
+    return fail(NKB_ERR_PLAN, "rmsnorm_rope_rows: merged row sets differ in width or weight dtype");
   return NKB_OK;
 }
 int rmsnorm_rope_launch(const LaunchArgs &a) {
-  const auto &q = a.step->ints;
-  RopeRows rp;
-  rp.cos = static_cast<const __nv_bfloat16 *>(a.ptrs[3]);
-  rp.sin = static_cast<const __nv_bfloat16 *>(a.ptrs[4]);
-  rp.tstride = q[5];
-  rp.pos = q[6] ? a.ptrs[5] : nullptr;
-  rp.pos_dt = (int)q[7];
-  rp.T = q[8];
-  rp.S = q[9];
-  rp.H = q[10];
-  rp.per_token = (int)q[11];
-  return rmsnorm_rope_any(a.ptrs[0], a.ptrs[1], a.ptrs[2], (int)q[2], q[0], q[1], a.step->floats[0], q[3], q[4], rp,
-                          a.stream, a.device, a.pdl);
+  const auto &all = a.step->ints;
+  RopeLaunch L;
+  L.nseg = (int)(all.size() / 12);
+  L.cols = (int)all[1];
+  L.eps = a.step->floats[0];
+  for (int i = 0; i < L.nseg; ++i) {
+    const int64_t *q = all.data() + 12 * i;
+    void *const *pp = a.ptrs + 6 * i;
+    RopeRows rp;
+    rp.cos = static_cast<const __nv_bfloat16 *>(pp[3]);
+    rp.sin = static_cast<const __nv_bfloat16 *>(pp[4]);
+    rp.tstride = q[5];
+    rp.pos = q[6] ? pp[5] : nullptr;
+    rp.pos_dt = (int)q[7];
+    rp.T = q[8];
+    rp.S = q[9];
+    rp.H = q[10];
+    rp.per_token = (int)q[11];
+    if (int e = rope_seg(pp[0], pp[1], pp[2], (int)q[2], q[0], q[1], q[3], q[4], rp, a.device, &L.seg[i])) return e;
+  }
+  return rope_launch(L, (int)all[2], a.stream, a.pdl);
 }
 
 // "argmax_rows": ptrs x out; ints rows cols dtype is_max

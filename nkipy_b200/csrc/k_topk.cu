@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -142,6 +143,7 @@ __device__ __forceinline__ void emit(const void *x, int64_t base, int64_t cols, 
 }
 
 constexpr int RES_V = 16;  // 16-byte vectors per thread in the register-resident path
+constexpr int kCand = kPartThreads;  // candidate keys a part may collect (one per thread to rank)
 
 // The kk-th largest (kk <= 32) of the block's per-thread values; every thread
 // of the block calls it and gets the same result.
@@ -233,6 +235,49 @@ __global__ void __launch_bounds__(kPartThreads) topk_part_kernel(const void *__r
       const int64_t i = tid + (int64_t)q * kPartThreads;
       u[q] = i < nv ? pv[i] : make_uint4(0, 0, 0, 0);
     }
+    // k <= 8 (KL == 8): the threshold is the smallest of the eight warps'
+    // maxima.  Those are eight distinct elements, so the part's kk <= 8
+    // largest keys all have images at or above it.  The elements that reach it
+    // (a few dozen on typical rows) are appended to a shared-memory list and
+    // each one's rank among them is counted directly: no merge rounds.  More
+    // than kCand of them (heavy ties, or a warp without elements) take the
+    // list path below.
+    __shared__ uint32_t s_wmax[kPartThreads / 32];
+    __shared__ uint64_t s_keys[kCand];
+    __shared__ int s_n;
+    auto append = [&](uint32_t img, int64_t c) {
+      const int slot = atomicAdd(&s_n, 1);
+      if (slot < kCand) s_keys[slot] = make_key(img, c);
+    };
+    // every thread: the warps' maxima in, the smallest of them out
+    auto warp_threshold = [&](uint32_t tm) -> uint32_t {
+      const uint32_t wm = __reduce_max_sync(0xffffffffu, tm);
+      if (lane == 0) s_wmax[warp] = wm;
+      if (tid == 0) s_n = 0;
+      __syncthreads();
+      uint32_t t8 = s_wmax[0];
+#pragma unroll
+      for (int w = 1; w < kPartThreads / 32; ++w) t8 = min(t8, s_wmax[w]);
+      return t8;
+    };
+    // after the appends: rank the candidates and hand on the kk largest; false
+    // when there were too many (every thread gets the same answer)
+    auto rank_candidates = [&]() -> bool {
+      __syncthreads();
+      const int n = s_n;
+      if (n > kCand) return false;
+      if (tid < n) {
+        const uint64_t key = s_keys[tid];
+        int rank = 0;
+        for (int j = 0; j < n; ++j) rank += s_keys[j] > key ? 1 : 0;
+        if (parts > 1) {
+          if (rank < kk) ws[((int64_t)row * parts + part) * KL + rank] = key;
+        } else if (rank < k) {
+          emit(x, base, cols, esize, key, vals, idx, row * k + rank);
+        }
+      }
+      return true;
+    };
     uint32_t tmax = 0;
 #pragma unroll
     for (int q = 0; q < RES_V; ++q) {
@@ -245,6 +290,25 @@ __global__ void __launch_bounds__(kPartThreads) topk_part_kernel(const void *__r
     }
     for (int64_t c = c0 + nv * per + tid; c < c1; c += kPartThreads)
       tmax = max(tmax, order_bits(load_as_reg(x, base + c, dt), dt));
+    if constexpr (KL == 8) {
+      const uint32_t T8 = warp_threshold(tmax);
+#pragma unroll
+      for (int q = 0; q < RES_V; ++q) {
+        const int64_t i = tid + (int64_t)q * kPartThreads;
+        if (i < nv) {
+          uint32_t img[8];
+          images(u[q], img);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (e < per && img[e] >= T8) append(img[e], c0 + i * per + e);
+        }
+      }
+      for (int64_t c = c0 + nv * per + tid; c < c1; c += kPartThreads) {
+        const uint32_t img = order_bits(load_as_reg(x, base + c, dt), dt);
+        if (img >= T8) append(img, c);
+      }
+      if (rank_candidates()) return;
+    }
     const uint32_t T = block_kth_largest(tmax, kk);
     // every lane runs every q (the vote needs the whole warp); the insert code
     // runs only when some lane of the warp holds a candidate
@@ -406,10 +470,14 @@ int topk_parts(const void *x, int dt, void *vals, uint32_t *idx, int64_t rows, i
   return launch_status("topk_merge_kernel");
 }
 
-// Parts per row for the one-pass path: enough CTAs for four per SM, at least
+// Parts per row for the one-pass path: enough CTAs for eight per SM, at least
 // 4096 columns per part, at most 64 parts.
 int topk_parts_for(int64_t rows, int64_t cols, int sms) {
-  int64_t p = (4 * (int64_t)sms + rows - 1) / std::max<int64_t>(rows, 1);
+  if (const char *e = getenv("NKB_TOPK_PARTS")) {  // override (sweeps); bounded like the default
+    const int64_t v = atoll(e);
+    if (v >= 1) return (int)std::min<int64_t>(std::min<int64_t>(v, 64), std::max<int64_t>(1, cols / 8));
+  }
+  int64_t p = (8 * (int64_t)sms + rows - 1) / std::max<int64_t>(rows, 1);
   p = std::min<int64_t>(p, std::max<int64_t>(1, cols / 4096));
   return (int)std::max<int64_t>(1, std::min<int64_t>(p, 64));
 }

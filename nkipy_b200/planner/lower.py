@@ -295,6 +295,7 @@ class Lowering:
             outputs.append(spec)
             self.bind_output(i, r, spec)
         self.split_k()
+        self.merge_launches()
         lifetimes = self.lifetimes()
         scratch = pack_arena(self.buffers, lifetimes)
         symm = pack_symmetric(self.buffers)
@@ -347,6 +348,54 @@ class Lowering:
             s.bufs.append((ws, 0))
             s.ints += [4, ks]
             s.note += f" split-k {ks}"
+
+    # kernel -> (buffer refs per row set, output ref index within a set, ints per set)
+    _MERGEABLE = {"rmsnorm_rope_rows": (6, 2, 12), "scatter_rows": (3, 0, 6)}
+
+    def merge_launches(self):
+        """Two adjacent launches of the same row kernel, neither of which reads or
+        writes what the other writes, run as one launch over both row sets (the
+        decode step's q and k RMSNorm + rotary, and its K and V cache-row
+        scatters): one launch gap less each."""
+        def disjoint(x, y):
+            return not ({i for i, _ in x.bufs} & {i for i, _ in y.bufs})
+
+        merged = []
+        for s in self.steps:
+            spec = self._MERGEABLE.get(s.kernel)
+            if spec and merged and merged[-1].kernel != s.kernel:
+                # an earlier launch of the same kernel behind at most two steps that
+                # touch none of its buffers (the copy of a mutated cache into its
+                # output): those steps move ahead of it, so that the two meet
+                for back in (2, 3):
+                    if len(merged) >= back and merged[-back].kernel == s.kernel and all(
+                            disjoint(merged[-back], m) for m in merged[-back + 1:]):
+                        merged.append(merged.pop(-back))
+                        break
+            prev = merged[-1] if merged else None
+            if prev is not None and spec and prev.kernel == s.kernel and self._independent(prev, s, spec):
+                nb, _, ni = spec
+                a, b = list(prev.ints), list(s.ints)
+                if s.kernel == "scatter_rows":  # both sets carry upd_pre_bytes
+                    a = a if len(a) == 6 else a + [a[4] * a[3]]
+                    b = b if len(b) == 6 else b + [b[4] * b[3]]
+                if (len(prev.bufs) == nb and len(s.bufs) == nb and len(a) == ni and len(b) == ni
+                        and prev.floats == s.floats
+                        and (s.kernel != "rmsnorm_rope_rows" or (a[1], a[2]) == (b[1], b[2]))):
+                    prev.bufs = prev.bufs + s.bufs
+                    prev.ints = a + b
+                    prev.note = f"{prev.note} | {s.note}"
+                    continue
+            merged.append(s)
+        self.steps = merged
+
+    def _independent(self, a, b, spec) -> bool:
+        """Neither launch touches the other's output buffer (by buffer, not range)."""
+        _, oi, _ = spec
+        if len(a.bufs) != spec[0] or len(b.bufs) != spec[0]:
+            return False
+        out_a, out_b = a.bufs[oi][0], b.bufs[oi][0]
+        return out_a not in {x for x, _ in b.bufs} and out_b not in {x for x, _ in a.bufs}
 
     def _skinny(self, s) -> bool:
         """At most 16 rows of A (K contiguous) against B (N contiguous): the

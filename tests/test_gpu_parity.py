@@ -351,6 +351,9 @@ def test_chunked_linear_attention_benchmark_shape():
         ((8, 32768), 16, BF16, False),  # 16-key lists, 8 parts per row
         ((4, 65536), 32, np.float16, True),  # 32-key lists, 16 parts
         ((6, 20000), 9, np.int32, False),  # ties in every part, 4 parts
+        ((128, 151936), 8, BF16, False),  # the sampling benchmark: candidates ranked in shared memory
+        ((4, 151936), 8, np.int32, False),  # thousands of ties above the threshold: the list path
+        ((2, 3000), 8, BF16, True),  # one part, warps without a full share of the row
     ],
 )
 def test_topk_exact(shape, k, dtype, asc):

@@ -160,9 +160,12 @@ def test_kv_cache_decode_updates_caches_in_place():
     assert [(p.buffers[s.bufs[0][0]].kind, p.buffers[s.bufs[0][0]].index) for s in copies] == [("in", 4), ("in", 5)]
     assert [(p.buffers[s.bufs[1][0]].kind, p.buffers[s.bufs[1][0]].index) for s in copies] == [("out", 1), ("out", 2)]
     assert all(s.ints == [cache_bytes] for s in copies)
-    # the new token's row is scattered into the output buffer; no other step writes a whole cache
-    sc = [s for s in p.steps if s.kernel == "scatter_rows"]
-    assert [p.buffers[s.bufs[0][0]].kind for s in sc] == ["out", "out"]
+    # the new token's rows are scattered into the output buffers (both caches in one
+    # launch: the copy of the V cache moves ahead of the K scatter); no other step
+    # writes a whole cache
+    (sc,) = [s for s in p.steps if s.kernel == "scatter_rows"]
+    assert [p.buffers[sc.bufs[i][0]].kind for i in (0, 3)] == ["out", "out"]
+    assert [p.buffers[sc.bufs[i][0]].index for i in (0, 3)] == [1, 2]
     cache_ins = {i for i, b in enumerate(p.buffers) if b.kind == "in" and b.index in (4, 5)}
     assert not any(s.kernel == "ew" and s.bufs[1][0] in cache_ins for s in p.steps)
     # the attention of the new token is one fused step reading the updated caches
@@ -172,13 +175,15 @@ def test_kv_cache_decode_updates_caches_in_place():
     assert kinds.index("attn_decode") > max(i for i, k in enumerate(kinds) if k == "scatter_rows")
     assert {p.buffers[dec.bufs[i][0]].kind for i in (1, 2)} == {"out"}
     assert dec.ints[:7] == [2, 4, 2, 64, 128, dec.ints[5], 3] and dec.floats == [pytest.approx(128 ** -0.5)]
-    # per-head q/k RMSNorm + rotary: one launch each, rows read in place from the QKV
-    # projection, the cos / sin rows read at the run-time position (no gather launch)
+    # per-head q/k RMSNorm + rotary: one launch over both row sets, rows read in place
+    # from the QKV projection, the cos / sin rows read at the run-time position (no
+    # gather launch)
     width = (4 + 2 * 2) * 128
-    rr = [s for s in p.steps if s.kernel == "rmsnorm_rope_rows"]
-    assert [s.ints[3:5] for s in rr] == [[4, width], [2, width]]
-    assert all(s.ints[6] == 1 and s.ints[8] == 64 and s.ints[11] == 0 for s in rr)
-    assert all(p.buffers[s.bufs[5][0]].kind == "in" and p.buffers[s.bufs[5][0]].index == 6 for s in rr)
+    (rr,) = [s for s in p.steps if s.kernel == "rmsnorm_rope_rows"]
+    sets = [rr.ints[:12], rr.ints[12:]]
+    assert [q[3:5] for q in sets] == [[4, width], [2, width]]
+    assert all(q[6] == 1 and q[8] == 64 and q[11] == 0 for q in sets)
+    assert all(p.buffers[rr.bufs[i][0]].kind == "in" and p.buffers[rr.bufs[i][0]].index == 6 for i in (5, 11))
     # the 2-row projections run on the skinny GEMM (rows as one m16 tile), K split into
     # 64-row ranges: 8 of them, each CTA's fp32 partial rows in the workspace; the
     # weights (inputs no step writes) may be read while the previous kernel drains
@@ -187,7 +192,7 @@ def test_kv_cache_decode_updates_caches_in_place():
     assert [p.buffers[s.bufs[3][0]].nbytes for s in gs] == [8 * 2 * width * 4, 8 * 2 * 512 * 4]
     assert "gemm_bf16" not in kinds
     # the new value row is scattered straight from the projection output
-    assert [len(s.ints) for s in sc] == [5, 6] and sc[1].ints[5] == width * 2
+    assert len(sc.ints) == 12 and sc.ints[11] == width * 2
     assert not {"ew", "take", "rmsnorm_rows"} & set(kinds)
 
 
@@ -197,13 +202,13 @@ def test_cache_prefill_norm_and_rotary_fused_per_token():
     z = np.zeros((B, L, nkv, hd), BF16)
     p = plan_of(W.cached_attention_kernel, np.zeros((B, S, D), BF16), np.zeros((D, (nq + 2 * nkv) * hd), BF16),
                 np.ones(hd, BF16), np.ones(hd, BF16), z, z, None, np.zeros((nq * hd, D), BF16), **kw)
-    rr = [s for s in p.steps if s.kernel == "rmsnorm_rope_rows"]
+    (rr,) = [s for s in p.steps if s.kernel == "rmsnorm_rope_rows"]  # q and k row sets in one launch
     # rows, cols, w dtype, block rows, block stride, table stride, has_pos, pos dtype, table rows, S, H, per token
     width = (nq + 2 * nkv) * hd
-    assert [s.ints for s in rr] == [[B * S * nq, hd, 1, nq, width, hd // 2, 0, 0, S, S, nq, 1],
-                                    [B * S * nkv, hd, 1, nkv, width, hd // 2, 0, 0, S, S, nkv, 1]]
+    assert rr.ints == [B * S * nq, hd, 1, nq, width, hd // 2, 0, 0, S, S, nq, 1,
+                       B * S * nkv, hd, 1, nkv, width, hd // 2, 0, 0, S, S, nkv, 1]
     # the NumPy cos / sin tables (one constant node per use) are read from one constant each
-    assert {p.buffers[s.bufs[i][0]].kind for s in rr for i in (3, 4)} == {"const"}
+    assert {p.buffers[rr.bufs[i][0]].kind for i in (3, 4, 9, 10)} == {"const"}
     assert "take" not in p.kernel_counts()
     # mask[:S, :L] is causal over the first S cache rows: one flash launch reading S keys
     # of the updated caches
