@@ -977,6 +977,10 @@ def run_nkb(args, wl, rank, world, local_rank):
     barrier()
     t0 = time.perf_counter()
     e2e_outs = kernel.run_steps(resident, host_in, host_out, args.steps, split=split, bind=bind)
+    # kernels one execute launches: the kernel nodes of the plan's CUDA graph (a
+    # step may launch none, e.g. a copy onto itself, one or two)
+    kg = kernel.model_ref.graph_kernels
+    kernels_per_step = kg if kg >= 0 else kernel.model_ref.num_launches
     barrier()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     clocks = sampler.stop()
@@ -1047,9 +1051,10 @@ def run_nkb(args, wl, rank, world, local_rank):
         "roofline": roof,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": kernel.model_ref.num_launches * args.steps,
+        "gpu_launches": kernels_per_step * args.steps,
         "clocks": clocks,
-        "launches_per_step": kernel.model_ref.num_launches,
+        "launches_per_step": kernels_per_step,
+        "plan_steps": kernel.model_ref.num_launches,
         "per_launch_ms": {f"{i}:{st['kernel']}": round(ms, 4) for i, (st, ms) in enumerate(zip(plan_steps, step_ms))}
         if len(step_ms) <= 24 else None,
     }
@@ -1102,7 +1107,7 @@ def measure_quick(wl, steps, warmup, local_rank, with_cpu, with_parity):
         "value": round(wl.units_per_step(1) / (ms / 1e3), 4),
         "unit": wl.unit,
         "ms": round(ms, 4),
-        "launches": kernel.model_ref.num_launches,
+        "launches": kernel.model_ref.graph_kernels if kernel.model_ref.graph_kernels >= 0 else kernel.model_ref.num_launches,
         "frac": round(roof["frac"], 3) if roof else None,
     }
     if with_cpu:

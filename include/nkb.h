@@ -100,6 +100,11 @@ NKB_API int nkb_plan_io_bytes(nkb_plan plan, int is_output, int index, size_t *b
 NKB_API int nkb_plan_num_consts(nkb_plan plan, int *n_consts);
 NKB_API int nkb_plan_set_const(nkb_plan plan, int const_index, const void *host, size_t bytes);
 NKB_API int nkb_plan_num_launches(nkb_plan plan, int *n_launches);
+/* Kernels one graph-replayed execute of `plan` launches: the kernel nodes of
+   the CUDA graph captured last (a step may launch none, one or two kernels);
+   -1 before the first graph execute.  No counterpart in the reference (its
+   NEFF is one program). */
+NKB_API int nkb_plan_graph_kernels(nkb_plan plan, int *n_kernels);
 NKB_API int nkb_plan_scratch_bytes(nkb_plan plan, size_t *bytes);
 
 /* ---- execution (Spike::execute spike.h:65-68, nrt_execute model.cpp:90-110).

@@ -37,6 +37,23 @@ struct Params {
   float *ws;  // [B][H][splits][D + 2]: max, sum, output
 };
 
+// out[b, h, d] from the chunks' partials (max, sum, unnormalised output)
+__device__ __forceinline__ void merge_head(const Params &p, int b, int h, int d) {
+  const float *src = p.ws + ((int64_t)b * p.H + h) * p.splits * (D + 2);
+  float M = -INFINITY;
+#pragma unroll 4  // the splits' loads in flight together
+  for (int c = 0; c < p.splits; ++c) M = fmaxf(M, __ldcg(src + c * (D + 2)));
+  float L = 0.f, O = 0.f;
+#pragma unroll 4
+  for (int c = 0; c < p.splits; ++c) {
+    const float mc = __ldcg(src + c * (D + 2));
+    const float f = mc == -INFINITY ? 0.f : __expf(mc - M);
+    L += __ldcg(src + c * (D + 2) + 1) * f;
+    O += __ldcg(src + c * (D + 2) + 2 + d) * f;
+  }
+  p.out[(int64_t)b * p.ob + (int64_t)h * p.oh + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+}
+
 __device__ __forceinline__ int64_t load_pos(const void *p, int dt) {
   const uint32_t raw = load_as_reg(p, 0, dt);
   return (dt == NKB_U32 || dt == NKB_U16 || dt == NKB_U8) ? (int64_t)raw : (int64_t)(int32_t)raw;
@@ -244,20 +261,9 @@ constexpr int smem_bytes() {
 // out[b, h, :] = merge of the chunks' partials
 __global__ void __launch_bounds__(D) attn_decode_combine_kernel(const __grid_constant__ Params p) {
   const int bh = blockIdx.x, d = threadIdx.x;
-  const int b = bh / p.H, h = bh % p.H;
   pdl_wait();
   pdl_trigger();
-  const float *src = p.ws + (int64_t)bh * p.splits * (D + 2);
-  float M = -INFINITY;
-  for (int c = 0; c < p.splits; ++c) M = fmaxf(M, src[c * (D + 2)]);
-  float L = 0.f, O = 0.f;
-  for (int c = 0; c < p.splits; ++c) {
-    const float mc = src[c * (D + 2)];
-    const float f = mc == -INFINITY ? 0.f : __expf(mc - M);
-    L += src[c * (D + 2) + 1] * f;
-    O += src[c * (D + 2) + 2 + d] * f;
-  }
-  p.out[(int64_t)b * p.ob + (int64_t)h * p.oh + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+  merge_head(p, bh / p.H, bh % p.H, d);
 }
 
 // The planner picks the chunk count (chunks of ~512 keys, at least one CTA per

@@ -773,6 +773,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restr
     const int64_t e = i * per, row = e / N, col = e - row * N;
     if (VEC) {
       float4 acc = *reinterpret_cast<const float4 *>(ws + e);
+#pragma unroll 8  // independent loads in flight, not one round trip per split
       for (int s = 1; s < ks; ++s) {
         const float4 v = *reinterpret_cast<const float4 *>(ws + s * plane + e);
         acc.x += v.x;
@@ -788,6 +789,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restr
       *reinterpret_cast<uint2 *>(dst) = u;
     } else {
       float acc = ws[e];
+#pragma unroll 8
       for (int s = 1; s < ks; ++s) acc += ws[s * plane + e];
       C[row * ldc + col] = __float2bfloat16_rn(acc);
     }

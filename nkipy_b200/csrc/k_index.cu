@@ -125,13 +125,24 @@ __global__ void scatter_rows_kernel(const __grid_constant__ ScatterLaunch L) {
   const int64_t pre = S.pre, axis_len = S.axis_len, post_bytes = S.post_bytes, n_idx = S.n_idx,
                 upd_pre_bytes = S.upd_pre_bytes;
   const int64_t bx = (int64_t)blockIdx.x - (si ? L.seg[0].blocks : 0);
+  // 16-byte copies when every row start is 16-byte aligned (a KV-cache row of
+  // 2 KB is one vector per thread), else bytes
+  const bool vec = ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(upd) | (uintptr_t)post_bytes |
+                     (uintptr_t)upd_pre_bytes) & 15) == 0;
   for (int64_t r = bx; r < pre * n_idx; r += S.blocks) {
     const int64_t p = r / n_idx, j = r - p * n_idx;
     const int64_t dst_row = load_index(ind, j, ind_dt);
     if (dst_row < 0 || dst_row >= axis_len) continue;  // out-of-range updates are skipped
     uint8_t *dst = out + (p * axis_len + dst_row) * post_bytes;
     const uint8_t *src = upd + p * upd_pre_bytes + j * post_bytes;
-    for (int64_t b = threadIdx.x; b < post_bytes; b += blockDim.x) dst[b] = src[b];
+    if (vec) {
+      const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+      uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll 4
+      for (int64_t b = threadIdx.x; b < post_bytes / 16; b += blockDim.x) d4[b] = s4[b];
+    } else {
+      for (int64_t b = threadIdx.x; b < post_bytes; b += blockDim.x) dst[b] = src[b];
+    }
   }
 }
 

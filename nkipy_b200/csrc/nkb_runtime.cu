@@ -801,6 +801,7 @@ struct nkb_plan_s {
   static constexpr size_t kGraphCache = 4;
   std::vector<GraphEntry> graphs;
   uint64_t graph_clock = 0;
+  int graph_kernels = -1;  // kernel nodes of the last captured graph (-1: none captured yet)
   ~nkb_plan_s() {
     for (auto &g : graphs)
       if (g.exec) cudaGraphExecDestroy(g.exec);
@@ -847,6 +848,7 @@ int parse_plan(const std::string &text, nkb_plan_s *p) {
       in >> p->scratch;
     } else if (tok == "symm") {
       in >> p->symm;
+
     } else if (tok == "buffers") {
       size_t n;
       in >> n;
@@ -871,6 +873,7 @@ int parse_plan(const std::string &text, nkb_plan_s *p) {
         b.kind = BK_SYMM;
         in >> b.offset >> b.bytes;
         if (b.offset + b.bytes > p->symm) return fail(NKB_ERR_PLAN, "symm buffer exceeds the plan's symmetric region");
+
       } else {
         return fail(NKB_ERR_PLAN, "unknown buffer kind " + kind);
       }
@@ -1000,6 +1003,12 @@ extern "C" int nkb_plan_num_launches(nkb_plan plan, int *n) {
   return NKB_OK;
 }
 
+extern "C" int nkb_plan_graph_kernels(nkb_plan plan, int *n) {
+  if (!plan || !n) return fail(NKB_ERR_INVALID, "NULL argument");
+  *n = plan->graph_kernels;
+  return NKB_OK;
+}
+
 extern "C" int nkb_plan_scratch_bytes(nkb_plan plan, size_t *bytes) {
   if (!plan || !bytes) return fail(NKB_ERR_INVALID, "NULL argument");
   *bytes = plan->scratch;
@@ -1108,6 +1117,20 @@ int execute_on(nkb_plan plan, const std::vector<void *> &base, cudaStream_t stre
       return s;
     }
     if (e != cudaSuccess) return fail(NKB_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    {
+      // the kernels one execute launches (steps may launch none, one or two)
+      size_t nn = 0;
+      int kernels = 0;
+      if (cudaGraphGetNodes(g, nullptr, &nn) == cudaSuccess && nn) {
+        std::vector<cudaGraphNode_t> nodes(nn);
+        if (cudaGraphGetNodes(g, nodes.data(), &nn) == cudaSuccess)
+          for (auto nd : nodes) {
+            cudaGraphNodeType t;
+            if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+          }
+      }
+      plan->graph_kernels = kernels;
+    }
     e = cudaGraphInstantiate(&hit->exec, g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) {

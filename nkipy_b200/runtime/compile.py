@@ -20,7 +20,7 @@ from nkipy_b200.core.trace import NKIPyKernel, _sanitize_array_dtype
 from nkipy_b200.planner import lower
 from nkipy_b200.spike.runtime import write_plan_files
 
-PLANNER_VERSION = "nkb-planner-1"
+PLANNER_VERSION = "nkb-planner-2"
 PLAN_SUFFIX = ".nkbplan"
 
 

@@ -96,6 +96,14 @@ class NkbModel:
         _nkb.call("nkb_plan_scratch_bytes", handle, ctypes.byref(s))
         self.scratch_bytes = s.value
 
+    @property
+    def graph_kernels(self) -> int:
+        """Kernels one graph-replayed execute launches (the kernel nodes of the
+        plan's last captured CUDA graph; -1 before the first one)."""
+        n = ctypes.c_int()
+        _nkb.call("nkb_plan_graph_kernels", self.handle, ctypes.byref(n))
+        return n.value
+
     def __del__(self):
         if self.handle and getattr(_nkb, "_lib", None) is not None:
             try:
