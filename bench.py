@@ -829,8 +829,10 @@ def run_reference(args, wl, rank, world):
 # B200 arm
 # ---------------------------------------------------------------------------
 def profile_traffic(wl):
-    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", f"{wl.dominant}_{wl.name}.md")
+    """dram bytes per launch of the dominant kernel (the whole step for the decode
+    step) from the committed ncu summary."""
+    stem = "attn_decode" if wl.dominant == "*step*" else wl.dominant
+    p = os.path.join(ROOT, "profiles", f"{stem}_{wl.name}.md")
     if not os.path.exists(p):
         return None
     with open(p) as f:
