@@ -140,6 +140,50 @@ __global__ void __launch_bounds__(VT) im2col8_kernel(const __grid_constant__ Par
   }
 }
 
+// 2-D 3x3 windows, stride 1, dilation 1, padding 1, bf16, rows of a multiple
+// of 8 (the common "same" convolution): thread g owns 16-byte group g of every
+// window row of its channel block.  For each (channel, kernel row) it loads the
+// input chunk under its group and the two beside it (16-byte loads, mostly L1
+// hits), and writes the three kernel columns as that chunk shifted by one
+// element left, not at all, and right (funnel shifts): 3 loads and 3 stores per
+// 24 outputs instead of 8 gathered elements per 8.
+constexpr int CB3 = 2;  // channels per block (18 window rows)
+__global__ void __launch_bounds__(VT) im2col3x3_kernel(const __grid_constant__ Params p) {
+  const int G = (int)(p.in[1] / 8), H = (int)p.in[0], W = (int)p.in[1], C = (int)p.C;
+  const int M8 = (int)(p.M / 8);
+  const int g = blockIdx.x * VT + threadIdx.x;  // group over (batch, output row, 8 columns)
+  if (g >= M8) return;
+  const int row = g / G, oc = g - row * G;
+  const int b = row / H, oh = row - b * H;
+  const uint4 *x4 = static_cast<const uint4 *>(p.x);
+  uint4 *cols4 = static_cast<uint4 *>(p.cols);
+  const int64_t M8l = M8;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  const int c0 = blockIdx.y * CB3, c1 = min(C, c0 + CB3);
+  for (int c = c0; c < c1; ++c) {
+#pragma unroll
+    for (int kh = 0; kh < 3; ++kh) {
+      const int ih = oh + kh - 1;
+      uint4 prev = zero, cur = zero, next = zero;
+      if (ih >= 0 && ih < H) {
+        const int64_t rb = (((int64_t)b * C + c) * H + ih) * G;  // 16-byte chunk index of the input row
+        cur = x4[rb + oc];
+        if (oc > 0) prev = x4[rb + oc - 1];
+        if (oc + 1 < G) next = x4[rb + oc + 1];
+      }
+      // kernel column 0: input elements o - 1; 1: o; 2: o + 1
+      const uint4 left = make_uint4(__funnelshift_l(prev.w, cur.x, 16), __funnelshift_l(cur.x, cur.y, 16),
+                                    __funnelshift_l(cur.y, cur.z, 16), __funnelshift_l(cur.z, cur.w, 16));
+      const uint4 right = make_uint4(__funnelshift_r(cur.x, cur.y, 16), __funnelshift_r(cur.y, cur.z, 16),
+                                     __funnelshift_r(cur.z, cur.w, 16), __funnelshift_r(cur.w, next.x, 16));
+      const int64_t kk = (int64_t)c * 9 + kh * 3;
+      cols4[kk * M8l + g] = left;
+      cols4[(kk + 1) * M8l + g] = cur;
+      cols4[(kk + 2) * M8l + g] = right;
+    }
+  }
+}
+
 // "im2col": ptrs x cols; ints n esize B C in[n] ks[n] out[n] stride[n] pad_lo[n] dil[n]
 int check(const Step &s) {
   if (s.buf_ids.size() != 2 || s.ints.size() < 4) return fail(NKB_ERR_PLAN, "im2col: bad parameters");
@@ -179,6 +223,16 @@ int launch(const LaunchArgs &a) {
   if (p.M == 0 || p.KK == 0) return NKB_OK;
   const int64_t rows = p.M / p.out[p.n - 1];
   const int64_t gy = (p.KK + KKB - 1) / KKB;
+  const bool same3 = p.n == 2 && p.esize == 2 && p.ks[0] == 3 && p.ks[1] == 3 && p.stride[0] == 1 &&
+                     p.stride[1] == 1 && p.dil[0] == 1 && p.dil[1] == 1 && p.pad[0] == 1 && p.pad[1] == 1 &&
+                     p.out[0] == p.in[0] && p.out[1] == p.in[1] && p.in[1] % 8 == 0;
+  if (same3 && ((reinterpret_cast<uintptr_t>(p.cols) | reinterpret_cast<uintptr_t>(p.x)) & 15) == 0 &&
+      p.M / 8 <= INT32_MAX / 2 && p.B * p.C * p.in_plane / 8 <= INT32_MAX / 2 && (p.C + CB3 - 1) / CB3 <= 65535 &&
+      !getenv("NKB_IM2COL_INDEX64")) {
+    dim3 grid((unsigned)((p.M / 8 + VT - 1) / VT), (unsigned)((p.C + CB3 - 1) / CB3));
+    im2col3x3_kernel<<<grid, VT, 0, a.stream>>>(p);
+    return launch_status("im2col3x3_kernel");
+  }
   if (p.esize == 2 && p.out[p.n - 1] % 8 == 0 && (reinterpret_cast<uintptr_t>(p.cols) & 15) == 0 &&
       gy <= 65535 && (p.M / 8 + VT - 1) / VT <= INT32_MAX) {
     dim3 grid((unsigned)((p.M / 8 + VT - 1) / VT), (unsigned)gy);

@@ -408,7 +408,7 @@ class Lowering:
         if s.bufs[0][1] % 16 or s.bufs[1][1] % 16 or s.bufs[2][1] % 4:
             return False
         col_blocks = -(-N // 256)
-        splits = -(-2 * self.SMS // col_blocks)
+        splits = max(1, 2 * self.SMS // col_blocks)  # at most one wave of two CTAs per SM
         kc = min(1024, max(64, -(-(-(-K // splits)) // 64) * 64))
         ks = -(-K // kc)
         ws = self.new_buf("tmp", -1, ks * M * N * 4 if ks > 1 else 16)

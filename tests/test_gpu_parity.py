@@ -399,6 +399,10 @@ def test_greedy_sampling_single_device():
         (2, (2, 8, 32, 32), (16, 8, 3, 3), dict(stride=2, padding=1), BF16, True),  # stride 2
         (2, (1, 4, 24, 24), (8, 4, 3, 3), dict(stride=1, padding=2, dilation=2), BF16, False),  # dilation 2
         (3, (1, 2, 6, 7, 16), (4, 2, 2, 3, 3), dict(stride=(1, 2, 1), padding=1), BF16, True),  # 3-D
+        # 3x3 "same" windows (stride 1, padding 1) on rows of 8k: the shifted-chunk kernel
+        (2, (3, 3, 5, 8), (4, 3, 3, 3), dict(stride=1, padding=1), BF16, True),  # odd channels, one chunk
+        (2, (1, 5, 1, 16), (2, 5, 3, 3), dict(stride=1, padding=1), BF16, False),  # one row
+        (2, (2, 6, 7, 40), (8, 6, 3, 3), dict(stride=1, padding=1), BF16, True),  # five chunks per row
     ],
 )
 def test_convolution(n, x_shape, w_shape, kw, dtype, bias):
