@@ -862,9 +862,10 @@ def _outputs_numpy(kernel, outs):
 
 def _roofline(wl, plan_steps, step_ms, ms_per_step, peaks, peak_kind):
     """Roofline record of the dominant kernel: algorithmic work per launch over its
-    mean CUDA-event launch time (``nkb_time_steps``), against the measured peak.
-    Every kernel here is timed on its own (a 0.06 s timed region of ms-long
-    steps), so GEMMs are set against the burst bf16 figure."""
+    mean CUDA-event launch time inside the timed graph replays
+    (``nkb_time_execute_steps``), against the measured peak.  The timed region
+    is short (tens of ms of steps, each after an L2 flush), so GEMMs are set
+    against the burst bf16 figure."""
     dom = [i for i, st in enumerate(plan_steps) if st["kernel"] == wl.dominant]
     if wl.dominant == "*step*":
         # no single dominant launch (the decode step): the whole step's algorithmic
@@ -928,22 +929,39 @@ def run_nkb(args, wl, rank, world, local_rank):
     # clocks are sampled from the start of warm-up to the end of the e2e region
     sampler = ClockSampler(local_rank)
     sampler.start()
+    # Each timed step replays the plan's CUDA graph with an event between every two
+    # launches, so the dominant kernel's launch times come from the timed region
+    # itself.  The decode step's roofline is the whole step: it replays the plain
+    # graph, whose launches overlap (programmatic dependent launch).
+    per_launch = wl.dominant != "*step*"
     for _ in range(args.warmup):
         spike.execute(kernel.model_ref, in_refs, out_refs, use_graph=True)
+        if per_launch:
+            spike.time_execute_steps(kernel.model_ref, in_refs, out_refs)
     barrier()
     total_ms = 0.0
+    step_acc = [0.0] * kernel.model_ref.num_launches
     for _ in range(args.steps):
         flush_l2(flush)
         # every rank's flush is done before any rank starts the step, so the
         # collectives inside it do not time another rank's flush
         barrier()
-        total_ms += spike.time_execute(kernel.model_ref, in_refs, out_refs, warmup=0, iters=1, use_graph=True)[0]
+        if per_launch:
+            t, per = spike.time_execute_steps(kernel.model_ref, in_refs, out_refs)
+            total_ms += t
+            step_acc = [a + b for a, b in zip(step_acc, per)]
+        else:
+            total_ms += spike.time_execute(kernel.model_ref, in_refs, out_refs, warmup=0, iters=1, use_graph=True)[0]
     barrier()
     total_ms = max_over_ranks(total_ms)
     ms_per_step = total_ms / args.steps
 
-    # per-launch times for the roofline of the dominant kernel
-    step_ms = spike.time_steps(kernel.model_ref, in_refs, out_refs, iters=max(3, min(args.steps, 10)))
+    # per-launch times (the roofline of the dominant kernel): inside the timed
+    # steps, else launch by launch after them
+    if per_launch:
+        step_ms = [a / args.steps for a in step_acc]
+    else:
+        step_ms = spike.time_steps(kernel.model_ref, in_refs, out_refs, iters=max(3, min(args.steps, 10)))
     plan_steps = _plan_steps(kernel.plan_path)
 
     # End to end through the public API, pinned host memory.  Per step the job
@@ -1094,15 +1112,27 @@ def measure_quick(wl, steps, warmup, local_rank, with_cpu, with_parity):
     douts = {t.name: dins.get(f"{t.name}.must_alias_input", t) for t in kernel.allocate_output_tensors()}
     outs = {n: t.tensor_ref for n, t in douts.items()}
     flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=f"cuda:{local_rank}")
+    per_launch = wl.dominant != "*step*"  # as in run_nkb
     for _ in range(warmup):
         spike.execute(kernel.model_ref, ins, outs, use_graph=True)
+        if per_launch:
+            spike.time_execute_steps(kernel.model_ref, ins, outs)
     total = 0.0
+    step_acc = [0.0] * kernel.model_ref.num_launches
     for _ in range(steps):
         flush_l2(flush)
         torch.cuda.synchronize()
-        total += spike.time_execute(kernel.model_ref, ins, outs, warmup=0, iters=1, use_graph=True)[0]
+        if per_launch:
+            t, per = spike.time_execute_steps(kernel.model_ref, ins, outs)
+            total += t
+            step_acc = [a + b for a, b in zip(step_acc, per)]
+        else:
+            total += spike.time_execute(kernel.model_ref, ins, outs, warmup=0, iters=1, use_graph=True)[0]
     ms = total / steps
-    step_ms = spike.time_steps(kernel.model_ref, ins, outs, iters=3)
+    if per_launch:
+        step_ms = [a / steps for a in step_acc]
+    else:
+        step_ms = spike.time_steps(kernel.model_ref, ins, outs, iters=3)
     peaks, peak_kind = load_peaks()
     roof = _roofline(wl, _plan_steps(kernel.plan_path), step_ms, ms, peaks, peak_kind)
     out = {

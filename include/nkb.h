@@ -105,6 +105,13 @@ NKB_API int nkb_plan_num_launches(nkb_plan plan, int *n_launches);
    -1 before the first graph execute.  No counterpart in the reference (its
    NEFF is one program). */
 NKB_API int nkb_plan_graph_kernels(nkb_plan plan, int *n_kernels);
+/* One graph replay of `plan` with an event record node before the first step
+   and after each step (graph captured once per io binding and cached):
+   *total_ms = the execute, step_ms[i] (num_launches entries) = step i inside
+   it.  Launches here do not use programmatic dependent launch.  No counterpart
+   in the reference (its profile is per NEFF). */
+NKB_API int nkb_time_execute_steps(nkb_plan plan, const nkb_buf *ins, int n_in, const nkb_buf *outs, int n_out,
+                                   float *total_ms, float *step_ms);
 NKB_API int nkb_plan_scratch_bytes(nkb_plan plan, size_t *bytes);
 
 /* ---- execution (Spike::execute spike.h:65-68, nrt_execute model.cpp:90-110).

@@ -802,9 +802,16 @@ struct nkb_plan_s {
   std::vector<GraphEntry> graphs;
   uint64_t graph_clock = 0;
   int graph_kernels = -1;  // kernel nodes of the last captured graph (-1: none captured yet)
+  // timing graph: the plan with an event record between every two steps (one
+  // io binding, rebuilt when the binding changes)
+  std::vector<void *> tkey;
+  cudaGraphExec_t texec = nullptr;
+  std::vector<cudaEvent_t> tev;
   ~nkb_plan_s() {
     for (auto &g : graphs)
       if (g.exec) cudaGraphExecDestroy(g.exec);
+    if (texec) cudaGraphExecDestroy(texec);
+    for (auto e : tev) cudaEventDestroy(e);
     for (void *p : const_ptrs)
       if (p) cudaFree(p);
     if (arena) cudaFree(arena);
@@ -1180,6 +1187,62 @@ extern "C" int nkb_time_execute(nkb_plan plan, const nkb_buf *ins, int n_in, con
     for (int i = 0; i < iters; ++i) cudaEventElapsedTime(&ms_out[i], ev[i], ev[i + 1]);
   for (auto &x : ev) cudaEventDestroy(x);
   return status;
+}
+
+// One graph replay of the plan with an event record node before the first
+// step and after every step: the execute's time and each step's share of it,
+// measured inside the replayed graph (steps keep their overlap with their
+// neighbours; the event nodes cost well under a microsecond each).
+extern "C" int nkb_time_execute_steps(nkb_plan plan, const nkb_buf *ins, int n_in, const nkb_buf *outs, int n_out,
+                                      float *total_ms, float *step_ms) {
+  if (int s = ensure_init()) return s;
+  if (!plan || !total_ms || !step_ms) return fail(NKB_ERR_INVALID, "bad timing arguments");
+  std::vector<void *> base;
+  if (int s = resolve_io(plan, ins, n_in, outs, n_out, base)) return s;
+  cudaStream_t st = g_rt.stream;
+  const size_t n = plan->steps.size();
+  if (!plan->texec || plan->tkey != base) {
+    if (plan->texec) cudaGraphExecDestroy(plan->texec);
+    plan->texec = nullptr;
+    for (auto e : plan->tev) cudaEventDestroy(e);
+    plan->tev.assign(n + 1, nullptr);
+    for (auto &e : plan->tev) NKB_CUDA_TRY(cudaEventCreate(&e));
+    std::vector<void *> ptrs;
+    cudaGraph_t g = nullptr;
+    NKB_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    int status = NKB_OK;
+    // external record nodes: the events are recorded when the graph runs (a plain
+    // record under capture only orders work inside the graph)
+    cudaEventRecordWithFlags(plan->tev[0], st, cudaEventRecordExternal);
+    for (size_t i = 0; i < n && !status; ++i) {
+      const nkb::Step &stp = plan->steps[i];
+      ptrs.resize(stp.buf_ids.size());
+      for (size_t j = 0; j < stp.buf_ids.size(); ++j)
+        ptrs[j] = static_cast<char *>(base[stp.buf_ids[j]]) + stp.buf_offsets[j];
+      nkb::LaunchArgs a{&stp, ptrs.data(), st, plan->comm ? (void *)plan->comm : nullptr, plan->device};
+      a.pdl = false;  // an event node sits between every two launches
+      status = plan->entries[i]->launch(a);
+      cudaEventRecordWithFlags(plan->tev[i + 1], st, cudaEventRecordExternal);
+    }
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (status) {
+      if (g) cudaGraphDestroy(g);
+      return status;
+    }
+    if (e != cudaSuccess) return fail(NKB_ERR_CUDA, std::string("timing graph capture: ") + cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&plan->texec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+      plan->texec = nullptr;
+      return fail(NKB_ERR_CUDA, std::string("timing graph instantiate: ") + cudaGetErrorString(e));
+    }
+    plan->tkey = base;
+  }
+  NKB_CUDA_TRY(cudaGraphLaunch(plan->texec, st));
+  NKB_CUDA_TRY(cudaStreamSynchronize(st));
+  NKB_CUDA_TRY(cudaEventElapsedTime(total_ms, plan->tev[0], plan->tev[n]));
+  for (size_t i = 0; i < n; ++i) NKB_CUDA_TRY(cudaEventElapsedTime(&step_ms[i], plan->tev[i], plan->tev[i + 1]));
+  return NKB_OK;
 }
 
 namespace {

@@ -77,6 +77,7 @@ def _declare(lib):
         "nkb_plan_set_const": [c_plan, i32, vp, sz],
         "nkb_plan_num_launches": [c_plan, ctypes.POINTER(i32)],
         "nkb_plan_graph_kernels": [c_plan, ctypes.POINTER(i32)],
+        "nkb_time_execute_steps": [c_plan, pp, i32, pp, i32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float)],
         "nkb_plan_scratch_bytes": [c_plan, ctypes.POINTER(sz)],
         "nkb_execute": [c_plan, pp, i32, pp, i32, vp, i32],
         "nkb_time_execute": [c_plan, pp, i32, pp, i32, i32, i32, i32, ctypes.POINTER(ctypes.c_float)],

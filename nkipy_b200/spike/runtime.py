@@ -391,6 +391,15 @@ class Spike:
         _nkb.call("nkb_time_execute", model.handle, I, ni, O, no, warmup, iters, int(use_graph), ms)
         return [float(v) for v in ms]
 
+    def time_execute_steps(self, model: NkbModel, inputs, outputs):
+        """One graph replay with an event between every two launches: (the
+        execute's device time, [each launch's time inside it]) in ms."""
+        I, ni, O, no = self._io_lists(model, inputs, outputs)
+        total = ctypes.c_float()
+        ms = (ctypes.c_float * max(1, model.num_launches))()
+        _nkb.call("nkb_time_execute_steps", model.handle, I, ni, O, no, ctypes.byref(total), ms)
+        return float(total.value), [float(ms[i]) for i in range(model.num_launches)]
+
     def time_steps(self, model: NkbModel, inputs, outputs, iters: int):
         """Mean device time of every launch of the plan (ms), in plan order."""
         I, ni, O, no = self._io_lists(model, inputs, outputs)

@@ -70,3 +70,33 @@ def test_run_steps_with_an_input_updated_in_place():
     want[:, 7:8] = vs[3]
     np.testing.assert_array_equal(a_dev.numpy(), want)
     assert_close(sums, want.sum(axis=1), FP32_RTOL, atol=FP32_RTOL * np.abs(want).sum(axis=1))
+
+
+def test_time_execute_steps_times_each_launch_inside_one_replay():
+    """The bench's timed steps replay a graph with an event between every two
+    launches: the per-launch times add up to the execute's time, and the result
+    is the plan's."""
+    from nkipy_b200.runtime import DeviceKernel, DeviceTensor
+    from nkipy_b200.spike import get_spike_singleton
+
+    rng = np.random.default_rng(52)
+    x = rng.standard_normal((256, 1024), dtype=np.float32)
+    r = rng.standard_normal((256, 1024), dtype=np.float32)
+    w = rng.uniform(0.5, 1.5, 1024).astype(np.float32)
+
+    def kern(x, r, w):  # two launches: a residual + RMSNorm, then a softmax
+        return W.softmax_kernel(W.residual_rmsnorm_kernel(x, r, w))
+
+    k = DeviceKernel.compile_and_load(kern, x, r, w, name="timing_two_launches", is_spmd=False)
+    model = k.model_ref
+    names = [t["name"] for t in model.io["inputs"]]
+    ins = {n: DeviceTensor.from_numpy(a, name=n).tensor_ref for n, a in zip(names, (x, r, w))}
+    outs = {t.name: t.tensor_ref for t in k.allocate_output_tensors()}
+    spike = get_spike_singleton()
+    for _ in range(2):
+        total, per = spike.time_execute_steps(model, ins, outs)
+    assert len(per) == model.num_launches >= 2
+    assert all(p > 0 for p in per) and total > 0
+    assert abs(sum(per) - total) <= 0.05 * total + 1e-3
+    got = np.frombuffer(spike.tensor_read(next(iter(outs.values()))), np.float32)[: x.size].reshape(x.shape)
+    assert_close(got, O.softmax(O.residual_rmsnorm(x, r, w)), 1e-5, atol=1e-6)
