@@ -185,7 +185,7 @@ __device__ __forceinline__ void compute(const Instr I, const uint32_t (&A)[VEC],
 }
 
 // Opcodes applied to the accumulator in place (operand a = the previous result).
-__device__ __forceinline__ bool inplace_op(uint8_t op) {
+__host__ __device__ __forceinline__ bool inplace_op(uint8_t op) {
   return op == FADD || op == FSUB || op == FMUL || op == FDIV || op == FNEG || op == FEXP || op == FRCP ||
          op == FMAX || op == FMIN;
 }
@@ -373,8 +373,10 @@ __device__ __forceinline__ void store_run(void *p, int64_t off, int64_t st, int 
 // an operand equal to the previous instruction's destination is read from
 // the accumulator (that result, still in registers); a result is written to
 // the shared-memory register file only when a later instruction reads it
-// from there or it is the output.
-constexpr uint8_t F_A_ACC = 1, F_B_ACC = 2, F_C_ACC = 4, F_KEEP = 8;
+// from there or it is the output.  F_INPL: the instruction reads the
+// accumulator as operand a and its opcode is applied in place (one test in
+// the kernel instead of the opcode comparisons of inplace_op).
+constexpr uint8_t F_A_ACC = 1, F_B_ACC = 2, F_C_ACC = 4, F_KEEP = 8, F_INPL = 16;
 constexpr int kPre = 4;  // inputs whose run is loaded up front, all loads in flight together
 
 template <typename IDX, int VEC>
@@ -387,7 +389,8 @@ __global__ void __launch_bounds__(256) ew_rows_kernel(const __grid_constant__ Pa
   const IDX runs_per_row = inner / VEC;
   const IDX runs = (IDX)(p.n / VEC);
   for (IDX c = (IDX)blockIdx.x * blockDim.x + threadIdx.x; c < runs; c += (IDX)gridDim.x * blockDim.x) {
-    const IDX row = c / runs_per_row;
+    // one axis (a collapsed dense view): no division per run
+    const IDX row = last == 0 ? (IDX)0 : c / runs_per_row;
     const IDX col = (c - row * runs_per_row) * VEC;
     int64_t oo = p.out_off + (int64_t)col * p.out_strides[last];
     int64_t base[kMaxIn];
@@ -422,7 +425,7 @@ __global__ void __launch_bounds__(256) ew_rows_kernel(const __grid_constant__ Pa
         }
 #pragma unroll
         for (int v = 0; v < VEC; ++v) d[v] = (uint32_t)(int32_t)(id + (I.a == last ? v : 0));
-      } else if ((I.pad & F_A_ACC) && inplace_op(I.op)) {
+      } else if (I.pad & F_INPL) {
         uint32_t B[VEC];
         if (I.bimm) {
 #pragma unroll
@@ -514,6 +517,8 @@ void set_row_flags(Params &p) {
     def[J.dst] = j;
   }
   if (p.prog[p.n_instr - 1].dst != p.out_reg && def[p.out_reg] >= 0) p.prog[def[p.out_reg]].pad |= F_KEEP;
+  for (int j = 0; j < p.n_instr; ++j)
+    if ((p.prog[j].pad & F_A_ACC) && inplace_op(p.prog[j].op)) p.prog[j].pad |= F_INPL;
 }
 
 // Step layout ("ew"):
