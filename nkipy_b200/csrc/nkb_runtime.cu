@@ -1192,7 +1192,7 @@ extern "C" int nkb_time_execute(nkb_plan plan, const nkb_buf *ins, int n_in, con
 // One graph replay of the plan with an event record node before the first
 // step and after every step: the execute's time and each step's share of it,
 // measured inside the replayed graph (steps keep their overlap with their
-// neighbours; the event nodes cost well under a microsecond each).
+// neighbours; the event nodes add a few microseconds to the replay).
 extern "C" int nkb_time_execute_steps(nkb_plan plan, const nkb_buf *ins, int n_in, const nkb_buf *outs, int n_out,
                                       float *total_ms, float *step_ms) {
   if (int s = ensure_init()) return s;
