@@ -2,7 +2,7 @@
 // 8 token rows against a weight matrix), bf16 in, fp32 accumulation, bf16 out.
 // Bound by the one read of B.  The rows of A, zero-padded to 16, are the A
 // fragment of bf16 mma.sync m16n8k16; B (K x N, N contiguous, as the traced
-// `x @ W` holds it) streams through a 4-stage cp.async ring of 32 k-rows x 256
+// `x @ W` holds it) streams through a 6-stage cp.async ring of 32 k-rows x 256
 // columns (16 KB, XOR-swizzled) and is read transposed by ldmatrix as the B
 // fragment.  CTA (column block, k-range): four warps of 64 columns each;
 // enough k-ranges for two CTAs per SM, their fp32 partial rows summed by
@@ -22,7 +22,7 @@ using namespace mma;
 constexpr int THREADS = 128;                 // four warps
 constexpr int NT = 256;                      // output columns per CTA
 constexpr int KT = 32;                       // k rows per stage
-constexpr int STAGES = 4;
+constexpr int STAGES = 6;
 constexpr int STAGE_BYTES = KT * NT * 2;     // 16 KB
 constexpr int MAX_KC = 1024;                 // k per CTA at most (A slice 16 x 1024 bf16 = 32 KB)
 
