@@ -434,6 +434,26 @@ __global__ void __launch_bounds__(256) rmsnorm_bf16_kernel(const __nv_bfloat16 *
   }
 }
 
+// CTAs of `kernel` (256 threads, no dynamic shared memory) that fit on the
+// device at once: a grid-stride kernel sized to this runs in one wave (a
+// larger grid leaves a second, partial wave of whole CTAs at the end).
+template <class K>
+int64_t resident_ctas_256(K kernel, int device) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<const void *, int>, int>> cache;
+  const void *key = reinterpret_cast<const void *>(kernel);
+  std::lock_guard<std::mutex> lk(mu);
+  for (auto &e : cache)
+    if (e.first.first == key && e.first.second == device) return (int64_t)num_sms(device) * e.second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, 256, 0) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    n = 1;
+  }
+  cache.push_back({{key, device}, n});
+  return (int64_t)num_sms(device) * n;
+}
+
 template <typename T, typename TW, bool RES, bool SUM_OUT>
 int rmsnorm_dispatch3(const void *x, const void *r, const void *w, void *y, void *hs, int64_t rows, int64_t cols,
                       float eps, int64_t xin, int64_t xos, cudaStream_t st, int device) {
@@ -450,13 +470,16 @@ int rmsnorm_dispatch3(const void *x, const void *r, const void *w, void *y, void
   if constexpr (sizeof(T) == 2) {
     const bool a16 = aligned && cols % 8 == 0 && xos % 8 == 0 && cols > 1024 && cols <= 8192;
     if (a16) {
-      const unsigned g = (unsigned)std::min<int64_t>(rows, (int64_t)num_sms(device) * 8);
+      auto go = [&](auto kern) {
+        const unsigned g = (unsigned)std::min<int64_t>(rows, resident_ctas_256(kern, device));
+        kern<<<g, 256, 0, st>>>(xi, ri, wi, yo, ho, rows, (int)cols, eps, xin, xos);
+      };
       if (cols <= 2048)
-        rmsnorm_bf16_kernel<1, TW, RES, SUM_OUT><<<g, 256, 0, st>>>(xi, ri, wi, yo, ho, rows, (int)cols, eps, xin, xos);
+        go(rmsnorm_bf16_kernel<1, TW, RES, SUM_OUT>);
       else if (cols <= 4096)
-        rmsnorm_bf16_kernel<2, TW, RES, SUM_OUT><<<g, 256, 0, st>>>(xi, ri, wi, yo, ho, rows, (int)cols, eps, xin, xos);
+        go(rmsnorm_bf16_kernel<2, TW, RES, SUM_OUT>);
       else
-        rmsnorm_bf16_kernel<4, TW, RES, SUM_OUT><<<g, 256, 0, st>>>(xi, ri, wi, yo, ho, rows, (int)cols, eps, xin, xos);
+        go(rmsnorm_bf16_kernel<4, TW, RES, SUM_OUT>);
       return launch_status("rmsnorm_rows");
     }
   }
