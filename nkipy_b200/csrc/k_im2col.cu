@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(VT) im2col8_kernel(const __grid_constant__ Par
 // 24 outputs instead of 8 gathered elements per 8.
 constexpr int CB3 = 2;  // channels per block (18 window rows)
 __global__ void __launch_bounds__(VT) im2col3x3_kernel(const __grid_constant__ Params p) {
-  const int G = (int)(p.in[1] / 8), H = (int)p.in[0], W = (int)p.in[1], C = (int)p.C;
+  const int G = (int)(p.in[1] / 8), H = (int)p.in[0], C = (int)p.C;
   const int M8 = (int)(p.M / 8);
   const int g = blockIdx.x * VT + threadIdx.x;  // group over (batch, output row, 8 columns)
   if (g >= M8) return;
