@@ -113,6 +113,12 @@ NKB_API int nkb_plan_graph_kernels(nkb_plan plan, int *n_kernels);
 NKB_API int nkb_time_execute_steps(nkb_plan plan, const nkb_buf *ins, int n_in, const nkb_buf *outs, int n_out,
                                    float *total_ms, float *step_ms);
 NKB_API int nkb_plan_scratch_bytes(nkb_plan plan, size_t *bytes);
+/* Counters of the elementwise chain compiler since the library was loaded:
+   distinct "ew" steps compiled to a specialised kernel (NVRTC, at plan load),
+   steps it could not compile (they run on the interpreter kernel) and launches
+   of compiled kernels.  Any pointer may be NULL.  No counterpart in the
+   reference (neuronx-cc compiles the whole kernel ahead of time). */
+NKB_API int nkb_ew_compiler_stats(int64_t *compiled, int64_t *failed, int64_t *launched);
 
 /* ---- execution (Spike::execute spike.h:65-68, nrt_execute model.cpp:90-110).
  * ins/outs are indexed as the plan's io table; stream may be NULL (the

@@ -6,8 +6,11 @@
 // Every operand is a strided view of a device buffer (offset + per-axis
 // element strides), so broadcast (stride 0), transpose, slice and reshape of
 // a dense buffer cost no copy: they are folded into the view by the planner.
-// The group's arithmetic is a short register program decoded per launch from
-// the kernel parameters (a fixed kernel, not generated code).  Registers hold
+// The group's arithmetic is a short register program.  Where the innermost
+// axis has a multiple of 4 elements the step normally runs on a kernel
+// compiled for it at plan load (ew_jit.cu); this file is the interpreter that
+// decodes the program from the kernel parameters at run time, used for the
+// other steps and wherever the compiler does not take one.  Registers hold
 // 32-bit values: fp32 for every float dtype, int32 for integers and bools.
 // Results of bf16/fp16-typed nodes are rounded to that type after each node
 // (program op RBF/RF16), matching NumPy's per-op rounding.
@@ -19,50 +22,10 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "ew_program.cuh"
 
 namespace nkb {
 namespace ew {
-
-constexpr int kMaxIn = 8;
-constexpr int kMaxRank = 6;
-constexpr int kMaxInstr = 64;
-constexpr int kRegs = 24;
-constexpr int kVec = 4;
-
-enum Opcode : uint8_t {
-  NOP = 0, LD = 1, CF = 2, CI = 3, IOTA = 4,
-  FADD = 10, FSUB, FMUL, FDIV, FPOW, FMAX, FMIN, FATAN2, FREM,
-  FNEG = 20, FABS, FEXP, FLOG, FSQRT, FRSQRT, FTANH, FSIN, FCOS, FFLOOR, FCEIL, FSIGN, RBF, RF16, FRCP,
-  FEQ = 40, FNE, FLT, FLE, FGT, FGE,
-  IADD = 50, ISUB, IMUL, IDIV, IMAX, IMIN, IAND, IOR, IXOR, IREM,
-  ISHL = 64, ISHR = 65,
-  INEG = 60, IABS, INOT, ISIGN,
-  IEQ = 70, INE, ILT, ILE, IGT, IGE, ULT, ULE, UGT, UGE, UDIV, UMAX, UMIN, UREM,
-  SEL = 90,
-  F2I = 100, I2F, U2F, F2U, INZ, FNZ
-};
-
-struct Instr {
-  uint8_t op, dst, a, b, c;
-  uint8_t rnd;   // round the result: 1 = to bf16, 2 = to fp16
-  uint8_t bimm;  // 1 = operand b is the immediate `imm`
-  uint8_t pad;
-  uint32_t imm;
-};
-
-struct Params {
-  int n_in, rank, n_instr, out_dtype, out_reg, contig;
-  int64_t n;
-  int64_t shape[kMaxRank];
-  void *out;
-  int64_t out_off;
-  int64_t out_strides[kMaxRank];
-  const void *in[kMaxIn];
-  int in_dtype[kMaxIn];
-  int64_t in_off[kMaxIn];
-  int64_t in_strides[kMaxIn][kMaxRank];
-  Instr prog[kMaxInstr];
-};
 
 __device__ __forceinline__ float rnd_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 __device__ __forceinline__ float rnd_f16(float x) { return __half2float(__float2half_rn(x)); }
@@ -521,6 +484,8 @@ void set_row_flags(Params &p) {
     if ((p.prog[j].pad & F_A_ACC) && inplace_op(p.prog[j].op)) p.prog[j].pad |= F_INPL;
 }
 
+void parse(const Step &s, void *const *ptrs, Params &p);
+
 // Step layout ("ew"):
 //   ptrs:  out, in_0 .. in_{n_in-1}
 //   ints:  n_in rank n_instr out_dtype out_reg contig n
@@ -544,12 +509,16 @@ int check(const Step &s) {
     if (q[0] == IOTA && (q[2] < 0 || q[2] >= rank)) return fail(NKB_ERR_PLAN, "ew: iota axis out of range");
   }
   if (s.ints[4] < 0 || s.ints[4] >= kRegs) return fail(NKB_ERR_PLAN, "ew: output register out of range");
+  // compile the step's specialised kernel now, outside any graph capture
+  Params p;
+  parse(s, nullptr, p);
+  if (p.n > 0 && p.shape[p.rank - 1] % 4 == 0) jit_prepare(p);
   return NKB_OK;
 }
 
-int launch(const LaunchArgs &a) {
-  const Step &s = *a.step;
-  Params p;
+// Fills the launch parameters from a checked step (device pointers from
+// `ptrs`, or none when only the program and view are needed).
+void parse(const Step &s, void *const *ptrs, Params &p) {
   memset(&p, 0, sizeof(p));
   const int64_t *q = s.ints.data();
   p.n_in = (int)q[0];
@@ -563,9 +532,9 @@ int launch(const LaunchArgs &a) {
   for (int d = 0; d < p.rank; ++d) p.shape[d] = *q++;
   p.out_off = *q++;
   for (int d = 0; d < p.rank; ++d) p.out_strides[d] = *q++;
-  p.out = a.ptrs[0];
+  p.out = ptrs ? ptrs[0] : nullptr;
   for (int k = 0; k < p.n_in; ++k) {
-    p.in[k] = a.ptrs[1 + k];
+    p.in[k] = ptrs ? ptrs[1 + k] : nullptr;
     p.in_dtype[k] = (int)*q++;
     p.in_off[k] = *q++;
     for (int d = 0; d < p.rank; ++d) p.in_strides[k][d] = *q++;
@@ -582,7 +551,17 @@ int launch(const LaunchArgs &a) {
     I.bimm = (uint8_t)q[7];
     q += 8;
   }
+}
+
+int launch(const LaunchArgs &a) {
+  Params p;
+  parse(*a.step, a.ptrs, p);
   if (p.n == 0) return NKB_OK;
+  if (p.shape[p.rank - 1] % 4 == 0) {
+    bool launched = false;
+    if (int st = jit_launch(p, a.stream, a.device, &launched)) return st;
+    if (launched) return NKB_OK;
+  }
   const int threads = 256;
   int64_t blocks = (p.n + (int64_t)threads * kVec - 1) / ((int64_t)threads * kVec);
   const int64_t cap = (int64_t)num_sms(a.device) * 16;
