@@ -142,7 +142,7 @@ __device__ __forceinline__ void emit(const void *x, int64_t base, int64_t cols, 
   for (int b = 0; b < esize; ++b) dst[b] = src[b];
 }
 
-constexpr int RES_V = 16;  // 16-byte vectors per thread in the register-resident path
+constexpr int RES_V = 8;  // 16-byte vectors per thread in the register-resident path (64 registers: 4 CTAs per SM)
 constexpr int kCand = kPartThreads;  // candidate keys a part may collect (one per thread to rank)
 
 // The kk-th largest (kk <= 32) of the block's per-thread values; every thread
