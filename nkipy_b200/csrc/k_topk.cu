@@ -182,6 +182,10 @@ __global__ void __launch_bounds__(kPartThreads) topk_part_kernel(const void *__r
                                                                  uint64_t *__restrict__ ws,
                                                                  void *__restrict__ vals, uint32_t *__restrict__ idx) {
   __shared__ uint64_t s_cand[kPartThreads / 32][KL];
+  // the merge kernel may launch once every part CTA has started (it waits for
+  // this grid to finish before reading the lists); the last wave is partial,
+  // so its CTAs find free slots
+  pdl_trigger();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t row = blockIdx.x / parts;
   const int part = (int)(blockIdx.x % parts);
@@ -425,6 +429,7 @@ __global__ void __launch_bounds__(256, 1) topk_merge_kernel(const void *__restri
                                                          const uint64_t *__restrict__ ws, void *__restrict__ vals,
                                                          uint32_t *__restrict__ idx) {
   __shared__ uint64_t s_out[8][KL];
+  pdl_wait();  // launched early (programmatic dependent launch): the parts' lists are complete after this
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + warp;
   if (row >= rows) return;  // whole warps leave together
@@ -466,7 +471,9 @@ int topk_parts(const void *x, int dt, void *vals, uint32_t *idx, int64_t rows, i
                                                                           vec, resident, ws, vals, idx);
   if (int e = launch_status("topk_part_kernel")) return e;
   if (parts == 1) return NKB_OK;
-  topk_merge_kernel<KL><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, rows, cols, parts, k, esize, ws, vals, idx);
+  if (cudaError_t e = launch_pdl(true, topk_merge_kernel<KL>, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, st, x, rows,
+                                 cols, parts, k, esize, (const uint64_t *)ws, vals, idx))
+    return fail(NKB_ERR_CUDA, std::string("topk_merge_kernel: ") + cudaGetErrorString(e));
   return launch_status("topk_merge_kernel");
 }
 
