@@ -93,6 +93,9 @@ NKB_API int nkb_copy(nkb_buf dst, size_t dst_offset, nkb_buf src, size_t src_off
 
 /* ---- plans (Spike::load_model / unload_model / get_tensor_info,
  *      spike.h:46-48,69; NrtModel model.h:12-55) ---------------------------- */
+/* `device` must be the device nkb_init was given (NKB_ERR_INVALID otherwise);
+   it is made current on the calling thread, and the plan's fused elementwise
+   steps are compiled and loaded there (nkb_ew_compiler_stats). */
 NKB_API int nkb_plan_load(const char *text, size_t len, int device, nkb_plan *out);
 NKB_API int nkb_plan_free(nkb_plan plan);
 NKB_API int nkb_plan_num_io(nkb_plan plan, int *n_inputs, int *n_outputs);

@@ -931,6 +931,10 @@ extern "C" int nkb_plan_load(const char *text, size_t len, int device, nkb_plan 
   if (!text || !out) return fail(NKB_ERR_INVALID, "NULL argument");
   auto p = std::make_unique<nkb_plan_s>();
   p->device = device;
+  if (device != g_rt.device) return fail(NKB_ERR_INVALID, "plan device differs from the runtime's device");
+  // the plan's device current on this thread: kernel checks below may load
+  // modules (the elementwise chain compiler) into its context
+  NKB_CUDA_TRY(cudaSetDevice(device));
   if (int s = parse_plan(std::string(text, len), p.get())) return s;
   for (const auto &st : p->steps) {
     const nkb::KernelEntry *e = nkb::find_kernel(st.kernel);
