@@ -207,7 +207,7 @@ bool known_op(int op) {
 }
 
 struct Kernel {
-  std::string key;                      // the generated source
+  std::string key;                      // the generated kernel body (without the prelude)
   std::vector<char> cubin;              // empty when compilation failed
   struct Loaded {
     CUcontext ctx;
@@ -268,7 +268,8 @@ const Driver &driver() {
 
 std::mutex g_mu;
 Nvrtc g_rtc;
-std::map<std::string, Kernel *> g_by_source;
+std::map<std::string, Kernel *> g_by_source;                // generated kernel body -> kernel
+std::map<std::vector<int64_t>, Kernel *> g_by_step;          // step parameters -> kernel (null: not taken)
 int64_t g_compiled = 0, g_failed = 0, g_launched = 0;
 
 bool enabled() {
@@ -345,8 +346,7 @@ std::string generate(const Params &p, int *vec_out) {
 
   std::string s;
   s.reserve(4096);
-  s += "#define VEC " + std::to_string(vec) + "\n";
-  s += kPrelude;
+  s += "// VEC " + std::to_string(vec) + "\n";  // the body alone is the cache key; the prelude is added to compile
   s += "extern \"C\" __global__ void __launch_bounds__(256) ew_gen(const EwPtrs p) {\n";
   s += std::string("  typedef ") + (small ? "int" : "long long") + " IDX;\n";
   const int64_t rpr = inner / vec, runs = p.n / vec;
@@ -423,7 +423,8 @@ std::string generate(const Params &p, int *vec_out) {
 bool compile(Kernel *k) {
   if (!open_nvrtc()) return false;
   nvrtcProgram prog = nullptr;
-  if (g_rtc.create(&prog, k->key.c_str(), "ew_gen.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS) return false;
+  const std::string src = "#define VEC " + std::to_string(k->vec) + "\n" + kPrelude + k->key;
+  if (g_rtc.create(&prog, src.c_str(), "ew_gen.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS) return false;
   const char *opts[] = {"--gpu-architecture=sm_100a", "--fmad=false", "-default-device", "--std=c++17"};
   const nvrtcResult r = g_rtc.compile(prog, 4, opts);
   bool ok = r == NVRTC_SUCCESS;
@@ -432,7 +433,7 @@ bool compile(Kernel *k) {
     g_rtc.log_size(prog, &n);
     std::string log(n, '\0');
     if (n) g_rtc.log(prog, &log[0]);
-    if (getenv("NKB_EW_JIT_LOG")) fprintf(stderr, "nkb ew compiler:\n%s\n%s\n", k->key.c_str(), log.c_str());
+    if (getenv("NKB_EW_JIT_LOG")) fprintf(stderr, "nkb ew compiler:\n%s\n%s\n", src.c_str(), log.c_str());
   } else {
     size_t n = 0;
     ok = g_rtc.cubin_size(prog, &n) == NVRTC_SUCCESS && n > 0;
@@ -466,40 +467,50 @@ const Kernel::Loaded *function_in_context(Kernel *k, bool may_load) {
   return &k->loaded.back();
 }
 
-Kernel *kernel_for(const Params &p) {
+// The kernel for a step (its parameters `ints`, parsed into `p`), generated
+// and compiled on first sight; null when the compiler does not take the step.
+Kernel *kernel_for(const Params &p, const std::vector<int64_t> &ints) {
+  auto hit = g_by_step.find(ints);
+  if (hit != g_by_step.end()) return hit->second;
   int vec = 8;
-  std::string src = generate(p, &vec);
-  if (src.empty()) return nullptr;
-  auto it = g_by_source.find(src);
-  if (it != g_by_source.end()) return it->second;
-  Kernel *k = new Kernel;  // kept for the life of the process (modules stay loaded)
-  k->key = std::move(src);
-  k->vec = vec;
-  k->runs = p.n / vec;
-  if (compile(k)) ++g_compiled;
-  else ++g_failed;
-  g_by_source.emplace(k->key, k);
+  std::string body = generate(p, &vec);
+  Kernel *k = nullptr;
+  if (!body.empty()) {
+    auto it = g_by_source.find(body);
+    if (it != g_by_source.end()) {
+      k = it->second;
+    } else {
+      k = new Kernel;  // kept for the life of the process (modules stay loaded)
+      k->key = std::move(body);
+      k->vec = vec;
+      k->runs = p.n / vec;
+      if (compile(k)) ++g_compiled;
+      else ++g_failed;
+      g_by_source.emplace(k->key, k);
+    }
+  }
+  g_by_step.emplace(ints, k);
   return k;
 }
 
 }  // namespace
 
-int jit_prepare(const Params &p) {
+int jit_prepare(const Params &p, const std::vector<int64_t> &ints) {
   if (!enabled()) return 0;
   std::lock_guard<std::mutex> lk(g_mu);
-  Kernel *k = kernel_for(p);
+  Kernel *k = kernel_for(p, ints);
   if (!k) return 0;
   return function_in_context(k, true) ? 1 : 0;
 }
 
-int jit_launch(const Params &p, cudaStream_t stream, int device, bool *launched) {
+int jit_launch(const Params &p, const std::vector<int64_t> &ints, cudaStream_t stream, int device, bool *launched) {
   *launched = false;
   if (!enabled()) return NKB_OK;
   Kernel::Loaded fn{};  // copied under the lock (the vector may grow later)
   Kernel *k = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_mu);
-    k = kernel_for(p);
+    k = kernel_for(p, ints);
     if (!k) return NKB_OK;
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {

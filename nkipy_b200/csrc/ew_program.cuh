@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <vector>
+
 namespace nkb {
 namespace ew {
 
@@ -57,8 +59,10 @@ struct Params {
 // interpreter (*launched false: compiler unavailable or disabled, or the module
 // not loaded in this context while a graph is being captured); it returns a
 // status.
-int jit_prepare(const Params &p);
-int jit_launch(const Params &p, cudaStream_t stream, int device, bool *launched);
+// `ints` are the step's integer parameters (from which `p` was parsed): the
+// key of the per-step kernel cache.
+int jit_prepare(const Params &p, const std::vector<int64_t> &ints);
+int jit_launch(const Params &p, const std::vector<int64_t> &ints, cudaStream_t stream, int device, bool *launched);
 
 }  // namespace ew
 }  // namespace nkb

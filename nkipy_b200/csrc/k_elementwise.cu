@@ -512,7 +512,7 @@ int check(const Step &s) {
   // compile the step's specialised kernel now, outside any graph capture
   Params p;
   parse(s, nullptr, p);
-  if (p.n > 0 && p.shape[p.rank - 1] % 4 == 0) jit_prepare(p);
+  if (p.n > 0 && p.shape[p.rank - 1] % 4 == 0) jit_prepare(p, s.ints);
   return NKB_OK;
 }
 
@@ -559,7 +559,7 @@ int launch(const LaunchArgs &a) {
   if (p.n == 0) return NKB_OK;
   if (p.shape[p.rank - 1] % 4 == 0) {
     bool launched = false;
-    if (int st = jit_launch(p, a.stream, a.device, &launched)) return st;
+    if (int st = jit_launch(p, a.step->ints, a.stream, a.device, &launched)) return st;
     if (launched) return NKB_OK;
   }
   const int threads = 256;
