@@ -772,14 +772,28 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restr
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = i * per, row = e / N, col = e - row * N;
     if (VEC) {
+      // up to kFlight partials loaded before the first add (one round trip),
+      // then summed in split order
+      constexpr int kFlight = 16;
       float4 acc = *reinterpret_cast<const float4 *>(ws + e);
-#pragma unroll 8  // independent loads in flight, not one round trip per split
-      for (int s = 1; s < ks; ++s) {
-        const float4 v = *reinterpret_cast<const float4 *>(ws + s * plane + e);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+      float4 v[kFlight - 1];
+#pragma unroll
+      for (int s = 1; s < kFlight; ++s)
+        if (s < ks) v[s - 1] = *reinterpret_cast<const float4 *>(ws + s * plane + e);
+#pragma unroll
+      for (int s = 1; s < kFlight; ++s)
+        if (s < ks) {
+          acc.x += v[s - 1].x;
+          acc.y += v[s - 1].y;
+          acc.z += v[s - 1].z;
+          acc.w += v[s - 1].w;
+        }
+      for (int s = kFlight; s < ks; ++s) {
+        const float4 u = *reinterpret_cast<const float4 *>(ws + s * plane + e);
+        acc.x += u.x;
+        acc.y += u.y;
+        acc.z += u.z;
+        acc.w += u.w;
       }
       __nv_bfloat16 *dst = C + row * ldc + col;
       const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
