@@ -122,6 +122,12 @@ NKB_API int nkb_plan_scratch_bytes(nkb_plan plan, size_t *bytes);
    of compiled kernels.  Any pointer may be NULL.  No counterpart in the
    reference (neuronx-cc compiles the whole kernel ahead of time). */
 NKB_API int nkb_ew_compiler_stats(int64_t *compiled, int64_t *failed, int64_t *launched);
+/* Compiles the specialised kernel of one elementwise step from its integer
+   parameters (the "ew" step of a plan), without a device: warms the compiler's
+   cache before nkb_plan_load, and lets a host without a GPU check that a
+   plan's chains compile.  *taken = 1 when the step will run on a compiled
+   kernel.  No counterpart in the reference. */
+NKB_API int nkb_ew_compile_step(const int64_t *ints, size_t n_ints, int *taken);
 
 /* ---- execution (Spike::execute spike.h:65-68, nrt_execute model.cpp:90-110).
  * ins/outs are indexed as the plan's io table; stream may be NULL (the

@@ -503,6 +503,13 @@ int jit_prepare(const Params &p, const std::vector<int64_t> &ints) {
   return function_in_context(k, true) ? 1 : 0;
 }
 
+int jit_compiled(const Params &p, const std::vector<int64_t> &ints) {
+  if (!enabled()) return 0;
+  std::lock_guard<std::mutex> lk(g_mu);
+  Kernel *k = kernel_for(p, ints);
+  return k && !k->cubin.empty() ? 1 : 0;
+}
+
 int jit_launch(const Params &p, const std::vector<int64_t> &ints, cudaStream_t stream, int device, bool *launched) {
   *launched = false;
   if (!enabled()) return NKB_OK;

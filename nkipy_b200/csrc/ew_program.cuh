@@ -63,6 +63,9 @@ struct Params {
 // key of the per-step kernel cache.
 int jit_prepare(const Params &p, const std::vector<int64_t> &ints);
 int jit_launch(const Params &p, const std::vector<int64_t> &ints, cudaStream_t stream, int device, bool *launched);
+// 1 when the step's kernel is compiled (compiling it now if needed; no device
+// is used), 0 when the compiler does not take the step or cannot compile it.
+int jit_compiled(const Params &p, const std::vector<int64_t> &ints);
 
 }  // namespace ew
 }  // namespace nkb

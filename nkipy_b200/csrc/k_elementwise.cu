@@ -613,4 +613,23 @@ int launch(const LaunchArgs &a) {
 
 NKB_REGISTER_KERNEL("ew", ew::launch, ew::check);
 
+// Compiles the specialised kernel of one "ew" step from its integer
+// parameters (the step layout above), with NVRTC only: no device, no runtime
+// initialisation.  *taken = 1 when the chain compiler took and compiled it.
+extern "C" NKB_API int nkb_ew_compile_step(const int64_t *ints, size_t n_ints, int *taken) {
+  if (!ints || !taken) return fail(NKB_ERR_INVALID, "NULL argument");
+  *taken = 0;
+  if (n_ints < 7 || ints[0] < 0 || ints[0] > ew::kMaxIn) return fail(NKB_ERR_PLAN, "ew: short or bad parameter list");
+  Step s;
+  s.kernel = "ew";
+  s.ints.assign(ints, ints + n_ints);
+  s.buf_ids.assign((size_t)ints[0] + 1, 0);
+  s.buf_offsets.assign((size_t)ints[0] + 1, 0);
+  if (int st = ew::check(s)) return st;
+  ew::Params p;
+  ew::parse(s, nullptr, p);
+  if (p.n > 0 && p.shape[p.rank - 1] % 4 == 0) *taken = ew::jit_compiled(p, s.ints);
+  return NKB_OK;
+}
+
 }  // namespace nkb

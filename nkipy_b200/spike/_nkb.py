@@ -80,6 +80,7 @@ def _declare(lib):
         "nkb_time_execute_steps": [c_plan, pp, i32, pp, i32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float)],
         "nkb_plan_scratch_bytes": [c_plan, ctypes.POINTER(sz)],
         "nkb_ew_compiler_stats": [ctypes.POINTER(ctypes.c_int64)] * 3,
+        "nkb_ew_compile_step": [ctypes.POINTER(ctypes.c_int64), sz, ctypes.POINTER(i32)],
         "nkb_execute": [c_plan, pp, i32, pp, i32, vp, i32],
         "nkb_time_execute": [c_plan, pp, i32, pp, i32, i32, i32, i32, ctypes.POINTER(ctypes.c_float)],
         "nkb_synchronize": [],
