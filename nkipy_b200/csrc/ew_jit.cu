@@ -210,7 +210,7 @@ struct Kernel {
   std::string key;                      // the generated kernel body (without the prelude)
   std::vector<char> cubin;              // empty when compilation failed
   struct Loaded {
-    CUcontext ctx;
+    unsigned long long ctx_id;  // cuCtxGetId: unique for the process's life (a handle may be reused)
     CUfunction fn;
     int per_sm;  // resident CTAs of 256 threads per SM
   };
@@ -235,6 +235,7 @@ struct Nvrtc {
 struct Driver {
   bool ok = false;
   decltype(&cuCtxGetCurrent) ctx_current = nullptr;
+  decltype(&cuCtxGetId) ctx_id = nullptr;
   decltype(&cuModuleLoadData) module_load = nullptr;
   decltype(&cuModuleGetFunction) module_function = nullptr;
   decltype(&cuLaunchKernel) launch = nullptr;
@@ -256,12 +257,13 @@ const Driver &driver() {
       return p;
     };
     d.ctx_current = reinterpret_cast<decltype(d.ctx_current)>(get("cuCtxGetCurrent"));
+    d.ctx_id = reinterpret_cast<decltype(d.ctx_id)>(get("cuCtxGetId"));
     d.module_load = reinterpret_cast<decltype(d.module_load)>(get("cuModuleLoadData"));
     d.module_function = reinterpret_cast<decltype(d.module_function)>(get("cuModuleGetFunction"));
     d.launch = reinterpret_cast<decltype(d.launch)>(get("cuLaunchKernel"));
     d.error_string = reinterpret_cast<decltype(d.error_string)>(get("cuGetErrorString"));
     d.occupancy = reinterpret_cast<decltype(d.occupancy)>(get("cuOccupancyMaxActiveBlocksPerMultiprocessor"));
-    d.ok = d.ctx_current && d.module_load && d.module_function && d.launch && d.error_string && d.occupancy;
+    d.ok = d.ctx_current && d.ctx_id && d.module_load && d.module_function && d.launch && d.error_string && d.occupancy;
   });
   return d;
 }
@@ -453,9 +455,10 @@ const Kernel::Loaded *function_in_context(Kernel *k, bool may_load) {
   const Driver &drv = driver();
   if (k->cubin.empty() || !drv.ok) return nullptr;
   CUcontext ctx = nullptr;
-  if (drv.ctx_current(&ctx) != CUDA_SUCCESS || !ctx) return nullptr;
+  unsigned long long id = 0;
+  if (drv.ctx_current(&ctx) != CUDA_SUCCESS || !ctx || drv.ctx_id(ctx, &id) != CUDA_SUCCESS) return nullptr;
   for (auto &e : k->loaded)
-    if (e.ctx == ctx) return &e;
+    if (e.ctx_id == id) return &e;
   if (!may_load) return nullptr;
   CUmodule mod = nullptr;
   CUfunction fn = nullptr;
@@ -463,7 +466,7 @@ const Kernel::Loaded *function_in_context(Kernel *k, bool may_load) {
   if (drv.module_function(&fn, mod, "ew_gen") != CUDA_SUCCESS) return nullptr;
   int per_sm = 0;
   if (drv.occupancy(&per_sm, fn, 256, 0) != CUDA_SUCCESS || per_sm < 1) per_sm = 1;
-  k->loaded.push_back(Kernel::Loaded{ctx, fn, per_sm});
+  k->loaded.push_back(Kernel::Loaded{id, fn, per_sm});
   return &k->loaded.back();
 }
 
