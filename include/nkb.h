@@ -119,7 +119,8 @@ NKB_API int nkb_plan_scratch_bytes(nkb_plan plan, size_t *bytes);
 /* Counters of the elementwise chain compiler since the library was loaded:
    distinct "ew" steps compiled to a specialised kernel (NVRTC, at plan load),
    steps it could not compile (they run on the interpreter kernel) and launches
-   of compiled kernels.  Any pointer may be NULL.  No counterpart in the
+   of compiled kernels issued by nkb_execute (a graph replay re-runs captured
+   launches without counting them).  Any pointer may be NULL.  No counterpart in the
    reference (neuronx-cc compiles the whole kernel ahead of time). */
 NKB_API int nkb_ew_compiler_stats(int64_t *compiled, int64_t *failed, int64_t *launched);
 /* Compiles the specialised kernel of one elementwise step from its integer

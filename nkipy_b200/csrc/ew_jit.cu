@@ -560,7 +560,8 @@ int jit_launch(const Params &p, const std::vector<int64_t> &ints, cudaStream_t s
 
 // Counters of the chain compiler since the library was loaded: programs
 // compiled, programs the compiler could not take (left to the interpreter) and
-// launches of compiled kernels.
+// launches of compiled kernels (issued, or captured into a graph; replays of a
+// captured graph are not counted).
 extern "C" NKB_API int nkb_ew_compiler_stats(int64_t *compiled, int64_t *failed, int64_t *launched) {
   std::lock_guard<std::mutex> lk(nkb::ew::g_mu);
   if (compiled) *compiled = nkb::ew::g_compiled;
